@@ -1,0 +1,446 @@
+#!/usr/bin/env python3
+"""Benchmark of the hot path: the batched fp32 CLIP ViT-B/32 forward.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (headline): ViT-B/32 fp32 forward over a batch of 256 images of
+3x224x224, sharded by image over N GPUs (one process per GPU; weights
+uploaded on rank 0 and broadcast once over NVLink by NCCL; no collective in
+the step). A step is one forward of the whole batch. Synthetic data: weights
+N(0, 0.02) (LayerNorm gamma 1 + N(0, 0.02)), seed 0; pixels U[-1, 1), seed 1.
+
+  value        images/s of the whole job, inputs already in HBM, device time
+               (CUDA events on the library stream), max over ranks.
+  e2e          the same through the host-buffer C entry point
+               tcg_vit_encode_batch: pinned pixels copied in and embeddings
+               copied out inside every timed step.
+  roofline     the tensor-core GEMM (dominant kernel): algorithmic GEMM
+               FLOP / its CUDA-event time, against the 3xTF32 peak derived
+               from the measured bf16 peak.
+  cpu_baseline the reference's own tc_vit_encode (oracle/_ref, built from the
+               reference sources) on the host cores, one image per thread.
+  aux          the K-quant rows: Q4_K / Q6_K dequant of 14336x4096 and the
+               fused dequant-matvec (4096x14336 Q4_K, 128256x4096 Q6_K), GB/s
+               against the measured HBM peak.
+
+--impl reference times the reference's CPU implementation alone (rank 0).
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [ROOT, os.path.join(ROOT, "roofline.c_b200")]
+
+import numpy as np  # noqa: E402
+
+import tcg_gguf as G  # noqa: E402
+
+CACHE = os.environ.get("TCG_BENCH_CACHE", "/tmp/roofline_b200_bench")
+PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+# DRAM bytes per launch of the dominant kernel from an ncu capture (see the
+# profiles/ summary of the same workload); None until captured.
+NCU_GEMM_TRAFFIC_PER_LAUNCH = None
+
+
+def peaks():
+    try:
+        with open(PEAKS_FILE) as fh:
+            p = json.load(fh)
+        return p, "measured"
+    except (OSError, ValueError):
+        return FALLBACK_PEAKS, "fallback"
+
+
+def vit_flops_per_image(cfg):
+    """Algorithmic FLOPs of one image: (gemm, attention, projection)."""
+    D, F, T, L = cfg["d_model"], cfg["d_ffn"], cfg["n_token"], cfg["n_layer"]
+    G2, K0 = (cfg["image"] // cfg["patch"]) ** 2, 3 * cfg["patch"] ** 2
+    gemm = 2 * G2 * D * K0 + L * (2 * T * D * 3 * D + 2 * T * D * D + 2 * 2 * T * D * F)
+    attn = L * 4 * T * T * D
+    proj = 2 * D * cfg["d_out"]
+    return gemm, attn, proj
+
+
+# ------------------------------------------------------------ distribution
+
+class Dist:
+    def __init__(self, want_gpus):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        if self.world != want_gpus:
+            raise SystemExit(f"--gpus {want_gpus} but WORLD_SIZE={self.world}: launch with torchrun")
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as td
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            td.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+            self.td = td
+
+    def barrier(self):
+        if self.world > 1:
+            self.td.barrier()
+
+    def max(self, x: float) -> float:
+        if self.world == 1:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64)
+        self.td.all_reduce(t, op=self.td.ReduceOp.MAX)
+        return float(t.item())
+
+    def bcast_bytes(self, b: bytes) -> bytes:
+        if self.world == 1:
+            return b
+        obj = [b]
+        self.td.broadcast_object_list(obj, src=0)
+        return obj[0]
+
+    def close(self):
+        if self.world > 1:
+            self.td.destroy_process_group()
+
+
+# ------------------------------------------------------------ clock sampler
+
+class Clocks:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.rows = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 8:
+                self.rows.append(parts)
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=5)
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        pw = [float(r[2]) for r in self.rows if r[2].replace(".", "", 1).isdigit()]
+        reasons = set()
+        for r in self.rows:
+            for name, val in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"),
+                                 r[4:8]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(pw) if pw else None, "samples": len(self.rows), "reasons": sorted(reasons)}
+
+
+# ------------------------------------------------------------ CPU reference
+
+def reference_rate(path, cfg, pixels, threads, rounds, warmup_rounds=0):
+    """Images/s of the reference's own tc_vit_encode (oracle/_ref when built,
+    else the oracle's C restatement): `threads` host threads, one image each
+    per round. Returns (images/s, kind, seconds)."""
+    import oracle
+    kind = "reference" if oracle.have_ref() else "port"
+    if kind == "reference":
+        models = [oracle.RefVit(path) for _ in range(threads)]
+        run = lambda i, px: models[i].encode(px, cfg["d_out"])        # noqa: E731
+    else:
+        w = G.make_vit_weights(cfg, 0)
+        port = oracle.PortVit(cfg, w)
+        run = lambda i, px: port.forward(px, taps=False)               # noqa: E731
+
+    def one_round(r):
+        ts = [threading.Thread(target=run, args=(i, pixels[(r * threads + i) % len(pixels)]))
+              for i in range(threads)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+
+    for r in range(warmup_rounds):
+        one_round(r)
+    t0 = time.perf_counter()
+    for r in range(rounds):
+        one_round(warmup_rounds + r)
+    dt = time.perf_counter() - t0
+    if kind == "reference":
+        for m in models:
+            m.close()
+    return threads * rounds / dt, kind, dt
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ------------------------------------------------------------ K-quant rows
+
+def kquant_aux(tcg, hbm_peak):
+    """GB/s of dequant (14336x4096) and fused matvec; each launch timed alone
+    with events, L2 flushed (a 256 MB memset) between launches."""
+    L = tcg.lib()
+    flush = tcg.DeviceBuffer(256 << 20)
+    out = {}
+
+    def timed(fn, reps=10):
+        ts = []
+        for _ in range(2):
+            fn()
+        for _ in range(reps):
+            tcg.check(L.tcg_memset(flush.ptr, 0, flush.nbytes))
+            ts.append(tcg.time_ms(fn, 2, 3))
+        return statistics.median(ts)
+
+    for name, qt, bb in (("q4k", G.Q4_K, 144), ("q6k", G.Q6_K, 210)):
+        rows, cols = 14336, 4096
+        raw = G.make_kquant(qt, rows, cols, seed=2)
+        n = rows * cols
+        with tcg.DeviceBuffer.from_array(raw) as src, tcg.DeviceBuffer(n * 4) as dst:
+            ms = timed(lambda: tcg.check(L.tcg_dequant(dst.ptr, src.ptr, n, qt)))
+        nbytes = n // 256 * bb + n * 4
+        gbs = nbytes / ms / 1e6
+        out[f"dequant_{name}_{rows}x{cols}"] = {"GB/s": round(gbs, 1), "us": round(ms * 1e3, 2),
+                                               "bytes": nbytes, "frac": round(gbs / hbm_peak, 3)}
+    for name, qt, bb, N, K, seed in (("q4k", G.Q4_K, 144, 4096, 14336, 3), ("q6k", G.Q6_K, 210, 128256, 4096, 5)):
+        raw = G.make_kquant(qt, N, K, seed=seed)
+        x = np.random.default_rng(seed + 1).standard_normal(K).astype(np.float32)
+        with tcg.DeviceBuffer.from_array(raw) as w, tcg.DeviceBuffer.from_array(x) as xb, \
+                tcg.DeviceBuffer(N * 4) as y:
+            ms = timed(lambda: tcg.check(L.tcg_matvec_q(y.ptr, w.ptr, xb.ptr, N, K, qt)))
+        nbytes = N * K // 256 * bb + K * 4 + N * 4
+        gbs = nbytes / ms / 1e6
+        out[f"matvec_{name}_{N}x{K}"] = {"GB/s": round(gbs, 1), "us": round(ms * 1e3, 2),
+                                        "bytes": nbytes, "frac": round(gbs / hbm_peak, 3)}
+    flush.close()
+    return out
+
+
+# ------------------------------------------------------------ our arm
+
+def run_ours(args, dist):
+    import tcg
+    pk, pk_kind = peaks()
+    cfg = G.vit_config(args.model)
+    if args.batch % dist.world:
+        raise SystemExit(f"batch {args.batch} does not shard over {dist.world} GPUs")
+    per = args.batch // dist.world
+    if dist.rank == 0:
+        G.cached_vit_gguf(CACHE, args.model, 0)
+    dist.barrier()
+    path, cfg = G.cached_vit_gguf(CACHE, args.model, 0)
+
+    tcg.init(dist.local)
+    L = tcg.lib()
+    model = tcg.VitModel(path)
+    if dist.world > 1:
+        import ctypes
+        uid = None
+        if dist.rank == 0:
+            buf = ctypes.create_string_buffer(128)
+            tcg.check(L.tcg_nccl_unique_id(buf), "tcg_nccl_unique_id")
+            uid = buf.raw
+        uid = dist.bcast_bytes(uid)
+        model.upload_bcast(per, dist.rank, dist.world, uid)
+    else:
+        model.upload(per)
+
+    pixels = G.make_pixels(args.batch, cfg["image"], 1)
+    shard = np.ascontiguousarray(pixels[dist.rank * per:(dist.rank + 1) * per])
+    d_out = cfg["d_out"]
+    dpx = tcg.DeviceBuffer.from_array(shard)
+    dout = tcg.DeviceBuffer(per * d_out * 4)
+
+    def step():
+        tcg.check(L.tcg_vit_encode_device(model.dev, dpx.ptr, per, dout.ptr), "tcg_vit_encode_device")
+
+    for _ in range(args.warmup):
+        step()
+    tcg.sync()
+    dist.barrier()
+    clocks = Clocks(dist.local)
+    clocks.start()
+    time.sleep(0.2)
+    tcg.sync()
+    dist.barrier()
+    ms = tcg.time_ms(lambda: [step() for _ in range(args.steps)], 0, 1) / args.steps
+    tcg.sync()
+    dist.barrier()
+
+    # end to end through the host-buffer entry point, pinned buffers
+    hpx = tcg.HostBuffer(shard.shape)
+    hpx.array[...] = shard
+    hout = tcg.HostBuffer((per, d_out))
+
+    def e2e_step():
+        tcg.check(L.tcg_vit_encode_batch(model.dev, hpx.ptr, per, hout.ptr, None, None), "tcg_vit_encode_batch")
+
+    for _ in range(args.warmup):
+        e2e_step()
+    dist.barrier()
+    e2e_ms = tcg.time_ms(lambda: [e2e_step() for _ in range(args.steps)], 4, 5) / args.steps
+    dist.barrier()
+    clk = clocks.stop()
+    emb_ok = bool(np.isfinite(hout.array).all())
+
+    # per-kernel-class device time: the same forward, eagerly, with events
+    L.tcg_vit_profile_begin()
+    for _ in range(args.steps):
+        step()
+    import ctypes as C
+    kms, kcount = (C.c_float * 4)(), (C.c_int * 4)()
+    tcg.check(L.tcg_vit_profile_end(kms, kcount), "profile")
+    launches = L.tcg_vit_launches_per_forward(model.dev)
+    derr = L.tcg_device_error()
+
+    ms_max = dist.max(ms)
+    e2e_max = dist.max(e2e_ms)
+    gemm_ms = dist.max(kms[0] / args.steps)
+    prof_step = dist.max(sum(kms) / args.steps)
+
+    result = None
+    if dist.rank == 0:
+        gf, af, pf = vit_flops_per_image(cfg)
+        gemm_launches = kcount[0] / args.steps
+        tf_peak = pk["bf16_tflops_sustained"] / 2.0 / 3.0
+        achieved = gf * per / (gemm_ms * 1e-3) / 1e12           # per rank, slowest rank's time
+        traffic = NCU_GEMM_TRAFFIC_PER_LAUNCH
+        result = {
+            "metric": "ViT-B/32 images/sec",
+            "value": round(args.batch / (ms_max * 1e-3), 2),
+            "unit": "images/s",
+            "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_max, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic: weights N(0,0.02) seed 0 (LN gamma 1+N(0,0.02)); pixels U[-1,1) seed 1",
+            "config": {"workload": f"{args.model} fp32 forward, {args.batch} images 3x224x224 sharded by image",
+                       "model": args.model, "global_batch": args.batch, "per_gpu_batch": per,
+                       "seq_len": cfg["n_token"], "parallelism": f"dp{dist.world} (image shards; weights "
+                       "broadcast once by NCCL)",
+                       "l2": "inputs larger than L2: 703 MB of tf32 hi/lo weights + activations per step",
+                       "gemm": "3xTF32 on tcgen05 (3 tf32 MMAs per product, fp32 TMEM accumulator)"},
+            "roofline": {"kernel": "gemm_tf32x3 (tcgen05, TMA-fed)", "bound": "tensor",
+                         "achieved": round(achieved, 1), "peak": round(tf_peak, 1), "unit": "TFLOP/s",
+                         "frac": round(achieved / tf_peak, 3),
+                         "peak_basis": f"{pk_kind} bf16_tflops_sustained {pk['bf16_tflops_sustained']} / 2 "
+                                       "(tf32 rate) / 3 (MMAs per fp32 product)",
+                         "traffic": traffic,
+                         "flop_per_launch": round(gf * per / gemm_launches) if gemm_launches else None,
+                         "avg_launch_ms": round(gemm_ms / gemm_launches, 4) if gemm_launches else None,
+                         "share_of_step": round(gemm_ms / prof_step, 3) if prof_step else None,
+                         "kernel_ms_per_step": {"gemm": round(kms[0] / args.steps, 4),
+                                                "attention": round(kms[1] / args.steps, 4),
+                                                "layernorm": round(kms[2] / args.steps, 4),
+                                                "other": round(kms[3] / args.steps, 4)}},
+            "e2e": {"value": round(args.batch / (e2e_max * 1e-3), 2), "unit": "images/s",
+                    "h2d_bytes_per_step": int(shard.nbytes) * dist.world,
+                    "d2h_bytes_per_step": per * d_out * 4 * dist.world,
+                    "api": "tcg_vit_encode_batch (host buffers, page-locked)"},
+            "gpu_launches": launches * args.steps,
+            "clocks": clk,
+            "model_flop_per_image": gf + af + pf,
+            "device_error": derr, "outputs_finite": emb_ok,
+        }
+    model.close()
+    dpx.close()
+    dout.close()
+    hpx.close()
+    hout.close()
+
+    if dist.rank == 0 and dist.world == 1:
+        if not args.no_aux:
+            result["aux"] = kquant_aux(tcg, pk["hbm_gbs"])
+            result["aux"]["hbm_peak_gbs"] = pk["hbm_gbs"]
+            result["aux"]["peak_kind"] = pk_kind
+        if not args.no_cpu:
+            threads = host_threads()
+            rate, kind, dt = reference_rate(path, cfg, pixels[:threads], threads, rounds=1)
+            result["cpu_baseline"] = {"value": round(rate, 4), "unit": "images/s", "cores": threads,
+                                      "kind": kind, "sample": f"{threads} images of the batch, one per "
+                                      f"thread, one round ({dt:.1f} s wall)"}
+    return result
+
+
+def run_reference(args, dist):
+    """The reference's own CPU forward (oracle/_ref) on the host cores; rank 0."""
+    if dist.rank != 0:
+        return None
+    cfg = G.vit_config(args.model)
+    path, cfg = G.cached_vit_gguf(CACHE, args.model, 0)
+    threads = host_threads()
+    pixels = G.make_pixels(min(args.batch, max(threads, 1)), cfg["image"], 1)
+    steps = args.steps
+    rate, kind, dt = reference_rate(path, cfg, pixels, threads, rounds=steps, warmup_rounds=args.warmup)
+    return {
+        "impl": "reference",
+        "metric": "ViT-B/32 images/sec", "value": round(rate, 4), "unit": "images/s",
+        "n_gpus": dist.world, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / steps * 1e3, 2), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: weights N(0,0.02) seed 0 (LN gamma 1+N(0,0.02)); pixels U[-1,1) seed 1",
+        "config": {"workload": f"{args.model} fp32 forward, {args.batch} images 3x224x224 sharded by image",
+                   "model": args.model, "global_batch": args.batch, "seq_len": cfg["n_token"],
+                   "parallelism": "host threads"},
+        "cpu_baseline": {"value": round(rate, 4), "unit": "images/s", "cores": threads, "kind": kind,
+                         "sample": f"each step: {threads} images of the batch, one per thread"},
+        "e2e": {"value": round(rate, 4), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--model", default="vit-b32", choices=sorted(G.VIT_CONFIGS))
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--no-aux", action="store_true", help="skip the K-quant rows")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    dist = Dist(args.gpus)
+    try:
+        res = run_reference(args, dist) if args.impl == "reference" else run_ours(args, dist)
+        if dist.rank == 0 and res is not None:
+            print(json.dumps(res), flush=True)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,172 @@
+/* tcg.h -- the C ABI of the B200 compute layer (libtcg.so).
+ *
+ * roofline.c has no backend layer (its ARCHITECTURE.md plans one as a
+ * vtable); this is it, for one target: hand-written sm_100a kernels behind
+ * plain C entry points taking raw pointers and sizes. Every function here
+ * takes DEVICE pointers unless its comment says host. The host-buffer API of
+ * the reference (dequant.h, vit.h) is built on top of these.
+ *
+ * Conventions
+ *   - bool return; on false, tcg_last_error() holds a one-line reason
+ *     (the reference's bool + err[256] convention, src/gguf.h:143).
+ *   - All work is queued on the calling thread's library stream (created by
+ *     tcg_init, replaceable with tcg_set_stream) and is asynchronous unless
+ *     stated; tcg_sync() waits for it.
+ *   - Nothing here falls back to the CPU: without a usable device every
+ *     compute entry point returns false.
+ */
+#ifndef TCG_H
+#define TCG_H
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "arena.h"
+#include "gguf.h"
+#include "vit.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------- status */
+
+const char *tcg_last_error(void);
+const char *tcg_version(void);
+
+/* --------------------------------------------------- device / stream */
+
+/* Select `device` for this thread and create its stream. Idempotent. */
+bool  tcg_init(int device);
+int   tcg_device_count(void);
+int   tcg_sm_count(void);
+bool  tcg_sync(void);
+void *tcg_get_stream(void);                 /* cudaStream_t                  */
+bool  tcg_set_stream(void *stream);         /* NULL: back to the library's   */
+
+/* Device-side failure flag shared by every kernel that waits on a barrier:
+ * non-zero after a bounded wait gave up. Reading it synchronizes. */
+int   tcg_device_error(void);
+bool  tcg_clear_device_error(void);
+
+/* -------------------------------------------------- memory plumbing */
+
+void *tcg_malloc(size_t bytes);
+bool  tcg_free(void *p);
+void *tcg_host_alloc(size_t bytes);         /* page-locked host memory       */
+bool  tcg_host_free(void *p);
+bool  tcg_h2d(void *dst, const void *src, size_t bytes);   /* async          */
+bool  tcg_d2h(void *dst, const void *src, size_t bytes);   /* async          */
+bool  tcg_d2d(void *dst, const void *src, size_t bytes);   /* async          */
+bool  tcg_memset(void *dst, int value, size_t bytes);      /* async          */
+
+/* CUDA events on the library stream, slots 0..63. elapsed() waits for b. */
+bool  tcg_event_record(int slot);
+float tcg_event_elapsed_ms(int slot_a, int slot_b);
+
+/* ------------------------------------------------------ device arena
+ * The reference's arena discipline (src/arena.h:37-69) over one device
+ * allocation: bump, LIFO mark/release, no per-object free. */
+
+typedef struct {
+    unsigned char *base;   /* device address                                */
+    size_t cap, used, peak;
+    const char *name;
+} tcg_arena_t;
+
+tcg_arena_t tcg_arena_create(size_t cap, const char *name);
+void   tcg_arena_destroy(tcg_arena_t *a);
+bool   tcg_arena_ok(const tcg_arena_t *a);
+void  *tcg_arena_alloc(tcg_arena_t *a, size_t size, size_t align);
+size_t tcg_arena_mark(const tcg_arena_t *a);
+void   tcg_arena_release(tcg_arena_t *a, size_t mark);
+void   tcg_arena_reset(tcg_arena_t *a);
+
+/* ------------------------------------------------ dequant (src/dequant.c)
+ * Replaces tc_dequant (src/dequant.c:40-63) on device buffers: F32 copy,
+ * F16 exact conversion (tc_f16_to_f32, src/dequant.c:5-38, for every one of
+ * the 65,536 inputs), and the Q4_K / Q6_K arms the reference leaves for
+ * later (src/dequant.c:60-61), bit-identical to ggml's block dequantization.
+ * One warp per superblock, 128-bit loads and stores. */
+bool tcg_dequant(float *dst, const void *src, size_t n, ggml_type_t t);
+
+/* Replaces tc_dequant_view (src/dequant.c:65-80) with device memory from
+ * `a`: the tensor's bytes are uploaded and converted to fp32. */
+const float *tcg_dequant_view(const gguf_tensor_t *t, tcg_arena_t *a, bool *converted);
+
+/* Raw upload of a tensor's payload (K-quant blocks stay packed for the
+ * fused consumers). */
+const void *tcg_tensor_upload(const gguf_tensor_t *t, tcg_arena_t *a);
+
+/* ------------------------------------------ fused dequant-matvec (new)
+ * y[N] = W[N,K] x[K] with W in Q4_K / Q6_K blocks (row-major, K a multiple
+ * of 256), dequantized in registers and never written out; fp32
+ * accumulation. Equivalent to tc_dequant followed by tc_ref_linear with M=1
+ * (src/ops.c:28-35), up to summation order. */
+bool tcg_matvec_q(float *y, const void *W, const float *x, int N, int K, ggml_type_t t);
+
+/* --------------------------------------------------- ops (src/ops.h)
+ * Same argument order and meaning as the reference's tc_ref_* (src/ops.h:
+ * 30-63), device pointers. GEMMs run on the tcgen05 tensor cores as 3xTF32
+ * (fp32-accurate) when K*4 and the row strides are 16-byte multiples and the
+ * pointers 16-byte aligned, else on an fp32 CUDA-core kernel. */
+bool tcg_gemm(float *C, const float *A, const float *B, int M, int N, int K, bool b_transposed);
+bool tcg_linear(float *y, const float *x, const float *W, const float *bias, int M, int N, int K);
+bool tcg_layernorm(float *out, const float *x, const float *gamma, const float *beta,
+                   int rows, int cols, float eps);
+bool tcg_gelu(float *out, const float *x, size_t n);
+bool tcg_gelu_quick(float *out, const float *x, size_t n);
+bool tcg_softmax_rows(float *out, const float *x, int rows, int cols);
+/* tc_ref_mha without the scratch argument: the scores stay on chip. */
+bool tcg_mha(float *out, const float *q, const float *k, const float *v,
+             int T, int n_head, int head_dim);
+bool tcg_add(float *out, const float *a, const float *b, size_t n);
+bool tcg_scale(float *out, const float *x, float s, size_t n);
+
+/* ------------------------------------------------- batched ViT (new)
+ * The forward of tc_vit_encode (src/vit.c:305-391) over a batch of images.
+ * Weights are uploaded once (fp32 plus the tf32 hi/lo split the 3xTF32
+ * GEMMs consume); activations live in a device arena sized for max_batch. */
+
+typedef struct tcg_vit tcg_vit_t;
+
+tcg_vit_t *tcg_vit_upload(const tc_vit_t *m, int max_batch);
+void       tcg_vit_release(tcg_vit_t *v);
+int        tcg_vit_max_batch(const tcg_vit_t *v);
+size_t     tcg_vit_device_bytes(const tcg_vit_t *v);
+/* Record the layer loop as a CUDA graph per batch size (default on). */
+void       tcg_vit_use_graphs(tcg_vit_t *v, bool on);
+
+/* HOST buffers: pixels [n, 3, image, image] (already normalised), out
+ * [n, d_out]. Copies in, runs, copies out, and returns after the result is
+ * in `out`. `tap` (may be NULL) is called once per image per tap point
+ * (ln_pre, blk0, blk_last, ln_post, embedding), in image order, with host
+ * data. Page-locked buffers (tcg_host_alloc) make the copies asynchronous. */
+bool tcg_vit_encode_batch(tcg_vit_t *v, const float *pixels, int n_images, float *out,
+                          tc_vit_tap_fn tap, void *ud);
+
+/* DEVICE buffers, asynchronous, no taps. */
+bool tcg_vit_encode_device(tcg_vit_t *v, const float *pixels, int n_images, float *out);
+
+/* Instrumentation. Kernel launches of one forward; and, between begin and
+ * end, every forward runs eagerly with CUDA events around each launch, whose
+ * device time end() sums per kernel class: [0] tensor-core GEMMs,
+ * [1] attention, [2] LayerNorm, [3] the rest (gather, CLS rows, projection). */
+int  tcg_vit_launches_per_forward(const tcg_vit_t *v);
+void tcg_vit_profile_begin(void);
+bool tcg_vit_profile_end(float ms[4], int count[4]);
+
+/* ------------------------------------------------ multi-GPU (NCCL)
+ * One process per GPU. Rank 0 creates the id and hands it to the others by
+ * any host channel; every rank then calls tcg_vit_upload_bcast with its
+ * own host model (only rank 0's weights are read: they are uploaded there
+ * and broadcast over NVLink once, with no collective in the forward). */
+bool tcg_nccl_unique_id(unsigned char id[128]);
+tcg_vit_t *tcg_vit_upload_bcast(const tc_vit_t *m, int max_batch, int rank, int nranks,
+                                const unsigned char id[128]);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TCG_H */

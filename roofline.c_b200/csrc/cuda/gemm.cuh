@@ -1,0 +1,46 @@
+// gemm.cuh -- the 3xTF32 tcgen05 GEMM that carries roofline.c's linears
+// (tc_ref_linear, src/ops.c:28-35: y = x W^T + b) and its fused epilogues.
+#pragma once
+
+#include <cuda.h>
+#include "ops.cuh"
+
+namespace tcg {
+
+// What happens to an accumulator element before it is stored.
+//   v = acc                         (fp32 sum of the three tf32 products)
+//   v = v + bias[n]                 if bias
+//   v = v + rowadd[src_row, n]      if rowadd (position embedding)
+//   v = act(v)                      act: 0 none, 1 gelu, 2 quick gelu
+//   v = residual[dst_row, n] + v    if residual (may alias out.plain)
+// GEMM row r is stored at dst_row(r) = (r / rgroup) * rstride + roff + r % rgroup,
+// and rowadd's row is src_row(r) = r % rgroup + roff.
+struct GemmEpi {
+    const float *bias = nullptr;
+    const float *rowadd = nullptr;
+    int ld_rowadd = 0;
+    const float *residual = nullptr;
+    int act = 0;
+    OutSpec out;
+    int rgroup = 1 << 30, rstride = 0, roff = 0;
+};
+
+// One GEMM: C[M,N] = A[M,K] * B[N,K]^T with both operands given as tf32
+// hi/lo pairs, row-major with row stride K. Tensor maps are encoded once.
+struct GemmPlan {
+    CUtensorMap a_hi, a_lo, b_hi, b_lo;
+    int M = 0, N = 0, K = 0;
+    int cfg = -1;        // kernel configuration index
+    int grid = 0;
+    GemmEpi epi;
+};
+
+bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo,
+               int M, int N, int K, const GemmEpi &epi, int force_cfg = -1);
+bool gemm_run(const GemmPlan &p, cudaStream_t s, int *err);
+
+// Tile widths available (index = cfg); for tests and tuning.
+int gemm_num_cfgs();
+int gemm_cfg_bn(int cfg);
+
+}  // namespace tcg

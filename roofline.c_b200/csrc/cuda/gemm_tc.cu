@@ -1,0 +1,525 @@
+// gemm_tc.cu -- fp32-accurate GEMM on the 5th-generation tensor cores.
+//
+// C[M,N] = A[M,K] * B[N,K]^T (+ epilogue), the shape of every linear in
+// roofline.c's ViT (tc_ref_linear, src/ops.c:28-35). Each fp32 operand comes
+// as a tf32 pair (hi = rn(v), lo = rn(v - hi)) and every K-step issues three
+// tcgen05.mma.kind::tf32 -- lo*hi, hi*lo, hi*hi -- into one fp32 TMEM
+// accumulator ("3xTF32"; the dropped lo*lo term is ~2^-22 relative).
+//
+// Persistent, warp-specialised CTA (one per SM, 192 threads):
+//   warp 0     one lane issues the TMA loads of a (A_hi, A_lo, B_hi, B_lo)
+//              K-slice into a STAGES-deep shared-memory ring;
+//   warp 1     allocates TMEM; one lane issues the MMAs and commits them to
+//              the ring's "empty" barriers and to the accumulator barriers;
+//   warps 2-5  the epilogue: tcgen05.ld of the 128 x BN accumulator (one
+//              row per thread), bias / position / GELU / residual, hi/lo
+//              split, global stores.
+// Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap
+// the MMAs of tile i+1. Operand tiles are K-major with the TMA swizzle that
+// matches the UMMA descriptor (BK*4 bytes: 128B for BK=32, 64B for BK=16).
+// Every mbarrier wait is bounded (globaltimer); a wait that gives up sets a
+// CTA-wide abort flag and the library's device error word, the roles wind
+// down, in-flight copies and MMAs are drained, and TMEM is freed.
+#include "gemm.cuh"
+#include "numerics.cuh"
+
+namespace tcg {
+namespace {
+
+constexpr int BM = 128;
+constexpr int NUM_THREADS = 192;
+constexpr unsigned long long WAIT_NS = 4000000000ull;   // 4 s per wait
+
+__device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void bar_init(uint32_t b, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(b), "r"(count) : "memory");
+}
+__device__ __forceinline__ void bar_expect_tx(uint32_t b, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(b), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bar_arrive(uint32_t b)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(b) : "memory");
+}
+__device__ __forceinline__ bool bar_test(uint32_t b, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(b), "r"(parity) : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ unsigned long long now_ns()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Wait for the phase of parity `parity` to complete. Gives up (false) when
+// `abort` is raised by another role or after WAIT_NS, in which case it
+// raises `abort` and records `code` in the device error word.
+__device__ bool bar_wait(uint32_t b, uint32_t parity, volatile int *abort, int *err, int code, bool heed_abort = true)
+{
+    if (bar_test(b, parity)) return true;
+    const unsigned long long t0 = now_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (bar_test(b, parity)) return true;
+        if ((it & 127) == 0) {
+            if (heed_abort && *abort) return false;
+            if (now_ns() - t0 > WAIT_NS) {
+                *abort = 1;
+                atomicExch(err, code);
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y)
+{
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%2, %3}], [%4];"
+                 ::"r"(dst), "l"((unsigned long long)map), "r"(x), "r"(y), "r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// UMMA shared-memory descriptor, K-major, swizzled rows of SWB bytes:
+// start>>4 @0, LBO (unused for swizzled K-major) = 1 @16, SBO = 8 rows @32,
+// version 1 @46, layout @61 (2 = 128B, 4 = 64B, 6 = 32B swizzle).
+template <int SWB>
+__device__ __forceinline__ unsigned long long sdesc(uint32_t addr)
+{
+    constexpr unsigned long long layout = SWB == 128 ? 2ull : (SWB == 64 ? 4ull : 6ull);
+    return (unsigned long long)((addr & 0x3FFFFu) >> 4) | (1ull << 16) |
+           ((unsigned long long)((8 * SWB) >> 4) << 32) | (1ull << 46) | (layout << 61);
+}
+
+// Instruction descriptor of kind::tf32, fp32 accumulator, both operands
+// K-major, M = 128, N = BN.
+template <int BN>
+__device__ __forceinline__ uint32_t idesc_tf32()
+{
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t d, unsigned long long a, unsigned long long b, uint32_t id, uint32_t acc)
+{
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+                 ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc));
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// 32 consecutive accumulator columns of this thread's TMEM lane; the wait
+// sits in the same asm block so no use of the registers can precede it.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float v[32])
+{
+    uint32_t r[32];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32"
+                 " {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                 "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+                 "tcgen05.wait::ld.sync.aligned;"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+                   "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+                   "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                 : "r"(taddr)
+                 : "memory");
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float epi_value(const GemmEpi &e, float x, int src_row, int n)
+{
+    if (e.bias) x = __fadd_rn(x, e.bias[n]);
+    if (e.rowadd) x = __fadd_rn(x, e.rowadd[(size_t)src_row * e.ld_rowadd + n]);
+    if (e.act == 1) x = gelu_exact(x);
+    else if (e.act == 2) x = gelu_quick(x);
+    return x;
+}
+
+__device__ __forceinline__ void store32(float *dst, const float (&src)[32], bool vec, int cnt)
+{
+    if (vec && (((uintptr_t)dst) & 15) == 0) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4 *>(dst + j) = make_float4(src[j], src[j + 1], src[j + 2], src[j + 3]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; j++)
+            if (j < cnt) dst[j] = src[j];
+    }
+}
+
+// Row r of the tile, columns n .. n+cnt-1 (cnt <= 32) from v[].
+__device__ __forceinline__ void epi_store(const GemmEpi &e, int r, int n, int cnt, float (&v)[32])
+{
+    const int src_row = r % e.rgroup + e.roff;
+    const size_t dst = (size_t)(r / e.rgroup) * e.rstride + e.roff + r % e.rgroup;
+    const size_t o = dst * (size_t)e.out.ld + n;
+#pragma unroll
+    for (int j = 0; j < 32; j++)
+        if (j < cnt) v[j] = epi_value(e, v[j], src_row, n + j);
+    const bool vec = cnt == 32 && (e.out.ld & 3) == 0 && (n & 3) == 0;
+    if (e.residual) {
+        const float *res = e.residual + o;
+        if (vec && (((uintptr_t)res) & 15) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+                const float4 q = *reinterpret_cast<const float4 *>(res + j);
+                v[j] = __fadd_rn(q.x, v[j]); v[j + 1] = __fadd_rn(q.y, v[j + 1]);
+                v[j + 2] = __fadd_rn(q.z, v[j + 2]); v[j + 3] = __fadd_rn(q.w, v[j + 3]);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+                if (j < cnt) v[j] = __fadd_rn(res[j], v[j]);
+        }
+    }
+    if (e.out.plain) store32(e.out.plain + o, v, vec, cnt);
+    if (e.out.hi) {
+        float hi[32], lo[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) split_tf32(v[j], hi[j], lo[j]);
+        store32(e.out.hi + o, hi, vec, cnt);
+        store32(e.out.lo + o, lo, vec, cnt);
+    }
+}
+
+template <int BN, int BK, int STAGES>
+struct Shape {
+    static constexpr uint32_t A_BYTES = BM * BK * 4;
+    static constexpr uint32_t B_BYTES = BN * BK * 4;
+    static constexpr uint32_t STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+    static constexpr uint32_t TMEM_COLS = 2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512);
+    static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+};
+
+template <int BN, int BK, int STAGES>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
+                   const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
+                   int M, int N, int K, GemmEpi epi, int *err)
+{
+    using S = Shape<BN, BK, STAGES>;
+    constexpr int SWB = BK * 4;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *tiles = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t *bars = (uint64_t *)(tiles + (size_t)STAGES * S::STAGE_BYTES);
+    uint32_t *tmem_slot = (uint32_t *)(bars + 2 * STAGES + 5);
+    volatile int *abort = (volatile int *)(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_tiles = (N + BN - 1) / BN;
+    const int num_tiles = ((M + BM - 1) / BM) * n_tiles;
+    const int num_kb = (K + BK - 1) / BK;
+    const uint32_t full0 = su32(bars), empty0 = su32(bars + STAGES);
+    const uint32_t tfull0 = su32(bars + 2 * STAGES), tempty0 = tfull0 + 16, drain = tfull0 + 32;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            bar_init(full0 + 8 * s, 1);
+            bar_init(empty0 + 8 * s, 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            bar_init(tfull0 + 8 * a, 1);
+            bar_init(tempty0 + 8 * a, 128);
+        }
+        bar_init(drain, 1);
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(su32(tmem_slot)), "r"(S::TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&a_hi) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&a_lo) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&b_hi) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&b_lo) : "memory");
+            int stage = 0;
+            uint32_t phase = 0;
+            long issued = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
+                const int m0 = (t / n_tiles) * BM, n0 = (t % n_tiles) * BN;
+                for (int kb = 0; kb < num_kb; kb++) {
+                    if (!bar_wait(empty0 + 8 * stage, phase ^ 1, abort, err, 1)) { ok = false; break; }
+                    const uint32_t fb = full0 + 8 * stage;
+                    const uint32_t base = su32(tiles + (size_t)stage * S::STAGE_BYTES);
+                    bar_expect_tx(fb, S::STAGE_BYTES);
+                    tma_load(base, &a_hi, fb, kb * BK, m0);
+                    tma_load(base + S::A_BYTES, &a_lo, fb, kb * BK, m0);
+                    tma_load(base + 2 * S::A_BYTES, &b_hi, fb, kb * BK, n0);
+                    tma_load(base + 2 * S::A_BYTES + S::B_BYTES, &b_lo, fb, kb * BK, n0);
+                    issued++;
+                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                }
+            }
+            // Let the last fills of every stage land before the CTA exits.
+            for (int i = 1; i <= STAGES && i <= issued; i++) {
+                int s = stage - i;
+                uint32_t ph = phase;
+                if (s < 0) { s += STAGES; ph ^= 1; }
+                bar_wait(full0 + 8 * s, ph, abort, err, 2, false);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t id = idesc_tf32<BN>();
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            int local = 0;
+            for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x, local++) {
+                const int acc = local & 1;
+                if (!bar_wait(tempty0 + 8 * acc, ((local >> 1) & 1) ^ 1, abort, err, 3)) break;
+                fence_after();
+                const uint32_t d = tmem + (uint32_t)(acc * BN);
+                for (int kb = 0; kb < num_kb; kb++) {
+                    if (!bar_wait(full0 + 8 * stage, phase, abort, err, 4)) { ok = false; break; }
+                    fence_after();
+                    const uint32_t base = su32(tiles + (size_t)stage * S::STAGE_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / 8; k++) {
+                        const uint32_t off = (uint32_t)k * 32u;
+                        const unsigned long long ah = sdesc<SWB>(base + off);
+                        const unsigned long long al = sdesc<SWB>(base + S::A_BYTES + off);
+                        const unsigned long long bh = sdesc<SWB>(base + 2 * S::A_BYTES + off);
+                        const unsigned long long bl = sdesc<SWB>(base + 2 * S::A_BYTES + S::B_BYTES + off);
+                        mma_tf32(d, al, bh, id, (kb | k) ? 1u : 0u);
+                        mma_tf32(d, ah, bl, id, 1u);
+                        mma_tf32(d, ah, bh, id, 1u);
+                    }
+                    mma_commit(empty0 + 8 * stage);
+                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                }
+                if (ok) mma_commit(tfull0 + 8 * acc);
+            }
+            // Every MMA issued above has retired once this barrier flips.
+            mma_commit(drain);
+            bar_wait(drain, 0, abort, err, 5, false);
+        }
+        __syncwarp();
+    } else {
+        const int q = warp & 3;                  // TMEM lanes 32q .. 32q+31
+        int local = 0;
+        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, local++) {
+            const int acc = local & 1;
+            if (!bar_wait(tfull0 + 8 * acc, (local >> 1) & 1, abort, err, 6)) break;
+            fence_after();
+            const int m0 = (t / n_tiles) * BM, n0 = (t % n_tiles) * BN;
+            const int r = m0 + q * 32 + lane;
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                float v[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c0), v);
+                const int n = n0 + c0;
+                if (r < M && n < N) epi_store(epi, r, n, min(32, N - n), v);
+            }
+            fence_before();
+            bar_arrive(tempty0 + 8 * acc);
+        }
+    }
+
+    fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(S::TMEM_COLS) : "memory");
+    }
+}
+
+// ------------------------------------------------------------------ host
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+                                  CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                  CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn()
+{
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+// [rows, K] fp32, row stride K, box = BK x box_rows, swizzle = BK*4 bytes.
+bool encode_kmajor(CUtensorMap *m, const float *ptr, int rows, int K, int box_rows, int BK)
+{
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail("cuTensorMapEncodeTiled is not available from the driver");
+    if (((uintptr_t)ptr & 15) || (K & 3)) return fail("GEMM operand not 16-byte aligned / K=%d not a multiple of 4", K);
+    cuuint64_t dims[2] = { (cuuint64_t)K, (cuuint64_t)rows };
+    cuuint64_t strides[1] = { (cuuint64_t)K * 4u };
+    cuuint32_t box[2] = { (cuuint32_t)BK, (cuuint32_t)box_rows };
+    cuuint32_t estr[2] = { 1, 1 };
+    const CUtensorMapSwizzle swz = BK == 32 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : (BK == 16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)ptr, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail("cuTensorMapEncodeTiled failed (%d) for [%d x %d]", (int)r, rows, K);
+    return true;
+}
+
+typedef void (*KernelFn)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, int, int, int, GemmEpi, int *);
+
+struct Cfg {
+    int bn, bk, stages;
+    size_t smem;
+    const void *fn;
+};
+
+#define TCG_CFG(BN, BK, ST) { BN, BK, ST, Shape<BN, BK, ST>::SMEM, (const void *)gemm_tf32x3_kernel<BN, BK, ST> }
+const Cfg CFGS[] = {
+    TCG_CFG(256, 16, 4), TCG_CFG(192, 16, 5), TCG_CFG(128, 16, 6), TCG_CFG(64, 16, 8),
+    TCG_CFG(256, 32, 2), TCG_CFG(192, 32, 2), TCG_CFG(128, 32, 3), TCG_CFG(64, 32, 4),
+};
+#undef TCG_CFG
+constexpr int NCFG = sizeof(CFGS) / sizeof(CFGS[0]);
+
+int choose_cfg(int M, int N)
+{
+    // Fewest tile rounds over the SMs, weighted by tile width plus a fixed
+    // per-tile cost; ties go to the wider tile (more reuse per byte).
+    const int sms = ctx().sms > 0 ? ctx().sms : 148;
+    int best = 0;
+    long best_cost = -1;
+    for (int i = 0; i < 4; i++) {
+        const long tiles = (long)((M + BM - 1) / BM) * ((N + CFGS[i].bn - 1) / CFGS[i].bn);
+        const long rounds = (tiles + sms - 1) / sms;
+        const long cost = rounds * (CFGS[i].bn + 32);
+        if (best_cost < 0 || cost < best_cost) { best = i; best_cost = cost; }
+    }
+    return best;
+}
+
+}  // namespace
+
+int gemm_num_cfgs() { return NCFG; }
+int gemm_cfg_bn(int cfg) { return cfg >= 0 && cfg < NCFG ? CFGS[cfg].bn : 0; }
+
+bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo,
+               int M, int N, int K, const GemmEpi &epi, int force_cfg)
+{
+    if (M <= 0 || N <= 0 || K <= 0) return fail("gemm_plan: empty shape %dx%dx%d", M, N, K);
+    const int cfg = force_cfg >= 0 ? force_cfg : choose_cfg(M, N);
+    if (cfg >= NCFG) return fail("gemm_plan: no configuration %d", cfg);
+    const Cfg &c = CFGS[cfg];
+    if (!encode_kmajor(&p.a_hi, a_hi, M, K, BM, c.bk) || !encode_kmajor(&p.a_lo, a_lo, M, K, BM, c.bk) ||
+        !encode_kmajor(&p.b_hi, b_hi, N, K, c.bn, c.bk) || !encode_kmajor(&p.b_lo, b_lo, N, K, c.bn, c.bk))
+        return false;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.cfg = cfg;
+    p.epi = epi;
+    const int tiles = ((M + BM - 1) / BM) * ((N + c.bn - 1) / c.bn);
+    const int sms = ctx().sms > 0 ? ctx().sms : 148;
+    p.grid = tiles < sms ? tiles : sms;
+    return true;
+}
+
+bool gemm_run(const GemmPlan &p, cudaStream_t s, int *err)
+{
+    if (p.cfg < 0) return fail("gemm_run: plan not built");
+    const Cfg &c = CFGS[p.cfg];
+    static unsigned long long attr_done[64];   // per device: bit per configuration
+    const int dev = ctx().device & 63;
+    if (!(attr_done[dev] >> p.cfg & 1ull)) {
+        TCG_CUDA(cudaFuncSetAttribute(c.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem));
+        attr_done[dev] |= 1ull << p.cfg;
+    }
+    void *args[] = { (void *)&p.a_hi, (void *)&p.a_lo, (void *)&p.b_hi, (void *)&p.b_lo,
+                     (void *)&p.M, (void *)&p.N, (void *)&p.K, (void *)&p.epi, (void *)&err };
+    TCG_CUDA(cudaLaunchKernel(c.fn, dim3(p.grid), dim3(NUM_THREADS), args, c.smem, s));
+    return true;
+}
+
+}  // namespace tcg
+
+// ------------------------------------------------------------ op-level ABI
+
+using namespace tcg;
+
+static bool linear_impl(float *y, const float *x, const float *W, const float *bias, int M, int N, int K,
+                        bool bt, int force_cfg)
+{
+    if (!need_ctx()) return false;
+    if (M < 0 || N < 0 || K < 0) return fail("gemm: negative size");
+    if (M == 0 || N == 0) return true;
+    cudaStream_t s = ctx().cur;
+    const bool tc_ok = bt && K > 0 && (K & 3) == 0 && !((uintptr_t)x & 15) && !((uintptr_t)W & 15);
+    if (!tc_ok || force_cfg == -2)
+        return launch_gemm_simt(y, N, x, K, W, bt ? K : N, bias, M, N, K, bt, s);
+    const size_t xa = (size_t)M * K, wa = (size_t)N * K;
+    float *buf = (float *)scratch((2 * xa + 2 * wa) * sizeof(float) + 64);
+    if (!buf) return false;
+    float *xh = buf, *xl = xh + xa, *wh = xl + xa, *wl = wh + wa;
+    // keep every operand 16-byte aligned
+    if ((xa & 3) != 0) {
+        xl = xh + ((xa + 3) & ~(size_t)3);
+        wh = xl + ((xa + 3) & ~(size_t)3);
+        wl = wh + ((wa + 3) & ~(size_t)3);
+    }
+    if (!launch_split(x, xh, xl, xa, s) || !launch_split(W, wh, wl, wa, s)) return false;
+    GemmEpi e;
+    e.bias = bias;
+    e.out.plain = y;
+    e.out.ld = N;
+    GemmPlan p;
+    if (!gemm_plan(p, xh, xl, wh, wl, M, N, K, e, force_cfg)) return false;
+    return gemm_run(p, s, ctx().d_err);
+}
+
+extern "C" {
+
+bool tcg_gemm(float *C, const float *A, const float *B, int M, int N, int K, bool b_transposed)
+{
+    return linear_impl(C, A, B, nullptr, M, N, K, b_transposed, -1);
+}
+
+bool tcg_linear(float *y, const float *x, const float *W, const float *bias, int M, int N, int K)
+{
+    return linear_impl(y, x, W, bias, M, N, K, true, -1);
+}
+
+// Test hook: force a GEMM configuration (cfg >= 0 a tcgen05 tile shape, -2
+// the CUDA-core kernel). Not part of the public header.
+bool tcg_linear_cfg(float *y, const float *x, const float *W, const float *bias, int M, int N, int K, int cfg)
+{
+    return linear_impl(y, x, W, bias, M, N, K, true, cfg);
+}
+
+int tcg_gemm_num_cfgs(void) { return gemm_num_cfgs(); }
+
+}  // extern "C"

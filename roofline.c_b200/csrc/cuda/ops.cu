@@ -1,0 +1,406 @@
+// ops.cu -- CUDA-core kernels for the O(T*D) ops of roofline.c src/ops.c and
+// the op-level C ABI (tcg_layernorm, tcg_gelu, ..., tcg_mha).
+#include "ops.cuh"
+#include "numerics.cuh"
+#include "gemm.cuh"
+
+namespace tcg {
+
+__device__ __forceinline__ void put(const OutSpec &o, size_t row, int col, float v)
+{
+    const size_t i = row * (size_t)o.ld + col;
+    if (o.plain) o.plain[i] = v;
+    if (o.hi) {
+        float h, l;
+        split_tf32(v, h, l);
+        o.hi[i] = h;
+        o.lo[i] = l;
+    }
+}
+
+// ---------------------------------------------------------------- LayerNorm
+// One warp per row. Pass 1: double sum -> mean. Pass 2: double sum of
+// squared deviations -> biased variance. inv = (float)(1/sqrt(var+eps)) in
+// double. Output (float)(x - mean) * inv, * gamma, + beta, each in float.
+__global__ void layernorm_kernel(const float *x, int ld_in, const float *__restrict__ g,
+                                 const float *__restrict__ b, int rows, int cols, float eps, OutSpec out)
+{
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const float *in = x + (size_t)row * ld_in;
+    double s = 0.0;
+    for (int c = lane; c < cols; c += 32) s += (double)in[c];
+    const double mean = warp_sum(s) / (double)cols;
+    double ss = 0.0;
+    for (int c = lane; c < cols; c += 32) {
+        const double dv = __dsub_rn((double)in[c], mean);
+        ss = __dadd_rn(ss, __dmul_rn(dv, dv));
+    }
+    const double var = warp_sum(ss) / (double)cols;
+    const float inv = (float)(1.0 / sqrt(var + (double)eps));
+    for (int c = lane; c < cols; c += 32) {
+        float v = __fmul_rn((float)((double)in[c] - mean), inv);
+        if (g) v = __fmul_rn(v, g[c]);
+        if (b) v = __fadd_rn(v, b[c]);
+        put(out, row, c, v);
+    }
+}
+
+bool launch_layernorm(const float *x, int ld_in, const float *g, const float *b, int rows, int cols,
+                      float eps, const OutSpec &out, cudaStream_t s)
+{
+    if (rows <= 0) return true;
+    layernorm_kernel<<<ceil_div(rows, 8), 256, 0, s>>>(x, ld_in, g, b, rows, cols, eps, out);
+    TCG_LAUNCHED();
+    return true;
+}
+
+// ---------------------------------------------------------------- attention
+// One CTA per (head, image); K with a padded row (hd+1 floats) so that lanes
+// walking different keys hit different banks; V unpadded (lanes walk d).
+// One warp per query row: lane j scores keys j, j+32, ...; the softmax is
+// max-subtracted with a double sum (src/ops.c:129-139); then lane d
+// accumulates o[d] over keys in order.
+template <int DPL>   // head dims per lane: hd <= 32*DPL
+__global__ void mha_kernel(const float *__restrict__ q, const float *__restrict__ k,
+                           const float *__restrict__ v, int ldi, int T, int hd, OutSpec out)
+{
+    extern __shared__ float sm[];
+    const int h = blockIdx.x, img = blockIdx.y;
+    const int nw = blockDim.x >> 5, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int kst = hd + 1;
+    float *Ks = sm;                           // [T][hd+1]
+    float *Vs = Ks + (size_t)T * kst;         // [T][hd]
+    float *Ps = Vs + (size_t)T * hd;          // [nw][T]
+    float *Qs = Ps + (size_t)nw * T;          // [nw][hd]
+    const size_t base = (size_t)img * T;
+    const int col = h * hd;
+
+    for (int i = threadIdx.x; i < T * hd; i += blockDim.x) {
+        const int t = i / hd, d = i - t * hd;
+        const size_t gi = (base + t) * (size_t)ldi + col + d;
+        Ks[t * kst + d] = k[gi];
+        Vs[t * hd + d] = v[gi];
+    }
+    __syncthreads();
+
+    const float scale = 1.0f / sqrtf((float)hd);
+    float *P = Ps + (size_t)wid * T, *Qr = Qs + (size_t)wid * hd;
+    for (int t = wid; t < T; t += nw) {
+        const float *qg = q + (base + t) * (size_t)ldi + col;
+        for (int d = lane; d < hd; d += 32) Qr[d] = qg[d];
+        __syncwarp();
+        float mx = -INFINITY;
+        for (int s = lane; s < T; s += 32) {
+            const float *kr = Ks + s * kst;
+            float acc = 0.0f;
+            for (int d = 0; d < hd; d++) acc = fmaf(Qr[d], kr[d], acc);
+            acc = __fmul_rn(acc, scale);
+            P[s] = acc;
+            mx = fmaxf(mx, acc);
+        }
+        mx = warp_max(mx);
+        double sum = 0.0;
+        for (int s = lane; s < T; s += 32) {
+            const float e = expf(__fsub_rn(P[s], mx));
+            P[s] = e;
+            sum += (double)e;
+        }
+        const float inv = (float)(1.0 / warp_sum(sum));
+        __syncwarp();
+        float o[DPL];
+#pragma unroll
+        for (int j = 0; j < DPL; j++) o[j] = 0.0f;
+        for (int s = 0; s < T; s++) {
+            const float w = __fmul_rn(P[s], inv);
+            const float *vr = Vs + s * hd;
+#pragma unroll
+            for (int j = 0; j < DPL; j++) {
+                const int d = lane + 32 * j;
+                if (d < hd) o[j] = fmaf(w, vr[d], o[j]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < DPL; j++) {
+            const int d = lane + 32 * j;
+            if (d < hd) put(out, base + t, col + d, o[j]);
+        }
+        __syncwarp();
+    }
+}
+
+bool launch_mha(const float *q, const float *k, const float *v, int ldi, int T, int n_head, int hd,
+                int n_img, const OutSpec &out, cudaStream_t s)
+{
+    if (T <= 0 || n_img <= 0 || n_head <= 0) return true;
+    if (hd <= 0 || hd > 128) return fail("attention: head_dim %d outside 1..128", hd);
+    const int nw = 8;
+    const size_t smem = ((size_t)T * (2 * hd + 1) + (size_t)nw * (T + hd)) * sizeof(float);
+    if (smem > 227 * 1024) return fail("attention: T=%d head_dim=%d needs %zu B of shared memory", T, hd, smem);
+    dim3 grid(n_head, n_img);
+    // Opt every variant in to the full shared-memory window once per device.
+    static unsigned attr_done[64];
+    const int dev = ctx().device & 63;
+    if (!attr_done[dev]) {
+        const int maxsm = 227 * 1024;
+        TCG_CUDA(cudaFuncSetAttribute(mha_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, maxsm));
+        TCG_CUDA(cudaFuncSetAttribute(mha_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, maxsm));
+        TCG_CUDA(cudaFuncSetAttribute(mha_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, maxsm));
+        attr_done[dev] = 1;
+    }
+    if (hd <= 32) mha_kernel<1><<<grid, nw * 32, smem, s>>>(q, k, v, ldi, T, hd, out);
+    else if (hd <= 64) mha_kernel<2><<<grid, nw * 32, smem, s>>>(q, k, v, ldi, T, hd, out);
+    else mha_kernel<4><<<grid, nw * 32, smem, s>>>(q, k, v, ldi, T, hd, out);
+    TCG_LAUNCHED();
+    return true;
+}
+
+// ------------------------------------------------------------ SIMT GEMM
+// 64x64 tile, 16-deep K slices in shared memory, 4x4 outputs per thread,
+// fp32 FMA accumulation in increasing k.
+constexpr int SG_BM = 64, SG_BN = 64, SG_BK = 16;
+
+__global__ void __launch_bounds__(256)
+gemm_simt_kernel(float *__restrict__ C, int ldc, const float *__restrict__ A, int lda,
+                 const float *__restrict__ B, int ldb, const float *__restrict__ bias,
+                 int M, int N, int K, bool bt)
+{
+    __shared__ float As[SG_BK][SG_BM + 4];
+    __shared__ float Bs[SG_BK][SG_BN + 4];
+    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+    const int m0 = blockIdx.y * SG_BM, n0 = blockIdx.x * SG_BN;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < K; k0 += SG_BK) {
+        for (int i = threadIdx.x; i < SG_BM * SG_BK; i += 256) {
+            const int r = i / SG_BK, kk = i % SG_BK;
+            const int m = m0 + r, kg = k0 + kk;
+            As[kk][r] = (m < M && kg < K) ? A[(size_t)m * lda + kg] : 0.0f;
+        }
+        for (int i = threadIdx.x; i < SG_BN * SG_BK; i += 256) {
+            int r, kk;
+            if (bt) { r = i / SG_BK; kk = i % SG_BK; } else { kk = i / SG_BN; r = i % SG_BN; }
+            const int n = n0 + r, kg = k0 + kk;
+            float val = 0.0f;
+            if (n < N && kg < K) val = bt ? B[(size_t)n * ldb + kg] : B[(size_t)kg * ldb + n];
+            Bs[kk][r] = val;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < SG_BK; kk++) {
+            float a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+            for (int j = 0; j < 4; j++) b[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int m = m0 + ty * 4 + i;
+        if (m >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int n = n0 + tx * 4 + j;
+            if (n < N) C[(size_t)m * ldc + n] = bias ? __fadd_rn(acc[i][j], bias[n]) : acc[i][j];
+        }
+    }
+}
+
+bool launch_gemm_simt(float *C, int ldc, const float *A, int lda, const float *B, int ldb,
+                      const float *bias, int M, int N, int K, bool bt, cudaStream_t s)
+{
+    if (M <= 0 || N <= 0) return true;
+    dim3 grid(ceil_div(N, SG_BN), ceil_div(M, SG_BM));
+    gemm_simt_kernel<<<grid, 256, 0, s>>>(C, ldc, A, lda, B, ldb, bias, M, N, K, bt);
+    TCG_LAUNCHED();
+    return true;
+}
+
+// ------------------------------------------------------------ elementwise
+
+__global__ void split_kernel(const float *__restrict__ src, float *__restrict__ hi, float *__restrict__ lo, size_t n)
+{
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        float h, l;
+        split_tf32(src[i], h, l);
+        hi[i] = h;
+        lo[i] = l;
+    }
+}
+
+static unsigned grid1d(size_t n)
+{
+    const size_t need = (n + 255) / 256, cap = (size_t)ctx().sms * 16;
+    return (unsigned)(need < cap ? (need ? need : 1) : cap);
+}
+
+bool launch_split(const float *src, float *hi, float *lo, size_t n, cudaStream_t s)
+{
+    if (n == 0) return true;
+    split_kernel<<<grid1d(n), 256, 0, s>>>(src, hi, lo, n);
+    TCG_LAUNCHED();
+    return true;
+}
+
+// Patch row r = i*G*G + gy*G + gx, column c = ch*P*P + ky*P + kx holds
+// pixel [i, ch, gy*P + ky, gx*P + kx].
+__global__ void patches_kernel(const float *__restrict__ px, int n_img, int S, int P,
+                               float *__restrict__ hi, float *__restrict__ lo)
+{
+    const int G = S / P, KP = 3 * P * P;
+    const size_t total = (size_t)n_img * G * G * KP;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = i / KP;
+        const int c = (int)(i - r * KP);
+        const int img = (int)(r / (G * G)), t = (int)(r % (G * G));
+        const int gy = t / G, gx = t % G;
+        const int ch = c / (P * P), rem = c % (P * P), ky = rem / P, kx = rem % P;
+        const float v = px[(((size_t)img * 3 + ch) * S + gy * P + ky) * S + gx * P + kx];
+        float h, l;
+        split_tf32(v, h, l);
+        hi[i] = h;
+        lo[i] = l;
+    }
+}
+
+bool launch_patches(const float *px, int n_img, int S, int P, float *hi, float *lo, cudaStream_t s)
+{
+    const size_t total = (size_t)n_img * (S / P) * (S / P) * 3 * P * P;
+    if (total == 0) return true;
+    patches_kernel<<<grid1d(total), 256, 0, s>>>(px, n_img, S, P, hi, lo);
+    TCG_LAUNCHED();
+    return true;
+}
+
+__global__ void cls_rows_kernel(float *__restrict__ x, const float *__restrict__ cls,
+                                const float *__restrict__ pos, int n_img, int T, int D)
+{
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_img * D; i += gridDim.x * blockDim.x) {
+        const int img = i / D, d = i % D;
+        x[(size_t)img * T * D + d] = __fadd_rn(cls[d], pos[d]);
+    }
+}
+
+bool launch_cls_rows(float *x, const float *cls, const float *pos, int n_img, int T, int D, cudaStream_t s)
+{
+    if (n_img <= 0) return true;
+    cls_rows_kernel<<<grid1d((size_t)n_img * D), 256, 0, s>>>(x, cls, pos, n_img, T, D);
+    TCG_LAUNCHED();
+    return true;
+}
+
+__global__ void gelu_kernel(float *__restrict__ out, const float *__restrict__ x, size_t n, bool quick)
+{
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = quick ? gelu_quick(x[i]) : gelu_exact(x[i]);
+}
+
+bool launch_gelu(float *out, const float *x, size_t n, bool quick, cudaStream_t s)
+{
+    if (n == 0) return true;
+    gelu_kernel<<<grid1d(n), 256, 0, s>>>(out, x, n, quick);
+    TCG_LAUNCHED();
+    return true;
+}
+
+__global__ void softmax_kernel(float *__restrict__ out, const float *__restrict__ x, int rows, int cols)
+{
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const float *in = x + (size_t)row * cols;
+    float *o = out + (size_t)row * cols;
+    float mx = -INFINITY;
+    for (int c = lane; c < cols; c += 32) mx = fmaxf(mx, in[c]);
+    mx = warp_max(mx);
+    double sum = 0.0;
+    for (int c = lane; c < cols; c += 32) {
+        const float e = expf(__fsub_rn(in[c], mx));
+        o[c] = e;
+        sum += (double)e;
+    }
+    const float inv = (float)(1.0 / warp_sum(sum));
+    for (int c = lane; c < cols; c += 32) o[c] = __fmul_rn(o[c], inv);
+}
+
+__global__ void add_kernel(float *__restrict__ out, const float *a, const float *b, size_t n)
+{
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = __fadd_rn(a[i], b[i]);
+}
+
+__global__ void scale_kernel(float *__restrict__ out, const float *x, float s, size_t n)
+{
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = __fmul_rn(x[i], s);
+}
+
+}  // namespace tcg
+
+using namespace tcg;
+
+extern "C" {
+
+bool tcg_layernorm(float *out, const float *x, const float *gamma, const float *beta, int rows, int cols, float eps)
+{
+    if (!need_ctx()) return false;
+    if (rows < 0 || cols <= 0) return rows == 0 || cols == 0 ? true : fail("tcg_layernorm: bad shape");
+    OutSpec o;
+    o.plain = out;
+    o.ld = cols;
+    return launch_layernorm(x, cols, gamma, beta, rows, cols, eps, o, ctx().cur);
+}
+
+bool tcg_gelu(float *out, const float *x, size_t n)
+{
+    return need_ctx() && launch_gelu(out, x, n, false, ctx().cur);
+}
+
+bool tcg_gelu_quick(float *out, const float *x, size_t n)
+{
+    return need_ctx() && launch_gelu(out, x, n, true, ctx().cur);
+}
+
+bool tcg_softmax_rows(float *out, const float *x, int rows, int cols)
+{
+    if (!need_ctx()) return false;
+    if (rows <= 0 || cols <= 0) return true;
+    softmax_kernel<<<ceil_div(rows, 8), 256, 0, ctx().cur>>>(out, x, rows, cols);
+    TCG_LAUNCHED();
+    return true;
+}
+
+bool tcg_mha(float *out, const float *q, const float *k, const float *v, int T, int n_head, int head_dim)
+{
+    if (!need_ctx()) return false;
+    OutSpec o;
+    o.plain = out;
+    o.ld = n_head * head_dim;
+    return launch_mha(q, k, v, n_head * head_dim, T, n_head, head_dim, 1, o, ctx().cur);
+}
+
+bool tcg_add(float *out, const float *a, const float *b, size_t n)
+{
+    if (!need_ctx()) return false;
+    if (n == 0) return true;
+    add_kernel<<<grid1d(n), 256, 0, ctx().cur>>>(out, a, b, n);
+    TCG_LAUNCHED();
+    return true;
+}
+
+bool tcg_scale(float *out, const float *x, float s, size_t n)
+{
+    if (!need_ctx()) return false;
+    if (n == 0) return true;
+    scale_kernel<<<grid1d(n), 256, 0, ctx().cur>>>(out, x, s, n);
+    TCG_LAUNCHED();
+    return true;
+}
+
+}  // extern "C"

@@ -1,0 +1,45 @@
+// ops.cuh -- launchers shared by the op API (ops.cu) and the ViT pipeline.
+#pragma once
+
+#include "tcg_common.cuh"
+
+namespace tcg {
+
+// Where an activation goes: plain fp32, and/or the tf32 hi/lo pair the
+// 3xTF32 GEMMs read (hi = rn_tf32(v), lo = rn_tf32(v - hi)). Row stride ld.
+struct OutSpec {
+    float *plain = nullptr;
+    float *hi = nullptr;
+    float *lo = nullptr;
+    int ld = 0;
+};
+
+// LayerNorm of `rows` rows of `cols` (src/ops.c:37-80 numerics: double
+// two-pass stats). Input row r at x + r*ld_in.
+bool launch_layernorm(const float *x, int ld_in, const float *g, const float *b, int rows, int cols,
+                      float eps, const OutSpec &out, cudaStream_t s);
+
+// Attention over n_img images of T tokens (src/ops.c:112-151). Image i,
+// token t, head h reads q at q + (i*T + t)*ldi + h*hd (same for k, v).
+bool launch_mha(const float *q, const float *k, const float *v, int ldi, int T, int n_head, int hd,
+                int n_img, const OutSpec &out, cudaStream_t s);
+
+// fp32 CUDA-core GEMM: C = A * op(B) (+ bias[n]); A [M,K] row stride lda,
+// op(B) = B^T for B [N,K] (b_transposed) else B [K,N]; C row stride ldc.
+bool launch_gemm_simt(float *C, int ldc, const float *A, int lda, const float *B, int ldb,
+                      const float *bias, int M, int N, int K, bool b_transposed, cudaStream_t s);
+
+// hi/lo split of n contiguous floats.
+bool launch_split(const float *src, float *hi, float *lo, size_t n, cudaStream_t s);
+
+// im2patch (src/vit.c:283-303) of n_img images [3, S, S] straight into the
+// hi/lo operand pair [n_img*G*G, 3*P*P].
+bool launch_patches(const float *px, int n_img, int S, int P, float *hi, float *lo, cudaStream_t s);
+
+// x[i*T + 0, :] = cls + pos[0, :] for every image (src/vit.c:346-347, row 0).
+bool launch_cls_rows(float *x, const float *cls, const float *pos, int n_img, int T, int D, cudaStream_t s);
+
+// out[n] = act(x[n]) elementwise: 0 identity-add, 1 gelu, 2 quick gelu.
+bool launch_gelu(float *out, const float *x, size_t n, bool quick, cudaStream_t s);
+
+}  // namespace tcg

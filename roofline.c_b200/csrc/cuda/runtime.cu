@@ -1,0 +1,276 @@
+// runtime.cu -- device selection, streams, errors, memory plumbing, events
+// and the device arena (the reference's arena discipline, src/arena.h:37-69,
+// over one cudaMalloc allocation).
+#include "tcg_common.cuh"
+
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+namespace tcg {
+
+static thread_local Ctx g_ctx;
+static thread_local char g_err[256];
+
+Ctx &ctx() { return g_ctx; }
+
+bool fail(const char *fmt, ...)
+{
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+    return false;
+}
+
+bool cuda_fail(cudaError_t e, const char *what, const char *file, int line)
+{
+    const char *base = strrchr(file, '/');
+    return fail("%s: %s (%s:%d)", what, cudaGetErrorString(e), base ? base + 1 : file, line);
+}
+
+bool need_ctx()
+{
+    if (g_ctx.ready) return true;
+    return fail("no device selected: call tcg_init() first");
+}
+
+void *scratch(size_t bytes)
+{
+    Ctx &c = g_ctx;
+    if (bytes <= c.scratch_bytes) return c.scratch;
+    if (c.scratch) {
+        cudaStreamSynchronize(c.cur);
+        cudaFree(c.scratch);
+        c.scratch = nullptr;
+        c.scratch_bytes = 0;
+    }
+    size_t want = bytes < (64u << 20) ? (64u << 20) : bytes;
+    if (cudaMalloc(&c.scratch, want) != cudaSuccess) {
+        cudaGetLastError();
+        fail("device scratch of %zu bytes: out of memory", want);
+        return nullptr;
+    }
+    c.scratch_bytes = want;
+    return c.scratch;
+}
+
+}  // namespace tcg
+
+using tcg::ctx;
+
+extern "C" {
+
+const char *tcg_last_error(void) { return tcg::g_err; }
+const char *tcg_version(void) { return "libtcg 0.1 (sm_100a)"; }
+
+bool tcg_init(int device)
+{
+    tcg::Ctx &c = ctx();
+    if (c.ready && c.device == device) return true;
+    if (c.ready) return tcg::fail("this thread already uses device %d", c.device);
+    int n = 0;
+    TCG_CUDA(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n) return tcg::fail("device %d out of range (%d present)", device, n);
+    TCG_CUDA(cudaSetDevice(device));
+    cudaDeviceProp p;
+    TCG_CUDA(cudaGetDeviceProperties(&p, device));
+    if (p.major != 10) return tcg::fail("device %d is sm_%d%d; libtcg is built for sm_100a", device, p.major, p.minor);
+    TCG_CUDA(cudaStreamCreateWithFlags(&c.own, cudaStreamNonBlocking));
+    TCG_CUDA(cudaMalloc(&c.d_err, sizeof(int)));
+    TCG_CUDA(cudaMemset(c.d_err, 0, sizeof(int)));
+    for (auto &e : c.ev) TCG_CUDA(cudaEventCreate(&e));
+    c.device = device;
+    c.sms = p.multiProcessorCount;
+    c.cur = c.own;
+    c.ready = true;
+    return true;
+}
+
+int tcg_device_count(void)
+{
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) { cudaGetLastError(); return 0; }
+    return n;
+}
+
+int tcg_sm_count(void) { return ctx().ready ? ctx().sms : 0; }
+
+bool tcg_sync(void)
+{
+    if (!tcg::need_ctx()) return false;
+    TCG_CUDA(cudaStreamSynchronize(ctx().cur));
+    return true;
+}
+
+void *tcg_get_stream(void) { return ctx().ready ? (void *)ctx().cur : nullptr; }
+
+bool tcg_set_stream(void *stream)
+{
+    if (!tcg::need_ctx()) return false;
+    ctx().cur = stream ? (cudaStream_t)stream : ctx().own;
+    return true;
+}
+
+int tcg_device_error(void)
+{
+    if (!ctx().ready) return -1;
+    int v = 0;
+    if (cudaMemcpyAsync(&v, ctx().d_err, sizeof v, cudaMemcpyDeviceToHost, ctx().cur) != cudaSuccess ||
+        cudaStreamSynchronize(ctx().cur) != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    return v;
+}
+
+bool tcg_clear_device_error(void)
+{
+    if (!tcg::need_ctx()) return false;
+    TCG_CUDA(cudaMemsetAsync(ctx().d_err, 0, sizeof(int), ctx().cur));
+    return true;
+}
+
+void *tcg_malloc(size_t bytes)
+{
+    if (!tcg::need_ctx()) return nullptr;
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes ? bytes : 1);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        tcg::fail("cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+        return nullptr;
+    }
+    return p;
+}
+
+bool tcg_free(void *p)
+{
+    if (!p) return true;
+    TCG_CUDA(cudaFree(p));
+    return true;
+}
+
+void *tcg_host_alloc(size_t bytes)
+{
+    void *p = nullptr;
+    cudaError_t e = cudaHostAlloc(&p, bytes ? bytes : 1, cudaHostAllocDefault);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        tcg::fail("cudaHostAlloc(%zu): %s", bytes, cudaGetErrorString(e));
+        return nullptr;
+    }
+    return p;
+}
+
+bool tcg_host_free(void *p)
+{
+    if (!p) return true;
+    TCG_CUDA(cudaFreeHost(p));
+    return true;
+}
+
+bool tcg_h2d(void *dst, const void *src, size_t bytes)
+{
+    if (!tcg::need_ctx()) return false;
+    TCG_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx().cur));
+    return true;
+}
+
+bool tcg_d2h(void *dst, const void *src, size_t bytes)
+{
+    if (!tcg::need_ctx()) return false;
+    TCG_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx().cur));
+    return true;
+}
+
+bool tcg_d2d(void *dst, const void *src, size_t bytes)
+{
+    if (!tcg::need_ctx()) return false;
+    TCG_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, ctx().cur));
+    return true;
+}
+
+bool tcg_memset(void *dst, int value, size_t bytes)
+{
+    if (!tcg::need_ctx()) return false;
+    TCG_CUDA(cudaMemsetAsync(dst, value, bytes, ctx().cur));
+    return true;
+}
+
+bool tcg_event_record(int slot)
+{
+    if (!tcg::need_ctx()) return false;
+    if (slot < 0 || slot >= 64) return tcg::fail("event slot %d out of range", slot);
+    TCG_CUDA(cudaEventRecord(ctx().ev[slot], ctx().cur));
+    return true;
+}
+
+float tcg_event_elapsed_ms(int a, int b)
+{
+    if (!ctx().ready || a < 0 || b < 0 || a >= 64 || b >= 64) return -1.0f;
+    float ms = -1.0f;
+    if (cudaEventSynchronize(ctx().ev[b]) != cudaSuccess ||
+        cudaEventElapsedTime(&ms, ctx().ev[a], ctx().ev[b]) != cudaSuccess) {
+        cudaGetLastError();
+        return -1.0f;
+    }
+    return ms;
+}
+
+/* ------------------------------------------------------------ device arena */
+
+tcg_arena_t tcg_arena_create(size_t cap, const char *name)
+{
+    tcg_arena_t a = { nullptr, 0, 0, 0, name ? name : "device arena" };
+    if (cap == 0 || !tcg::need_ctx()) return a;
+    void *p = nullptr;
+    if (cudaMalloc(&p, cap) != cudaSuccess) {
+        cudaGetLastError();
+        tcg::fail("device arena '%s': cannot reserve %zu bytes", a.name, cap);
+        return a;
+    }
+    a.base = (unsigned char *)p;
+    a.cap = cap;
+    return a;
+}
+
+void tcg_arena_destroy(tcg_arena_t *a)
+{
+    if (!a || !a->base) return;
+    cudaFree(a->base);
+    a->base = nullptr;
+    a->cap = a->used = a->peak = 0;
+}
+
+bool tcg_arena_ok(const tcg_arena_t *a) { return a && a->base; }
+
+void *tcg_arena_alloc(tcg_arena_t *a, size_t size, size_t align)
+{
+    if (!tcg_arena_ok(a)) return nullptr;
+    if (align == 0) align = 256;
+    if (align & (align - 1)) { tcg::fail("arena alignment %zu is not a power of two", align); return nullptr; }
+    size_t start = (a->used + align - 1) & ~(align - 1);
+    if (start < a->used || start > a->cap || size > a->cap - start) {
+        tcg::fail("device arena '%s' exhausted: wanted %zu, %zu free of %zu",
+                  a->name, size, a->cap - a->used, a->cap);
+        return nullptr;
+    }
+    a->used = start + size;
+    if (a->used > a->peak) a->peak = a->used;
+    return a->base + start;
+}
+
+size_t tcg_arena_mark(const tcg_arena_t *a) { return a ? a->used : 0; }
+
+void tcg_arena_release(tcg_arena_t *a, size_t mark)
+{
+    if (a && mark <= a->used) a->used = mark;
+}
+
+void tcg_arena_reset(tcg_arena_t *a)
+{
+    if (a) a->used = 0;
+}
+
+}  // extern "C"

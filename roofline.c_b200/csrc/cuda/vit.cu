@@ -1,0 +1,539 @@
+// vit.cu -- the batched CLIP ViT forward on one B200 (tcg_vit_*), the device
+// counterpart of roofline.c's tc_vit_encode (src/vit.c:305-391).
+//
+// Per forward of n images (M = n*T token rows):
+//   patches    pixels -> im2patch tf32 hi/lo                      [n*G*G, 3P^2]
+//   GEMM       patch embed; epilogue adds the position row and stores token
+//              r of image i at row i*T + 1 + r                    -> x
+//   cls        x[i*T] = cls + pos[0]
+//   LN         ln_pre in place on x                               (tap ln_pre)
+//   L blocks   LN1 -> h(hi/lo); GEMM qkv (+bias) -> qkv; attention -> a(hi/lo);
+//              GEMM out (+bias, +x) -> x; LN2 -> h; GEMM up (+bias, GELU)
+//              -> f(hi/lo); GEMM down (+bias, +x) -> x      (taps blk0, blk_last)
+//   LN         ln_post on the CLS rows (all rows when tapping)   (tap ln_post)
+//   proj       pooled[n, D] x proj[D, d_out], fp32 CUDA cores     (tap embedding)
+// All GEMMs are the 3xTF32 tcgen05 kernel; the layer stack between the patch
+// gather and the projection is recorded once per batch size as a CUDA graph.
+#include "gemm.cuh"
+#include "tcg_internal.h"
+
+#include <map>
+#include <memory>
+#include <string.h>
+#include <vector>
+
+struct tcg_vit {
+    int L, D, H, hd, F, P, S, G, T, d_out;
+    float eps;
+    bool quick;
+    int max_batch;
+    int device;
+    bool graphs = true;
+
+    // fp32 weights, one allocation (the unit of the NCCL broadcast)
+    float *wslab = nullptr;
+    size_t wslab_floats = 0;
+    // tf32 hi/lo of every GEMM weight
+    float *sslab = nullptr;
+    size_t sslab_floats = 0;
+
+    struct Layer {
+        const float *ln1_g, *ln1_b, *qkv_b, *out_b, *ln2_g, *ln2_b, *up_b, *down_b;
+        const float *qkv_h, *qkv_l, *out_h, *out_l, *up_h, *up_l, *down_h, *down_l;
+    };
+    std::vector<Layer> layers;
+    const float *patch_h = nullptr, *patch_l = nullptr, *cls = nullptr, *pos = nullptr;
+    const float *ln_pre_g = nullptr, *ln_pre_b = nullptr, *ln_post_g = nullptr, *ln_post_b = nullptr;
+    const float *proj = nullptr;
+
+    // activations
+    tcg_arena_t act{};
+    float *px = nullptr, *x = nullptr, *h_hi = nullptr, *h_lo = nullptr, *qkv = nullptr;
+    float *f_hi = nullptr, *f_lo = nullptr, *pooled = nullptr, *out = nullptr;
+    float *p_hi = nullptr, *p_lo = nullptr;   // alias f_hi / f_lo
+
+    struct Plans {
+        tcg::GemmPlan patch;
+        std::vector<tcg::GemmPlan> qkv, out, up, down;
+        cudaGraphExec_t graph = nullptr;
+    };
+    std::map<int, std::unique_ptr<Plans>> plans;
+
+    ~tcg_vit()
+    {
+        for (auto &kv : plans)
+            if (kv.second->graph) cudaGraphExecDestroy(kv.second->graph);
+        tcg_arena_destroy(&act);
+        if (wslab) cudaFree(wslab);
+        if (sslab) cudaFree(sslab);
+    }
+};
+
+namespace tcg {
+
+// Weight tensors in slab order: (element count, host pointer, device slot).
+struct WEntry {
+    size_t n;
+    const float *host;
+    const float **dev;
+};
+
+static size_t align_floats(size_t n) { return (n + 63) & ~(size_t)63; }   // 256-byte slots
+
+static std::vector<WEntry> weight_table(tcg_vit *v, const tc_vit_t *m)
+{
+    const size_t D = v->D, F = v->F, P = v->P, T = v->T;
+    std::vector<WEntry> t;
+    t.push_back({ D * 3 * P * P, m->patch_embd, nullptr });   // [0] patch_embd (split only)
+    t.push_back({ D, m->cls_token, &v->cls });
+    t.push_back({ T * D, m->pos_embd, &v->pos });
+    t.push_back({ D, m->ln_pre_g, &v->ln_pre_g });
+    t.push_back({ D, m->ln_pre_b, &v->ln_pre_b });
+    t.push_back({ D, m->ln_post_g, &v->ln_post_g });
+    t.push_back({ D, m->ln_post_b, &v->ln_post_b });
+    t.push_back({ D * (size_t)v->d_out, m->proj, &v->proj });
+    for (int i = 0; i < v->L; i++) {
+        const tc_vit_block_t &b = m->blocks[i];
+        tcg_vit::Layer &y = v->layers[i];
+        t.push_back({ D, b.ln1_g, &y.ln1_g });
+        t.push_back({ D, b.ln1_b, &y.ln1_b });
+        t.push_back({ 3 * D * D, b.qkv_w, nullptr });
+        t.push_back({ 3 * D, b.qkv_b, &y.qkv_b });
+        t.push_back({ D * D, b.out_w, nullptr });
+        t.push_back({ D, b.out_b, &y.out_b });
+        t.push_back({ D, b.ln2_g, &y.ln2_g });
+        t.push_back({ D, b.ln2_b, &y.ln2_b });
+        t.push_back({ F * D, b.up_w, nullptr });
+        t.push_back({ F, b.up_b, &y.up_b });
+        t.push_back({ D * F, b.down_w, nullptr });
+        t.push_back({ D, b.down_b, &y.down_b });
+    }
+    return t;
+}
+
+// Allocate the slabs and activation arena, point every field; weights are
+// not copied here.
+static tcg_vit *vit_alloc(const tc_vit_t *m, int max_batch, std::vector<WEntry> &table,
+                          std::vector<size_t> &offsets)
+{
+    if (max_batch <= 0) { fail("tcg_vit_upload: max_batch must be positive"); return nullptr; }
+    if (m->image % m->patch || m->d_model % m->n_head) { fail("tcg_vit_upload: inconsistent model dims"); return nullptr; }
+    std::unique_ptr<tcg_vit> v(new tcg_vit());
+    v->L = m->n_layer; v->D = m->d_model; v->H = m->n_head; v->hd = m->head_dim; v->F = m->d_ffn;
+    v->P = m->patch; v->S = m->image; v->G = m->grid; v->T = m->n_token; v->d_out = m->d_out;
+    v->eps = m->ln_eps; v->quick = m->quick_gelu; v->max_batch = max_batch; v->device = ctx().device;
+    if (v->T != v->G * v->G + 1 || v->hd * v->H != v->D) { fail("tcg_vit_upload: inconsistent model dims"); return nullptr; }
+    if ((v->D & 3) || (v->F & 3) || ((3 * v->P * v->P) & 3))
+        { fail("tcg_vit_upload: d_model, d_ffn and 3*patch^2 must be multiples of 4"); return nullptr; }
+    v->layers.resize(v->L);
+
+    table = weight_table(v.get(), m);
+    offsets.resize(table.size());
+    size_t total = 0;
+    for (size_t i = 0; i < table.size(); i++) {
+        offsets[i] = total;
+        total += align_floats(table[i].n);
+    }
+    v->wslab_floats = total;
+    if (cudaMalloc(&v->wslab, total * sizeof(float)) != cudaSuccess) {
+        cudaGetLastError();
+        fail("tcg_vit_upload: cannot allocate %zu MB of weights", total * 4 >> 20);
+        return nullptr;
+    }
+    for (size_t i = 0; i < table.size(); i++)
+        if (table[i].dev) *table[i].dev = v->wslab + offsets[i];
+
+    const size_t D = v->D, F = v->F, K0 = 3 * (size_t)v->P * v->P;
+    const size_t per_layer = 2 * align_floats(3 * D * D) + 2 * align_floats(D * D) + 2 * align_floats(F * D) +
+                             2 * align_floats(D * F);
+    v->sslab_floats = 2 * align_floats(D * K0) + per_layer * v->L;
+    if (cudaMalloc(&v->sslab, v->sslab_floats * sizeof(float)) != cudaSuccess) {
+        cudaGetLastError();
+        fail("tcg_vit_upload: cannot allocate %zu MB of split weights", v->sslab_floats * 4 >> 20);
+        return nullptr;
+    }
+    float *s = v->sslab;
+    auto take = [&](size_t n) { float *p = s; s += align_floats(n); return p; };
+    v->patch_h = take(D * K0); v->patch_l = take(D * K0);
+    for (auto &y : v->layers) {
+        y.qkv_h = take(3 * D * D); y.qkv_l = take(3 * D * D);
+        y.out_h = take(D * D); y.out_l = take(D * D);
+        y.up_h = take(F * D); y.up_l = take(F * D);
+        y.down_h = take(D * F); y.down_l = take(D * F);
+    }
+
+    const size_t n = (size_t)max_batch, T = v->T, G2 = (size_t)v->G * v->G;
+    const size_t f_floats = std::max(n * T * F, n * G2 * K0);
+    const size_t want = (n * 3 * v->S * v->S + n * T * D * 3 + n * T * 3 * D + 2 * f_floats +
+                         n * D + n * v->d_out) * sizeof(float) + 16 * 256;
+    v->act = tcg_arena_create(want, "vit activations");
+    if (!tcg_arena_ok(&v->act)) return nullptr;
+    auto alloc = [&](size_t floats) { return (float *)tcg_arena_alloc(&v->act, floats * sizeof(float), 256); };
+    v->px = alloc(n * 3 * v->S * v->S);
+    v->x = alloc(n * T * D);
+    v->h_hi = alloc(n * T * D);
+    v->h_lo = alloc(n * T * D);
+    v->qkv = alloc(n * T * 3 * D);
+    v->f_hi = alloc(f_floats);
+    v->f_lo = alloc(f_floats);
+    v->pooled = alloc(n * D);
+    v->out = alloc(n * v->d_out);
+    v->p_hi = v->f_hi;
+    v->p_lo = v->f_lo;
+    if (!v->out) return nullptr;
+    return v.release();
+}
+
+// Device-side split of the GEMM weights out of the fp32 slab.
+static bool split_weights(tcg_vit *v, const std::vector<WEntry> &table, const std::vector<size_t> &off)
+{
+    cudaStream_t s = ctx().cur;
+    const size_t D = v->D, F = v->F, K0 = 3 * (size_t)v->P * v->P;
+    if (!launch_split(v->wslab + off[0], (float *)v->patch_h, (float *)v->patch_l, D * K0, s)) return false;
+    for (int i = 0; i < v->L; i++) {
+        const size_t b = 8 + 12 * (size_t)i;   // first entry of block i in weight_table
+        tcg_vit::Layer &y = v->layers[i];
+        if (!launch_split(v->wslab + off[b + 2], (float *)y.qkv_h, (float *)y.qkv_l, 3 * D * D, s) ||
+            !launch_split(v->wslab + off[b + 4], (float *)y.out_h, (float *)y.out_l, D * D, s) ||
+            !launch_split(v->wslab + off[b + 8], (float *)y.up_h, (float *)y.up_l, F * D, s) ||
+            !launch_split(v->wslab + off[b + 10], (float *)y.down_h, (float *)y.down_l, D * F, s))
+            return false;
+    }
+    (void)table;
+    return true;
+}
+
+static tcg_vit::Plans *plans_for(tcg_vit *v, int n)
+{
+    auto it = v->plans.find(n);
+    if (it != v->plans.end()) return it->second.get();
+    std::unique_ptr<tcg_vit::Plans> p(new tcg_vit::Plans());
+    const int D = v->D, F = v->F, T = v->T, G2 = v->G * v->G, K0 = 3 * v->P * v->P, M = n * T;
+
+    GemmEpi e;
+    e.rowadd = v->pos;
+    e.ld_rowadd = D;
+    e.rgroup = G2;
+    e.rstride = T;
+    e.roff = 1;
+    e.out.plain = v->x;
+    e.out.ld = D;
+    if (!gemm_plan(p->patch, v->p_hi, v->p_lo, v->patch_h, v->patch_l, n * G2, D, K0, e)) return nullptr;
+
+    p->qkv.resize(v->L); p->out.resize(v->L); p->up.resize(v->L); p->down.resize(v->L);
+    for (int i = 0; i < v->L; i++) {
+        const tcg_vit::Layer &y = v->layers[i];
+        GemmEpi q;
+        q.bias = y.qkv_b;
+        q.out.plain = v->qkv;
+        q.out.ld = 3 * D;
+        GemmEpi o;
+        o.bias = y.out_b;
+        o.residual = v->x;
+        o.out.plain = v->x;
+        o.out.ld = D;
+        GemmEpi u;
+        u.bias = y.up_b;
+        u.act = v->quick ? 2 : 1;
+        u.out.hi = v->f_hi;
+        u.out.lo = v->f_lo;
+        u.out.ld = F;
+        GemmEpi d;
+        d.bias = y.down_b;
+        d.residual = v->x;
+        d.out.plain = v->x;
+        d.out.ld = D;
+        if (!gemm_plan(p->qkv[i], v->h_hi, v->h_lo, y.qkv_h, y.qkv_l, M, 3 * D, D, q) ||
+            !gemm_plan(p->out[i], v->h_hi, v->h_lo, y.out_h, y.out_l, M, D, D, o) ||   // a aliases h
+            !gemm_plan(p->up[i], v->h_hi, v->h_lo, y.up_h, y.up_l, M, F, D, u) ||
+            !gemm_plan(p->down[i], v->f_hi, v->f_lo, y.down_h, y.down_l, M, D, F, d))
+            return nullptr;
+    }
+    tcg_vit::Plans *raw = p.get();
+    v->plans[n] = std::move(p);
+    return raw;
+}
+
+typedef void (*TapFn)(void *ud, const char *name, const float *data, int rows, int cols);
+
+// Optional CUDA-event bracketing of every launch of an eager forward, by
+// kernel class, for the benchmark's per-kernel roofline figures.
+enum { K_GEMM = 0, K_ATTN = 1, K_NORM = 2, K_OTHER = 3, K_KINDS = 4 };
+
+struct Prof {
+    std::vector<cudaEvent_t> pool;
+    std::vector<int> kind;       // per recorded launch
+    size_t used = 0;
+    long launches = 0;           // all launches, profiled or not
+    bool on = false;
+
+    void begin(int k)
+    {
+        launches++;
+        if (!on) return;
+        if (used + 2 > pool.size()) {
+            for (int i = 0; i < 256; i++) {
+                cudaEvent_t e;
+                cudaEventCreate(&e);
+                pool.push_back(e);
+            }
+        }
+        cudaEventRecord(pool[used], ctx().cur);
+        kind.push_back(k);
+    }
+    void end()
+    {
+        if (!on) return;
+        cudaEventRecord(pool[used + 1], ctx().cur);
+        used += 2;
+    }
+};
+static Prof g_prof;   // one benchmark thread drives it
+
+#define PROF(kind, stmt)              \
+    do {                              \
+        g_prof.begin(kind);           \
+        const bool ok_ = (stmt);      \
+        g_prof.end();                 \
+        if (!ok_) return false;       \
+    } while (0)
+
+// Host-side tap delivery: copy `rows_per_img` x D rows of each image (row
+// stride ld between images) and call the user callback per image.
+struct Tapper {
+    TapFn fn;
+    void *ud;
+    float *host;          // staging, at least n*T*max(D, d_out) floats
+    bool deliver(const char *name, const float *dev, int n, int rows, int cols, size_t img_stride)
+    {
+        if (!fn) return true;
+        cudaStream_t s = ctx().cur;
+        TCG_CUDA(cudaMemcpy2DAsync(host, (size_t)rows * cols * sizeof(float), dev, img_stride * sizeof(float),
+                                   (size_t)rows * cols * sizeof(float), n, cudaMemcpyDeviceToHost, s));
+        TCG_CUDA(cudaStreamSynchronize(s));
+        for (int i = 0; i < n; i++) fn(ud, name, host + (size_t)i * rows * cols, rows, cols);
+        return true;
+    }
+};
+
+// Everything between the patch gather and the projection.
+static bool forward_body(tcg_vit *v, tcg_vit::Plans *p, int n, Tapper *tap)
+{
+    cudaStream_t s = ctx().cur;
+    int *err = ctx().d_err;
+    const int D = v->D, T = v->T, M = n * T;
+    OutSpec xs; xs.plain = v->x; xs.ld = D;
+    OutSpec hs; hs.hi = v->h_hi; hs.lo = v->h_lo; hs.ld = D;
+
+    PROF(K_GEMM, gemm_run(p->patch, s, err));
+    PROF(K_OTHER, launch_cls_rows(v->x, v->cls, v->pos, n, T, D, s));
+    PROF(K_NORM, launch_layernorm(v->x, D, v->ln_pre_g, v->ln_pre_b, M, D, v->eps, xs, s));
+    if (tap && !tap->deliver("ln_pre", v->x, n, T, D, (size_t)T * D)) return false;
+
+    for (int i = 0; i < v->L; i++) {
+        const tcg_vit::Layer &y = v->layers[i];
+        PROF(K_NORM, launch_layernorm(v->x, D, y.ln1_g, y.ln1_b, M, D, v->eps, hs, s));
+        PROF(K_GEMM, gemm_run(p->qkv[i], s, err));
+        PROF(K_ATTN, launch_mha(v->qkv, v->qkv + D, v->qkv + 2 * D, 3 * D, T, v->H, v->hd, n, hs, s));
+        PROF(K_GEMM, gemm_run(p->out[i], s, err));
+        PROF(K_NORM, launch_layernorm(v->x, D, y.ln2_g, y.ln2_b, M, D, v->eps, hs, s));
+        PROF(K_GEMM, gemm_run(p->up[i], s, err));
+        PROF(K_GEMM, gemm_run(p->down[i], s, err));
+        if (tap && i == 0 && !tap->deliver("blk0", v->x, n, T, D, (size_t)T * D)) return false;
+        if (tap && i == v->L - 1 && !tap->deliver("blk_last", v->x, n, T, D, (size_t)T * D)) return false;
+    }
+
+    if (tap) {
+        // ln_post over every row (into the free qkv buffer), then the CLS rows
+        OutSpec ls; ls.plain = v->qkv; ls.ld = D;
+        PROF(K_NORM, launch_layernorm(v->x, D, v->ln_post_g, v->ln_post_b, M, D, v->eps, ls, s));
+        if (!tap->deliver("ln_post", v->qkv, n, T, D, (size_t)T * D)) return false;
+        TCG_CUDA(cudaMemcpy2DAsync(v->pooled, D * sizeof(float), v->qkv, (size_t)T * D * sizeof(float),
+                                   D * sizeof(float), n, cudaMemcpyDeviceToDevice, s));
+    } else {
+        OutSpec ps; ps.plain = v->pooled; ps.ld = D;
+        PROF(K_NORM, launch_layernorm(v->x, T * D, v->ln_post_g, v->ln_post_b, n, D, v->eps, ps, s));
+    }
+    return true;
+}
+
+static bool forward(tcg_vit *v, const float *px, int n, float *out, Tapper *tap)
+{
+    if (ctx().device != v->device) return fail("model lives on device %d, thread uses %d", v->device, ctx().device);
+    if (n <= 0) return true;
+    if (n > v->max_batch) return fail("batch of %d exceeds the model's max_batch %d", n, v->max_batch);
+    cudaStream_t s = ctx().cur;
+    tcg_vit::Plans *p = plans_for(v, n);
+    if (!p) return false;
+    PROF(K_OTHER, launch_patches(px, n, v->S, v->P, v->p_hi, v->p_lo, s));
+    if (tap || !v->graphs || g_prof.on) {
+        if (!forward_body(v, p, n, tap)) return false;
+    } else if (!p->graph) {
+        // First call at this batch size: run eagerly (this also performs the
+        // one-time kernel attribute setup outside any capture), then record
+        // the same launches for the next calls.
+        if (!forward_body(v, p, n, nullptr)) return false;
+        cudaGraph_t g = nullptr;
+        TCG_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        const bool ok = forward_body(v, p, n, nullptr);
+        const cudaError_t ce = cudaStreamEndCapture(s, &g);
+        if (!ok) { if (g) cudaGraphDestroy(g); return false; }
+        TCG_CUDA(ce);
+        const cudaError_t ie = cudaGraphInstantiate(&p->graph, g, 0);
+        cudaGraphDestroy(g);
+        TCG_CUDA(ie);
+    } else {
+        TCG_CUDA(cudaGraphLaunch(p->graph, s));
+    }
+    PROF(K_OTHER, launch_gemm_simt(out, v->d_out, v->pooled, v->D, v->proj, v->d_out, nullptr, n, v->d_out,
+                                   v->D, false, s));
+    if (tap && !tap->deliver("embedding", out, n, 1, v->d_out, (size_t)v->d_out)) return false;
+    return true;
+}
+
+// Kernel launches of one tap-free forward (graph or eager: the same kernels).
+static int launches_per_forward(const tcg_vit *v) { return 2 + 4 + 7 * v->L; }
+
+}  // namespace tcg
+
+using namespace tcg;
+
+extern "C" {
+
+tcg_vit_t *tcg_vit_upload(const tc_vit_t *m, int max_batch)
+{
+    if (!need_ctx()) return nullptr;
+    std::vector<WEntry> table;
+    std::vector<size_t> off;
+    tcg_vit *v = vit_alloc(m, max_batch, table, off);
+    if (!v) return nullptr;
+    cudaStream_t s = ctx().cur;
+    for (size_t i = 0; i < table.size(); i++) {
+        if (!table[i].host) { delete v; fail("tcg_vit_upload: weight %zu unresolved", i); return nullptr; }
+        if (cudaMemcpyAsync(v->wslab + off[i], table[i].host, table[i].n * sizeof(float),
+                            cudaMemcpyHostToDevice, s) != cudaSuccess) {
+            cudaGetLastError();
+            delete v;
+            fail("tcg_vit_upload: weight copy failed");
+            return nullptr;
+        }
+    }
+    if (!split_weights(v, table, off) || cudaStreamSynchronize(s) != cudaSuccess) {
+        cudaGetLastError();
+        delete v;
+        if (!tcg_last_error()[0]) fail("tcg_vit_upload: weight preparation failed");
+        return nullptr;
+    }
+    return v;
+}
+
+void tcg_vit_release(tcg_vit_t *v)
+{
+    if (!v) return;
+    if (ctx().ready) cudaStreamSynchronize(ctx().cur);
+    delete v;
+}
+
+int tcg_vit_max_batch(const tcg_vit_t *v) { return v ? v->max_batch : 0; }
+
+size_t tcg_vit_device_bytes(const tcg_vit_t *v)
+{
+    return v ? (v->wslab_floats + v->sslab_floats) * sizeof(float) + v->act.cap : 0;
+}
+
+void tcg_vit_use_graphs(tcg_vit_t *v, bool on)
+{
+    if (v) v->graphs = on;
+}
+
+bool tcg_vit_encode_device(tcg_vit_t *v, const float *pixels, int n_images, float *out)
+{
+    if (!need_ctx()) return false;
+    if (!v) return fail("tcg_vit_encode_device: null model");
+    return forward(v, pixels, n_images, out, nullptr);
+}
+
+int tcg_vit_launches_per_forward(const tcg_vit_t *v) { return v ? launches_per_forward(v) : 0; }
+
+void tcg_vit_profile_begin(void)
+{
+    g_prof.kind.clear();
+    g_prof.used = 0;
+    g_prof.on = true;
+}
+
+bool tcg_vit_profile_end(float ms[4], int count[4])
+{
+    g_prof.on = false;
+    for (int k = 0; k < K_KINDS; k++) { ms[k] = 0.0f; count[k] = 0; }
+    if (!need_ctx()) return false;
+    TCG_CUDA(cudaStreamSynchronize(ctx().cur));
+    for (size_t i = 0; i < g_prof.kind.size(); i++) {
+        float t = 0.0f;
+        TCG_CUDA(cudaEventElapsedTime(&t, g_prof.pool[2 * i], g_prof.pool[2 * i + 1]));
+        ms[g_prof.kind[i]] += t;
+        count[g_prof.kind[i]]++;
+    }
+    g_prof.kind.clear();
+    g_prof.used = 0;
+    return true;
+}
+
+size_t tcg_vit_tap_staging_floats(const tcg_vit_t *v, int n_images)
+{
+    return v ? (size_t)n_images * v->T * (v->D > v->d_out ? v->D : v->d_out) : 0;
+}
+
+bool tcg_vit_encode_batch_staged(tcg_vit_t *v, const float *pixels, int n_images, float *out,
+                                 tc_vit_tap_fn tap, void *ud, float *staging)
+{
+    if (!need_ctx()) return false;
+    if (!v) return fail("tcg_vit_encode_batch: null model");
+    if (n_images <= 0) return true;
+    if (n_images > v->max_batch) return fail("batch of %d exceeds the model's max_batch %d", n_images, v->max_batch);
+    if (tap && !staging) return fail("tcg_vit_encode_batch: no tap staging");
+    cudaStream_t s = ctx().cur;
+    const size_t px_bytes = (size_t)n_images * 3 * v->S * v->S * sizeof(float);
+    TCG_CUDA(cudaMemcpyAsync(v->px, pixels, px_bytes, cudaMemcpyHostToDevice, s));
+    Tapper t{ (TapFn)tap, ud, staging };
+    if (!forward(v, v->px, n_images, v->out, tap ? &t : nullptr)) return false;
+    TCG_CUDA(cudaMemcpyAsync(out, v->out, (size_t)n_images * v->d_out * sizeof(float), cudaMemcpyDeviceToHost, s));
+    TCG_CUDA(cudaStreamSynchronize(s));
+    return true;
+}
+
+bool tcg_vit_encode_batch(tcg_vit_t *v, const float *pixels, int n_images, float *out, tc_vit_tap_fn tap, void *ud)
+{
+    std::vector<float> staging;
+    if (tap && v && n_images > 0) staging.resize(tcg_vit_tap_staging_floats(v, n_images));
+    return tcg_vit_encode_batch_staged(v, pixels, n_images, out, tap, ud, tap ? staging.data() : nullptr);
+}
+
+tcg_vit_t *tcg_vit_upload_bcast(const tc_vit_t *m, int max_batch, int rank, int nranks, const unsigned char id[128])
+{
+    if (!need_ctx()) return nullptr;
+    std::vector<WEntry> table;
+    std::vector<size_t> off;
+    tcg_vit *v = vit_alloc(m, max_batch, table, off);
+    if (!v) return nullptr;
+    cudaStream_t s = ctx().cur;
+    bool ok = true;
+    if (rank == 0) {
+        for (size_t i = 0; ok && i < table.size(); i++)
+            ok = table[i].host && cudaMemcpyAsync(v->wslab + off[i], table[i].host, table[i].n * sizeof(float),
+                                                  cudaMemcpyHostToDevice, s) == cudaSuccess;
+        if (!ok) { cudaGetLastError(); fail("tcg_vit_upload_bcast: weight copy failed"); }
+    }
+    // every rank enters the collective, so a failed upload on rank 0 still
+    // lets the others finish (they receive whatever rank 0 holds)
+    if (!broadcast_once(v->wslab, v->wslab_floats, rank, nranks, id)) ok = false;
+    if (ok) ok = split_weights(v, table, off) && cudaStreamSynchronize(s) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        delete v;
+        return nullptr;
+    }
+    return v;
+}
+
+}  // extern "C"

@@ -1,0 +1,125 @@
+#!/usr/bin/env python3
+"""Regenerate the committed golden fixtures in tests/golden/.
+
+Runs only where the reference tree and the third-party `gguf` package are
+available (the build container); the fixtures it writes travel with the
+repository, so the GPU tests never need either.
+
+  ops.gguf           byte copy of roofline.c's op golden vectors
+                     (tests/fixtures/ops.gguf, written by its
+                     tools/gen_op_fixtures.py, numpy fp64 references), checked
+                     against the sha256 recorded below.
+  kquant_golden.npz  seeded Q4_K / Q6_K superblocks, including edge cases
+                     (zero, subnormal, negative and largest fp16 scales; all-0
+                     and all-1 bit patterns), with the fp32 values produced by
+                     gguf 0.19.0's gguf.quants.dequantize -- an implementation
+                     independent of this repository's oracle.
+  vit_golden.npz     outputs of the reference's own tc_vit_encode
+                     (oracle/_ref/libtcref.so, built from the reference
+                     sources) on seeded synthetic models: embedding, CLS row
+                     and per-tap float64 sums for two shapes.
+
+    python tests/golden/make_golden.py
+"""
+import hashlib
+import os
+import shutil
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path[:0] = [ROOT, os.path.join(ROOT, "roofline.c_b200")]
+import oracle  # noqa: E402
+import tcg_gguf as G  # noqa: E402
+
+OUT = os.path.dirname(os.path.abspath(__file__))
+REF = os.environ.get("TC_REFERENCE", "/root/reference")
+OPS_SHA256 = "56160063ceb733fe6ad2f8022bb8c2f75b64181511109fb657cc3b040537279a"
+
+
+def ops_fixture():
+    src = os.path.join(REF, "tests", "fixtures", "ops.gguf")
+    digest = hashlib.sha256(open(src, "rb").read()).hexdigest()
+    assert digest == OPS_SHA256, f"reference fixture changed: {digest}"
+    shutil.copyfile(src, os.path.join(OUT, "ops.gguf"))
+
+
+def _edge_q4k():
+    rows = []
+    for d, dmin, fill in ((0x0000, 0x0000, 0x5A), (0x0001, 0x03FF, 0xFF), (0x8400, 0x3C00, 0x00),
+                          (0x7BFF, 0x7BFF, 0xFF), (0xBC00, 0x0001, 0x0F), (0x3555, 0x8001, 0xF0)):
+        b = np.full(144, fill, np.uint8)
+        b[0:2] = np.array([d], np.uint16).view(np.uint8)
+        b[2:4] = np.array([dmin], np.uint16).view(np.uint8)
+        rows.append(b)
+    b = G.make_q4k_blocks(1, 99)[0].copy()
+    b[4:16] = 0xFF          # every 6-bit scale and min = 63, top bits set
+    rows.append(b)
+    return np.stack(rows)
+
+
+def _edge_q6k():
+    rows = []
+    for d, fill, sc in ((0x0000, 0x33, 5), (0x0001, 0xFF, -128), (0x8400, 0x00, 127),
+                        (0x7BFF, 0xFF, 127), (0xBC00, 0x0F, -1), (0x03FF, 0xF0, -128)):
+        b = np.full(210, fill, np.uint8)
+        b[192:208] = np.array([sc] * 16, np.int8).view(np.uint8)
+        b[208:210] = np.array([d], np.uint16).view(np.uint8)
+        rows.append(b)
+    return np.stack(rows)
+
+
+def kquant_fixture():
+    import gguf
+    from gguf import quants
+    out = {}
+    for tag, qt, rand, edge in (("q4k", G.Q4_K, G.make_q4k_blocks(57, 2), _edge_q4k()),
+                                ("q6k", G.Q6_K, G.make_q6k_blocks(57, 2), _edge_q6k())):
+        blocks = np.concatenate([rand, edge])
+        vals = quants.dequantize(blocks.reshape(-1), gguf.GGMLQuantizationType(qt)).reshape(-1)
+        vals = np.ascontiguousarray(vals, np.float32)
+        mine = oracle.dequant(blocks.reshape(-1), vals.size, qt)
+        assert np.array_equal(mine.view(np.uint32), vals.view(np.uint32)), tag
+        out[f"{tag}_blocks"] = blocks
+        out[f"{tag}_values"] = vals
+    out["gguf_version"] = np.array(gguf.__name__ + " 0.19.0")
+    np.savez_compressed(os.path.join(OUT, "kquant_golden.npz"), **out)
+
+
+# (name, config overrides, weight seed, pixel seed)
+VIT_CASES = (
+    ("b32x2", dict(name="vit-b32", n_layer=2), 0, 1),
+    ("l14x1", dict(name="vit-l14", n_layer=1), 0, 1),
+)
+
+
+def vit_fixture():
+    import tempfile
+    out = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        for tag, over, wseed, pseed in VIT_CASES:
+            over = dict(over)
+            name = over.pop("name")
+            cfg = G.vit_config(name, **over)
+            w = G.make_vit_weights(cfg, wseed)
+            path = os.path.join(tmp, tag + ".gguf")
+            G.write_vit_gguf(path, cfg, w)
+            px = G.make_pixels(1, cfg["image"], pseed)[0]
+            rv = oracle.RefVit(path)
+            taps = rv.encode(px, cfg["d_out"], taps=True)
+            rv.close()
+            out[f"{tag}.embedding"] = taps["embedding"]
+            for k in ("ln_pre", "blk0", "blk_last", "ln_post"):
+                t = taps[k].astype(np.float64)
+                out[f"{tag}.{k}.cls"] = taps[k][0]
+                out[f"{tag}.{k}.sum"] = np.array([t.sum(), (t * t).sum()])
+    np.savez_compressed(os.path.join(OUT, "vit_golden.npz"), **out)
+
+
+if __name__ == "__main__":
+    oracle.build(with_ref=True)
+    ops_fixture()
+    kquant_fixture()
+    vit_fixture()
+    print("golden fixtures written to", OUT)

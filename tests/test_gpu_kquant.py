@@ -1,0 +1,144 @@
+"""K-quant dequant and fused dequant-matvec on the GPU against the oracle.
+
+Dequant is integer unpacking plus fp32 scaling in the restatement's exact
+rounding order, so the bar is bit-exact. The matvec sums in a different
+order from the reference's sequential dot product, so its bar is
+max|y - y_ref| <= 1e-4 * max|y_ref|.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle
+import tcg
+import tcg_gguf as G
+from fixtures_io import kquant_golden
+
+pytestmark = pytest.mark.gpu
+
+MATVEC_TOL = 1e-4
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def dev_dequant(raw: np.ndarray, n: int, qtype: int, src_offset: int = 0) -> np.ndarray:
+    L = tcg.lib()
+    with tcg.DeviceBuffer(raw.nbytes + 64) as src, tcg.DeviceBuffer(n * 4) as dst:
+        src.upload(raw, offset=src_offset)
+        tcg.check(L.tcg_dequant(dst.ptr, src.ptr + src_offset, n, qtype), "tcg_dequant")
+        return dst.download(n)
+
+
+def test_f16_every_input_bit_exact(gpu):
+    h = np.arange(65536, dtype=np.uint16)
+    got = dev_dequant(h.view(np.uint8), 65536, G.F16)
+    assert np.array_equal(bits(got), bits(oracle.f16_to_f32_all()))
+
+
+@pytest.mark.parametrize("tag,qt", [("q4k", G.Q4_K), ("q6k", G.Q6_K)])
+def test_golden_blocks_bit_exact(gpu, tag, qt):
+    g = kquant_golden()
+    got = dev_dequant(g[f"{tag}_blocks"].reshape(-1), g[f"{tag}_values"].size, qt)
+    assert np.array_equal(bits(got), bits(g[f"{tag}_values"]))
+
+
+@pytest.mark.parametrize("qt", [G.Q4_K, G.Q6_K])
+def test_full_size_bit_exact(gpu, qt):
+    # the 14336 x 4096 tensor of the dequant benchmark, seeded as there
+    raw = G.make_kquant(qt, 14336, 4096, seed=2)
+    n = 14336 * 4096
+    got = dev_dequant(raw, n, qt)
+    assert np.array_equal(bits(got), bits(oracle.dequant(raw, n, qt)))
+
+
+@pytest.mark.parametrize("qt", [G.Q4_K, G.Q6_K])
+@pytest.mark.parametrize("nblocks", [1, 7, 8, 9, 13, 1001])
+@pytest.mark.parametrize("offset", [0, 2, 1])
+def test_ragged_counts_and_alignment(gpu, qt, nblocks, offset):
+    raw = G.make_kquant(qt, nblocks, 256, seed=nblocks + 17 * offset)
+    got = dev_dequant(raw, nblocks * 256, qt, src_offset=offset)
+    assert np.array_equal(bits(got), bits(oracle.dequant(raw, nblocks * 256, qt)))
+
+
+def test_rejections(gpu):
+    L = tcg.lib()
+    with tcg.DeviceBuffer(4096) as b:
+        assert not L.tcg_dequant(b.ptr, b.ptr, 300, G.Q4_K)
+        assert b"superblocks" in L.tcg_last_error()
+        assert not L.tcg_dequant(b.ptr, b.ptr, 256, 13)
+        assert not L.tcg_dequant(b.ptr + 4, b.ptr, 256, G.Q4_K)     # dst not 16-byte aligned
+        assert L.tcg_dequant(b.ptr, b.ptr, 0, G.Q4_K)              # empty is fine
+
+
+@pytest.mark.parametrize("qt", [G.F16, G.Q4_K, G.Q6_K])
+def test_host_seam_tc_dequant(gpu, qt):
+    L = tcg.lib()
+    if qt == G.F16:
+        raw = np.random.default_rng(4).integers(0, 65536, 4096, dtype=np.uint16).view(np.uint8)
+        n = 4096
+    else:
+        raw = G.make_kquant(qt, 37, 256, seed=9)
+        n = 37 * 256
+    out = np.empty(n, np.float32)
+    assert L.tc_dequant(out.ctypes.data, raw.ctypes.data, n, qt), tcg.err()
+    want = oracle.dequant(raw, n, qt)
+    same = (bits(out) == bits(want)) | (np.isnan(out) & np.isnan(want))
+    assert same.all()
+
+
+def test_dequant_view_from_gguf(gpu, tmp_path):
+    L = tcg.lib()
+    raw = G.make_kquant(G.Q4_K, 8, 1024, seed=5)
+    path = str(tmp_path / "q.gguf")
+    G.write_gguf(path, {"general.architecture": "x"}, [("w", raw, G.Q4_K, (8, 1024))])
+    a = L.arena_create(1 << 20, b"x")
+    g = tcg.Gguf()
+    assert L.gguf_open(C.byref(g), path.encode(), C.byref(a))
+    t = L.gguf_tensor(C.byref(g), b"w")
+    da = L.tcg_arena_create(1 << 22, b"dev")
+    conv = C.c_bool(False)
+    p = L.tcg_dequant_view(t, C.byref(da), C.byref(conv))
+    assert p and conv.value
+    got = np.empty(8192, np.float32)
+    assert L.tcg_d2h(got.ctypes.data, p, got.nbytes) and L.tcg_sync()
+    assert np.array_equal(bits(got), bits(oracle.dequant(raw, 8192, G.Q4_K)))
+    # host view through the reference-named seam
+    hv = L.tc_dequant_view(t, C.byref(a), C.byref(conv))
+    assert hv and conv.value
+    assert np.array_equal(np.frombuffer(C.string_at(hv, 8192 * 4), np.uint32), bits(got))
+    L.tcg_arena_destroy(C.byref(da))
+    L.gguf_close(C.byref(g))
+    L.arena_destroy(C.byref(a))
+
+
+def dev_matvec(raw, x, N, K, qt):
+    L = tcg.lib()
+    with tcg.DeviceBuffer.from_array(raw) as w, tcg.DeviceBuffer.from_array(x) as xb, \
+            tcg.DeviceBuffer(N * 4) as y:
+        tcg.check(L.tcg_matvec_q(y.ptr, w.ptr, xb.ptr, N, K, qt), "tcg_matvec_q")
+        return y.download(N)
+
+
+@pytest.mark.parametrize("qt,N,K,seed", [
+    (G.Q4_K, 4096, 14336, 3),      # the decode matvec
+    (G.Q6_K, 128256, 4096, 5),     # the output head
+    (G.Q4_K, 1, 256, 7), (G.Q6_K, 3, 768, 8), (G.Q4_K, 100, 2304, 9),
+    (G.Q6_K, 5000, 512, 10), (G.Q4_K, 70, 4096, 11),
+])
+def test_matvec_vs_dequant_then_linear(gpu, qt, N, K, seed):
+    raw = G.make_kquant(qt, N, K, seed=seed)
+    x = np.random.default_rng(seed + 100).standard_normal(K).astype(np.float32)
+    got = dev_matvec(raw, x, N, K, qt)
+    want = oracle.matvec_q(raw, x, N, K, qt)
+    err = np.abs(got.astype(np.float64) - want).max() / np.abs(want).max()
+    assert err <= MATVEC_TOL, err
+
+
+def test_matvec_rejections(gpu):
+    L = tcg.lib()
+    assert not L.tcg_matvec_q(None, None, None, 4, 300, G.Q4_K)
+    assert b"multiple of 256" in L.tcg_last_error()
+    assert not L.tcg_matvec_q(None, None, None, 4, 256, G.F16)

@@ -1,0 +1,152 @@
+"""Op-level parity of the device kernels (tcg_* in include/tcg.h).
+
+* the reference's golden vectors (tests/fixtures/ops.gguf) with the
+  reference's own per-op tolerances (tests/test_ops.c:74-148);
+* LayerNorm against the oracle on ViT-width rows (one offset by 1e4);
+* the 3xTF32 tcgen05 GEMM in every tile configuration on ragged shapes,
+  against the oracle's sequential fp32 GEMM: max|err| <= 1e-5 * max|y|.
+"""
+import numpy as np
+import pytest
+
+import oracle
+import tcg
+from fixtures_io import check_close, ops_golden
+
+pytestmark = pytest.mark.gpu
+
+GEMM_TOL = 1e-5
+
+
+class Dev:
+    """Upload numpy arrays, run, download."""
+
+    def __init__(self):
+        self.bufs = []
+
+    def put(self, a):
+        b = tcg.DeviceBuffer.from_array(np.ascontiguousarray(a, np.float32))
+        self.bufs.append(b)
+        return b.ptr
+
+    def empty(self, n):
+        b = tcg.DeviceBuffer(int(n) * 4)
+        self.bufs.append(b)
+        return b
+
+    def close(self):
+        for b in self.bufs:
+            b.close()
+
+
+@pytest.fixture()
+def dev(gpu):
+    d = Dev()
+    yield d
+    d.close()
+
+
+def test_golden_vectors(dev):
+    L = tcg.lib()
+    kv, t = ops_golden()
+    for tag in ("small", "wide"):
+        M, N, K = kv[f"gemm.{tag}.M"], kv[f"gemm.{tag}.N"], kv[f"gemm.{tag}.K"]
+        y = dev.empty(M * N)
+        tcg.check(L.tcg_gemm(y.ptr, dev.put(t[f"gemm.{tag}.A"]), dev.put(t[f"gemm.{tag}.B"]), M, N, K, True))
+        check_close(y.download(M * N), t[f"gemm.{tag}.C"], 2e-4, 1e-5, f"gemm {tag}")
+    M, N, K = kv["linear.M"], kv["linear.N"], kv["linear.K"]
+    y = dev.empty(M * N)
+    tcg.check(L.tcg_linear(y.ptr, dev.put(t["linear.x"]), dev.put(t["linear.W"]), dev.put(t["linear.b"]), M, N, K))
+    check_close(y.download(M * N), t["linear.y"], 1e-5, 1e-5, "linear")
+    rows, cols = kv["ln.rows"], kv["ln.cols"]
+    y = dev.empty(rows * cols)
+    tcg.check(L.tcg_layernorm(y.ptr, dev.put(t["ln.x"]), dev.put(t["ln.gamma"]), dev.put(t["ln.beta"]),
+                              rows, cols, kv["ln.eps"]))
+    check_close(y.download(rows * cols), t["ln.out"], 1e-4, 1e-4, "layernorm")
+    n = t["gelu.x"].size
+    y, q = dev.empty(n), dev.empty(n)
+    gx = dev.put(t["gelu.x"])
+    tcg.check(L.tcg_gelu(y.ptr, gx, n))
+    tcg.check(L.tcg_gelu_quick(q.ptr, gx, n))
+    ge, gq = y.download(n), q.download(n)
+    check_close(ge, t["gelu.exact"], 1e-6, 1e-6, "gelu")
+    check_close(gq, t["gelu.quick"], 1e-6, 1e-6, "gelu quick")
+    assert np.abs(ge - gq).max() > 0.01
+    rows, cols = kv["softmax.rows"], kv["softmax.cols"]
+    y = dev.empty(rows * cols)
+    tcg.check(L.tcg_softmax_rows(y.ptr, dev.put(t["softmax.x"]), rows, cols))
+    sm = y.download((rows, cols))
+    check_close(sm, t["softmax.out"], 1e-6, 1e-5, "softmax")
+    assert np.all(np.abs(sm.astype(np.float64).sum(1) - 1.0) < 1e-5)
+    T, H, HD = kv["mha.T"], kv["mha.n_head"], kv["mha.head_dim"]
+    y = dev.empty(T * H * HD)
+    tcg.check(L.tcg_mha(y.ptr, dev.put(t["mha.q"]), dev.put(t["mha.k"]), dev.put(t["mha.v"]), T, H, HD))
+    check_close(y.download(T * H * HD), t["mha.out"], 1e-5, 1e-5, "mha")
+
+
+def test_add_and_scale(dev):
+    L = tcg.lib()
+    rng = np.random.default_rng(1)
+    a, b = rng.standard_normal(1000).astype(np.float32), rng.standard_normal(1000).astype(np.float32)
+    y = dev.empty(1000)
+    tcg.check(L.tcg_add(y.ptr, dev.put(a), dev.put(b), 1000))
+    assert np.array_equal(y.download(1000), oracle.add(a, b))
+    tcg.check(L.tcg_scale(y.ptr, dev.put(a), 0.37, 1000))
+    assert np.array_equal(y.download(1000), oracle.scale(a, np.float32(0.37)))
+
+
+@pytest.mark.parametrize("rows,cols", [(300, 768), (17, 1024), (5, 64), (3, 100)])
+def test_layernorm_vs_oracle(dev, rows, cols):
+    L = tcg.lib()
+    rng = np.random.default_rng(rows)
+    x = rng.standard_normal((rows, cols)).astype(np.float32)
+    x[rows // 2] += 1e4
+    g = (1 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(cols)).astype(np.float32)
+    y = dev.empty(rows * cols)
+    tcg.check(L.tcg_layernorm(y.ptr, dev.put(x), dev.put(g), dev.put(b), rows, cols, 1e-5))
+    got, want = y.download((rows, cols)), oracle.layernorm(x, g, b, rows, cols, 1e-5)
+    # double statistics summed in another order: identical but for rare 1-ulp ties
+    ulp = np.abs(got.view(np.int32).astype(np.int64) - want.view(np.int32).astype(np.int64))
+    assert ulp.max() <= 2 and (ulp == 0).mean() > 0.999
+
+
+@pytest.mark.parametrize("T,H,HD", [(50, 12, 64), (257, 16, 64), (17, 4, 16), (33, 2, 96)])
+def test_mha_vs_oracle(dev, T, H, HD):
+    L = tcg.lib()
+    rng = np.random.default_rng(T)
+    q, k, v = (rng.standard_normal((T, H * HD)).astype(np.float32) for _ in range(3))
+    y = dev.empty(T * H * HD)
+    tcg.check(L.tcg_mha(y.ptr, dev.put(q), dev.put(k), dev.put(v), T, H, HD))
+    got, want = y.download((T, H * HD)), oracle.mha(q, k, v, T, H, HD)
+    assert np.abs(got - want).max() <= 1e-5 * np.abs(want).max()
+
+
+SHAPES = [(1, 64, 4), (127, 100, 12), (129, 200, 588), (300, 768, 768), (50, 2304, 768), (261, 130, 3072)]
+
+
+@pytest.mark.parametrize("cfg", list(range(8)) + [-2])
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_linear_every_config(dev, cfg, M, N, K):
+    L = tcg.lib()
+    rng = np.random.default_rng(M * 7 + N + K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    W = (rng.standard_normal((N, K)) * 0.05).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    y = dev.empty(M * N)
+    tcg.check(L.tcg_linear_cfg(y.ptr, dev.put(x), dev.put(W), dev.put(b), M, N, K, cfg), f"cfg {cfg}")
+    got, want = y.download((M, N)), oracle.linear(x, W, b, M, N, K)
+    err = np.abs(got.astype(np.float64) - want).max() / np.abs(want).max()
+    assert err <= GEMM_TOL, (cfg, err)
+    assert tcg.lib().tcg_device_error() == 0
+
+
+def test_gemm_untransposed_and_odd_k(dev):
+    L = tcg.lib()
+    rng = np.random.default_rng(2)
+    A = rng.standard_normal((9, 11)).astype(np.float32)
+    B = rng.standard_normal((11, 7)).astype(np.float32)
+    y = dev.empty(63)
+    tcg.check(L.tcg_gemm(y.ptr, dev.put(A), dev.put(B), 9, 7, 11, False))
+    want = oracle.gemm(A, B, 9, 7, 11, b_transposed=False)
+    assert np.abs(y.download((9, 7)) - want).max() <= 1e-5 * np.abs(want).max()

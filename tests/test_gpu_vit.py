@@ -1,0 +1,150 @@
+"""The batched ViT forward against the reference.
+
+Bar (stated in the hot-path spec): every tap and the embedding within
+max|err| <= 1e-4 * max|ref| per image, plus the reference's end-to-end gate
+of embedding cosine >= 0.9999 (tests/test_vit.c:197).
+
+* the committed outputs of the reference's own tc_vit_encode (vit_golden.npz)
+  through the reference-shaped entry point tc_vit_encode;
+* the full-depth ViT-B/32 over a batch, per image, against the oracle;
+* batch invariance, graph replay == eager, and the argument checks.
+"""
+import numpy as np
+import pytest
+
+import oracle
+import tcg
+import tcg_gguf as G
+from fixtures_io import rel_inf, vit_golden
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-4
+TAPS = ("ln_pre", "blk0", "blk_last", "ln_post")
+
+
+def cosine(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(a @ b / np.linalg.norm(a) / np.linalg.norm(b))
+
+
+def model(cache_dir, name, seed=0, **over):
+    path, cfg = G.cached_vit_gguf(cache_dir, name, seed, **over)
+    return path, cfg
+
+
+CASES = {"b32x2": ("vit-b32", dict(n_layer=2)), "l14x1": ("vit-l14", dict(n_layer=1))}
+
+
+@pytest.mark.parametrize("tag", sorted(CASES))
+def test_reference_golden_through_tc_vit_encode(gpu, cache_dir, tag):
+    g = vit_golden()
+    name, over = CASES[tag]
+    path, cfg = model(cache_dir, name, **over)
+    m = tcg.VitModel(path)
+    try:
+        px = G.make_pixels(1, cfg["image"], 1)[0]
+        out, taps = m.encode_single(px, taps=True)
+        assert set(taps) == set(TAPS) | {"embedding"}
+        assert rel_inf(out, g[f"{tag}.embedding"]) <= TOL
+        assert cosine(out, g[f"{tag}.embedding"]) >= 0.9999
+        for k in TAPS:
+            assert taps[k].shape == (cfg["n_token"], cfg["d_model"])
+            assert rel_inf(taps[k][0], g[f"{tag}.{k}.cls"]) <= TOL, k
+            t64 = taps[k].astype(np.float64)
+            s, ss = g[f"{tag}.{k}.sum"]
+            assert abs(t64.sum() - s) <= TOL * np.abs(t64).sum()
+            assert abs((t64 * t64).sum() - ss) <= 10 * TOL * ss
+    finally:
+        m.close()
+
+
+def test_b32_full_depth_batch_vs_oracle(gpu, cache_dir):
+    path, cfg = model(cache_dir, "vit-b32")
+    w = G.make_vit_weights(cfg, 0)
+    px = G.make_pixels(3, cfg["image"], 1)
+    port = oracle.PortVit(cfg, w)
+    m = tcg.VitModel(path)
+    try:
+        m.upload(8)
+        out, taps = m.encode(px, taps=True)
+        for i in (0, 2):
+            ref = port.forward(px[i])
+            assert rel_inf(out[i], ref["embedding"]) <= TOL
+            assert cosine(out[i], ref["embedding"]) >= 0.9999
+            for k in TAPS:
+                assert rel_inf(taps[k][i], ref[k]) <= TOL, (i, k, rel_inf(taps[k][i], ref[k]))
+    finally:
+        m.close()
+
+
+def test_l14_two_layers_vs_oracle(gpu, cache_dir):
+    path, cfg = model(cache_dir, "vit-l14", n_layer=2)
+    w = G.make_vit_weights(cfg, 0)
+    px = G.make_pixels(2, cfg["image"], 4)
+    m = tcg.VitModel(path)
+    try:
+        m.upload(2)
+        out, taps = m.encode(px, taps=True)
+        ref = oracle.PortVit(cfg, w).forward(px[1])
+        assert rel_inf(out[1], ref["embedding"]) <= TOL
+        for k in TAPS:
+            assert rel_inf(taps[k][1], ref[k]) <= TOL, k
+    finally:
+        m.close()
+
+
+def test_batch_invariance_and_graph_replay(gpu, cache_dir):
+    path, cfg = model(cache_dir, "vit-b32", n_layer=3)
+    px = G.make_pixels(9, cfg["image"], 7)
+    m = tcg.VitModel(path)
+    try:
+        m.upload(9)
+        full, _ = m.encode(px)                  # first call: eager, then recorded
+        again, _ = m.encode(px)                 # graph replay
+        assert np.array_equal(full, again)
+        one, _ = m.encode(px[4:5])
+        assert np.array_equal(one[0], full[4])  # same K order whatever the batch
+        tcg.lib().tcg_vit_use_graphs(m.dev, False)
+        eager, _ = m.encode(px)
+        assert np.array_equal(eager, full)
+        assert tcg.lib().tcg_device_error() == 0
+    finally:
+        m.close()
+
+
+def test_quick_gelu_model(gpu, tmp_path):
+    cfg = G.vit_config("vit-b32", n_layer=1)
+    w = G.make_vit_weights(cfg, 3)
+    path = str(tmp_path / "q.gguf")
+    G.write_vit_gguf(path, cfg, w, activation="gelu_quick")
+    px = G.make_pixels(1, cfg["image"], 2)
+    m = tcg.VitModel(path)
+    try:
+        m.upload(1)
+        out, _ = m.encode(px)
+        ref = oracle.PortVit(cfg, w, quick_gelu=True).forward(px[0], taps=False)
+        assert rel_inf(out[0], ref["embedding"]) <= TOL
+    finally:
+        m.close()
+
+
+def test_device_entry_and_limits(gpu, cache_dir):
+    L = tcg.lib()
+    path, cfg = model(cache_dir, "vit-b32", n_layer=1)
+    px = G.make_pixels(4, cfg["image"], 3)
+    m = tcg.VitModel(path)
+    try:
+        m.upload(4)
+        host_out, _ = m.encode(px)
+        with tcg.DeviceBuffer.from_array(px) as dpx, tcg.DeviceBuffer(4 * cfg["d_out"] * 4) as dout:
+            tcg.check(L.tcg_vit_encode_device(m.dev, dpx.ptr, 4, dout.ptr))
+            tcg.sync()
+            assert np.array_equal(dout.download((4, cfg["d_out"])), host_out)
+            assert not L.tcg_vit_encode_device(m.dev, dpx.ptr, 5, dout.ptr)
+            assert b"max_batch" in L.tcg_last_error()
+            assert L.tcg_vit_encode_device(m.dev, dpx.ptr, 0, dout.ptr)
+        assert L.tcg_vit_max_batch(m.dev) == 4
+        assert L.tcg_vit_device_bytes(m.dev) > 0
+    finally:
+        m.close()
