@@ -59,6 +59,17 @@ def peaks():
         return FALLBACK_PEAKS, "fallback"
 
 
+def shard_range(batch: int, world: int, rank: int) -> tuple:
+    """Contiguous image range [lo, hi) of `rank`; the batch must divide evenly
+    so every rank runs the same shapes (and the same recorded graph)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} of {world}")
+    if batch % world:
+        raise ValueError(f"batch {batch} does not shard over {world} GPUs")
+    per = batch // world
+    return rank * per, (rank + 1) * per
+
+
 def vit_flops_per_image(cfg):
     """Algorithmic FLOPs of one image: (gemm, attention, projection)."""
     D, F, T, L = cfg["d_model"], cfg["d_ffn"], cfg["n_token"], cfg["n_layer"]
@@ -84,7 +95,8 @@ class Dist:
 
             import torch.distributed as td
             os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-            td.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+            secs = float(os.environ.get("TCG_PG_TIMEOUT", "300"))
+            td.init_process_group("gloo", timeout=datetime.timedelta(seconds=secs))
             self.td = td
 
     def barrier(self):
@@ -254,9 +266,8 @@ def run_ours(args, dist):
     import tcg
     pk, pk_kind = peaks()
     cfg = G.vit_config(args.model)
-    if args.batch % dist.world:
-        raise SystemExit(f"batch {args.batch} does not shard over {dist.world} GPUs")
-    per = args.batch // dist.world
+    lo, hi = shard_range(args.batch, dist.world, dist.rank)
+    per = hi - lo
     if dist.rank == 0:
         G.cached_vit_gguf(CACHE, args.model, 0)
     dist.barrier()
@@ -278,7 +289,7 @@ def run_ours(args, dist):
         model.upload(per)
 
     pixels = G.make_pixels(args.batch, cfg["image"], 1)
-    shard = np.ascontiguousarray(pixels[dist.rank * per:(dist.rank + 1) * per])
+    shard = np.ascontiguousarray(pixels[lo:hi])
     d_out = cfg["d_out"]
     dpx = tcg.DeviceBuffer.from_array(shard)
     dout = tcg.DeviceBuffer(per * d_out * 4)

@@ -6,17 +6,27 @@
 // tcgen05.mma.kind::tf32 -- lo*hi, hi*lo, hi*hi -- into one fp32 TMEM
 // accumulator ("3xTF32"; the dropped lo*lo term is ~2^-22 relative).
 //
-// Persistent, warp-specialised CTA (one per SM, 192 threads):
+// Accuracy. The tensor core's own fp32 accumulation truncates, and that
+// error grows linearly with the number of MMAs folded into one accumulator
+// (measured: ~1.7e-5 of max|C| at K=1024 when a whole K loop accumulates in
+// TMEM). So the K loop is cut into chunks of 32: each chunk accumulates in
+// a fresh TMEM buffer (two, ping-pong), and the epilogue warps fold every
+// chunk into fp32 registers with round-to-nearest adds while the MMAs of the
+// next chunk run. Per product the error is then a few fp32 ulps of the
+// result, like a sequential fp32 dot product.
+//
+// Persistent, warp-specialised CTA (one per SM, 320 threads):
 //   warp 0     one lane issues the TMA loads of a (A_hi, A_lo, B_hi, B_lo)
 //              K-slice into a STAGES-deep shared-memory ring;
 //   warp 1     allocates TMEM; one lane issues the MMAs and commits them to
-//              the ring's "empty" barriers and to the accumulator barriers;
-//   warps 2-5  the epilogue: tcgen05.ld of the 128 x BN accumulator (one
-//              row per thread), bias / position / GELU / residual, hi/lo
-//              split, global stores.
-// Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap
-// the MMAs of tile i+1. Operand tiles are K-major with the TMA swizzle that
-// matches the UMMA descriptor (BK*4 bytes: 128B for BK=32, 64B for BK=16).
+//              the ring's "empty" barriers and to the chunk barriers;
+//   warps 2-9  two epilogue warpgroups: the warp's TMEM lane quarter gives its
+//              32 rows, its warpgroup one half of the BN columns. They drain
+//              each chunk into registers and, after the last chunk of a tile,
+//              apply bias / position / GELU / residual, split hi/lo and store.
+// Operand tiles are K-major with the TMA swizzle that matches the UMMA
+// descriptor (BK*4 bytes: 128B for BK=32, 64B for BK=16). No TMA load uses
+// cluster features: each CTA loads its own tiles.
 // Every mbarrier wait is bounded (globaltimer); a wait that gives up sets a
 // CTA-wide abort flag and the library's device error word, the roles wind
 // down, in-flight copies and MMAs are drained, and TMEM is freed.
@@ -27,7 +37,8 @@ namespace tcg {
 namespace {
 
 constexpr int BM = 128;
-constexpr int NUM_THREADS = 192;
+constexpr int EPI_WARPS = 8;
+constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
 constexpr unsigned long long WAIT_NS = 4000000000ull;   // 4 s per wait
 
 __device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -123,9 +134,8 @@ __device__ __forceinline__ void mma_commit(uint32_t bar)
 
 // 32 consecutive accumulator columns of this thread's TMEM lane; the wait
 // sits in the same asm block so no use of the registers can precede it.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float v[32])
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
 {
-    uint32_t r[32];
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32"
                  " {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
                  "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
@@ -136,8 +146,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float v[32])
                    "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
                  : "r"(taddr)
                  : "memory");
-#pragma unroll
-    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
 
 __device__ __forceinline__ float epi_value(const GemmEpi &e, float x, int src_row, int n)
@@ -149,70 +157,71 @@ __device__ __forceinline__ float epi_value(const GemmEpi &e, float x, int src_ro
     return x;
 }
 
-__device__ __forceinline__ void store32(float *dst, const float (&src)[32], bool vec, int cnt)
+// Finish and store columns n .. n+3 of GEMM row r (cnt of them in range).
+__device__ __forceinline__ void epi_store4(const GemmEpi &e, int src_row, size_t dst_row, int n, int cnt,
+                                           float v0, float v1, float v2, float v3)
 {
-    if (vec && (((uintptr_t)dst) & 15) == 0) {
+    float v[4] = { v0, v1, v2, v3 };
 #pragma unroll
-        for (int j = 0; j < 32; j += 4)
-            *reinterpret_cast<float4 *>(dst + j) = make_float4(src[j], src[j + 1], src[j + 2], src[j + 3]);
-    } else {
-#pragma unroll
-        for (int j = 0; j < 32; j++)
-            if (j < cnt) dst[j] = src[j];
-    }
-}
-
-// Row r of the tile, columns n .. n+cnt-1 (cnt <= 32) from v[].
-__device__ __forceinline__ void epi_store(const GemmEpi &e, int r, int n, int cnt, float (&v)[32])
-{
-    const int src_row = r % e.rgroup + e.roff;
-    const size_t dst = (size_t)(r / e.rgroup) * e.rstride + e.roff + r % e.rgroup;
-    const size_t o = dst * (size_t)e.out.ld + n;
-#pragma unroll
-    for (int j = 0; j < 32; j++)
+    for (int j = 0; j < 4; j++)
         if (j < cnt) v[j] = epi_value(e, v[j], src_row, n + j);
-    const bool vec = cnt == 32 && (e.out.ld & 3) == 0 && (n & 3) == 0;
+    const size_t o = dst_row * (size_t)e.out.ld + n;
+    const bool vec = cnt == 4 && ((e.out.ld | n) & 3) == 0;
     if (e.residual) {
         const float *res = e.residual + o;
-        if (vec && (((uintptr_t)res) & 15) == 0) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-                const float4 q = *reinterpret_cast<const float4 *>(res + j);
-                v[j] = __fadd_rn(q.x, v[j]); v[j + 1] = __fadd_rn(q.y, v[j + 1]);
-                v[j + 2] = __fadd_rn(q.z, v[j + 2]); v[j + 3] = __fadd_rn(q.w, v[j + 3]);
-            }
+        if (vec && !((uintptr_t)res & 15)) {
+            const float4 q = *reinterpret_cast<const float4 *>(res);
+            v[0] = __fadd_rn(q.x, v[0]); v[1] = __fadd_rn(q.y, v[1]);
+            v[2] = __fadd_rn(q.z, v[2]); v[3] = __fadd_rn(q.w, v[3]);
         } else {
 #pragma unroll
-            for (int j = 0; j < 32; j++)
+            for (int j = 0; j < 4; j++)
                 if (j < cnt) v[j] = __fadd_rn(res[j], v[j]);
         }
     }
-    if (e.out.plain) store32(e.out.plain + o, v, vec, cnt);
-    if (e.out.hi) {
-        float hi[32], lo[32];
+    if (e.out.plain) {
+        float *d = e.out.plain + o;
+        if (vec && !((uintptr_t)d & 15)) *reinterpret_cast<float4 *>(d) = make_float4(v[0], v[1], v[2], v[3]);
+        else
 #pragma unroll
-        for (int j = 0; j < 32; j++) split_tf32(v[j], hi[j], lo[j]);
-        store32(e.out.hi + o, hi, vec, cnt);
-        store32(e.out.lo + o, lo, vec, cnt);
+            for (int j = 0; j < 4; j++)
+                if (j < cnt) d[j] = v[j];
+    }
+    if (e.out.hi) {
+        float h[4], l[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) split_tf32(v[j], h[j], l[j]);
+        float *dh = e.out.hi + o, *dl = e.out.lo + o;
+        if (vec && !(((uintptr_t)dh | (uintptr_t)dl) & 15)) {
+            *reinterpret_cast<float4 *>(dh) = make_float4(h[0], h[1], h[2], h[3]);
+            *reinterpret_cast<float4 *>(dl) = make_float4(l[0], l[1], l[2], l[3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if (j < cnt) { dh[j] = h[j]; dl[j] = l[j]; }
+        }
     }
 }
 
-template <int BN, int BK, int STAGES>
+template <int BN, int BK, int STAGES, int CH>
 struct Shape {
     static constexpr uint32_t A_BYTES = BM * BK * 4;
     static constexpr uint32_t B_BYTES = BN * BK * 4;
     static constexpr uint32_t STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
     static constexpr uint32_t TMEM_COLS = 2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512);
+    static constexpr int HALF = BN / 2;               // columns per epilogue thread
     static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+    static_assert(HALF % 32 == 0, "each epilogue warpgroup drains whole 32-column slices");
+    static_assert(CH * BK == 32, "chunks of 32 K-elements");
 };
 
-template <int BN, int BK, int STAGES>
+template <int BN, int BK, int STAGES, int CH>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
                    const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
                    int M, int N, int K, GemmEpi epi, int *err)
 {
-    using S = Shape<BN, BK, STAGES>;
+    using S = Shape<BN, BK, STAGES, CH>;
     constexpr int SWB = BK * 4;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *tiles = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -224,17 +233,18 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
     const int n_tiles = (N + BN - 1) / BN;
     const int num_tiles = ((M + BM - 1) / BM) * n_tiles;
     const int num_kb = (K + BK - 1) / BK;
+    const int n_chunks = (num_kb + CH - 1) / CH;
     const uint32_t full0 = su32(bars), empty0 = su32(bars + STAGES);
-    const uint32_t tfull0 = su32(bars + 2 * STAGES), tempty0 = tfull0 + 16, drain = tfull0 + 32;
+    const uint32_t cfull0 = su32(bars + 2 * STAGES), cempty0 = cfull0 + 16, drain = cfull0 + 32;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
             bar_init(full0 + 8 * s, 1);
             bar_init(empty0 + 8 * s, 1);
         }
-        for (int a = 0; a < 2; a++) {
-            bar_init(tfull0 + 8 * a, 1);
-            bar_init(tempty0 + 8 * a, 128);
+        for (int b = 0; b < 2; b++) {
+            bar_init(cfull0 + 8 * b, 1);
+            bar_init(cempty0 + 8 * b, EPI_WARPS);
         }
         bar_init(drain, 1);
         *abort = 0;
@@ -275,7 +285,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                     if (++stage == STAGES) { stage = 0; phase ^= 1; }
                 }
             }
-            // Let the last fills of every stage land before the CTA exits.
+            // Let the last fill of every stage land before the CTA exits.
             for (int i = 1; i <= STAGES && i <= issued; i++) {
                 int s = stage - i;
                 uint32_t ph = phase;
@@ -288,33 +298,35 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
         if (lane == 0) {
             const uint32_t id = idesc_tf32<BN>();
             int stage = 0;
-            uint32_t phase = 0;
+            uint32_t phase = 0, chunk = 0;
             bool ok = true;
-            int local = 0;
-            for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x, local++) {
-                const int acc = local & 1;
-                if (!bar_wait(tempty0 + 8 * acc, ((local >> 1) & 1) ^ 1, abort, err, 3)) break;
-                fence_after();
-                const uint32_t d = tmem + (uint32_t)(acc * BN);
-                for (int kb = 0; kb < num_kb; kb++) {
-                    if (!bar_wait(full0 + 8 * stage, phase, abort, err, 4)) { ok = false; break; }
+            for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
+                for (int c = 0; ok && c < n_chunks; c++, chunk++) {
+                    const uint32_t b = chunk & 1;
+                    if (!bar_wait(cempty0 + 8 * b, ((chunk >> 1) & 1) ^ 1, abort, err, 3)) { ok = false; break; }
                     fence_after();
-                    const uint32_t base = su32(tiles + (size_t)stage * S::STAGE_BYTES);
+                    const uint32_t d = tmem + b * (uint32_t)BN;
+                    const int kb0 = c * CH, kb1 = min(kb0 + CH, num_kb);
+                    for (int kb = kb0; kb < kb1; kb++) {
+                        if (!bar_wait(full0 + 8 * stage, phase, abort, err, 4)) { ok = false; break; }
+                        fence_after();
+                        const uint32_t base = su32(tiles + (size_t)stage * S::STAGE_BYTES);
 #pragma unroll
-                    for (int k = 0; k < BK / 8; k++) {
-                        const uint32_t off = (uint32_t)k * 32u;
-                        const unsigned long long ah = sdesc<SWB>(base + off);
-                        const unsigned long long al = sdesc<SWB>(base + S::A_BYTES + off);
-                        const unsigned long long bh = sdesc<SWB>(base + 2 * S::A_BYTES + off);
-                        const unsigned long long bl = sdesc<SWB>(base + 2 * S::A_BYTES + S::B_BYTES + off);
-                        mma_tf32(d, al, bh, id, (kb | k) ? 1u : 0u);
-                        mma_tf32(d, ah, bl, id, 1u);
-                        mma_tf32(d, ah, bh, id, 1u);
+                        for (int k = 0; k < BK / 8; k++) {
+                            const uint32_t off = (uint32_t)k * 32u;
+                            const unsigned long long ah = sdesc<SWB>(base + off);
+                            const unsigned long long al = sdesc<SWB>(base + S::A_BYTES + off);
+                            const unsigned long long bh = sdesc<SWB>(base + 2 * S::A_BYTES + off);
+                            const unsigned long long bl = sdesc<SWB>(base + 2 * S::A_BYTES + S::B_BYTES + off);
+                            mma_tf32(d, al, bh, id, (kb > kb0 || k > 0) ? 1u : 0u);
+                            mma_tf32(d, ah, bl, id, 1u);
+                            mma_tf32(d, ah, bh, id, 1u);
+                        }
+                        mma_commit(empty0 + 8 * stage);
+                        if (++stage == STAGES) { stage = 0; phase ^= 1; }
                     }
-                    mma_commit(empty0 + 8 * stage);
-                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                    if (ok) mma_commit(cfull0 + 8 * b);
                 }
-                if (ok) mma_commit(tfull0 + 8 * acc);
             }
             // Every MMA issued above has retired once this barrier flips.
             mma_commit(drain);
@@ -322,23 +334,44 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
         }
         __syncwarp();
     } else {
-        const int q = warp & 3;                  // TMEM lanes 32q .. 32q+31
-        int local = 0;
-        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, local++) {
-            const int acc = local & 1;
-            if (!bar_wait(tfull0 + 8 * acc, (local >> 1) & 1, abort, err, 6)) break;
-            fence_after();
+        const int q = warp & 3;                    // TMEM lanes 32q .. 32q+31 = tile rows
+        const int h = (warp - 2) >> 2;             // column half of the tile
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        uint32_t chunk = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
+            float acc[S::HALF];
+#pragma unroll
+            for (int j = 0; j < S::HALF; j++) acc[j] = 0.0f;
+            for (int c = 0; c < n_chunks; c++, chunk++) {
+                const uint32_t b = chunk & 1;
+                if (!bar_wait(cfull0 + 8 * b, (chunk >> 1) & 1, abort, err, 6)) { ok = false; break; }
+                fence_after();
+#pragma unroll
+                for (int j = 0; j < S::HALF; j += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(tmem + lane_addr + b * (uint32_t)BN + (uint32_t)(h * S::HALF + j), r);
+#pragma unroll
+                    for (int i = 0; i < 32; i++) acc[j + i] = __fadd_rn(acc[j + i], __uint_as_float(r[i]));
+                }
+                fence_before();
+                __syncwarp();
+                if (lane == 0) bar_arrive(cempty0 + 8 * b);
+            }
+            if (!ok) break;
             const int m0 = (t / n_tiles) * BM, n0 = (t % n_tiles) * BN;
             const int r = m0 + q * 32 + lane;
-#pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32) {
-                float v[32];
-                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c0), v);
-                const int n = n0 + c0;
-                if (r < M && n < N) epi_store(epi, r, n, min(32, N - n), v);
+            if (r < M) {
+                const int src_row = r % epi.rgroup + epi.roff;
+                const size_t dst_row = (size_t)(r / epi.rgroup) * epi.rstride + epi.roff + r % epi.rgroup;
+                const int nb = n0 + h * S::HALF;
+#pragma unroll
+                for (int j = 0; j < S::HALF; j += 4) {
+                    const int n = nb + j;
+                    if (n < N)
+                        epi_store4(epi, src_row, dst_row, n, min(4, N - n), acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+                }
             }
-            fence_before();
-            bar_arrive(tempty0 + 8 * acc);
         }
     }
 
@@ -391,15 +424,14 @@ bool encode_kmajor(CUtensorMap *m, const float *ptr, int rows, int K, int box_ro
     return true;
 }
 
-typedef void (*KernelFn)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, int, int, int, GemmEpi, int *);
-
 struct Cfg {
     int bn, bk, stages;
     size_t smem;
     const void *fn;
 };
 
-#define TCG_CFG(BN, BK, ST) { BN, BK, ST, Shape<BN, BK, ST>::SMEM, (const void *)gemm_tf32x3_kernel<BN, BK, ST> }
+#define TCG_CFG(BN, BK, ST) \
+    { BN, BK, ST, Shape<BN, BK, ST, 32 / BK>::SMEM, (const void *)gemm_tf32x3_kernel<BN, BK, ST, 32 / BK> }
 const Cfg CFGS[] = {
     TCG_CFG(256, 16, 4), TCG_CFG(192, 16, 5), TCG_CFG(128, 16, 6), TCG_CFG(64, 16, 8),
     TCG_CFG(256, 32, 2), TCG_CFG(192, 32, 2), TCG_CFG(128, 32, 3), TCG_CFG(64, 32, 4),
@@ -481,17 +513,12 @@ static bool linear_impl(float *y, const float *x, const float *W, const float *b
     const bool tc_ok = bt && K > 0 && (K & 3) == 0 && !((uintptr_t)x & 15) && !((uintptr_t)W & 15);
     if (!tc_ok || force_cfg == -2)
         return launch_gemm_simt(y, N, x, K, W, bt ? K : N, bias, M, N, K, bt, s);
-    const size_t xa = (size_t)M * K, wa = (size_t)N * K;
-    float *buf = (float *)scratch((2 * xa + 2 * wa) * sizeof(float) + 64);
+    // tf32 hi/lo copies of both operands, each 16-byte aligned
+    const size_t xa = ((size_t)M * K + 3) & ~(size_t)3, wa = ((size_t)N * K + 3) & ~(size_t)3;
+    float *buf = (float *)scratch((2 * xa + 2 * wa) * sizeof(float));
     if (!buf) return false;
     float *xh = buf, *xl = xh + xa, *wh = xl + xa, *wl = wh + wa;
-    // keep every operand 16-byte aligned
-    if ((xa & 3) != 0) {
-        xl = xh + ((xa + 3) & ~(size_t)3);
-        wh = xl + ((xa + 3) & ~(size_t)3);
-        wl = wh + ((wa + 3) & ~(size_t)3);
-    }
-    if (!launch_split(x, xh, xl, xa, s) || !launch_split(W, wh, wl, wa, s)) return false;
+    if (!launch_split(x, xh, xl, (size_t)M * K, s) || !launch_split(W, wh, wl, (size_t)N * K, s)) return false;
     GemmEpi e;
     e.bias = bias;
     e.out.plain = y;
