@@ -113,6 +113,14 @@ bool tcg_matvec_q(float *y, const void *W, const float *x, int N, int K, ggml_ty
  * pointers 16-byte aligned, else on an fp32 CUDA-core kernel. */
 bool tcg_gemm(float *C, const float *A, const float *B, int M, int N, int K, bool b_transposed);
 bool tcg_linear(float *y, const float *x, const float *W, const float *bias, int M, int N, int K);
+/* The tf32 operand pair of the 3xTF32 GEMMs: hi = rn_tf32(v),
+ * lo = rn_tf32(v - hi), so v = hi + lo to ~2^-22 relative. */
+bool tcg_split_tf32(float *hi, float *lo, const float *src, size_t n);
+/* tcg_linear on operands already held as tf32 pairs (both row-major with
+ * row stride K, 16-byte aligned, K a multiple of 4): the tensor-core kernel
+ * alone, for callers that keep weights split once and reuse them. */
+bool tcg_linear_split(float *y, const float *x_hi, const float *x_lo, const float *w_hi, const float *w_lo,
+                      const float *bias, int M, int N, int K);
 bool tcg_layernorm(float *out, const float *x, const float *gamma, const float *beta,
                    int rows, int cols, float eps);
 bool tcg_gelu(float *out, const float *x, size_t n);

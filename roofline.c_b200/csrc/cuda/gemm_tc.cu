@@ -203,7 +203,7 @@ __device__ __forceinline__ void epi_store4(const GemmEpi &e, int src_row, size_t
     }
 }
 
-template <int BN, int BK, int STAGES, int CH>
+template <int BN, int BK, int STAGES>
 struct Shape {
     static constexpr uint32_t A_BYTES = BM * BK * 4;
     static constexpr uint32_t B_BYTES = BN * BK * 4;
@@ -212,16 +212,16 @@ struct Shape {
     static constexpr int HALF = BN / 2;               // columns per epilogue thread
     static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
     static_assert(HALF % 32 == 0, "each epilogue warpgroup drains whole 32-column slices");
-    static_assert(CH * BK == 32, "chunks of 32 K-elements");
 };
 
-template <int BN, int BK, int STAGES, int CH>
+// chunk_kb: K-blocks folded into one TMEM buffer before it is drained.
+template <int BN, int BK, int STAGES>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
                    const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
-                   int M, int N, int K, GemmEpi epi, int *err)
+                   int M, int N, int K, int chunk_kb, GemmEpi epi, int *err)
 {
-    using S = Shape<BN, BK, STAGES, CH>;
+    using S = Shape<BN, BK, STAGES>;
     constexpr int SWB = BK * 4;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *tiles = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -233,7 +233,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
     const int n_tiles = (N + BN - 1) / BN;
     const int num_tiles = ((M + BM - 1) / BM) * n_tiles;
     const int num_kb = (K + BK - 1) / BK;
-    const int n_chunks = (num_kb + CH - 1) / CH;
+    const int n_chunks = (num_kb + chunk_kb - 1) / chunk_kb;
     const uint32_t full0 = su32(bars), empty0 = su32(bars + STAGES);
     const uint32_t cfull0 = su32(bars + 2 * STAGES), cempty0 = cfull0 + 16, drain = cfull0 + 32;
 
@@ -306,7 +306,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                     if (!bar_wait(cempty0 + 8 * b, ((chunk >> 1) & 1) ^ 1, abort, err, 3)) { ok = false; break; }
                     fence_after();
                     const uint32_t d = tmem + b * (uint32_t)BN;
-                    const int kb0 = c * CH, kb1 = min(kb0 + CH, num_kb);
+                    const int kb0 = c * chunk_kb, kb1 = min(kb0 + chunk_kb, num_kb);
                     for (int kb = kb0; kb < kb1; kb++) {
                         if (!bar_wait(full0 + 8 * stage, phase, abort, err, 4)) { ok = false; break; }
                         fence_after();
@@ -430,8 +430,7 @@ struct Cfg {
     const void *fn;
 };
 
-#define TCG_CFG(BN, BK, ST) \
-    { BN, BK, ST, Shape<BN, BK, ST, 32 / BK>::SMEM, (const void *)gemm_tf32x3_kernel<BN, BK, ST, 32 / BK> }
+#define TCG_CFG(BN, BK, ST) { BN, BK, ST, Shape<BN, BK, ST>::SMEM, (const void *)gemm_tf32x3_kernel<BN, BK, ST> }
 const Cfg CFGS[] = {
     TCG_CFG(256, 16, 4), TCG_CFG(192, 16, 5), TCG_CFG(128, 16, 6), TCG_CFG(64, 16, 8),
     TCG_CFG(256, 32, 2), TCG_CFG(192, 32, 2), TCG_CFG(128, 32, 3), TCG_CFG(64, 32, 4),
@@ -456,6 +455,9 @@ int choose_cfg(int M, int N)
 }
 
 }  // namespace
+
+// K-elements accumulated in TMEM between two drains into fp32 registers.
+int g_chunk_k = 32;
 
 int gemm_num_cfgs() { return NCFG; }
 int gemm_cfg_bn(int cfg) { return cfg >= 0 && cfg < NCFG ? CFGS[cfg].bn : 0; }
@@ -491,8 +493,10 @@ bool gemm_run(const GemmPlan &p, cudaStream_t s, int *err)
         TCG_CUDA(cudaFuncSetAttribute(c.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem));
         attr_done[dev] |= 1ull << p.cfg;
     }
+    int chunk_kb = g_chunk_k / c.bk;
+    if (chunk_kb < 1) chunk_kb = 1;
     void *args[] = { (void *)&p.a_hi, (void *)&p.a_lo, (void *)&p.b_hi, (void *)&p.b_lo,
-                     (void *)&p.M, (void *)&p.N, (void *)&p.K, (void *)&p.epi, (void *)&err };
+                     (void *)&p.M, (void *)&p.N, (void *)&p.K, (void *)&chunk_kb, (void *)&p.epi, (void *)&err };
     TCG_CUDA(cudaLaunchKernel(c.fn, dim3(p.grid), dim3(NUM_THREADS), args, c.smem, s));
     return true;
 }
@@ -540,6 +544,33 @@ bool tcg_linear(float *y, const float *x, const float *W, const float *bias, int
     return linear_impl(y, x, W, bias, M, N, K, true, -1);
 }
 
+bool tcg_split_tf32(float *hi, float *lo, const float *src, size_t n)
+{
+    return need_ctx() && launch_split(src, hi, lo, n, ctx().cur);
+}
+
+// Test and tuning hook: tcg_linear_split with a forced tile configuration.
+bool tcg_linear_split_cfg(float *y, const float *x_hi, const float *x_lo, const float *w_hi, const float *w_lo,
+                          const float *bias, int M, int N, int K, int cfg)
+{
+    if (!need_ctx()) return false;
+    if (M < 0 || N < 0 || K <= 0) return fail("tcg_linear_split: bad shape %dx%dx%d", M, N, K);
+    if (M == 0 || N == 0) return true;
+    GemmEpi e;
+    e.bias = bias;
+    e.out.plain = y;
+    e.out.ld = N;
+    GemmPlan p;
+    if (!gemm_plan(p, x_hi, x_lo, w_hi, w_lo, M, N, K, e, cfg)) return false;
+    return gemm_run(p, ctx().cur, ctx().d_err);
+}
+
+bool tcg_linear_split(float *y, const float *x_hi, const float *x_lo, const float *w_hi, const float *w_lo,
+                      const float *bias, int M, int N, int K)
+{
+    return tcg_linear_split_cfg(y, x_hi, x_lo, w_hi, w_lo, bias, M, N, K, -1);
+}
+
 // Test hook: force a GEMM configuration (cfg >= 0 a tcgen05 tile shape, -2
 // the CUDA-core kernel). Not part of the public header.
 bool tcg_linear_cfg(float *y, const float *x, const float *W, const float *bias, int M, int N, int K, int cfg)
@@ -548,5 +579,14 @@ bool tcg_linear_cfg(float *y, const float *x, const float *W, const float *bias,
 }
 
 int tcg_gemm_num_cfgs(void) { return gemm_num_cfgs(); }
+
+// Test hook: K-elements per TMEM chunk (a multiple of 32; larger is faster
+// and less accurate). Returns the previous value.
+int tcg_gemm_set_chunk_k(int k)
+{
+    const int old = g_chunk_k;
+    if (k >= 32 && k % 32 == 0) g_chunk_k = k;
+    return old;
+}
 
 }  // extern "C"

@@ -130,11 +130,151 @@ __global__ void mha_kernel(const float *__restrict__ q, const float *__restrict_
     }
 }
 
+// head_dim 64 (every ViT here): one CTA per (head, image, block of 64
+// queries), 16 x 16 threads, each owning a 4 x 4 register tile of the scores
+// and then of the output. Keys are held transposed (d-major) so a thread's 4
+// key columns are one 128-bit shared load; query and probability rows are
+// read as per-row scalars that the 16 threads of a row share (broadcast).
+// Softmax is exact two-pass per row as in src/ops.c:129-139 (max, expf, double
+// sum, one reciprocal); the weighted sum runs over keys in order.
+constexpr int MHA_BQ = 64;
+
+__device__ __forceinline__ void put4(const OutSpec &o, size_t row, int col, const float (&v)[4])
+{
+    const size_t i = row * (size_t)o.ld + col;
+    if (o.plain) *reinterpret_cast<float4 *>(o.plain + i) = make_float4(v[0], v[1], v[2], v[3]);
+    if (o.hi) {
+        float h[4], l[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) split_tf32(v[j], h[j], l[j]);
+        *reinterpret_cast<float4 *>(o.hi + i) = make_float4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<float4 *>(o.lo + i) = make_float4(l[0], l[1], l[2], l[3]);
+    }
+}
+
+__global__ void __launch_bounds__(256)
+mha64_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
+             int ldi, int T, OutSpec out)
+{
+    extern __shared__ float4 sm4[];
+    float *sm = reinterpret_cast<float *>(sm4);
+    const int T4 = (T + 3) & ~3;
+    float *Qs = sm;                      // [64][64]
+    float *Kt = Qs + MHA_BQ * 64;        // [64][T4]
+    float *Vs = Kt + 64 * T4;            // [T4][64]
+    float *Ss = Vs + (size_t)T4 * 64;    // [64][T4]
+    const int col = blockIdx.x * 64;
+    const size_t base = (size_t)blockIdx.y * T;
+    const int q0 = blockIdx.z * MHA_BQ, nq = min(MHA_BQ, T - q0);
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+
+    for (int i = threadIdx.x; i < T4 * 16; i += 256) {
+        const int t = i >> 4, d = (i & 15) * 4;
+        float4 kv = zero, vv = zero;
+        if (t < T) {
+            const size_t g = (base + t) * (size_t)ldi + col + d;
+            kv = __ldg(reinterpret_cast<const float4 *>(k + g));
+            vv = __ldg(reinterpret_cast<const float4 *>(v + g));
+        }
+        Kt[(d + 0) * T4 + t] = kv.x;
+        Kt[(d + 1) * T4 + t] = kv.y;
+        Kt[(d + 2) * T4 + t] = kv.z;
+        Kt[(d + 3) * T4 + t] = kv.w;
+        *reinterpret_cast<float4 *>(Vs + t * 64 + d) = vv;
+    }
+    for (int i = threadIdx.x; i < MHA_BQ * 16; i += 256) {
+        const int t = i >> 4, d = (i & 15) * 4;
+        float4 qv = zero;
+        if (t < nq) qv = __ldg(reinterpret_cast<const float4 *>(q + (base + q0 + t) * (size_t)ldi + col + d));
+        *reinterpret_cast<float4 *>(Qs + t * 64 + d) = qv;
+    }
+    __syncthreads();
+
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const float scale = 1.0f / sqrtf(64.0f);
+    for (int c0 = 0; c0 < T4; c0 += 64) {
+        const int cc = c0 + 4 * tx;
+        if (cc >= T4) continue;
+        float acc[4][4] = {};
+#pragma unroll 8
+        for (int d = 0; d < 64; d++) {
+            const float4 kk = *reinterpret_cast<const float4 *>(Kt + d * T4 + cc);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float a = Qs[(4 * ty + i) * 64 + d];
+                acc[i][0] = fmaf(a, kk.x, acc[i][0]);
+                acc[i][1] = fmaf(a, kk.y, acc[i][1]);
+                acc[i][2] = fmaf(a, kk.z, acc[i][2]);
+                acc[i][3] = fmaf(a, kk.w, acc[i][3]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            *reinterpret_cast<float4 *>(Ss + (4 * ty + i) * T4 + cc) =
+                make_float4(__fmul_rn(acc[i][0], scale), __fmul_rn(acc[i][1], scale),
+                            __fmul_rn(acc[i][2], scale), __fmul_rn(acc[i][3], scale));
+    }
+    __syncthreads();
+
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    for (int r = wid; r < nq; r += 8) {
+        float *row = Ss + r * T4;
+        float mx = -INFINITY;
+        for (int s = lane; s < T; s += 32) mx = fmaxf(mx, row[s]);
+        mx = warp_max(mx);
+        double sum = 0.0;
+        for (int s = lane; s < T; s += 32) {
+            const float e = expf(__fsub_rn(row[s], mx));
+            row[s] = e;
+            sum += (double)e;
+        }
+        const float inv = (float)(1.0 / warp_sum(sum));
+        for (int s = lane; s < T; s += 32) row[s] = __fmul_rn(row[s], inv);
+    }
+    __syncthreads();
+
+    float o[4][4] = {};
+    for (int s = 0; s < T; s++) {
+        const float4 vv = *reinterpret_cast<const float4 *>(Vs + s * 64 + 4 * tx);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float p = Ss[(4 * ty + i) * T4 + s];
+            o[i][0] = fmaf(p, vv.x, o[i][0]);
+            o[i][1] = fmaf(p, vv.y, o[i][1]);
+            o[i][2] = fmaf(p, vv.z, o[i][2]);
+            o[i][3] = fmaf(p, vv.w, o[i][3]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+        if (4 * ty + i < nq) put4(out, base + q0 + 4 * ty + i, col + 4 * tx, o[i]);
+}
+
+static size_t mha64_smem(int T)
+{
+    const size_t T4 = (size_t)((T + 3) & ~3);
+    return (MHA_BQ * 64 + 3 * 64 * T4) * sizeof(float);
+}
+
 bool launch_mha(const float *q, const float *k, const float *v, int ldi, int T, int n_head, int hd,
                 int n_img, const OutSpec &out, cudaStream_t s)
 {
     if (T <= 0 || n_img <= 0 || n_head <= 0) return true;
     if (hd <= 0 || hd > 128) return fail("attention: head_dim %d outside 1..128", hd);
+    const bool aligned = !(((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) & 15) && !(ldi & 3) &&
+                         !(out.ld & 3) && !(((uintptr_t)out.plain | (uintptr_t)out.hi | (uintptr_t)out.lo) & 15);
+    if (hd == 64 && aligned && mha64_smem(T) <= 227 * 1024) {
+        static unsigned done64[64];
+        const int dev = ctx().device & 63;
+        if (!done64[dev]) {
+            TCG_CUDA(cudaFuncSetAttribute(mha64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+            done64[dev] = 1;
+        }
+        dim3 grid(n_head, n_img, (T + MHA_BQ - 1) / MHA_BQ);
+        mha64_kernel<<<grid, 256, mha64_smem(T), s>>>(q, k, v, ldi, T, out);
+        TCG_LAUNCHED();
+        return true;
+    }
     const int nw = 8;
     const size_t smem = ((size_t)T * (2 * hd + 1) + (size_t)nw * (T + hd)) * sizeof(float);
     if (smem > 227 * 1024) return fail("attention: T=%d head_dim=%d needs %zu B of shared memory", T, hd, smem);

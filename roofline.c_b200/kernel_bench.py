@@ -41,22 +41,77 @@ def timed(fn, warmup, reps, flush=None):
     return statistics.median(ts), ts
 
 
+class SplitOperands:
+    """x [M,K] and W [N,K] uploaded once and split into tf32 hi/lo on the
+    device, so that a timed launch is the GEMM kernel alone."""
+
+    def __init__(self, M, N, K, seed=0):
+        L = tcg.lib()
+        rng = np.random.default_rng(seed)
+        self.x = rng.standard_normal((M, K), dtype=np.float32)
+        self.W = (rng.standard_normal((N, K), dtype=np.float32) * 0.02).astype(np.float32)
+        self.b = rng.standard_normal(N, dtype=np.float32)
+        self.bufs = [tcg.DeviceBuffer.from_array(a) for a in (self.x, self.W, self.b)]
+        self.xh, self.xl = tcg.DeviceBuffer(M * K * 4), tcg.DeviceBuffer(M * K * 4)
+        self.wh, self.wl = tcg.DeviceBuffer(N * K * 4), tcg.DeviceBuffer(N * K * 4)
+        self.y = tcg.DeviceBuffer(M * N * 4)
+        self.bufs += [self.xh, self.xl, self.wh, self.wl, self.y]
+        tcg.check(L.tcg_split_tf32(self.xh.ptr, self.xl.ptr, self.bufs[0].ptr, M * K))
+        tcg.check(L.tcg_split_tf32(self.wh.ptr, self.wl.ptr, self.bufs[1].ptr, N * K))
+        self.M, self.N, self.K = M, N, K
+
+    def run(self, cfg):
+        tcg.check(tcg.lib().tcg_linear_split_cfg(self.y.ptr, self.xh.ptr, self.xl.ptr, self.wh.ptr, self.wl.ptr,
+                                                 self.bufs[2].ptr, self.M, self.N, self.K, cfg), f"cfg {cfg}")
+
+    def rel_err(self):
+        got = self.y.download((self.M, self.N)).astype(np.float64)
+        want = self.x.astype(np.float64) @ self.W.astype(np.float64).T + self.b.astype(np.float64)
+        return float(np.abs(got - want).max() / np.abs(want).max())
+
+    def close(self):
+        for b in self.bufs:
+            b.close()
+
+
 def case_gemm(a):
-    L = tcg.lib()
-    rng = np.random.default_rng(0)
-    x = rng.standard_normal((a.M, a.K), dtype=np.float32)
-    W = (rng.standard_normal((a.N, a.K), dtype=np.float32) * 0.02).astype(np.float32)
-    b = rng.standard_normal(a.N, dtype=np.float32)
-    with tcg.DeviceBuffer.from_array(x) as dx, tcg.DeviceBuffer.from_array(W) as dw, \
-            tcg.DeviceBuffer.from_array(b) as db, tcg.DeviceBuffer(a.M * a.N * 4) as dy, \
-            tcg.DeviceBuffer(256 << 20) as flush:
-        # the op entry point first splits both operands into tf32 hi/lo (two
-        # small bandwidth-bound kernels), then runs the GEMM kernel
-        run = lambda: tcg.check(L.tcg_linear_cfg(dy.ptr, dx.ptr, dw.ptr, db.ptr, a.M, a.N, a.K, a.cfg))  # noqa
-        total, _ = timed(run, a.warmup, a.reps, flush)
+    ops = SplitOperands(a.M, a.N, a.K)
+    with tcg.DeviceBuffer(256 << 20) as flush:
+        ms, _ = timed(lambda: ops.run(a.cfg), a.warmup, a.reps, flush)
+    ops.close()
     flops = 2.0 * a.M * a.N * a.K
-    return {"case": "gemm", "M": a.M, "N": a.N, "K": a.K, "cfg": a.cfg, "ms_split_plus_gemm": round(total, 4),
-            "tflops_incl_split": round(flops / total / 1e9, 1)}
+    return {"case": "gemm", "M": a.M, "N": a.N, "K": a.K, "cfg": a.cfg, "ms": round(ms, 4),
+            "tflops": round(flops / ms / 1e9, 1)}
+
+
+def case_gemmsweep(a):
+    """Every tile configuration x TMEM chunk length on the four ViT-B/32
+    GEMM shapes at batch 256; accuracy against a float64 product at M=256."""
+    L = tcg.lib()
+    shapes = {"qkv": (12800, 2304, 768), "out": (12800, 768, 768), "up": (12800, 3072, 768),
+              "down": (12800, 768, 3072)}
+    chunks = [int(c) for c in a.chunks.split(",")]
+    cfgs = range(L.tcg_gemm_num_cfgs()) if a.cfgs == "all" else [int(c) for c in a.cfgs.split(",")]
+    res = {"perf_ms": {}, "rel_err": {}}
+    flush = tcg.DeviceBuffer(256 << 20)
+    for name, (M, N, K) in shapes.items():
+        ops = SplitOperands(M, N, K)
+        for ck in chunks:
+            L.tcg_gemm_set_chunk_k(ck)
+            for cfg in list(cfgs) + [-1]:
+                ms, _ = timed(lambda: ops.run(cfg), a.warmup, a.reps, flush)
+                res["perf_ms"][f"{name}/chunk{ck}/cfg{cfg}"] = round(ms, 4)
+        ops.close()
+    for K in (768, 3072):
+        ops = SplitOperands(256, 768, K, seed=1)
+        for ck in chunks:
+            L.tcg_gemm_set_chunk_k(ck)
+            ops.run(-1)
+            res["rel_err"][f"K{K}/chunk{ck}"] = ops.rel_err()
+        ops.close()
+    L.tcg_gemm_set_chunk_k(32)
+    flush.close()
+    return {"case": "gemmsweep", **res}
 
 
 def case_matvec(a):
@@ -109,6 +164,9 @@ def main():
     g.add_argument("--N", type=int, default=3072)
     g.add_argument("--K", type=int, default=768)
     g.add_argument("--cfg", type=int, default=-1)
+    gs = sub.add_parser("gemmsweep")
+    gs.add_argument("--chunks", default="32,64,128,256,4096")
+    gs.add_argument("--cfgs", default="all")
     mv = sub.add_parser("matvec")
     mv.add_argument("--type", choices=sorted(QTYPES), default="q4k")
     mv.add_argument("--N", type=int, default=4096)
@@ -122,13 +180,14 @@ def main():
     v.add_argument("--batch", type=int, default=256)
     v.add_argument("--layers", type=int, default=0)
     v.add_argument("--steps", type=int, default=3)
-    for p in (g, mv, dq, v):
+    for p in (g, gs, mv, dq, v):
         p.add_argument("--warmup", type=int, default=3)
         p.add_argument("--reps", type=int, default=5)
         p.add_argument("--device", type=int, default=0)
     a = ap.parse_args()
     tcg.init(a.device)
-    res = {"gemm": case_gemm, "matvec": case_matvec, "dequant": case_dequant, "vit": case_vit}[a.case](a)
+    res = {"gemm": case_gemm, "gemmsweep": case_gemmsweep, "matvec": case_matvec, "dequant": case_dequant,
+           "vit": case_vit}[a.case](a)
     res["device_error"] = tcg.lib().tcg_device_error()
     print(json.dumps(res), flush=True)
 

@@ -139,7 +139,10 @@ _SIGS = [
     ("tcg_gemm", boolean, [vp, vp, vp, i32, i32, i32, boolean]),
     ("tcg_linear", boolean, [vp, vp, vp, vp, i32, i32, i32]),
     ("tcg_linear_cfg", boolean, [vp, vp, vp, vp, i32, i32, i32, i32]),
-    ("tcg_gemm_num_cfgs", i32, []),
+    ("tcg_gemm_num_cfgs", i32, []), ("tcg_gemm_set_chunk_k", i32, [i32]),
+    ("tcg_split_tf32", boolean, [vp, vp, vp, sz]),
+    ("tcg_linear_split", boolean, [vp, vp, vp, vp, vp, vp, i32, i32, i32]),
+    ("tcg_linear_split_cfg", boolean, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32]),
     ("tcg_layernorm", boolean, [vp, vp, vp, vp, i32, i32, f32]),
     ("tcg_gelu", boolean, [vp, vp, sz]), ("tcg_gelu_quick", boolean, [vp, vp, sz]),
     ("tcg_softmax_rows", boolean, [vp, vp, i32, i32]),
