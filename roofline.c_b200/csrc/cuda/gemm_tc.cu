@@ -148,6 +148,27 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
                  : "memory");
 }
 
+// 64 columns in one load, one wait.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64])
+{
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x64.b32"
+                 " {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                 "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+                 "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+                 "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
+                 "tcgen05.wait::ld.sync.aligned;"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+                   "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+                   "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+                   "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+                   "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+                   "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+                   "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+                 : "r"(taddr)
+                 : "memory");
+}
+
 __device__ __forceinline__ float epi_value(const GemmEpi &e, float x, int src_row, int n)
 {
     if (e.bias) x = __fadd_rn(x, e.bias[n]);
@@ -208,13 +229,40 @@ struct Shape {
     static constexpr uint32_t A_BYTES = BM * BK * 4;
     static constexpr uint32_t B_BYTES = BN * BK * 4;
     static constexpr uint32_t STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
-    static constexpr uint32_t TMEM_COLS = 2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512);
+    // TMEM: two chunk buffers for the hi*hi term and two tile buffers for the
+    // small lo*hi + hi*lo terms, BN columns each.
+    static constexpr uint32_t TMEM_COLS = 4 * BN <= 256 ? 256 : 512;
     static constexpr int HALF = BN / 2;               // columns per epilogue thread
-    static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+    static constexpr int NBAR = 2 * STAGES + 8 + 1;
+    static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 8 * NBAR + 16;
     static_assert(HALF % 32 == 0, "each epilogue warpgroup drains whole 32-column slices");
+    static_assert(4 * BN <= 512, "four accumulators must fit the 512 TMEM columns");
 };
 
-// chunk_kb: K-blocks folded into one TMEM buffer before it is drained.
+// acc[0..HALF) += the HALF fp32 columns at TMEM address taddr (this warp's
+// lanes), in 64-column loads where possible.
+template <int HALF>
+__device__ __forceinline__ void drain_add(uint32_t taddr, float (&acc)[HALF])
+{
+    constexpr int W64 = HALF / 64 * 64;
+#pragma unroll
+    for (int j = 0; j < W64; j += 64) {
+        uint32_t r[64];
+        tmem_ld64(taddr + (uint32_t)j, r);
+#pragma unroll
+        for (int i = 0; i < 64; i++) acc[j + i] = __fadd_rn(acc[j + i], __uint_as_float(r[i]));
+    }
+#pragma unroll
+    for (int j = W64; j < HALF; j += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + (uint32_t)j, r);
+#pragma unroll
+        for (int i = 0; i < 32; i++) acc[j + i] = __fadd_rn(acc[j + i], __uint_as_float(r[i]));
+    }
+}
+
+// chunk_kb: K-blocks whose hi*hi products share one TMEM chunk buffer before
+// it is drained into the fp32 registers.
 template <int BN, int BK, int STAGES>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
@@ -226,7 +274,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
     extern __shared__ uint8_t smem_raw[];
     uint8_t *tiles = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t *bars = (uint64_t *)(tiles + (size_t)STAGES * S::STAGE_BYTES);
-    uint32_t *tmem_slot = (uint32_t *)(bars + 2 * STAGES + 5);
+    uint32_t *tmem_slot = (uint32_t *)(bars + S::NBAR);
     volatile int *abort = (volatile int *)(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -235,7 +283,8 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
     const int num_kb = (K + BK - 1) / BK;
     const int n_chunks = (num_kb + chunk_kb - 1) / chunk_kb;
     const uint32_t full0 = su32(bars), empty0 = su32(bars + STAGES);
-    const uint32_t cfull0 = su32(bars + 2 * STAGES), cempty0 = cfull0 + 16, drain = cfull0 + 32;
+    const uint32_t cfull0 = su32(bars + 2 * STAGES), cempty0 = cfull0 + 16;
+    const uint32_t sfull0 = cempty0 + 16, sempty0 = sfull0 + 16, drain = sempty0 + 16;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
@@ -245,6 +294,8 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
         for (int b = 0; b < 2; b++) {
             bar_init(cfull0 + 8 * b, 1);
             bar_init(cempty0 + 8 * b, EPI_WARPS);
+            bar_init(sfull0 + 8 * b, 1);
+            bar_init(sempty0 + 8 * b, EPI_WARPS);
         }
         bar_init(drain, 1);
         *abort = 0;
@@ -300,12 +351,17 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
             int stage = 0;
             uint32_t phase = 0, chunk = 0;
             bool ok = true;
-            for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
+            int local = 0;
+            for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x, local++) {
+                const uint32_t ts = local & 1;
+                if (!bar_wait(sempty0 + 8 * ts, ((local >> 1) & 1) ^ 1, abort, err, 3)) break;
+                fence_after();
+                const uint32_t ds = tmem + (2 + ts) * (uint32_t)BN;
                 for (int c = 0; ok && c < n_chunks; c++, chunk++) {
                     const uint32_t b = chunk & 1;
                     if (!bar_wait(cempty0 + 8 * b, ((chunk >> 1) & 1) ^ 1, abort, err, 3)) { ok = false; break; }
                     fence_after();
-                    const uint32_t d = tmem + b * (uint32_t)BN;
+                    const uint32_t db = tmem + b * (uint32_t)BN;
                     const int kb0 = c * chunk_kb, kb1 = min(kb0 + chunk_kb, num_kb);
                     for (int kb = kb0; kb < kb1; kb++) {
                         if (!bar_wait(full0 + 8 * stage, phase, abort, err, 4)) { ok = false; break; }
@@ -318,15 +374,16 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                             const unsigned long long al = sdesc<SWB>(base + S::A_BYTES + off);
                             const unsigned long long bh = sdesc<SWB>(base + 2 * S::A_BYTES + off);
                             const unsigned long long bl = sdesc<SWB>(base + 2 * S::A_BYTES + S::B_BYTES + off);
-                            mma_tf32(d, al, bh, id, (kb > kb0 || k > 0) ? 1u : 0u);
-                            mma_tf32(d, ah, bl, id, 1u);
-                            mma_tf32(d, ah, bh, id, 1u);
+                            mma_tf32(db, ah, bh, id, (kb > kb0 || k > 0) ? 1u : 0u);
+                            mma_tf32(ds, al, bh, id, (kb > 0 || k > 0) ? 1u : 0u);
+                            mma_tf32(ds, ah, bl, id, 1u);
                         }
                         mma_commit(empty0 + 8 * stage);
                         if (++stage == STAGES) { stage = 0; phase ^= 1; }
                     }
                     if (ok) mma_commit(cfull0 + 8 * b);
                 }
+                if (ok) mma_commit(sfull0 + 8 * ts);
             }
             // Every MMA issued above has retired once this barrier flips.
             mma_commit(drain);
@@ -336,10 +393,11 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
     } else {
         const int q = warp & 3;                    // TMEM lanes 32q .. 32q+31 = tile rows
         const int h = (warp - 2) >> 2;             // column half of the tile
-        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        const uint32_t lane_cols = ((uint32_t)(q * 32) << 16) + (uint32_t)(h * S::HALF);
         uint32_t chunk = 0;
         bool ok = true;
-        for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
+        int local = 0;
+        for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x, local++) {
             float acc[S::HALF];
 #pragma unroll
             for (int j = 0; j < S::HALF; j++) acc[j] = 0.0f;
@@ -347,18 +405,20 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                 const uint32_t b = chunk & 1;
                 if (!bar_wait(cfull0 + 8 * b, (chunk >> 1) & 1, abort, err, 6)) { ok = false; break; }
                 fence_after();
-#pragma unroll
-                for (int j = 0; j < S::HALF; j += 32) {
-                    uint32_t r[32];
-                    tmem_ld32(tmem + lane_addr + b * (uint32_t)BN + (uint32_t)(h * S::HALF + j), r);
-#pragma unroll
-                    for (int i = 0; i < 32; i++) acc[j + i] = __fadd_rn(acc[j + i], __uint_as_float(r[i]));
-                }
+                drain_add<S::HALF>(tmem + lane_cols + b * (uint32_t)BN, acc);
                 fence_before();
                 __syncwarp();
                 if (lane == 0) bar_arrive(cempty0 + 8 * b);
             }
             if (!ok) break;
+            const uint32_t ts = local & 1;
+            if (!bar_wait(sfull0 + 8 * ts, (local >> 1) & 1, abort, err, 7)) break;
+            fence_after();
+            drain_add<S::HALF>(tmem + lane_cols + (2 + ts) * (uint32_t)BN, acc);
+            fence_before();
+            __syncwarp();
+            if (lane == 0) bar_arrive(sempty0 + 8 * ts);
+
             const int m0 = (t / n_tiles) * BM, n0 = (t % n_tiles) * BN;
             const int r = m0 + q * 32 + lane;
             if (r < M) {
@@ -432,8 +492,7 @@ struct Cfg {
 
 #define TCG_CFG(BN, BK, ST) { BN, BK, ST, Shape<BN, BK, ST>::SMEM, (const void *)gemm_tf32x3_kernel<BN, BK, ST> }
 const Cfg CFGS[] = {
-    TCG_CFG(256, 16, 4), TCG_CFG(192, 16, 5), TCG_CFG(128, 16, 6), TCG_CFG(64, 16, 8),
-    TCG_CFG(256, 32, 2), TCG_CFG(192, 32, 2), TCG_CFG(128, 32, 3), TCG_CFG(64, 32, 4),
+    TCG_CFG(128, 32, 3), TCG_CFG(64, 32, 4), TCG_CFG(128, 16, 6), TCG_CFG(64, 16, 8),
 };
 #undef TCG_CFG
 constexpr int NCFG = sizeof(CFGS) / sizeof(CFGS[0]);
@@ -445,7 +504,7 @@ int choose_cfg(int M, int N)
     const int sms = ctx().sms > 0 ? ctx().sms : 148;
     int best = 0;
     long best_cost = -1;
-    for (int i = 0; i < 4; i++) {
+    for (int i = 0; i < 2; i++) {
         const long tiles = (long)((M + BM - 1) / BM) * ((N + CFGS[i].bn - 1) / CFGS[i].bn);
         const long rounds = (tiles + sms - 1) / sms;
         const long cost = rounds * (CFGS[i].bn + 32);
@@ -457,7 +516,7 @@ int choose_cfg(int M, int N)
 }  // namespace
 
 // K-elements accumulated in TMEM between two drains into fp32 registers.
-int g_chunk_k = 32;
+int g_chunk_k = 256;
 
 int gemm_num_cfgs() { return NCFG; }
 int gemm_cfg_bn(int cfg) { return cfg >= 0 && cfg < NCFG ? CFGS[cfg].bn : 0; }

@@ -11,6 +11,7 @@
 #include "tcg_common.cuh"
 #include "tcg_internal.h"
 
+#include <cuda_fp16.h>
 #include <string.h>
 
 namespace tcg {
@@ -199,6 +200,226 @@ matvec_kq_kernel(const uint8_t *__restrict__ W, const float *__restrict__ x, flo
     }
 }
 
+// ----------------------------------------------------- streaming matvec
+// Persistent CTAs of 16 warps, one per SM. x stays in shared memory for the
+// whole launch (for Q4_K also the sum of every 8 consecutive x, for the min
+// term). Every warp streams its weight segments (a quarter row of Q4_K, a
+// whole row of Q6_K) through a two-slot cp.async ring and computes one slot
+// while the next lands. A superblock is handled by a half-warp, 16 weights
+// per lane: the quant bytes are turned into floats 2^23 + q with byte
+// permutes, shifted back exactly with packed f32x2 adds, and dotted with x
+// by packed f32x2 FMAs:
+//   Q4_K  sum (a q - c) x  =  a * sum(q x) - c * sum(x)   per 8 weights
+//   Q6_K  sum (d sc) q x   =  (d sc) * sum(q x)
+constexpr int MV_WARPS = 16;
+typedef unsigned long long u64;
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ u64 fma2(u64 a, u64 b, u64 c)
+{
+    u64 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ u64 add2(u64 a, u64 b)
+{
+    u64 d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// bytes j and j+1 of w as the float pair (2^23 + byte_j, 2^23 + byte_j+1)
+__device__ __forceinline__ u64 magic2(uint32_t w, int j)
+{
+    const uint32_t a = __byte_perm(w, 0x4B000000u, 0x7440u | (unsigned)j);
+    const uint32_t b = __byte_perm(w, 0x4B000000u, 0x7440u | (unsigned)(j + 1));
+    return (u64)a | ((u64)b << 32);
+}
+
+// sum_i (v_i - off) x_i over the 8 bytes v of (w0, w1); x 16-byte aligned in
+// shared memory; neg_off2 holds -(2^23 + off) twice.
+__device__ __forceinline__ float dot8(uint32_t w0, uint32_t w1, u64 neg_off2, const float *x)
+{
+    const ulonglong2 xa = *reinterpret_cast<const ulonglong2 *>(x);
+    const ulonglong2 xb = *reinterpret_cast<const ulonglong2 *>(x + 4);
+    u64 acc = 0ull;
+    acc = fma2(add2(magic2(w0, 0), neg_off2), xa.x, acc);
+    acc = fma2(add2(magic2(w0, 2), neg_off2), xa.y, acc);
+    acc = fma2(add2(magic2(w1, 0), neg_off2), xb.x, acc);
+    acc = fma2(add2(magic2(w1, 2), neg_off2), xb.y, acc);
+    return __uint_as_float((uint32_t)acc) + __uint_as_float((uint32_t)(acc >> 32));
+}
+
+// 8 bytes at a 2-byte-aligned shared-memory address.
+__device__ __forceinline__ uint2 lds8_unaligned(const uint8_t *p)
+{
+    const uintptr_t a = (uintptr_t)p;
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(a & ~(uintptr_t)3);
+    const uint32_t sh = (uint32_t)(a & 3) * 8u;
+    const uint32_t w0 = w[0], w1 = w[1], w2 = w[2];
+    return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
+}
+
+__device__ __forceinline__ float sb_dot_q4k(const uint8_t *blk, int l16, const float *xs, const float *x8, int k0)
+{
+    const int g = l16 >> 2, p = (l16 & 3) * 8;
+    const uint4 hd = *reinterpret_cast<const uint4 *>(blk);
+    const uint2 q = *reinterpret_cast<const uint2 *>(blk + 16 + 32 * g + p);
+    const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFFu)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
+    // 6-bit scale / min of sub-blocks 2g (lo nibbles) and 2g+1 (hi nibbles)
+    const int k = 2 * (g & 1);
+    float a[2], c[2];
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+        const uint32_t by = (hd.y >> (8 * (k + u))) & 0xFFu, bz = (hd.z >> (8 * (k + u))) & 0xFFu;
+        const uint32_t bw = (hd.w >> (8 * (k + u))) & 0xFFu;
+        const uint32_t sc = g < 2 ? (by & 63u) : ((bw & 15u) | ((by >> 6) << 4));
+        const uint32_t mn = g < 2 ? (bz & 63u) : ((bw >> 4) | ((bz >> 6) << 4));
+        a[u] = d * (float)sc;
+        c[u] = dmin * (float)mn;
+    }
+    const u64 neg = 0xCB000000CB000000ull;          // (-2^23, -2^23)
+    const int xo = k0 + 64 * g + p;
+    const float dl = dot8(q.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, neg, xs + xo);
+    const float dh = dot8((q.x >> 4) & 0x0F0F0F0Fu, (q.y >> 4) & 0x0F0F0F0Fu, neg, xs + xo + 32);
+    float r = a[0] * dl;
+    r = fmaf(-c[0], x8[xo >> 3], r);
+    r = fmaf(a[1], dh, r);
+    return fmaf(-c[1], x8[(xo + 32) >> 3], r);
+}
+
+__device__ __forceinline__ float sb_dot_q6k(const uint8_t *blk, int l16, const float *xs, int k0)
+{
+    const int h = l16 >> 3, rr = (l16 >> 2) & 1, l0 = (l16 & 3) * 8;
+    const uint2 ql = lds8_unaligned(blk + 64 * h + 32 * rr + l0);
+    const uint2 qh = lds8_unaligned(blk + 128 + 32 * h + l0);
+    const float d = __half2float(__ushort_as_half((unsigned short)(blk[208] | (blk[209] << 8))));
+    const float sa = d * (float)(int8_t)blk[192 + 8 * h + 2 * rr + (l0 >> 4)];
+    const float sb = d * (float)(int8_t)blk[192 + 8 * h + 2 * (rr + 2) + (l0 >> 4)];
+    const u64 neg = 0xCB000020CB000020ull;          // (-(2^23 + 32), twice)
+    const uint32_t s0 = 2 * rr, s1 = 2 * rr + 4;
+    const uint32_t a0 = (ql.x & 0x0F0F0F0Fu) | (((qh.x >> s0) & 0x03030303u) << 4);
+    const uint32_t a1 = (ql.y & 0x0F0F0F0Fu) | (((qh.y >> s0) & 0x03030303u) << 4);
+    const uint32_t b0 = ((ql.x >> 4) & 0x0F0F0F0Fu) | (((qh.x >> s1) & 0x03030303u) << 4);
+    const uint32_t b1 = ((ql.y >> 4) & 0x0F0F0F0Fu) | (((qh.y >> s1) & 0x03030303u) << 4);
+    const int xo = k0 + 128 * h + 32 * rr + l0;
+    const float da = dot8(a0, a1, neg, xs + xo);
+    const float db = dot8(b0, b1, neg, xs + xo + 64);
+    return fmaf(sb, db, sa * da);
+}
+
+template <int TYPE, int SEGS>
+__global__ void __launch_bounds__(MV_WARPS * 32, 1)
+matvec_stream_kernel(const uint8_t *__restrict__ W, const float *__restrict__ x, float *__restrict__ y,
+                     int N, int K)
+{
+    constexpr int BB = KQ<TYPE>::BYTES;
+    constexpr int RPI = MV_WARPS / SEGS;                 // rows per CTA iteration
+    extern __shared__ uint4 sm4[];
+    float *xs = reinterpret_cast<float *>(sm4);
+    float *x8 = xs + K;
+    const int bpr = K / QK, bps = bpr / SEGS;            // superblocks per row / segment
+    const int seg_bytes = bps * BB;
+    uint8_t *ring = reinterpret_cast<uint8_t *>(x8 + ((K / 8 + 3) & ~3));
+    __shared__ float part[MV_WARPS];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int half = lane >> 4, l16 = lane & 15;
+    const int seg = wid % SEGS, rloc = wid / SEGS;
+    uint8_t *slot[2] = { ring + (size_t)wid * 2 * seg_bytes, ring + (size_t)wid * 2 * seg_bytes + seg_bytes };
+
+    auto prefetch = [&](int it, uint8_t *dst) {
+        const int row = it * RPI + rloc;
+        if (row < N) {
+            const uint8_t *src = W + ((size_t)row * bpr + (size_t)seg * bps) * BB;
+            const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+            for (int i = lane; i < seg_bytes / 16; i += 32) cp_async16(d + 16 * i, src + 16 * i);
+        }
+        cp_commit();
+    };
+
+    int it = blockIdx.x;
+    prefetch(it, slot[0]);
+    for (int i = threadIdx.x; i < K / 4; i += blockDim.x)
+        reinterpret_cast<float4 *>(xs)[i] = __ldg(reinterpret_cast<const float4 *>(x) + i);
+    __syncthreads();
+    if (TYPE == GGML_TYPE_Q4_K)
+        for (int i = threadIdx.x; i < K / 8; i += blockDim.x) {
+            float s = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; j++) s += xs[8 * i + j];
+            x8[i] = s;
+        }
+    __syncthreads();
+
+    for (int n = 0; it * RPI < N; it += gridDim.x, n++) {
+        const int nxt = it + gridDim.x;
+        prefetch(nxt, slot[(n + 1) & 1]);           // empty group past the end
+        cp_wait1();
+        __syncwarp();
+        const uint8_t *buf = slot[n & 1];
+        const int row = it * RPI + rloc;
+        float acc = 0.0f;
+        if (row < N) {
+            for (int b = half; b < bps + half; b += 2) {
+                if (b < bps) {
+                    const int k0 = (seg * bps + b) * QK;
+                    if (TYPE == GGML_TYPE_Q4_K) acc += sb_dot_q4k(buf + (size_t)b * BB, l16, xs, x8, k0);
+                    else acc += sb_dot_q6k(buf + (size_t)b * BB, l16, xs, k0);
+                }
+            }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+        if (SEGS == 1) {
+            if (lane == 0 && row < N) y[row] = acc;
+        } else {
+            if (lane == 0) part[wid] = acc;
+            __syncthreads();
+            if (seg == 0 && lane == 0 && row < N) {
+                float s = 0.0f;
+                for (int j = 0; j < SEGS; j++) s += part[wid + j];
+                y[row] = s;
+            }
+            __syncthreads();
+        }
+    }
+    cp_wait0();
+}
+
+template <int TYPE, int SEGS>
+static bool try_matvec_stream(float *y, const void *W, const float *x, int N, int K)
+{
+    constexpr int BB = KQ<TYPE>::BYTES;
+    const int bpr = K / QK;
+    if (bpr % SEGS || ((size_t)(bpr / SEGS) * BB) % 16 || ((uintptr_t)W & 15)) return false;
+    const size_t ring = (size_t)MV_WARPS * 2 * (bpr / SEGS) * BB;
+    const size_t smem = (size_t)K * 4 + (size_t)((K / 8 + 3) & ~3) * 4 + ring;
+    if (smem > 200 * 1024) return false;
+    static unsigned done[64];
+    const int dev = ctx().device & 63;
+    if (!done[dev]) {
+        if (cudaFuncSetAttribute(matvec_stream_kernel<TYPE, SEGS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 200 * 1024) != cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        done[dev] = 1;
+    }
+    constexpr int RPI = MV_WARPS / SEGS;
+    const long iters = ((long)N + RPI - 1) / RPI;
+    const int grid = (int)(iters < ctx().sms ? iters : ctx().sms);
+    matvec_stream_kernel<TYPE, SEGS><<<grid, MV_WARPS * 32, smem, ctx().cur>>>((const uint8_t *)W, x, y, N, K);
+    return cudaGetLastError() == cudaSuccess || fail("matvec launch failed");
+}
+
 static unsigned grid_for(size_t warps_needed)
 {
     const size_t cap = (size_t)ctx().sms * 8;   // 8 CTAs x 8 warps per SM
@@ -221,7 +442,14 @@ static bool launch_matvec(float *y, const void *W, const float *x, int N, int K)
 template <int TYPE>
 static bool matvec_dispatch(float *y, const void *W, const float *x, int N, int K)
 {
-    // Enough warps to keep ~48 resident per SM streaming weight bytes.
+    // The streaming kernel whenever its segments tile the rows in 16-byte
+    // units and x fits on chip; rows split in 4 when there are few of them.
+    const long rows_per_sm = (long)N / (ctx().sms > 0 ? ctx().sms : 148);
+    if (rows_per_sm < 64 && try_matvec_stream<TYPE, 4>(y, W, x, N, K)) return true;
+    if (try_matvec_stream<TYPE, 1>(y, W, x, N, K)) return true;
+    if (try_matvec_stream<TYPE, 2>(y, W, x, N, K)) return true;
+    // Otherwise the staged kernel, with enough warps per row to keep ~48
+    // resident per SM streaming weight bytes.
     const long want = (long)ctx().sms * 48;
     if ((long)N >= want) return launch_matvec<TYPE, 1>(y, W, x, N, K);
     if ((long)N * 2 >= want) return launch_matvec<TYPE, 2>(y, W, x, N, K);
