@@ -121,6 +121,23 @@ bool tcg_split_tf32(float *hi, float *lo, const float *src, size_t n);
  * alone, for callers that keep weights split once and reuse them. */
 bool tcg_linear_split(float *y, const float *x_hi, const float *x_lo, const float *w_hi, const float *w_lo,
                       const float *bias, int M, int N, int K);
+/* tcg_linear for callers that must not have a call allocate device memory
+ * (no counterpart in the reference): a latency-critical loop that cannot
+ * afford the device-wide synchronization cudaFree brings, or a program that
+ * divides the GPU's memory once at start-up with its own allocator. The tf32
+ * copies of x and W go to a fixed array inside the library instead of
+ * tcg_linear's grow-on-demand buffer, so the call itself never allocates
+ * (tcg_init still sets up the device once, before).
+ * Limits: K a positive multiple of 4, x and W 16-byte aligned, and
+ * (M + N) * K at most TCG_NOALLOC_SCRATCH_BYTES / 8 (2,097,152 floats);
+ * anything larger is refused with a message.
+ * The array lives on every device that runs this call, from the first call
+ * until the process exits. That first call on each device looks up the
+ * array's device address, so make it before any stream capture. All calls
+ * share the array: calls whose kernels could overlap on the GPU (other
+ * streams or host threads) race on it and must be serialised by the caller. */
+#define TCG_NOALLOC_SCRATCH_BYTES (16u << 20)
+bool tcg_linear_noalloc(float *y, const float *x, const float *W, const float *bias, int M, int N, int K);
 bool tcg_layernorm(float *out, const float *x, const float *gamma, const float *beta,
                    int rows, int cols, float eps);
 bool tcg_gelu(float *out, const float *x, size_t n);
