@@ -321,10 +321,38 @@ def run_ours(args, dist):
     for _ in range(args.warmup):
         e2e_step()
     dist.barrier()
-    e2e_ms = tcg.time_ms(lambda: [e2e_step() for _ in range(args.steps)], 4, 5) / args.steps
+    e2e_block_ms = tcg.time_ms(lambda: [e2e_step() for _ in range(args.steps)], 4, 5) / args.steps
+    dist.barrier()
+
+    # the serving form: tcg_vit_submit / tcg_vit_wait with two steps in flight,
+    # so a step's pixel copy overlaps the previous step's forward; wall clock
+    # from the first submission to the last embeddings on the host
+    import ctypes
+    hpx2 = tcg.HostBuffer(shard.shape)
+    hpx2.array[...] = shard
+    hout2 = tcg.HostBuffer((per, d_out))
+    ins, outs = (hpx, hpx2), (hout, hout2)
+    tk = ctypes.c_int(0)
+
+    def pipelined(steps):
+        prev = None
+        for i in range(steps):
+            tcg.check(L.tcg_vit_submit(model.dev, ins[i & 1].ptr, per, outs[i & 1].ptr, ctypes.byref(tk)),
+                      "tcg_vit_submit")
+            if prev is not None:
+                tcg.check(L.tcg_vit_wait(model.dev, prev), "tcg_vit_wait")
+            prev = tk.value
+        tcg.check(L.tcg_vit_wait(model.dev, prev), "tcg_vit_wait")
+
+    pipelined(args.warmup)
+    tcg.sync()
+    dist.barrier()
+    t0 = time.perf_counter()
+    pipelined(args.steps)
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
     dist.barrier()
     clk = clocks.stop()
-    emb_ok = bool(np.isfinite(hout.array).all())
+    emb_ok = bool(np.isfinite(hout.array).all() and np.array_equal(hout.array, hout2.array))
 
     # per-kernel-class device time: the same forward, eagerly, with events
     L.tcg_vit_profile_begin()
@@ -338,6 +366,7 @@ def run_ours(args, dist):
 
     ms_max = dist.max(ms)
     e2e_max = dist.max(e2e_ms)
+    e2e_block_max = dist.max(e2e_block_ms)
     gemm_ms = dist.max(kms[0] / args.steps)
     prof_step = dist.max(sum(kms) / args.steps)
 
@@ -379,7 +408,10 @@ def run_ours(args, dist):
             "e2e": {"value": round(args.batch / (e2e_max * 1e-3), 2), "unit": "images/s",
                     "h2d_bytes_per_step": int(shard.nbytes) * dist.world,
                     "d2h_bytes_per_step": per * d_out * 4 * dist.world,
-                    "api": "tcg_vit_encode_batch (host buffers, page-locked)"},
+                    "api": "tcg_vit_submit + tcg_vit_wait (page-locked host buffers, two steps in flight; "
+                           "wall clock, max over ranks)",
+                    "blocking_value": round(args.batch / (e2e_block_max * 1e-3), 2),
+                    "blocking_api": "tcg_vit_encode_batch (one blocking call per step; CUDA events)"},
             "gpu_launches": launches * args.steps,
             "clocks": clk,
             "model_flop_per_image": gf + af + pf,
@@ -388,8 +420,8 @@ def run_ours(args, dist):
     model.close()
     dpx.close()
     dout.close()
-    hpx.close()
-    hout.close()
+    for b in (hpx, hout, hpx2, hout2):
+        b.close()
 
     if dist.rank == 0 and dist.world == 1:
         if not args.no_aux:

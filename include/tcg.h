@@ -174,6 +174,17 @@ bool tcg_vit_encode_batch(tcg_vit_t *v, const float *pixels, int n_images, float
 /* DEVICE buffers, asynchronous, no taps. */
 bool tcg_vit_encode_device(tcg_vit_t *v, const float *pixels, int n_images, float *out);
 
+/* HOST buffers, asynchronous (for serving loops): the pixels are copied in
+ * on the model's own copy stream, the forward runs on the library stream
+ * once they have landed, and the embeddings are copied to `out`; the call
+ * returns at once with a ticket. Two submissions can be in flight (the
+ * copy of one overlaps the forward of the other); a third waits for the
+ * oldest. `pixels` and `out` must stay untouched until tcg_vit_wait
+ * returns for that ticket; page-locked buffers make the copies truly
+ * asynchronous. tcg_vit_encode_batch first finishes any pending submission. */
+bool tcg_vit_submit(tcg_vit_t *v, const float *pixels, int n_images, float *out, int *ticket);
+bool tcg_vit_wait(tcg_vit_t *v, int ticket);
+
 /* Instrumentation. Kernel launches of one forward; and, between begin and
  * end, every forward runs eagerly with CUDA events around each launch, whose
  * device time end() sums per kernel class: [0] tensor-core GEMMs,

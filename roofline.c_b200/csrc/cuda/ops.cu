@@ -4,6 +4,8 @@
 #include "numerics.cuh"
 #include "gemm.cuh"
 
+#include <type_traits>
+
 namespace tcg {
 
 __device__ __forceinline__ void put(const OutSpec &o, size_t row, int col, float v)
@@ -389,23 +391,29 @@ bool launch_split(const float *src, float *hi, float *lo, size_t n, cudaStream_t
 }
 
 // Patch row r = i*G*G + gy*G + gx, column c = ch*P*P + ky*P + kx holds
-// pixel [i, ch, gy*P + ky, gx*P + kx].
+// pixel [i, ch, gy*P + ky, gx*P + kx]. A patch row's kx run is contiguous in
+// the image, so each thread moves VEC consecutive floats (VEC | P).
+template <int VEC>
 __global__ void patches_kernel(const float *__restrict__ px, int n_img, int S, int P,
                                float *__restrict__ hi, float *__restrict__ lo)
 {
-    const int G = S / P, KP = 3 * P * P;
-    const size_t total = (size_t)n_img * G * G * KP;
+    typedef typename std::conditional<VEC == 4, float4, typename std::conditional<VEC == 2, float2, float>::type>::type V;
+    const int G = S / P, PV = P / VEC, KPV = 3 * P * PV;          // vectors per patch row
+    const size_t total = (size_t)n_img * G * G * KPV;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-        const size_t r = i / KP;
-        const int c = (int)(i - r * KP);
+        const size_t r = i / KPV;
+        const int c = (int)(i - r * KPV);                  // vector index within the row
         const int img = (int)(r / (G * G)), t = (int)(r % (G * G));
         const int gy = t / G, gx = t % G;
-        const int ch = c / (P * P), rem = c % (P * P), ky = rem / P, kx = rem % P;
-        const float v = px[(((size_t)img * 3 + ch) * S + gy * P + ky) * S + gx * P + kx];
-        float h, l;
-        split_tf32(v, h, l);
-        hi[i] = h;
-        lo[i] = l;
+        const int ch = c / (P * PV), rem = c % (P * PV), ky = rem / PV, kv = rem % PV;
+        const V v = *reinterpret_cast<const V *>(px + (((size_t)img * 3 + ch) * S + gy * P + ky) * S + gx * P + kv * VEC);
+        const float *f = reinterpret_cast<const float *>(&v);
+        V h, l;
+        float *hf = reinterpret_cast<float *>(&h), *lf = reinterpret_cast<float *>(&l);
+#pragma unroll
+        for (int j = 0; j < VEC; j++) split_tf32(f[j], hf[j], lf[j]);
+        reinterpret_cast<V *>(hi)[i] = h;
+        reinterpret_cast<V *>(lo)[i] = l;
     }
 }
 
@@ -413,7 +421,41 @@ bool launch_patches(const float *px, int n_img, int S, int P, float *hi, float *
 {
     const size_t total = (size_t)n_img * (S / P) * (S / P) * 3 * P * P;
     if (total == 0) return true;
-    patches_kernel<<<grid1d(total), 256, 0, s>>>(px, n_img, S, P, hi, lo);
+    const bool a16 = !(((uintptr_t)px | (uintptr_t)hi | (uintptr_t)lo) & 15) && !(S & 3);
+    const bool a8 = !(((uintptr_t)px | (uintptr_t)hi | (uintptr_t)lo) & 7) && !(S & 1);
+    if (P % 4 == 0 && a16) patches_kernel<4><<<grid1d(total / 4), 256, 0, s>>>(px, n_img, S, P, hi, lo);
+    else if (P % 2 == 0 && a8) patches_kernel<2><<<grid1d(total / 2), 256, 0, s>>>(px, n_img, S, P, hi, lo);
+    else patches_kernel<1><<<grid1d(total), 256, 0, s>>>(px, n_img, S, P, hi, lo);
+    TCG_LAUNCHED();
+    return true;
+}
+
+// dst_hi/lo [C, R] = tf32 pair of src [R, C] transposed.
+__global__ void transpose_split_kernel(const float *__restrict__ src, int R, int C,
+                                       float *__restrict__ hi, float *__restrict__ lo)
+{
+    __shared__ float tile[32][33];
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int r = r0 + i, c = c0 + threadIdx.x;
+        if (r < R && c < C) tile[i][threadIdx.x] = src[(size_t)r * C + c];
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int c = c0 + i, r = r0 + threadIdx.x;
+        if (r < R && c < C) {
+            float h, l;
+            split_tf32(tile[threadIdx.x][i], h, l);
+            hi[(size_t)c * R + r] = h;
+            lo[(size_t)c * R + r] = l;
+        }
+    }
+}
+
+bool launch_transpose_split(const float *src, int R, int C, float *hi, float *lo, cudaStream_t s)
+{
+    if (R <= 0 || C <= 0) return true;
+    transpose_split_kernel<<<dim3(ceil_div(C, 32), ceil_div(R, 32)), dim3(32, 8), 0, s>>>(src, R, C, hi, lo);
     TCG_LAUNCHED();
     return true;
 }

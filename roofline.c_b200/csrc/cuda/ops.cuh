@@ -32,6 +32,9 @@ bool launch_gemm_simt(float *C, int ldc, const float *A, int lda, const float *B
 // hi/lo split of n contiguous floats.
 bool launch_split(const float *src, float *hi, float *lo, size_t n, cudaStream_t s);
 
+// dst pair [C, R] = tf32 hi/lo of src [R, C] transposed.
+bool launch_transpose_split(const float *src, int R, int C, float *hi, float *lo, cudaStream_t s);
+
 // im2patch (src/vit.c:283-303) of n_img images [3, S, S] straight into the
 // hi/lo operand pair [n_img*G*G, 3*P*P].
 bool launch_patches(const float *px, int n_img, int S, int P, float *hi, float *lo, cudaStream_t s);

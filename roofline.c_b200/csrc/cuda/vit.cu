@@ -10,10 +10,11 @@
 //   L blocks   LN1 -> h(hi/lo); GEMM qkv (+bias) -> qkv; attention -> a(hi/lo);
 //              GEMM out (+bias, +x) -> x; LN2 -> h; GEMM up (+bias, GELU)
 //              -> f(hi/lo); GEMM down (+bias, +x) -> x      (taps blk0, blk_last)
-//   LN         ln_post on the CLS rows (all rows when tapping)   (tap ln_post)
-//   proj       pooled[n, D] x proj[D, d_out], fp32 CUDA cores     (tap embedding)
-// All GEMMs are the 3xTF32 tcgen05 kernel; the layer stack between the patch
-// gather and the projection is recorded once per batch size as a CUDA graph.
+//   LN         ln_post on the CLS rows, as a tf32 pair (all rows too, plain,
+//              when tapping)                                       (tap ln_post)
+//   GEMM       pooled[n, D] x proj[D, d_out] (proj held transposed) (tap embedding)
+// All GEMMs are the 3xTF32 tcgen05 kernel; everything after the patch gather
+// is recorded once per batch size as a CUDA graph.
 #include "gemm.cuh"
 #include "tcg_internal.h"
 
@@ -45,19 +46,27 @@ struct tcg_vit {
     const float *patch_h = nullptr, *patch_l = nullptr, *cls = nullptr, *pos = nullptr;
     const float *ln_pre_g = nullptr, *ln_pre_b = nullptr, *ln_post_g = nullptr, *ln_post_b = nullptr;
     const float *proj = nullptr;
+    const float *projT_h = nullptr, *projT_l = nullptr;   // v.proj transposed to [d_out, D], split
 
     // activations
     tcg_arena_t act{};
     float *px = nullptr, *x = nullptr, *h_hi = nullptr, *h_lo = nullptr, *qkv = nullptr;
-    float *f_hi = nullptr, *f_lo = nullptr, *pooled = nullptr, *out = nullptr;
+    float *f_hi = nullptr, *f_lo = nullptr, *pooled_hi = nullptr, *pooled_lo = nullptr, *out = nullptr;
     float *p_hi = nullptr, *p_lo = nullptr;   // alias f_hi / f_lo
 
     struct Plans {
-        tcg::GemmPlan patch;
+        tcg::GemmPlan patch, proj;
         std::vector<tcg::GemmPlan> qkv, out, up, down;
         cudaGraphExec_t graph = nullptr;
     };
     std::map<int, std::unique_ptr<Plans>> plans;
+
+    // asynchronous submissions: two pixel slots and a copy stream
+    float *px_slot[2] = { nullptr, nullptr };   // [0] is px; [1] allocated on first submission
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t copied[2] = {}, done[2] = {};
+    bool in_flight[2] = { false, false };
+    int next_ticket = 0;
 
     ~tcg_vit()
     {
@@ -66,6 +75,12 @@ struct tcg_vit {
         tcg_arena_destroy(&act);
         if (wslab) cudaFree(wslab);
         if (sslab) cudaFree(sslab);
+        for (int i = 0; i < 2; i++) {
+            if (px_slot[i] && px_slot[i] != px) cudaFree(px_slot[i]);
+            if (copied[i]) cudaEventDestroy(copied[i]);
+            if (done[i]) cudaEventDestroy(done[i]);
+        }
+        if (copy_stream) cudaStreamDestroy(copy_stream);
     }
 };
 
@@ -146,7 +161,7 @@ static tcg_vit *vit_alloc(const tc_vit_t *m, int max_batch, std::vector<WEntry> 
     const size_t D = v->D, F = v->F, K0 = 3 * (size_t)v->P * v->P;
     const size_t per_layer = 2 * align_floats(3 * D * D) + 2 * align_floats(D * D) + 2 * align_floats(F * D) +
                              2 * align_floats(D * F);
-    v->sslab_floats = 2 * align_floats(D * K0) + per_layer * v->L;
+    v->sslab_floats = 2 * align_floats(D * K0) + per_layer * v->L + 2 * align_floats(D * (size_t)v->d_out);
     if (cudaMalloc(&v->sslab, v->sslab_floats * sizeof(float)) != cudaSuccess) {
         cudaGetLastError();
         fail("tcg_vit_upload: cannot allocate %zu MB of split weights", v->sslab_floats * 4 >> 20);
@@ -161,11 +176,12 @@ static tcg_vit *vit_alloc(const tc_vit_t *m, int max_batch, std::vector<WEntry> 
         y.up_h = take(F * D); y.up_l = take(F * D);
         y.down_h = take(D * F); y.down_l = take(D * F);
     }
+    v->projT_h = take(D * (size_t)v->d_out); v->projT_l = take(D * (size_t)v->d_out);
 
     const size_t n = (size_t)max_batch, T = v->T, G2 = (size_t)v->G * v->G;
     const size_t f_floats = std::max(n * T * F, n * G2 * K0);
     const size_t want = (n * 3 * v->S * v->S + n * T * D * 3 + n * T * 3 * D + 2 * f_floats +
-                         n * D + n * v->d_out) * sizeof(float) + 16 * 256;
+                         2 * n * D + n * v->d_out) * sizeof(float) + 16 * 256;
     v->act = tcg_arena_create(want, "vit activations");
     if (!tcg_arena_ok(&v->act)) return nullptr;
     auto alloc = [&](size_t floats) { return (float *)tcg_arena_alloc(&v->act, floats * sizeof(float), 256); };
@@ -176,7 +192,8 @@ static tcg_vit *vit_alloc(const tc_vit_t *m, int max_batch, std::vector<WEntry> 
     v->qkv = alloc(n * T * 3 * D);
     v->f_hi = alloc(f_floats);
     v->f_lo = alloc(f_floats);
-    v->pooled = alloc(n * D);
+    v->pooled_hi = alloc(n * D);
+    v->pooled_lo = alloc(n * D);
     v->out = alloc(n * v->d_out);
     v->p_hi = v->f_hi;
     v->p_lo = v->f_lo;
@@ -199,6 +216,10 @@ static bool split_weights(tcg_vit *v, const std::vector<WEntry> &table, const st
             !launch_split(v->wslab + off[b + 10], (float *)y.down_h, (float *)y.down_l, D * F, s))
             return false;
     }
+    {   // v.proj is [D, d_out] (used untransposed, src/vit.c:384-386): store it as the [d_out, D] operand
+        if (!launch_transpose_split(v->proj, v->D, v->d_out, (float *)v->projT_h, (float *)v->projT_l, s))
+            return false;
+    }
     (void)table;
     return true;
 }
@@ -219,6 +240,11 @@ static tcg_vit::Plans *plans_for(tcg_vit *v, int n)
     e.out.plain = v->x;
     e.out.ld = D;
     if (!gemm_plan(p->patch, v->p_hi, v->p_lo, v->patch_h, v->patch_l, n * G2, D, K0, e)) return nullptr;
+
+    GemmEpi pe;                                   // embedding = pooled x proj, into v->out
+    pe.out.plain = v->out;
+    pe.out.ld = v->d_out;
+    if (!gemm_plan(p->proj, v->pooled_hi, v->pooled_lo, v->projT_h, v->projT_l, n, v->d_out, D, pe)) return nullptr;
 
     p->qkv.resize(v->L); p->out.resize(v->L); p->up.resize(v->L); p->down.resize(v->L);
     for (int i = 0; i < v->L; i++) {
@@ -344,16 +370,15 @@ static bool forward_body(tcg_vit *v, tcg_vit::Plans *p, int n, Tapper *tap)
     }
 
     if (tap) {
-        // ln_post over every row (into the free qkv buffer), then the CLS rows
+        // ln_post over every row (into the free qkv buffer) for the tap
         OutSpec ls; ls.plain = v->qkv; ls.ld = D;
         PROF(K_NORM, launch_layernorm(v->x, D, v->ln_post_g, v->ln_post_b, M, D, v->eps, ls, s));
         if (!tap->deliver("ln_post", v->qkv, n, T, D, (size_t)T * D)) return false;
-        TCG_CUDA(cudaMemcpy2DAsync(v->pooled, D * sizeof(float), v->qkv, (size_t)T * D * sizeof(float),
-                                   D * sizeof(float), n, cudaMemcpyDeviceToDevice, s));
-    } else {
-        OutSpec ps; ps.plain = v->pooled; ps.ld = D;
-        PROF(K_NORM, launch_layernorm(v->x, T * D, v->ln_post_g, v->ln_post_b, n, D, v->eps, ps, s));
     }
+    // ln_post of the CLS rows as the tf32 pair the projection GEMM reads
+    OutSpec ps; ps.hi = v->pooled_hi; ps.lo = v->pooled_lo; ps.ld = D;
+    PROF(K_NORM, launch_layernorm(v->x, T * D, v->ln_post_g, v->ln_post_b, n, D, v->eps, ps, s));
+    PROF(K_GEMM, gemm_run(p->proj, s, err));
     return true;
 }
 
@@ -385,8 +410,8 @@ static bool forward(tcg_vit *v, const float *px, int n, float *out, Tapper *tap)
     } else {
         TCG_CUDA(cudaGraphLaunch(p->graph, s));
     }
-    PROF(K_OTHER, launch_gemm_simt(out, v->d_out, v->pooled, v->D, v->proj, v->d_out, nullptr, n, v->d_out,
-                                   v->D, false, s));
+    if (out != v->out)
+        TCG_CUDA(cudaMemcpyAsync(out, v->out, (size_t)n * v->d_out * sizeof(float), cudaMemcpyDeviceToDevice, s));
     if (tap && !tap->deliver("embedding", out, n, 1, v->d_out, (size_t)v->d_out)) return false;
     return true;
 }
@@ -492,6 +517,11 @@ bool tcg_vit_encode_batch_staged(tcg_vit_t *v, const float *pixels, int n_images
     if (n_images <= 0) return true;
     if (n_images > v->max_batch) return fail("batch of %d exceeds the model's max_batch %d", n_images, v->max_batch);
     if (tap && !staging) return fail("tcg_vit_encode_batch: no tap staging");
+    for (int i = 0; i < 2; i++)         // finish asynchronous submissions first: they share the buffers
+        if (v->in_flight[i]) {
+            TCG_CUDA(cudaEventSynchronize(v->done[i]));
+            v->in_flight[i] = false;
+        }
     cudaStream_t s = ctx().cur;
     const size_t px_bytes = (size_t)n_images * 3 * v->S * v->S * sizeof(float);
     TCG_CUDA(cudaMemcpyAsync(v->px, pixels, px_bytes, cudaMemcpyHostToDevice, s));
@@ -499,6 +529,53 @@ bool tcg_vit_encode_batch_staged(tcg_vit_t *v, const float *pixels, int n_images
     if (!forward(v, v->px, n_images, v->out, tap ? &t : nullptr)) return false;
     TCG_CUDA(cudaMemcpyAsync(out, v->out, (size_t)n_images * v->d_out * sizeof(float), cudaMemcpyDeviceToHost, s));
     TCG_CUDA(cudaStreamSynchronize(s));
+    return true;
+}
+
+bool tcg_vit_submit(tcg_vit_t *v, const float *pixels, int n_images, float *out, int *ticket)
+{
+    if (!need_ctx()) return false;
+    if (!v) return fail("tcg_vit_submit: null model");
+    if (n_images <= 0 || n_images > v->max_batch)
+        return fail("tcg_vit_submit: batch of %d outside 1..max_batch %d", n_images, v->max_batch);
+    if (ctx().device != v->device) return fail("model lives on device %d, thread uses %d", v->device, ctx().device);
+    const size_t px_bytes = (size_t)v->max_batch * 3 * v->S * v->S * sizeof(float);
+    if (!v->copy_stream) {      // first submission: the second pixel slot and the copy stream
+        TCG_CUDA(cudaStreamCreateWithFlags(&v->copy_stream, cudaStreamNonBlocking));
+        for (int i = 0; i < 2; i++) {
+            TCG_CUDA(cudaEventCreateWithFlags(&v->copied[i], cudaEventDisableTiming));
+            TCG_CUDA(cudaEventCreateWithFlags(&v->done[i], cudaEventDisableTiming));
+        }
+        v->px_slot[0] = v->px;
+        TCG_CUDA(cudaMalloc(&v->px_slot[1], px_bytes));
+    }
+    const int slot = v->next_ticket & 1;
+    if (v->in_flight[slot]) {   // the submission two back used this slot: let it finish
+        TCG_CUDA(cudaEventSynchronize(v->done[slot]));
+        v->in_flight[slot] = false;
+    }
+    cudaStream_t s = ctx().cur;
+    const size_t bytes = (size_t)n_images * 3 * v->S * v->S * sizeof(float);
+    TCG_CUDA(cudaMemcpyAsync(v->px_slot[slot], pixels, bytes, cudaMemcpyHostToDevice, v->copy_stream));
+    TCG_CUDA(cudaEventRecord(v->copied[slot], v->copy_stream));
+    TCG_CUDA(cudaStreamWaitEvent(s, v->copied[slot], 0));
+    if (!forward(v, v->px_slot[slot], n_images, v->out, nullptr)) return false;
+    TCG_CUDA(cudaMemcpyAsync(out, v->out, (size_t)n_images * v->d_out * sizeof(float), cudaMemcpyDeviceToHost, s));
+    TCG_CUDA(cudaEventRecord(v->done[slot], s));
+    v->in_flight[slot] = true;
+    if (ticket) *ticket = v->next_ticket;
+    v->next_ticket++;
+    return true;
+}
+
+bool tcg_vit_wait(tcg_vit_t *v, int ticket)
+{
+    if (!need_ctx()) return false;
+    if (!v || ticket < 0 || ticket >= v->next_ticket) return fail("tcg_vit_wait: no such submission");
+    const int slot = ticket & 1;
+    if (!v->in_flight[slot]) return true;
+    TCG_CUDA(cudaEventSynchronize(v->done[slot]));      // this ticket or the newer one in its slot
+    if (ticket == v->next_ticket - 1 || ticket == v->next_ticket - 2) v->in_flight[slot] = false;
     return true;
 }
 

@@ -154,6 +154,8 @@ _SIGS = [
     ("tcg_vit_use_graphs", None, [vp, boolean]),
     ("tcg_vit_encode_batch", boolean, [vp, vp, i32, vp, vp, vp]),
     ("tcg_vit_encode_device", boolean, [vp, vp, i32, vp]),
+    ("tcg_vit_submit", boolean, [vp, vp, i32, vp, C.POINTER(C.c_int)]),
+    ("tcg_vit_wait", boolean, [vp, i32]),
     ("tcg_vit_launches_per_forward", i32, [vp]), ("tcg_vit_profile_begin", None, []),
     ("tcg_vit_profile_end", boolean, [C.POINTER(C.c_float), C.POINTER(C.c_int)]),
     ("tcg_nccl_unique_id", boolean, [C.c_char_p]),

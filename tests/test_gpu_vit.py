@@ -113,6 +113,40 @@ def test_batch_invariance_and_graph_replay(gpu, cache_dir):
         m.close()
 
 
+def test_async_submit_matches_blocking(gpu, cache_dir):
+    import ctypes
+    L = tcg.lib()
+    path, cfg = model(cache_dir, "vit-b32", n_layer=2)
+    m = tcg.VitModel(path)
+    bufs = []
+    try:
+        m.upload(4)
+        batches = [G.make_pixels(n, cfg["image"], 20 + i) for i, n in enumerate((4, 3, 4, 2))]
+        want = [m.encode(b)[0] for b in batches]
+        ins = [tcg.HostBuffer(b.shape) for b in batches]
+        outs = [tcg.HostBuffer((b.shape[0], cfg["d_out"])) for b in batches]
+        bufs = ins + outs
+        tickets = []
+        for hb, ob, b in zip(ins, outs, batches):       # the third submission waits for the first
+            hb.array[...] = b
+            t = ctypes.c_int(-1)
+            tcg.check(L.tcg_vit_submit(m.dev, hb.ptr, b.shape[0], ob.ptr, ctypes.byref(t)), "submit")
+            tickets.append(t.value)
+        assert tickets == sorted(tickets) and len(set(tickets)) == 4
+        for t in reversed(tickets):
+            tcg.check(L.tcg_vit_wait(m.dev, t), "wait")
+        for ob, w in zip(outs, want):
+            assert np.array_equal(ob.array, w)
+        again, _ = m.encode(batches[0])                 # a blocking call after the async ones
+        assert np.array_equal(again, want[0])
+        assert not L.tcg_vit_submit(m.dev, ins[0].ptr, 5, outs[0].ptr, None)     # > max_batch
+        assert not L.tcg_vit_wait(m.dev, 99)
+    finally:
+        for b in bufs:
+            b.close()
+        m.close()
+
+
 def test_quick_gelu_model(gpu, tmp_path):
     cfg = G.vit_config("vit-b32", n_layer=1)
     w = G.make_vit_weights(cfg, 3)
