@@ -9,11 +9,13 @@
 // Accuracy. The tensor core's own fp32 accumulation truncates, and that
 // error grows linearly with the number of MMAs folded into one accumulator
 // (measured: ~1.7e-5 of max|C| at K=1024 when a whole K loop accumulates in
-// TMEM). So the K loop is cut into chunks of 32: each chunk accumulates in
-// a fresh TMEM buffer (two, ping-pong), and the epilogue warps fold every
-// chunk into fp32 registers with round-to-nearest adds while the MMAs of the
-// next chunk run. Per product the error is then a few fp32 ulps of the
-// result, like a sequential fp32 dot product.
+// TMEM). So the large hi*hi term accumulates per K chunk (256 by default,
+// tcg_gemm_set_chunk_k) in a fresh TMEM buffer (two, ping-pong), and the
+// epilogue warps fold every chunk into fp32 registers with round-to-nearest
+// adds while the MMAs of the next chunk run. The two small correction terms
+// (lo*hi, hi*lo; ~2^-11 of the result) accumulate over the whole tile in their
+// own TMEM buffers, where truncation costs nothing measurable. Per product
+// the error is a few fp32 ulps of the result, like a sequential fp32 dot.
 //
 // Persistent, warp-specialised CTA (one per SM, 320 threads):
 //   warp 0     one lane issues the TMA loads of a (A_hi, A_lo, B_hi, B_lo)
@@ -25,8 +27,12 @@
 //              each chunk into registers and, after the last chunk of a tile,
 //              apply bias / position / GELU / residual, split hi/lo and store.
 // Operand tiles are K-major with the TMA swizzle that matches the UMMA
-// descriptor (BK*4 bytes: 128B for BK=32, 64B for BK=16). No TMA load uses
-// cluster features: each CTA loads its own tiles.
+// descriptor (BK*4 bytes: 128B for BK=32, 64B for BK=16).
+// gemm_tf32x3_pair_kernel is the CTA-pair variant (cta_group::2, M=256 per
+// cluster of two): each CTA loads its own A rows and half of the B tile with
+// plain (unicast) TMA loads; only the MMA completion commit signals both CTAs.
+// It is correct but measured no faster than the one-CTA kernel on the ViT
+// shapes, so the automatic choice never picks it.
 // Every mbarrier wait is bounded (globaltimer); a wait that gives up sets a
 // CTA-wide abort flag and the library's device error word, the roles wind
 // down, in-flight copies and MMAs are drained, and TMEM is freed.
@@ -148,6 +154,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
                  : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16])
+{
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32"
+                 " {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+                 "tcgen05.wait::ld.sync.aligned;"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+                 : "r"(taddr)
+                 : "memory");
+}
+
 // 64 columns in one load, one wait.
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64])
 {
@@ -235,7 +252,7 @@ struct Shape {
     static constexpr int HALF = BN / 2;               // columns per epilogue thread
     static constexpr int NBAR = 2 * STAGES + 8 + 1;
     static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 8 * NBAR + 16;
-    static_assert(HALF % 32 == 0, "each epilogue warpgroup drains whole 32-column slices");
+    static_assert(HALF % 16 == 0, "each epilogue warpgroup drains whole 16-column slices");
     static_assert(4 * BN <= 512, "four accumulators must fit the 512 TMEM columns");
 };
 
@@ -252,12 +269,20 @@ __device__ __forceinline__ void drain_add(uint32_t taddr, float (&acc)[HALF])
 #pragma unroll
         for (int i = 0; i < 64; i++) acc[j + i] = __fadd_rn(acc[j + i], __uint_as_float(r[i]));
     }
+    constexpr int W32 = W64 + (HALF - W64) / 32 * 32;
 #pragma unroll
-    for (int j = W64; j < HALF; j += 32) {
+    for (int j = W64; j < W32; j += 32) {
         uint32_t r[32];
         tmem_ld32(taddr + (uint32_t)j, r);
 #pragma unroll
         for (int i = 0; i < 32; i++) acc[j + i] = __fadd_rn(acc[j + i], __uint_as_float(r[i]));
+    }
+#pragma unroll
+    for (int j = W32; j < HALF; j += 16) {
+        uint32_t r[16];
+        tmem_ld16(taddr + (uint32_t)j, r);
+#pragma unroll
+        for (int i = 0; i < 16; i++) acc[j + i] = __fadd_rn(acc[j + i], __uint_as_float(r[i]));
     }
 }
 
@@ -443,6 +468,264 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
     }
 }
 
+// ------------------------------------------------------- CTA-pair variant
+// The same GEMM on pairs of CTAs (a cluster of 2, tcgen05 cta_group::2):
+// one 256 x 128 tile per pair, CTA r owning rows 128r..128r+127 of it. Each
+// CTA loads its own 128 rows of A and half of B (64 of the 128 columns), so a
+// stage is 48 KB instead of 64 KB and the ring is 4 deep. The even CTA is the
+// leader: its producer arms the stage barrier with the bytes of both CTAs,
+// both CTAs' TMA loads complete on that barrier, and one lane of the leader
+// issues the M=256 MMAs, committing to both CTAs' barriers at once. Each CTA
+// drains its own 128 TMEM lanes; the drains are acknowledged to the leader.
+
+__device__ __forceinline__ uint32_t cta_rank_in_cluster()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// address of the same shared-memory offset in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t peer_addr(uint32_t addr, uint32_t rank)
+{
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void bar_arrive_cluster(uint32_t cluster_addr)
+{
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void cluster_sync()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// TMA load into this CTA's shared memory whose bytes complete on the
+// leader's barrier (cluster address).
+__device__ __forceinline__ void tma_load_pair(uint32_t dst, const CUtensorMap *map, uint32_t bar_cluster, int x, int y)
+{
+    asm volatile("cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%2, %3}], [%4];"
+                 ::"r"(dst), "l"((unsigned long long)map), "r"(x), "r"(y), "r"(bar_cluster) : "memory");
+}
+__device__ __forceinline__ void mma_tf32_pair(uint32_t d, unsigned long long a, unsigned long long b, uint32_t id, uint32_t acc)
+{
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+                 ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc));
+}
+// commit the leader's MMAs to the barrier at this offset in both CTAs
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+                 ::"r"(bar), "h"((unsigned short)3) : "memory");
+}
+// commit the leader's MMAs to one of its own barriers
+__device__ __forceinline__ void mma_commit_pair_local(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+template <int STAGES>
+struct PairShape {
+    static constexpr int BN = 128;                        // tile columns (both CTAs)
+    static constexpr uint32_t A_BYTES = BM * 32 * 4;      // this CTA's 128 rows, BK = 32
+    static constexpr uint32_t B_BYTES = (BN / 2) * 32 * 4; // this CTA's 64 columns
+    static constexpr uint32_t STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+    static constexpr uint32_t TMEM_COLS = 512;
+    static constexpr int HALF = BN / 2;
+    static constexpr int NBAR = 2 * STAGES + 8 + 1;
+    static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 8 * NBAR + 16;
+};
+
+template <int STAGES>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
+                        const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
+                        int M, int N, int K, int chunk_kb, GemmEpi epi, int *err)
+{
+    using S = PairShape<STAGES>;
+    constexpr int BN = S::BN, BK = 32, SWB = 128;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *tiles = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t *bars = (uint64_t *)(tiles + (size_t)STAGES * S::STAGE_BYTES);
+    uint32_t *tmem_slot = (uint32_t *)(bars + S::NBAR);
+    volatile int *abort = (volatile int *)(tmem_slot + 1);
+
+    const uint32_t rank = cta_rank_in_cluster();
+    const bool leader = rank == 0;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const int n_tiles = (N + BN - 1) / BN;
+    const int num_tiles = ((M + 2 * BM - 1) / (2 * BM)) * n_tiles;
+    const int num_kb = (K + BK - 1) / BK;
+    const int n_chunks = (num_kb + chunk_kb - 1) / chunk_kb;
+    const uint32_t full0 = su32(bars), empty0 = su32(bars + STAGES);
+    const uint32_t cfull0 = su32(bars + 2 * STAGES), cempty0 = cfull0 + 16;
+    const uint32_t sfull0 = cempty0 + 16, sempty0 = sfull0 + 16, drain = sempty0 + 16;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            bar_init(full0 + 8 * s, 1);
+            bar_init(empty0 + 8 * s, 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            bar_init(cfull0 + 8 * b, 1);
+            bar_init(cempty0 + 8 * b, 2 * EPI_WARPS);    // epilogue warps of both CTAs
+            bar_init(sfull0 + 8 * b, 1);
+            bar_init(sempty0 + 8 * b, 2 * EPI_WARPS);
+        }
+        bar_init(drain, 1);
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(su32(tmem_slot)), "r"(S::TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    fence_before();
+    cluster_sync();          // barriers initialised and TMEM allocated in both CTAs
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&a_hi) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&a_lo) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&b_hi) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&b_lo) : "memory");
+            int stage = 0;
+            uint32_t phase = 0;
+            long issued = 0;
+            bool ok = true;
+            for (int t = pair; ok && t < num_tiles; t += npairs) {
+                const int m0 = (t / n_tiles) * 2 * BM + (int)rank * BM;
+                const int nb = (t % n_tiles) * BN + (int)rank * (BN / 2);
+                for (int kb = 0; kb < num_kb; kb++) {
+                    if (!bar_wait(empty0 + 8 * stage, phase ^ 1, abort, err, 1)) { ok = false; break; }
+                    const uint32_t fb = peer_addr(full0 + 8 * stage, 0);
+                    const uint32_t base = su32(tiles + (size_t)stage * S::STAGE_BYTES);
+                    if (leader) bar_expect_tx(full0 + 8 * stage, 2 * S::STAGE_BYTES);
+                    tma_load_pair(base, &a_hi, fb, kb * BK, m0);
+                    tma_load_pair(base + S::A_BYTES, &a_lo, fb, kb * BK, m0);
+                    tma_load_pair(base + 2 * S::A_BYTES, &b_hi, fb, kb * BK, nb);
+                    tma_load_pair(base + 2 * S::A_BYTES + S::B_BYTES, &b_lo, fb, kb * BK, nb);
+                    issued++;
+                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                }
+            }
+            // The leader lets the last fill of every stage land before exiting;
+            // the follower's copies complete on that same barrier.
+            if (leader)
+                for (int i = 1; i <= STAGES && i <= issued; i++) {
+                    int s = stage - i;
+                    uint32_t ph = phase;
+                    if (s < 0) { s += STAGES; ph ^= 1; }
+                    bar_wait(full0 + 8 * s, ph, abort, err, 2, false);
+                }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (leader && lane == 0) {
+            const uint32_t id = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                ((uint32_t)((2 * BM) >> 4) << 24);
+            int stage = 0;
+            uint32_t phase = 0, chunk = 0;
+            bool ok = true;
+            int local = 0;
+            for (int t = pair; ok && t < num_tiles; t += npairs, local++) {
+                const uint32_t ts = local & 1;
+                if (!bar_wait(sempty0 + 8 * ts, ((local >> 1) & 1) ^ 1, abort, err, 3)) break;
+                fence_after();
+                const uint32_t ds = tmem + (2 + ts) * (uint32_t)BN;
+                for (int c = 0; ok && c < n_chunks; c++, chunk++) {
+                    const uint32_t b = chunk & 1;
+                    if (!bar_wait(cempty0 + 8 * b, ((chunk >> 1) & 1) ^ 1, abort, err, 3)) { ok = false; break; }
+                    fence_after();
+                    const uint32_t db = tmem + b * (uint32_t)BN;
+                    const int kb0 = c * chunk_kb, kb1 = min(kb0 + chunk_kb, num_kb);
+                    for (int kb = kb0; kb < kb1; kb++) {
+                        if (!bar_wait(full0 + 8 * stage, phase, abort, err, 4)) { ok = false; break; }
+                        fence_after();
+                        const uint32_t base = su32(tiles + (size_t)stage * S::STAGE_BYTES);
+#pragma unroll
+                        for (int k = 0; k < BK / 8; k++) {
+                            const uint32_t off = (uint32_t)k * 32u;
+                            const unsigned long long ah = sdesc<SWB>(base + off);
+                            const unsigned long long al = sdesc<SWB>(base + S::A_BYTES + off);
+                            const unsigned long long bh = sdesc<SWB>(base + 2 * S::A_BYTES + off);
+                            const unsigned long long bl = sdesc<SWB>(base + 2 * S::A_BYTES + S::B_BYTES + off);
+                            mma_tf32_pair(db, ah, bh, id, (kb > kb0 || k > 0) ? 1u : 0u);
+                            mma_tf32_pair(ds, al, bh, id, (kb > 0 || k > 0) ? 1u : 0u);
+                            mma_tf32_pair(ds, ah, bl, id, 1u);
+                        }
+                        mma_commit_pair(empty0 + 8 * stage);
+                        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                    }
+                    if (ok) mma_commit_pair(cfull0 + 8 * b);
+                }
+                if (ok) mma_commit_pair(sfull0 + 8 * ts);
+            }
+            // Every MMA issued above has retired once this barrier flips.
+            mma_commit_pair_local(drain);
+            bar_wait(drain, 0, abort, err, 5, false);
+        }
+        __syncwarp();
+    } else {
+        const int q = warp & 3;
+        const int h = (warp - 2) >> 2;
+        const uint32_t lane_cols = ((uint32_t)(q * 32) << 16) + (uint32_t)(h * S::HALF);
+        const uint32_t cempty_l = peer_addr(cempty0, 0), sempty_l = peer_addr(sempty0, 0);
+        uint32_t chunk = 0;
+        bool ok = true;
+        int local = 0;
+        for (int t = pair; ok && t < num_tiles; t += npairs, local++) {
+            float acc[S::HALF];
+#pragma unroll
+            for (int j = 0; j < S::HALF; j++) acc[j] = 0.0f;
+            for (int c = 0; c < n_chunks; c++, chunk++) {
+                const uint32_t b = chunk & 1;
+                if (!bar_wait(cfull0 + 8 * b, (chunk >> 1) & 1, abort, err, 6)) { ok = false; break; }
+                fence_after();
+                drain_add<S::HALF>(tmem + lane_cols + b * (uint32_t)BN, acc);
+                fence_before();
+                __syncwarp();
+                if (lane == 0) bar_arrive_cluster(cempty_l + 8 * b);
+            }
+            if (!ok) break;
+            const uint32_t ts = local & 1;
+            if (!bar_wait(sfull0 + 8 * ts, (local >> 1) & 1, abort, err, 7)) break;
+            fence_after();
+            drain_add<S::HALF>(tmem + lane_cols + (2 + ts) * (uint32_t)BN, acc);
+            fence_before();
+            __syncwarp();
+            if (lane == 0) bar_arrive_cluster(sempty_l + 8 * ts);
+
+            const int m0 = (t / n_tiles) * 2 * BM + (int)rank * BM, n0 = (t % n_tiles) * BN;
+            const int r = m0 + q * 32 + lane;
+            if (r < M) {
+                const int src_row = r % epi.rgroup + epi.roff;
+                const size_t dst_row = (size_t)(r / epi.rgroup) * epi.rstride + epi.roff + r % epi.rgroup;
+                const int nb = n0 + h * S::HALF;
+#pragma unroll
+                for (int j = 0; j < S::HALF; j += 4) {
+                    const int n = nb + j;
+                    if (n < N)
+                        epi_store4(epi, src_row, dst_row, n, min(4, N - n), acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+                }
+            }
+        }
+    }
+
+    fence_before();
+    __syncthreads();
+    cluster_sync();          // the leader's MMAs into this CTA's TMEM are done
+    if (warp == 1) {
+        fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(S::TMEM_COLS) : "memory");
+    }
+}
+
 // ------------------------------------------------------------------ host
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -488,11 +771,14 @@ struct Cfg {
     int bn, bk, stages;
     size_t smem;
     const void *fn;
+    bool pair;          // CTA-pair kernel: 256-row tiles, B boxes of bn/2 rows
 };
 
-#define TCG_CFG(BN, BK, ST) { BN, BK, ST, Shape<BN, BK, ST>::SMEM, (const void *)gemm_tf32x3_kernel<BN, BK, ST> }
+#define TCG_CFG(BN, BK, ST) { BN, BK, ST, Shape<BN, BK, ST>::SMEM, (const void *)gemm_tf32x3_kernel<BN, BK, ST>, false }
 const Cfg CFGS[] = {
     TCG_CFG(128, 32, 3), TCG_CFG(64, 32, 4), TCG_CFG(128, 16, 6), TCG_CFG(64, 16, 8),
+    TCG_CFG(96, 32, 4), TCG_CFG(96, 16, 7),
+    { 128, 32, 4, PairShape<4>::SMEM, (const void *)gemm_tf32x3_pair_kernel<4>, true },
 };
 #undef TCG_CFG
 constexpr int NCFG = sizeof(CFGS) / sizeof(CFGS[0]);
@@ -501,10 +787,13 @@ int choose_cfg(int M, int N)
 {
     // Fewest tile rounds over the SMs, weighted by tile width plus a fixed
     // per-tile cost; ties go to the wider tile (more reuse per byte).
+    // Candidates: the BK=32 shapes 128 and 64 wide (96 measured slower per
+    // tile on every ViT shape, even where it packs the SMs better).
     const int sms = ctx().sms > 0 ? ctx().sms : 148;
+    static const int cand[] = { 0, 1 };
     int best = 0;
     long best_cost = -1;
-    for (int i = 0; i < 2; i++) {
+    for (int i : cand) {
         const long tiles = (long)((M + BM - 1) / BM) * ((N + CFGS[i].bn - 1) / CFGS[i].bn);
         const long rounds = (tiles + sms - 1) / sms;
         const long cost = rounds * (CFGS[i].bn + 32);
@@ -528,17 +817,43 @@ bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b
     const int cfg = force_cfg >= 0 ? force_cfg : choose_cfg(M, N);
     if (cfg >= NCFG) return fail("gemm_plan: no configuration %d", cfg);
     const Cfg &c = CFGS[cfg];
+    const int b_rows = c.pair ? c.bn / 2 : c.bn;         // B box: this CTA's share of the tile columns
     if (!encode_kmajor(&p.a_hi, a_hi, M, K, BM, c.bk) || !encode_kmajor(&p.a_lo, a_lo, M, K, BM, c.bk) ||
-        !encode_kmajor(&p.b_hi, b_hi, N, K, c.bn, c.bk) || !encode_kmajor(&p.b_lo, b_lo, N, K, c.bn, c.bk))
+        !encode_kmajor(&p.b_hi, b_hi, N, K, b_rows, c.bk) || !encode_kmajor(&p.b_lo, b_lo, N, K, b_rows, c.bk))
         return false;
     p.M = M;
     p.N = N;
     p.K = K;
     p.cfg = cfg;
     p.epi = epi;
-    const int tiles = ((M + BM - 1) / BM) * ((N + c.bn - 1) / c.bn);
     const int sms = ctx().sms > 0 ? ctx().sms : 148;
-    p.grid = tiles < sms ? tiles : sms;
+    if (c.pair) {           // one cluster of two CTAs per 256-row tile, as many as fit at once
+        static int max_clusters[64];
+        const int dev = ctx().device & 63;
+        if (!max_clusters[dev]) {
+            int n = 0;
+            cudaLaunchConfig_t lc = {};
+            cudaLaunchAttribute at;
+            at.id = cudaLaunchAttributeClusterDimension;
+            at.val.clusterDim.x = 2; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
+            lc.gridDim = dim3(2);
+            lc.blockDim = dim3(NUM_THREADS);
+            lc.dynamicSmemBytes = c.smem;
+            lc.attrs = &at;
+            lc.numAttrs = 1;
+            if (cudaFuncSetAttribute(c.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem) != cudaSuccess ||
+                cudaOccupancyMaxActiveClusters(&n, c.fn, &lc) != cudaSuccess || n < 1) {
+                cudaGetLastError();
+                n = sms / 2;
+            }
+            max_clusters[dev] = n < sms / 2 ? n : sms / 2;
+        }
+        const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + c.bn - 1) / c.bn);
+        p.grid = 2 * (tiles < max_clusters[dev] ? tiles : max_clusters[dev]);
+    } else {
+        const int tiles = ((M + BM - 1) / BM) * ((N + c.bn - 1) / c.bn);
+        p.grid = tiles < sms ? tiles : sms;
+    }
     return true;
 }
 
