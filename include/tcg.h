@@ -46,7 +46,9 @@ void *tcg_get_stream(void);                 /* cudaStream_t                  */
 bool  tcg_set_stream(void *stream);         /* NULL: back to the library's   */
 
 /* Device-side failure flag shared by every kernel that waits on a barrier:
- * non-zero after a bounded wait gave up. Reading it synchronizes. */
+ * non-zero after a bounded wait gave up. Reading it synchronizes. Clearing it
+ * also resets the op API's GEMM stream-K flags; a ViT model (tcg_vit_*) that
+ * saw a device error is released and uploaded again. */
 int   tcg_device_error(void);
 bool  tcg_clear_device_error(void);
 

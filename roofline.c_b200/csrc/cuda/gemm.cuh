@@ -23,7 +23,25 @@ struct GemmEpi {
     int act = 0;
     OutSpec out;
     int rgroup = 1 << 30, rstride = 0, roff = 0;
+    // set by gemm_plan: N, every leading dimension a multiple of 4 and every
+    // pointer 16-byte aligned, so the epilogue may move float4s
+    bool vec = false;
 };
+
+// Device memory for the stream-K split of a GEMM's last, partial wave of
+// tiles: one partial accumulator tile (128 x 256 fp32 at most) per CTA and one
+// flag per epilogue warp of each CTA. The flags are zero between launches
+// (each owner clears what it consumed), so a GemmWork serves any number of
+// GEMMs that run one after another on one stream, never two at once.
+struct GemmWork {
+    float *ws = nullptr;
+    int *flags = nullptr;
+    int ctas = 0;        // CTAs it has room for
+};
+size_t gemm_work_ws_floats(int ctas);
+size_t gemm_work_flag_count(int ctas);
+GemmWork *ctx_gemm_work();                         // the context's own, allocated on first use
+bool gemm_work_reset(const GemmWork &w, cudaStream_t s);   // zero the flags after an aborted launch
 
 // One GEMM: C[M,N] = A[M,K] * B[N,K]^T with both operands given as tf32
 // hi/lo pairs, row-major with row stride K. Tensor maps are encoded once.
@@ -33,11 +51,18 @@ struct GemmPlan {
     int cfg = -1;        // kernel configuration index
     int grid = 0;
     GemmEpi epi;
+    GemmWork work;       // stream-K memory (null: every tile whole)
+    int sk = 0;          // 1: the last partial wave of tiles is split by K chunks
 };
 
+// work: memory for stream-K; without it every tile is computed whole.
 bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo,
-               int M, int N, int K, const GemmEpi &epi, int force_cfg = -1);
+               int M, int N, int K, const GemmEpi &epi, int force_cfg = -1, const GemmWork *work = nullptr);
 bool gemm_run(const GemmPlan &p, cudaStream_t s, int *err);
+
+// The configuration for throughput (the ViT forward): folded small terms,
+// stream-K capable; the automatic choice (force_cfg -1) is the accurate one.
+int gemm_throughput_cfg();
 
 // Tile widths available (index = cfg); for tests and tuning.
 int gemm_num_cfgs();

@@ -241,27 +241,128 @@ __device__ __forceinline__ void epi_store4(const GemmEpi &e, int src_row, size_t
     }
 }
 
-template <int BN, int BK, int STAGES>
+// EPI_W epilogue warps (8 or 16): warp w drains TMEM lane quarter w & 3 and
+// column group (w - 2) / 4 of the tile. SEP: the small lo*hi + hi*lo terms
+// have their own per-tile TMEM buffers (two chunk and two tile accumulators
+// of BN columns); without it they fold into the chunk buffers with the hi*hi
+// term, and the 512 TMEM columns hold as many chunk buffers as fit (four at
+// BN = 128, two at BN = 256) at the price of three MMAs per K-step truncating
+// into each chunk instead of one.
+template <int BN, int BK, int STAGES, int EPI_W = 8, bool SEP = true>
 struct Shape {
     static constexpr uint32_t A_BYTES = BM * BK * 4;
     static constexpr uint32_t B_BYTES = BN * BK * 4;
     static constexpr uint32_t STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
-    // TMEM: two chunk buffers for the hi*hi term and two tile buffers for the
-    // small lo*hi + hi*lo terms, BN columns each.
-    static constexpr uint32_t TMEM_COLS = 4 * BN <= 256 ? 256 : 512;
-    static constexpr int HALF = BN / 2;               // columns per epilogue thread
-    static constexpr int NBAR = 2 * STAGES + 8 + 1;
-    static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 8 * NBAR + 16;
-    static_assert(HALF % 16 == 0, "each epilogue warpgroup drains whole 16-column slices");
-    static_assert(4 * BN <= 512, "four accumulators must fit the 512 TMEM columns");
+    static constexpr int NBUF = SEP ? 2 : (4 * BN <= 512 ? 4 : 2);   // chunk buffers
+    static constexpr int NACC = SEP ? 4 : NBUF;
+    static constexpr uint32_t TMEM_COLS = NACC * BN <= 256 ? 256 : 512;
+    static constexpr int GROUPS = EPI_W / 4;
+    static constexpr int HALF = BN / GROUPS;           // columns per epilogue thread
+    static constexpr int THREADS = 64 + 32 * EPI_W;
+    static constexpr int LDW = EPI_W > 8 ? 16 : 64;    // widest TMEM load of the drain
+    static constexpr uint32_t EPI_STAGE_BYTES = 32 * 16 * 4;   // per epilogue warp: 32 rows x 16 columns
+    static constexpr int NBAR = 2 * STAGES + 2 * NBUF + 4 + 1;
+    static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + EPI_W * EPI_STAGE_BYTES + 8 * NBAR + 16;
+    static_assert(EPI_W == 8 || EPI_W == 16, "two or four epilogue warps per TMEM lane quarter");
+    static_assert(HALF % 16 == 0, "each epilogue warp drains whole 16-column slices");
+    static_assert(NACC * BN <= 512, "the accumulators must fit the 512 TMEM columns");
+    static_assert(SMEM <= 232448, "shared memory per block");
 };
 
-// acc[0..HALF) += the HALF fp32 columns at TMEM address taddr (this warp's
-// lanes), in 64-column loads where possible.
+__device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+
+// Stores this warp's 32 tile rows x HALF columns (acc: lane = row) through a
+// 32 x 16 shared-memory slice, so that the global stores and the bias,
+// position and residual loads are row-contiguous (four lanes per 16 columns
+// of a row) instead of one row per lane. The slice's float4 chunks are
+// XOR-swizzled by (row >> 1) & 3, which keeps both the row-wise writes and the
+// column-wise reads free of bank conflicts. Every load of a slice is issued
+// before its first store (the residual may be the output itself, so the
+// compiler could not reorder them).
 template <int HALF>
+__device__ __forceinline__ void epi_store_tile(const GemmEpi &e, const float (&acc)[HALF], float *stage, int row0,
+                                               int n0, int M, int N)
+{
+    constexpr int NS = HALF / 16;
+    const int lane = threadIdx.x & 31;
+    const int c = lane & 3;
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    int src_row[4];
+    size_t dst_row[4];
+    bool row_ok[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int r = row0 + i * 8 + (lane >> 2);
+        row_ok[i] = r < M;
+        src_row[i] = r % e.rgroup + e.roff;
+        dst_row[i] = (size_t)(r / e.rgroup) * e.rstride + e.roff + r % e.rgroup;
+    }
+#pragma unroll
+    for (int s = 0; s < NS; s++) {
+        const int j = 16 * s;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int pc = k ^ ((lane >> 1) & 3);
+            *reinterpret_cast<float4 *>(stage + lane * 16 + pc * 4) =
+                make_float4(acc[j + 4 * k], acc[j + 4 * k + 1], acc[j + 4 * k + 2], acc[j + 4 * k + 3]);
+        }
+        __syncwarp();
+        float4 v[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int rr = i * 8 + (lane >> 2);
+            v[i] = *reinterpret_cast<const float4 *>(stage + rr * 16 + (c ^ ((rr >> 1) & 3)) * 4);
+        }
+        __syncwarp();
+        const int n = n0 + j + 4 * c;
+        if (n >= N) continue;
+        if (!e.vec) {
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                if (row_ok[i]) epi_store4(e, src_row[i], dst_row[i], n, min(4, N - n), v[i].x, v[i].y, v[i].z, v[i].w);
+            continue;
+        }
+        // the one extra operand of a row: its residual, or else its position row
+        const float4 b4 = e.bias ? ld4(e.bias + n) : zero;
+        float4 ex[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            ex[i] = !row_ok[i] ? zero
+                  : e.residual ? ld4(e.residual + dst_row[i] * (size_t)e.out.ld + n)
+                  : e.rowadd   ? ld4(e.rowadd + (size_t)src_row[i] * e.ld_rowadd + n) : zero;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            if (!row_ok[i]) continue;
+            float x[4] = { v[i].x, v[i].y, v[i].z, v[i].w };
+            const float bb[4] = { b4.x, b4.y, b4.z, b4.w };
+            const float xx[4] = { ex[i].x, ex[i].y, ex[i].z, ex[i].w };
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                if (e.bias) x[k] = __fadd_rn(x[k], bb[k]);
+                if (e.rowadd) x[k] = __fadd_rn(x[k], xx[k]);
+                if (e.act == 1) x[k] = gelu_exact(x[k]);
+                else if (e.act == 2) x[k] = gelu_quick(x[k]);
+                if (e.residual) x[k] = __fadd_rn(xx[k], x[k]);
+            }
+            const size_t o = dst_row[i] * (size_t)e.out.ld + n;
+            if (e.out.plain) *reinterpret_cast<float4 *>(e.out.plain + o) = make_float4(x[0], x[1], x[2], x[3]);
+            if (e.out.hi) {
+                float h[4], l[4];
+#pragma unroll
+                for (int k = 0; k < 4; k++) split_tf32(x[k], h[k], l[k]);
+                *reinterpret_cast<float4 *>(e.out.hi + o) = make_float4(h[0], h[1], h[2], h[3]);
+                *reinterpret_cast<float4 *>(e.out.lo + o) = make_float4(l[0], l[1], l[2], l[3]);
+            }
+        }
+    }
+}
+
+// acc[0..HALF) += the HALF fp32 columns at TMEM address taddr (this warp's
+// lanes), in loads of at most LDW columns.
+template <int HALF, int LDW = 64>
 __device__ __forceinline__ void drain_add(uint32_t taddr, float (&acc)[HALF])
 {
-    constexpr int W64 = HALF / 64 * 64;
+    constexpr int W64 = LDW >= 64 ? HALF / 64 * 64 : 0;
 #pragma unroll
     for (int j = 0; j < W64; j += 64) {
         uint32_t r[64];
@@ -286,19 +387,95 @@ __device__ __forceinline__ void drain_add(uint32_t taddr, float (&acc)[HALF])
     }
 }
 
+// Work order of one CTA of a persistent GEMM launch (P = gridDim.x CTAs).
+// Whole tiles: blockIdx.x, + P, + 2P, ... With stream-K (sk), only the
+// R = num_tiles / P full waves run that way; the L = num_tiles % P tiles of the
+// last wave become L * C chunk units (C = K chunks per tile) dealt out in
+// contiguous, equal ranges [first(p), first(p + 1)), so no SM idles through a
+// partial wave. A tile cut by a range boundary is finished by its owner, the
+// CTA holding its chunk 0: the later CTAs (contributors) hand their partial
+// sums over through global memory. A contributor segment is always the first
+// of its CTA's stream-K range and never waits; an owner segment is always the
+// last, and waits only for contributor segments, so no wait can be circular.
+struct Seg {
+    int tile, c0, c1;    // chunks [c0, c1) of tile
+};
+
+struct Sched {
+    int C, P, p, num_tiles, R, i = 0;
+    long long u = 0, ue = 0, LC = 0;
+    __device__ Sched(int num_tiles_, int C_, bool sk) : C(C_), P(gridDim.x), p(blockIdx.x), num_tiles(num_tiles_)
+    {
+        if (sk) {
+            R = num_tiles / P;
+            LC = (long long)(num_tiles % P) * C;
+            u = first(p);
+            ue = first(p + 1);
+        } else {
+            R = (num_tiles + P - 1) / P;
+        }
+    }
+    __device__ long long first(int q) const { return LC * q / P; }
+    __device__ bool next(Seg &s)
+    {
+        while (i < R) {
+            const int t = i++ * P + p;
+            if (t < num_tiles) {
+                s.tile = t; s.c0 = 0; s.c1 = C;
+                return true;
+            }
+        }
+        if (u >= ue) return false;
+        s.tile = R * P + (int)(u / C);
+        s.c0 = (int)(u % C);
+        s.c1 = (int)min((long long)C, s.c0 + (ue - u));
+        u += s.c1 - s.c0;
+        return true;
+    }
+};
+
+__device__ __forceinline__ void st_release(int *f, int v)
+{
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire(const int *f)
+{
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+    return v;
+}
+
+// Wait (bounded, like bar_wait) until a contributor has raised flag f.
+__device__ bool flag_wait(const int *f, volatile int *abort, int *err, int code)
+{
+    const unsigned long long t0 = now_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (ld_acquire(f) != 0) return true;
+        if ((it & 63) == 0) {
+            if (*abort) return false;
+            if (now_ns() - t0 > WAIT_NS) {
+                *abort = 1;
+                atomicExch(err, code);
+                return false;
+            }
+        }
+    }
+}
+
 // chunk_kb: K-blocks whose hi*hi products share one TMEM chunk buffer before
 // it is drained into the fp32 registers.
-template <int BN, int BK, int STAGES>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+template <int BN, int BK, int STAGES, int EPI_W, bool SEP>
+__global__ void __launch_bounds__(Shape<BN, BK, STAGES, EPI_W, SEP>::THREADS, 1)
 gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
                    const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
-                   int M, int N, int K, int chunk_kb, GemmEpi epi, int *err)
+                   int M, int N, int K, int chunk_kb, GemmEpi epi, int *err, float *ws, int *flags, int sk)
 {
-    using S = Shape<BN, BK, STAGES>;
+    using S = Shape<BN, BK, STAGES, EPI_W, SEP>;
     constexpr int SWB = BK * 4;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *tiles = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t *bars = (uint64_t *)(tiles + (size_t)STAGES * S::STAGE_BYTES);
+    float *epi_stage = (float *)(tiles + (size_t)STAGES * S::STAGE_BYTES);
+    uint64_t *bars = (uint64_t *)(tiles + (size_t)STAGES * S::STAGE_BYTES + EPI_W * S::EPI_STAGE_BYTES);
     uint32_t *tmem_slot = (uint32_t *)(bars + S::NBAR);
     volatile int *abort = (volatile int *)(tmem_slot + 1);
 
@@ -307,20 +484,24 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
     const int num_tiles = ((M + BM - 1) / BM) * n_tiles;
     const int num_kb = (K + BK - 1) / BK;
     const int n_chunks = (num_kb + chunk_kb - 1) / chunk_kb;
+    const bool skm = !SEP && sk && ws && flags;    // stream-K needs per-chunk partials: fold mode only
     const uint32_t full0 = su32(bars), empty0 = su32(bars + STAGES);
-    const uint32_t cfull0 = su32(bars + 2 * STAGES), cempty0 = cfull0 + 16;
-    const uint32_t sfull0 = cempty0 + 16, sempty0 = sfull0 + 16, drain = sempty0 + 16;
+    constexpr int NBUF = S::NBUF;
+    const uint32_t cfull0 = su32(bars + 2 * STAGES), cempty0 = cfull0 + 8 * NBUF;
+    const uint32_t sfull0 = cempty0 + 8 * NBUF, sempty0 = sfull0 + 16, drain = sempty0 + 16;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
             bar_init(full0 + 8 * s, 1);
             bar_init(empty0 + 8 * s, 1);
         }
-        for (int b = 0; b < 2; b++) {
+        for (int b = 0; b < NBUF; b++) {
             bar_init(cfull0 + 8 * b, 1);
-            bar_init(cempty0 + 8 * b, EPI_WARPS);
+            bar_init(cempty0 + 8 * b, EPI_W);
+        }
+        for (int b = 0; b < 2; b++) {
             bar_init(sfull0 + 8 * b, 1);
-            bar_init(sempty0 + 8 * b, EPI_WARPS);
+            bar_init(sempty0 + 8 * b, EPI_W);
         }
         bar_init(drain, 1);
         *abort = 0;
@@ -346,9 +527,12 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
             uint32_t phase = 0;
             long issued = 0;
             bool ok = true;
-            for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
-                const int m0 = (t / n_tiles) * BM, n0 = (t % n_tiles) * BN;
-                for (int kb = 0; kb < num_kb; kb++) {
+            Sched sc(num_tiles, n_chunks, skm);
+            Seg sg;
+            while (ok && sc.next(sg)) {
+                const int m0 = (sg.tile / n_tiles) * BM, n0 = (sg.tile % n_tiles) * BN;
+                const int kb_end = min(sg.c1 * chunk_kb, num_kb);
+                for (int kb = sg.c0 * chunk_kb; kb < kb_end; kb++) {
                     if (!bar_wait(empty0 + 8 * stage, phase ^ 1, abort, err, 1)) { ok = false; break; }
                     const uint32_t fb = full0 + 8 * stage;
                     const uint32_t base = su32(tiles + (size_t)stage * S::STAGE_BYTES);
@@ -376,18 +560,20 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
             int stage = 0;
             uint32_t phase = 0, chunk = 0;
             bool ok = true;
-            int local = 0;
-            for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x, local++) {
+            Sched sc(num_tiles, n_chunks, skm);
+            Seg sg;
+            for (int local = 0; ok && sc.next(sg); local++) {
                 const uint32_t ts = local & 1;
-                if (!bar_wait(sempty0 + 8 * ts, ((local >> 1) & 1) ^ 1, abort, err, 3)) break;
+                if (SEP && !bar_wait(sempty0 + 8 * ts, ((local >> 1) & 1) ^ 1, abort, err, 3)) break;
                 fence_after();
-                const uint32_t ds = tmem + (2 + ts) * (uint32_t)BN;
-                for (int c = 0; ok && c < n_chunks; c++, chunk++) {
-                    const uint32_t b = chunk & 1;
-                    if (!bar_wait(cempty0 + 8 * b, ((chunk >> 1) & 1) ^ 1, abort, err, 3)) { ok = false; break; }
+                for (int c = sg.c0; ok && c < sg.c1; c++, chunk++) {
+                    const uint32_t b = chunk % NBUF;
+                    if (!bar_wait(cempty0 + 8 * b, ((chunk / NBUF) & 1) ^ 1, abort, err, 3)) { ok = false; break; }
                     fence_after();
                     const uint32_t db = tmem + b * (uint32_t)BN;
+                    const uint32_t ds = SEP ? tmem + (NBUF + ts) * (uint32_t)BN : db;
                     const int kb0 = c * chunk_kb, kb1 = min(kb0 + chunk_kb, num_kb);
+                    const int ks0 = SEP ? 0 : kb0;          // first K-block of the small-term accumulator
                     for (int kb = kb0; kb < kb1; kb++) {
                         if (!bar_wait(full0 + 8 * stage, phase, abort, err, 4)) { ok = false; break; }
                         fence_after();
@@ -400,7 +586,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                             const unsigned long long bh = sdesc<SWB>(base + 2 * S::A_BYTES + off);
                             const unsigned long long bl = sdesc<SWB>(base + 2 * S::A_BYTES + S::B_BYTES + off);
                             mma_tf32(db, ah, bh, id, (kb > kb0 || k > 0) ? 1u : 0u);
-                            mma_tf32(ds, al, bh, id, (kb > 0 || k > 0) ? 1u : 0u);
+                            mma_tf32(ds, al, bh, id, (!SEP || kb > ks0 || k > 0) ? 1u : 0u);
                             mma_tf32(ds, ah, bl, id, 1u);
                         }
                         mma_commit(empty0 + 8 * stage);
@@ -408,7 +594,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                     }
                     if (ok) mma_commit(cfull0 + 8 * b);
                 }
-                if (ok) mma_commit(sfull0 + 8 * ts);
+                if (SEP && ok) mma_commit(sfull0 + 8 * ts);
             }
             // Every MMA issued above has retired once this barrier flips.
             mma_commit(drain);
@@ -419,44 +605,66 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
         const int q = warp & 3;                    // TMEM lanes 32q .. 32q+31 = tile rows
         const int h = (warp - 2) >> 2;             // column half of the tile
         const uint32_t lane_cols = ((uint32_t)(q * 32) << 16) + (uint32_t)(h * S::HALF);
+        const int ew = warp - 2;                   // epilogue warp index: its stream-K flag and slot part
         uint32_t chunk = 0;
         bool ok = true;
-        int local = 0;
-        for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x, local++) {
+        Sched sc(num_tiles, n_chunks, skm);
+        Seg sg;
+        for (int local = 0; ok && sc.next(sg); local++) {
             float acc[S::HALF];
 #pragma unroll
             for (int j = 0; j < S::HALF; j++) acc[j] = 0.0f;
-            for (int c = 0; c < n_chunks; c++, chunk++) {
-                const uint32_t b = chunk & 1;
-                if (!bar_wait(cfull0 + 8 * b, (chunk >> 1) & 1, abort, err, 6)) { ok = false; break; }
+            for (int c = sg.c0; c < sg.c1; c++, chunk++) {
+                const uint32_t b = chunk % NBUF;
+                if (!bar_wait(cfull0 + 8 * b, (chunk / NBUF) & 1, abort, err, 6)) { ok = false; break; }
                 fence_after();
-                drain_add<S::HALF>(tmem + lane_cols + b * (uint32_t)BN, acc);
+                drain_add<S::HALF, S::LDW>(tmem + lane_cols + b * (uint32_t)BN, acc);
                 fence_before();
                 __syncwarp();
                 if (lane == 0) bar_arrive(cempty0 + 8 * b);
             }
             if (!ok) break;
-            const uint32_t ts = local & 1;
-            if (!bar_wait(sfull0 + 8 * ts, (local >> 1) & 1, abort, err, 7)) break;
-            fence_after();
-            drain_add<S::HALF>(tmem + lane_cols + (2 + ts) * (uint32_t)BN, acc);
-            fence_before();
-            __syncwarp();
-            if (lane == 0) bar_arrive(sempty0 + 8 * ts);
-
-            const int m0 = (t / n_tiles) * BM, n0 = (t % n_tiles) * BN;
-            const int r = m0 + q * 32 + lane;
-            if (r < M) {
-                const int src_row = r % epi.rgroup + epi.roff;
-                const size_t dst_row = (size_t)(r / epi.rgroup) * epi.rstride + epi.roff + r % epi.rgroup;
-                const int nb = n0 + h * S::HALF;
-#pragma unroll
-                for (int j = 0; j < S::HALF; j += 4) {
-                    const int n = nb + j;
-                    if (n < N)
-                        epi_store4(epi, src_row, dst_row, n, min(4, N - n), acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
-                }
+            if (SEP) {
+                const uint32_t ts = local & 1;
+                if (!bar_wait(sfull0 + 8 * ts, (local >> 1) & 1, abort, err, 7)) break;
+                fence_after();
+                drain_add<S::HALF, S::LDW>(tmem + lane_cols + (NBUF + ts) * (uint32_t)BN, acc);
+                fence_before();
+                __syncwarp();
+                if (lane == 0) bar_arrive(sempty0 + 8 * ts);
             }
+
+            if (skm && sg.c0 > 0) {
+                // contributor: this warp's 32 x HALF partial sums to its part of
+                // the CTA's slot (column-major, so each column is one 128-byte
+                // line), then the flag the owner's matching warp waits on
+                float *slot = ws + ((size_t)blockIdx.x * EPI_W + ew) * 32 * S::HALF;
+#pragma unroll
+                for (int j = 0; j < S::HALF; j++) slot[j * 32 + lane] = acc[j];
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) st_release(flags + blockIdx.x * EPI_W + ew, 1);
+                continue;
+            }
+            if (skm && sg.c1 < n_chunks) {
+                // owner: add the contributors' partial sums in chunk order, then
+                // clear their flags for the next launch
+                const long long end = (long long)(sg.tile - sc.R * sc.P + 1) * n_chunks;
+                for (int qq = blockIdx.x + 1; ok && qq < sc.P && sc.first(qq) < end; qq++) {
+                    if (sc.first(qq + 1) == sc.first(qq)) continue;          // a CTA with no units
+                    int *f = flags + qq * EPI_W + ew;
+                    if (!flag_wait(f, abort, err, 8)) { ok = false; break; }
+                    const float *slot = ws + ((size_t)qq * EPI_W + ew) * 32 * S::HALF;
+#pragma unroll
+                    for (int j = 0; j < S::HALF; j++) acc[j] = __fadd_rn(acc[j], slot[j * 32 + lane]);
+                    __syncwarp();
+                    if (lane == 0) *f = 0;
+                }
+                if (!ok) break;
+            }
+            const int m0 = (sg.tile / n_tiles) * BM, n0 = (sg.tile % n_tiles) * BN;
+            epi_store_tile<S::HALF>(epi, acc, epi_stage + ew * (S::EPI_STAGE_BYTES / 4), m0 + q * 32,
+                                    n0 + h * S::HALF, M, N);
         }
     }
 
@@ -772,35 +980,52 @@ struct Cfg {
     size_t smem;
     const void *fn;
     bool pair;          // CTA-pair kernel: 256-row tiles, B boxes of bn/2 rows
+    int threads;
+    bool sep;           // separate small-term accumulators (no stream-K)
+    int epi_warps;
 };
 
-#define TCG_CFG(BN, BK, ST) { BN, BK, ST, Shape<BN, BK, ST>::SMEM, (const void *)gemm_tf32x3_kernel<BN, BK, ST>, false }
+#define TCG_CFG(BN, BK, ST, EW, SEP)                                                            \
+    { BN, BK, ST, Shape<BN, BK, ST, EW, SEP>::SMEM, (const void *)gemm_tf32x3_kernel<BN, BK, ST, EW, SEP>, \
+      false, Shape<BN, BK, ST, EW, SEP>::THREADS, SEP, EW }
 const Cfg CFGS[] = {
-    TCG_CFG(128, 32, 3), TCG_CFG(64, 32, 4), TCG_CFG(128, 16, 6), TCG_CFG(64, 16, 8),
-    TCG_CFG(96, 32, 4), TCG_CFG(96, 16, 7),
-    { 128, 32, 4, PairShape<4>::SMEM, (const void *)gemm_tf32x3_pair_kernel<4>, true },
+    TCG_CFG(128, 32, 3, 8, true), TCG_CFG(64, 32, 4, 8, true), TCG_CFG(128, 16, 6, 8, true),
+    TCG_CFG(64, 16, 8, 8, true), TCG_CFG(96, 32, 3, 8, true), TCG_CFG(96, 16, 7, 8, true),
+    { 128, 32, 4, PairShape<4>::SMEM, (const void *)gemm_tf32x3_pair_kernel<4>, true, NUM_THREADS, true, EPI_WARPS },
+    // 128 x 256 tiles: the small terms fold into the chunk buffers
+    TCG_CFG(256, 16, 4, 16, false), TCG_CFG(256, 32, 2, 16, false),
+    TCG_CFG(128, 32, 3, 8, false), TCG_CFG(128, 32, 3, 16, true), TCG_CFG(128, 32, 3, 16, false),
 };
 #undef TCG_CFG
 constexpr int NCFG = sizeof(CFGS) / sizeof(CFGS[0]);
 
+int g_force_cfg = -1;     // tuning hook: a configuration every automatic choice takes
+
 int choose_cfg(int M, int N)
 {
-    // Fewest tile rounds over the SMs, weighted by tile width plus a fixed
-    // per-tile cost; ties go to the wider tile (more reuse per byte).
-    // Candidates: the BK=32 shapes 128 and 64 wide (96 measured slower per
-    // tile on every ViT shape, even where it packs the SMs better).
-    const int sms = ctx().sms > 0 ? ctx().sms : 148;
-    static const int cand[] = { 0, 1 };
-    int best = 0;
-    long best_cost = -1;
-    for (int i : cand) {
-        const long tiles = (long)((M + BM - 1) / BM) * ((N + CFGS[i].bn - 1) / CFGS[i].bn);
-        const long rounds = (tiles + sms - 1) / sms;
-        const long cost = rounds * (CFGS[i].bn + 32);
-        if (best_cost < 0 || cost < best_cost) { best = i; best_cost = cost; }
-    }
-    return best;
+    // 128 x 128 tiles with separate small-term accumulators and 16 epilogue
+    // warps: the most accurate shape (a few fp32 ulps per product, inside the
+    // reference's 1e-5 per-op tolerance) and the fastest of the accurate ones.
+    (void)M;
+    (void)N;
+    if (g_force_cfg >= 0 && g_force_cfg < NCFG) return g_force_cfg;
+    return 10;
 }
+
+}  // namespace
+
+int gemm_throughput_cfg()
+{
+    // The small terms folded into four TMEM chunk buffers, which lets the last
+    // partial wave of tiles be split by stream-K: the fastest shape on every
+    // ViT GEMM (three truncating tensor-core adds per K-step in a chunk instead
+    // of one: ~1e-6 of max|C| at K = 3072). BN=64 or 96 tiles, the CTA pair
+    // and 128 x 256 tiles measured slower.
+    if (g_force_cfg >= 0 && g_force_cfg < NCFG) return g_force_cfg;
+    return 11;
+}
+
+namespace {
 
 }  // namespace
 
@@ -810,8 +1035,41 @@ int g_chunk_k = 256;
 int gemm_num_cfgs() { return NCFG; }
 int gemm_cfg_bn(int cfg) { return cfg >= 0 && cfg < NCFG ? CFGS[cfg].bn : 0; }
 
+size_t gemm_work_ws_floats(int ctas) { return (size_t)ctas * BM * 256; }
+size_t gemm_work_flag_count(int ctas) { return (size_t)ctas * 16; }
+
+GemmWork *ctx_gemm_work()
+{
+    Ctx &c = ctx();
+    if (c.gemm_work) return (GemmWork *)c.gemm_work;
+    const int ctas = c.sms > 0 ? c.sms : 148;
+    GemmWork *w = new GemmWork;
+    w->ctas = ctas;
+    if (cudaMalloc(&w->ws, gemm_work_ws_floats(ctas) * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&w->flags, gemm_work_flag_count(ctas) * sizeof(int)) != cudaSuccess ||
+        cudaMemset(w->flags, 0, gemm_work_flag_count(ctas) * sizeof(int)) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(w->ws);
+        cudaFree(w->flags);
+        delete w;
+        fail("GEMM stream-K workspace: out of memory");
+        return nullptr;
+    }
+    c.gemm_work = w;
+    return w;
+}
+
+bool gemm_work_reset(const GemmWork &w, cudaStream_t s)
+{
+    if (!w.flags) return true;
+    TCG_CUDA(cudaMemsetAsync(w.flags, 0, gemm_work_flag_count(w.ctas) * sizeof(int), s));
+    return true;
+}
+
+int g_streamk = 1;        // tuning hook: 0 computes every tile whole
+
 bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo,
-               int M, int N, int K, const GemmEpi &epi, int force_cfg)
+               int M, int N, int K, const GemmEpi &epi, int force_cfg, const GemmWork *work)
 {
     if (M <= 0 || N <= 0 || K <= 0) return fail("gemm_plan: empty shape %dx%dx%d", M, N, K);
     const int cfg = force_cfg >= 0 ? force_cfg : choose_cfg(M, N);
@@ -826,6 +1084,12 @@ bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b
     p.K = K;
     p.cfg = cfg;
     p.epi = epi;
+    {
+        const auto a16 = [](const void *q) { return ((uintptr_t)q & 15) == 0; };
+        p.epi.vec = N % 4 == 0 && epi.out.ld % 4 == 0 && a16(epi.bias) && a16(epi.residual) && a16(epi.out.plain) &&
+                    a16(epi.out.hi) && a16(epi.out.lo) && a16(epi.rowadd) && (!epi.rowadd || epi.ld_rowadd % 4 == 0) &&
+                    !(epi.rowadd && epi.residual);
+    }
     const int sms = ctx().sms > 0 ? ctx().sms : 148;
     if (c.pair) {           // one cluster of two CTAs per 256-row tile, as many as fit at once
         static int max_clusters[64];
@@ -853,6 +1117,23 @@ bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b
     } else {
         const int tiles = ((M + BM - 1) / BM) * ((N + c.bn - 1) / c.bn);
         p.grid = tiles < sms ? tiles : sms;
+        // stream-K for a partial last wave; the grid then has room for every
+        // chunk unit when there is less than one wave of tiles
+        // Worth it when the last wave leaves at least half the SMs idle, or
+        // when a tile has many chunks (fine units); with 2-5 chunks and a
+        // fuller last wave the partial-sum hand-over costs what it saves.
+        const int chunks = (K + g_chunk_k - 1) / g_chunk_k;
+        const int last = tiles % sms;
+        const bool pays = last <= sms / 2 || chunks >= 6;
+        if (g_streamk && work && work->ws && work->flags && !c.sep && last != 0 && chunks > 1 && pays) {
+            const long units = (long)tiles * chunks;
+            const int grid = tiles >= sms ? sms : (int)(units < sms ? units : sms);
+            if (grid <= work->ctas) {
+                p.grid = grid;
+                p.sk = 1;
+                p.work = *work;
+            }
+        }
     }
     return true;
 }
@@ -869,9 +1150,13 @@ bool gemm_run(const GemmPlan &p, cudaStream_t s, int *err)
     }
     int chunk_kb = g_chunk_k / c.bk;
     if (chunk_kb < 1) chunk_kb = 1;
+    float *ws = p.work.ws;
+    int *flags = p.work.flags;
+    int sk = p.sk;
     void *args[] = { (void *)&p.a_hi, (void *)&p.a_lo, (void *)&p.b_hi, (void *)&p.b_lo,
-                     (void *)&p.M, (void *)&p.N, (void *)&p.K, (void *)&chunk_kb, (void *)&p.epi, (void *)&err };
-    TCG_CUDA(cudaLaunchKernel(c.fn, dim3(p.grid), dim3(NUM_THREADS), args, c.smem, s));
+                     (void *)&p.M, (void *)&p.N, (void *)&p.K, (void *)&chunk_kb, (void *)&p.epi, (void *)&err,
+                     (void *)&ws, (void *)&flags, (void *)&sk };
+    TCG_CUDA(cudaLaunchKernel(c.fn, dim3(p.grid), dim3(c.threads), args, c.smem, s));
     return true;
 }
 
@@ -902,7 +1187,8 @@ static bool linear_impl(float *y, const float *x, const float *W, const float *b
     e.out.plain = y;
     e.out.ld = N;
     GemmPlan p;
-    if (!gemm_plan(p, xh, xl, wh, wl, M, N, K, e, force_cfg)) return false;
+    const GemmWork *w = ctx_gemm_work();
+    if (!w || !gemm_plan(p, xh, xl, wh, wl, M, N, K, e, force_cfg, w)) return false;
     return gemm_run(p, s, ctx().d_err);
 }
 
@@ -935,7 +1221,8 @@ bool tcg_linear_split_cfg(float *y, const float *x_hi, const float *x_lo, const 
     e.out.plain = y;
     e.out.ld = N;
     GemmPlan p;
-    if (!gemm_plan(p, x_hi, x_lo, w_hi, w_lo, M, N, K, e, cfg)) return false;
+    const GemmWork *w = ctx_gemm_work();
+    if (!w || !gemm_plan(p, x_hi, x_lo, w_hi, w_lo, M, N, K, e, cfg, w)) return false;
     return gemm_run(p, ctx().cur, ctx().d_err);
 }
 
@@ -953,6 +1240,26 @@ bool tcg_linear_cfg(float *y, const float *x, const float *W, const float *bias,
 }
 
 int tcg_gemm_num_cfgs(void) { return gemm_num_cfgs(); }
+
+// Tuning and test hook: 0 turns the stream-K split of a GEMM's last, partial
+// wave off (every tile computed whole, results independent of M), 1 on.
+// Applies to GEMMs planned afterwards. Returns the previous setting.
+int tcg_gemm_set_streamk(int on)
+{
+    const int old = g_streamk;
+    g_streamk = on ? 1 : 0;
+    return old;
+}
+
+// Tuning hook: make every automatic configuration choice (tcg_linear, the
+// ViT's plans, built at upload) take configuration cfg; -1 restores the
+// automatic choice. Returns the previous setting.
+int tcg_gemm_force_cfg(int cfg)
+{
+    const int old = g_force_cfg;
+    g_force_cfg = cfg >= 0 && cfg < gemm_num_cfgs() ? cfg : -1;
+    return old;
+}
 
 // Test hook: K-elements per TMEM chunk (a multiple of 32; larger is faster
 // and less accurate). Returns the previous value.

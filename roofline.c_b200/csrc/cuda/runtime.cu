@@ -2,6 +2,7 @@
 // and the device arena (the reference's arena discipline, src/arena.h:37-69,
 // over one cudaMalloc allocation).
 #include "tcg_common.cuh"
+#include "gemm.cuh"
 
 #include <stdarg.h>
 #include <stdio.h>
@@ -128,6 +129,8 @@ bool tcg_clear_device_error(void)
 {
     if (!tcg::need_ctx()) return false;
     TCG_CUDA(cudaMemsetAsync(ctx().d_err, 0, sizeof(int), ctx().cur));
+    // a GEMM that gave up may have left stream-K flags raised
+    if (ctx().gemm_work && !tcg::gemm_work_reset(*(tcg::GemmWork *)ctx().gemm_work, ctx().cur)) return false;
     return true;
 }
 

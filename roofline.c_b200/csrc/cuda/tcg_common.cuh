@@ -25,6 +25,7 @@ struct Ctx {
     cudaEvent_t ev[64] = {};
     void *scratch = nullptr;      // grow-only device scratch for the op API
     size_t scratch_bytes = 0;
+    void *gemm_work = nullptr;    // the op API's GemmWork (gemm_tc.cu)
 };
 
 Ctx &ctx();

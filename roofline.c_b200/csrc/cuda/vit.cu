@@ -53,6 +53,7 @@ struct tcg_vit {
     float *px = nullptr, *x = nullptr, *h_hi = nullptr, *h_lo = nullptr, *qkv = nullptr;
     float *f_hi = nullptr, *f_lo = nullptr, *pooled_hi = nullptr, *pooled_lo = nullptr, *out = nullptr;
     float *p_hi = nullptr, *p_lo = nullptr;   // alias f_hi / f_lo
+    tcg::GemmWork work;                       // this model's GEMM stream-K memory (in the arena)
 
     struct Plans {
         tcg::GemmPlan patch, proj;
@@ -180,8 +181,10 @@ static tcg_vit *vit_alloc(const tc_vit_t *m, int max_batch, std::vector<WEntry> 
 
     const size_t n = (size_t)max_batch, T = v->T, G2 = (size_t)v->G * v->G;
     const size_t f_floats = std::max(n * T * F, n * G2 * K0);
+    const int ctas = ctx().sms > 0 ? ctx().sms : 148;
+    const size_t ws_floats = gemm_work_ws_floats(ctas), flag_count = gemm_work_flag_count(ctas);
     const size_t want = (n * 3 * v->S * v->S + n * T * D * 3 + n * T * 3 * D + 2 * f_floats +
-                         2 * n * D + n * v->d_out) * sizeof(float) + 16 * 256;
+                         2 * n * D + n * v->d_out + ws_floats + flag_count) * sizeof(float) + 16 * 256;
     v->act = tcg_arena_create(want, "vit activations");
     if (!tcg_arena_ok(&v->act)) return nullptr;
     auto alloc = [&](size_t floats) { return (float *)tcg_arena_alloc(&v->act, floats * sizeof(float), 256); };
@@ -197,7 +200,15 @@ static tcg_vit *vit_alloc(const tc_vit_t *m, int max_batch, std::vector<WEntry> 
     v->out = alloc(n * v->d_out);
     v->p_hi = v->f_hi;
     v->p_lo = v->f_lo;
-    if (!v->out) return nullptr;
+    v->work.ws = alloc(ws_floats);
+    v->work.flags = (int *)alloc(flag_count);
+    v->work.ctas = ctas;
+    if (!v->work.flags) return nullptr;
+    if (cudaMemset(v->work.flags, 0, flag_count * sizeof(int)) != cudaSuccess) {
+        cudaGetLastError();
+        fail("tcg_vit_upload: cannot clear the GEMM flags");
+        return nullptr;
+    }
     return v.release();
 }
 
@@ -239,12 +250,15 @@ static tcg_vit::Plans *plans_for(tcg_vit *v, int n)
     e.roff = 1;
     e.out.plain = v->x;
     e.out.ld = D;
-    if (!gemm_plan(p->patch, v->p_hi, v->p_lo, v->patch_h, v->patch_l, n * G2, D, K0, e)) return nullptr;
+    const GemmWork *w = &v->work;
+    const int tp = gemm_throughput_cfg();
+    if (!gemm_plan(p->patch, v->p_hi, v->p_lo, v->patch_h, v->patch_l, n * G2, D, K0, e, tp, w)) return nullptr;
 
     GemmEpi pe;                                   // embedding = pooled x proj, into v->out
     pe.out.plain = v->out;
     pe.out.ld = v->d_out;
-    if (!gemm_plan(p->proj, v->pooled_hi, v->pooled_lo, v->projT_h, v->projT_l, n, v->d_out, D, pe)) return nullptr;
+    if (!gemm_plan(p->proj, v->pooled_hi, v->pooled_lo, v->projT_h, v->projT_l, n, v->d_out, D, pe, tp, w))
+        return nullptr;
 
     p->qkv.resize(v->L); p->out.resize(v->L); p->up.resize(v->L); p->down.resize(v->L);
     for (int i = 0; i < v->L; i++) {
@@ -269,10 +283,10 @@ static tcg_vit::Plans *plans_for(tcg_vit *v, int n)
         d.residual = v->x;
         d.out.plain = v->x;
         d.out.ld = D;
-        if (!gemm_plan(p->qkv[i], v->h_hi, v->h_lo, y.qkv_h, y.qkv_l, M, 3 * D, D, q) ||
-            !gemm_plan(p->out[i], v->h_hi, v->h_lo, y.out_h, y.out_l, M, D, D, o) ||   // a aliases h
-            !gemm_plan(p->up[i], v->h_hi, v->h_lo, y.up_h, y.up_l, M, F, D, u) ||
-            !gemm_plan(p->down[i], v->f_hi, v->f_lo, y.down_h, y.down_l, M, D, F, d))
+        if (!gemm_plan(p->qkv[i], v->h_hi, v->h_lo, y.qkv_h, y.qkv_l, M, 3 * D, D, q, tp, w) ||
+            !gemm_plan(p->out[i], v->h_hi, v->h_lo, y.out_h, y.out_l, M, D, D, o, tp, w) ||   // a aliases h
+            !gemm_plan(p->up[i], v->h_hi, v->h_lo, y.up_h, y.up_l, M, F, D, u, tp, w) ||
+            !gemm_plan(p->down[i], v->f_hi, v->f_lo, y.down_h, y.down_l, M, D, F, d, tp, w))
             return nullptr;
     }
     tcg_vit::Plans *raw = p.get();

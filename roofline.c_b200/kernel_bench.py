@@ -75,12 +75,14 @@ class SplitOperands:
 
 
 def case_gemm(a):
+    old_sk = tcg.lib().tcg_gemm_set_streamk(a.streamk)
     ops = SplitOperands(a.M, a.N, a.K)
     with tcg.DeviceBuffer(256 << 20) as flush:
         ms, _ = timed(lambda: ops.run(a.cfg), a.warmup, a.reps, flush)
     ops.close()
+    tcg.lib().tcg_gemm_set_streamk(old_sk)
     flops = 2.0 * a.M * a.N * a.K
-    return {"case": "gemm", "M": a.M, "N": a.N, "K": a.K, "cfg": a.cfg, "ms": round(ms, 4),
+    return {"case": "gemm", "M": a.M, "N": a.N, "K": a.K, "cfg": a.cfg, "streamk": a.streamk, "ms": round(ms, 4),
             "tflops": round(flops / ms / 1e9, 1)}
 
 
@@ -93,6 +95,7 @@ def case_gemmsweep(a):
     chunks = [int(c) for c in a.chunks.split(",")]
     cfgs = range(L.tcg_gemm_num_cfgs()) if a.cfgs == "all" else [int(c) for c in a.cfgs.split(",")]
     res = {"perf_ms": {}, "rel_err": {}}
+    default_chunk = L.tcg_gemm_set_chunk_k(0)         # an invalid length only reads the current one
     flush = tcg.DeviceBuffer(256 << 20)
     for name, (M, N, K) in shapes.items():
         ops = SplitOperands(M, N, K)
@@ -106,10 +109,11 @@ def case_gemmsweep(a):
         ops = SplitOperands(256, 768, K, seed=1)
         for ck in chunks:
             L.tcg_gemm_set_chunk_k(ck)
-            ops.run(-1)
-            res["rel_err"][f"K{K}/chunk{ck}"] = ops.rel_err()
+            for cfg in list(cfgs) + [-1]:
+                ops.run(cfg)
+                res["rel_err"][f"K{K}/chunk{ck}/cfg{cfg}"] = ops.rel_err()
         ops.close()
-    L.tcg_gemm_set_chunk_k(32)
+    L.tcg_gemm_set_chunk_k(default_chunk)
     flush.close()
     return {"case": "gemmsweep", **res}
 
@@ -145,6 +149,8 @@ def case_vit(a):
     cache = os.environ.get("TCG_BENCH_CACHE", "/tmp/roofline_b200_bench")
     over = {"n_layer": a.layers} if a.layers else {}
     path, cfg = G.cached_vit_gguf(cache, a.model, 0, **over)
+    # the GEMM plans of a batch size are made at its first forward
+    old_cfg, old_sk = L.tcg_gemm_force_cfg(a.cfg), L.tcg_gemm_set_streamk(a.streamk)
     m = tcg.VitModel(path)
     m.upload(a.batch)
     px = G.make_pixels(a.batch, cfg["image"], 1)
@@ -152,7 +158,10 @@ def case_vit(a):
         step = lambda: tcg.check(L.tcg_vit_encode_device(m.dev, dpx.ptr, a.batch, dout.ptr))  # noqa: E731
         ms, _ = timed(step, a.warmup, a.steps)
     m.close()
-    return {"case": "vit", "model": a.model, "layers": cfg["n_layer"], "batch": a.batch, "ms": round(ms, 4),
+    L.tcg_gemm_force_cfg(old_cfg)
+    L.tcg_gemm_set_streamk(old_sk)
+    return {"case": "vit", "model": a.model, "layers": cfg["n_layer"], "batch": a.batch, "cfg": a.cfg,
+            "streamk": a.streamk, "ms": round(ms, 4),
             "images/s": round(a.batch / ms * 1e3, 1)}
 
 
@@ -164,6 +173,7 @@ def main():
     g.add_argument("--N", type=int, default=3072)
     g.add_argument("--K", type=int, default=768)
     g.add_argument("--cfg", type=int, default=-1)
+    g.add_argument("--streamk", type=int, default=1)
     gs = sub.add_parser("gemmsweep")
     gs.add_argument("--chunks", default="32,64,128,256,4096")
     gs.add_argument("--cfgs", default="all")
@@ -180,6 +190,8 @@ def main():
     v.add_argument("--batch", type=int, default=256)
     v.add_argument("--layers", type=int, default=0)
     v.add_argument("--steps", type=int, default=3)
+    v.add_argument("--cfg", type=int, default=-1, help="GEMM configuration for every linear (-1: automatic)")
+    v.add_argument("--streamk", type=int, default=1, help="0: every GEMM tile computed whole")
     for p in (g, gs, mv, dq, v):
         p.add_argument("--warmup", type=int, default=3)
         p.add_argument("--reps", type=int, default=5)

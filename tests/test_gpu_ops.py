@@ -4,7 +4,10 @@
   reference's own per-op tolerances (tests/test_ops.c:74-148);
 * LayerNorm against the oracle on ViT-width rows (one offset by 1e4);
 * the 3xTF32 tcgen05 GEMM in every tile configuration on ragged shapes,
-  against the oracle's sequential fp32 GEMM: max|err| <= 1e-5 * max|y|.
+  against the oracle's sequential fp32 GEMM: max|err| <= 1e-5 * max|y|;
+* the stream-K split of a GEMM's last, partial wave of tiles (less than one
+  wave, one wave and a part, a K of 12 chunks): deterministic, and within the
+  same bound of a float64 product as the whole-tile schedule.
 """
 import numpy as np
 import pytest
@@ -125,7 +128,7 @@ def test_mha_vs_oracle(dev, T, H, HD):
 SHAPES = [(1, 64, 4), (127, 100, 12), (129, 200, 588), (300, 768, 768), (50, 2304, 768), (261, 130, 3072)]
 
 
-@pytest.mark.parametrize("cfg", [0, 1, 2, 3, 4, 5, 6, -2])
+@pytest.mark.parametrize("cfg", [0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, -2])
 @pytest.mark.parametrize("M,N,K", SHAPES)
 def test_linear_every_config(dev, cfg, M, N, K):
     L = tcg.lib()
@@ -150,3 +153,30 @@ def test_gemm_untransposed_and_odd_k(dev):
     tcg.check(L.tcg_gemm(y.ptr, dev.put(A), dev.put(B), 9, 7, 11, False))
     want = oracle.gemm(A, B, 9, 7, 11, b_transposed=False)
     assert np.abs(y.download((9, 7)) - want).max() <= 1e-5 * np.abs(want).max()
+
+
+@pytest.mark.parametrize("M,N,K", [(700, 512, 768), (2000, 2304, 768), (1600, 768, 3072)])
+def test_streamk_split(dev, M, N, K):
+    L = tcg.lib()
+    rng = np.random.default_rng(M + N + K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    W = (rng.standard_normal((N, K)) * 0.05).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    want = x.astype(np.float64) @ W.astype(np.float64).T + b
+    xp, wp, bp = dev.put(x), dev.put(W), dev.put(b)
+    y = dev.empty(M * N)
+    got = {}
+    for sk in (1, 1, 0):
+        old = L.tcg_gemm_set_streamk(sk)
+        try:
+            tcg.check(L.tcg_linear_cfg(y.ptr, xp, wp, bp, M, N, K, 9), f"streamk {sk}")
+        finally:
+            L.tcg_gemm_set_streamk(old)
+        r = y.download((M, N))
+        if sk in got:
+            assert np.array_equal(r, got[sk])            # the split is deterministic
+        got[sk] = r
+    for sk, r in got.items():
+        err = np.abs(r.astype(np.float64) - want).max() / np.abs(want).max()
+        assert err <= GEMM_TOL, (sk, err)
+    assert L.tcg_device_error() == 0

@@ -95,8 +95,10 @@ def test_l14_two_layers_vs_oracle(gpu, cache_dir):
 
 
 def test_batch_invariance_and_graph_replay(gpu, cache_dir):
+    L = tcg.lib()
     path, cfg = model(cache_dir, "vit-b32", n_layer=3)
     px = G.make_pixels(9, cfg["image"], 7)
+    old = L.tcg_gemm_set_streamk(0)             # whole tiles: each row's K order is the batch's
     m = tcg.VitModel(path)
     try:
         m.upload(9)
@@ -105,12 +107,38 @@ def test_batch_invariance_and_graph_replay(gpu, cache_dir):
         assert np.array_equal(full, again)
         one, _ = m.encode(px[4:5])
         assert np.array_equal(one[0], full[4])  # same K order whatever the batch
-        tcg.lib().tcg_vit_use_graphs(m.dev, False)
+        L.tcg_vit_use_graphs(m.dev, False)
         eager, _ = m.encode(px)
         assert np.array_equal(eager, full)
-        assert tcg.lib().tcg_device_error() == 0
+        assert L.tcg_device_error() == 0
     finally:
         m.close()
+        L.tcg_gemm_set_streamk(old)
+
+
+def test_streamk_forward(gpu, cache_dir):
+    """With the stream-K split (the default) a batch's result depends on how
+    its GEMMs' last waves are cut, so it is deterministic per batch size and
+    within the tolerance of the whole-tile result."""
+    L = tcg.lib()
+    path, cfg = model(cache_dir, "vit-b32", n_layer=3)
+    px = G.make_pixels(9, cfg["image"], 7)
+    outs = {}
+    for sk in (0, 1):
+        old = L.tcg_gemm_set_streamk(sk)
+        m = tcg.VitModel(path)
+        try:
+            m.upload(9)
+            a, _ = m.encode(px)
+            b, _ = m.encode(px)                 # graph replay
+            assert np.array_equal(a, b)
+            outs[sk] = a
+        finally:
+            m.close()
+            L.tcg_gemm_set_streamk(old)
+    for i in range(9):
+        assert rel_inf(outs[1][i], outs[0][i]) <= TOL
+    assert L.tcg_device_error() == 0
 
 
 def test_async_submit_matches_blocking(gpu, cache_dir):
