@@ -28,11 +28,10 @@
 //              apply bias / position / GELU / residual, split hi/lo and store.
 // Operand tiles are K-major with the TMA swizzle that matches the UMMA
 // descriptor (BK*4 bytes: 128B for BK=32, 64B for BK=16).
-// gemm_tf32x3_pair_kernel is the CTA-pair variant (cta_group::2, M=256 per
-// cluster of two): each CTA loads its own A rows and half of the B tile with
-// plain (unicast) TMA loads; only the MMA completion commit signals both CTAs.
-// It is correct but measured no faster than the one-CTA kernel on the ViT
-// shapes, so the automatic choice never picks it.
+// With CG = 2 a cluster of two CTAs (tcgen05 cta_group::2) computes one
+// 256-row tile; each CTA loads its own A rows and half of the B tile with
+// plain (unicast) TMA loads, and only the MMA completion commit signals both
+// CTAs.
 // Every mbarrier wait is bounded (globaltimer); a wait that gives up sets a
 // CTA-wide abort flag and the library's device error word, the roles wind
 // down, in-flight copies and MMAs are drained, and TMEM is freed.
@@ -43,8 +42,6 @@ namespace tcg {
 namespace {
 
 constexpr int BM = 128;
-constexpr int EPI_WARPS = 8;
-constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
 constexpr unsigned long long WAIT_NS = 4000000000ull;   // 4 s per wait
 
 __device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -241,21 +238,90 @@ __device__ __forceinline__ void epi_store4(const GemmEpi &e, int src_row, size_t
     }
 }
 
+// ---------------------------------------------- CTA pairs (cta_group::2)
+// With CG = 2 a cluster of two CTAs computes one 256 x BN tile: CTA r owns
+// rows 128r..128r+127 and loads its 128 rows of A and half of B (BN/2 rows);
+// the MMA reads A from each CTA and B from both halves, so each SM's shared
+// memory serves 25% fewer operand bytes per FLOP than with one CTA per tile.
+// The leader's producer arms the stage barrier with both CTAs' bytes, both
+// CTAs' (unicast) TMA loads complete on it, and one lane of the leader issues
+// the M = 256 MMAs and commits them to the barrier at the same offset in both
+// CTAs. Each CTA drains its own 128 TMEM lanes and releases chunk buffers on
+// the leader's barriers.
+
+__device__ __forceinline__ uint32_t cta_rank_in_cluster()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// address of the same shared-memory offset in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t peer_addr(uint32_t addr, uint32_t rank)
+{
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void bar_arrive_cluster(uint32_t cluster_addr)
+{
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void cluster_sync()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// TMA load into this CTA's shared memory whose bytes complete on the
+// leader's barrier (cluster address).
+__device__ __forceinline__ void tma_load_pair(uint32_t dst, const CUtensorMap *map, uint32_t bar_cluster, int x, int y)
+{
+    asm volatile("cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%2, %3}], [%4];"
+                 ::"r"(dst), "l"((unsigned long long)map), "r"(x), "r"(y), "r"(bar_cluster) : "memory");
+}
+__device__ __forceinline__ void mma_tf32_pair(uint32_t d, unsigned long long a, unsigned long long b, uint32_t id, uint32_t acc)
+{
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+                 ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc));
+}
+// commit the leader's MMAs to the barrier at this offset in both CTAs
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+                 ::"r"(bar), "h"((unsigned short)3) : "memory");
+}
+// commit the leader's MMAs to one of its own barriers
+__device__ __forceinline__ void mma_commit_pair_local(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
 // EPI_W epilogue warps (8 or 16): warp w drains TMEM lane quarter w & 3 and
-// column group (w - 2) / 4 of the tile. SEP: the small lo*hi + hi*lo terms
-// have their own per-tile TMEM buffers (two chunk and two tile accumulators
-// of BN columns); without it they fold into the chunk buffers with the hi*hi
-// term, and the 512 TMEM columns hold as many chunk buffers as fit (four at
-// BN = 128, two at BN = 256) at the price of three MMAs per K-step truncating
-// into each chunk instead of one.
-template <int BN, int BK, int STAGES, int EPI_W = 8, bool SEP = true>
+// column group (w - 2) / 4 of the tile. ACC, where the three products of a
+// K-step accumulate:
+//   ACC_SEP   the small lo*hi + hi*lo terms in their own per-tile TMEM
+//             buffers (two chunk and two tile accumulators of BN columns): one
+//             truncating tensor-core add per K-step into a chunk, the most
+//             accurate;
+//   ACC_FOLD  all three into the chunk buffer, as many BN-column chunk buffers
+//             as the 512 TMEM columns hold (three truncating adds per K-step);
+//   ACC_WIDE  one N = 2*BN MMA of A_hi against B_hi and B_lo stacked (they are
+//             adjacent in shared memory) puts hi*hi and hi*lo side by side in
+//             a 2*BN-column chunk buffer, and one N = BN MMA adds lo*hi to the
+//             first half: two MMA instructions per K-step instead of three,
+//             each twice as long on average, and two truncating adds into
+//             the hi*hi half. The drain adds the halves.
+enum { ACC_SEP = 0, ACC_FOLD = 1, ACC_WIDE = 2 };
+
+template <int BN, int BK, int STAGES, int EPI_W = 8, int ACC = ACC_SEP, int CG = 1>
 struct Shape {
     static constexpr uint32_t A_BYTES = BM * BK * 4;
-    static constexpr uint32_t B_BYTES = BN * BK * 4;
+    static constexpr uint32_t B_BYTES = (BN / CG) * BK * 4;     // this CTA's share of the B tile
     static constexpr uint32_t STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
-    static constexpr int NBUF = SEP ? 2 : (4 * BN <= 512 ? 4 : 2);   // chunk buffers
-    static constexpr int NACC = SEP ? 4 : NBUF;
-    static constexpr uint32_t TMEM_COLS = NACC * BN <= 256 ? 256 : 512;
+    static constexpr int CW = ACC == ACC_WIDE ? 2 * BN : BN;    // columns of a chunk buffer
+    static constexpr int NBUF = ACC == ACC_SEP ? 2 : (4 * CW <= 512 ? 4 : 2);   // chunk buffers
+    static constexpr int NACC = ACC == ACC_SEP ? 4 : NBUF;
+    static constexpr uint32_t TMEM_COLS = NACC * CW <= 256 ? 256 : 512;
     static constexpr int GROUPS = EPI_W / 4;
     static constexpr int HALF = BN / GROUPS;           // columns per epilogue thread
     static constexpr int THREADS = 64 + 32 * EPI_W;
@@ -264,10 +330,28 @@ struct Shape {
     static constexpr int NBAR = 2 * STAGES + 2 * NBUF + 4 + 1;
     static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + EPI_W * EPI_STAGE_BYTES + 8 * NBAR + 16;
     static_assert(EPI_W == 8 || EPI_W == 16, "two or four epilogue warps per TMEM lane quarter");
+    static_assert(CG == 1 || CG == 2, "one CTA or a CTA pair per tile");
     static_assert(HALF % 16 == 0, "each epilogue warp drains whole 16-column slices");
-    static_assert(NACC * BN <= 512, "the accumulators must fit the 512 TMEM columns");
+    static_assert(NACC * CW <= 512, "the accumulators must fit the 512 TMEM columns");
+    static_assert(ACC != ACC_WIDE || (2 * BN <= 256 && CG == 1), "a wide MMA is at most 256 columns, one CTA");
     static_assert(SMEM <= 232448, "shared memory per block");
 };
+
+// acc[0..HALF) += (first + second) where first and second are the HALF fp32
+// columns at TMEM addresses ta and tb (this warp's lanes), 16 at a time.
+template <int HALF>
+__device__ __forceinline__ void drain_add2(uint32_t ta, uint32_t tb, float (&acc)[HALF])
+{
+#pragma unroll
+    for (int j = 0; j < HALF; j += 16) {
+        uint32_t x[16], y[16];
+        tmem_ld16(ta + (uint32_t)j, x);
+        tmem_ld16(tb + (uint32_t)j, y);
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+            acc[j + i] = __fadd_rn(acc[j + i], __fadd_rn(__uint_as_float(x[i]), __uint_as_float(y[i])));
+    }
+}
 
 __device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
 
@@ -387,8 +471,8 @@ __device__ __forceinline__ void drain_add(uint32_t taddr, float (&acc)[HALF])
     }
 }
 
-// Work order of one CTA of a persistent GEMM launch (P = gridDim.x CTAs).
-// Whole tiles: blockIdx.x, + P, + 2P, ... With stream-K (sk), only the
+// Work order of one CTA (or CTA pair) p of a persistent GEMM launch of P
+// CTAs (pairs). Whole tiles: p, p + P, p + 2P, ... With stream-K (sk), only the
 // R = num_tiles / P full waves run that way; the L = num_tiles % P tiles of the
 // last wave become L * C chunk units (C = K chunks per tile) dealt out in
 // contiguous, equal ranges [first(p), first(p + 1)), so no SM idles through a
@@ -404,7 +488,7 @@ struct Seg {
 struct Sched {
     int C, P, p, num_tiles, R, i = 0;
     long long u = 0, ue = 0, LC = 0;
-    __device__ Sched(int num_tiles_, int C_, bool sk) : C(C_), P(gridDim.x), p(blockIdx.x), num_tiles(num_tiles_)
+    __device__ Sched(int num_tiles_, int C_, bool sk, int P_, int p_) : C(C_), P(P_), p(p_), num_tiles(num_tiles_)
     {
         if (sk) {
             R = num_tiles / P;
@@ -464,13 +548,15 @@ __device__ bool flag_wait(const int *f, volatile int *abort, int *err, int code)
 
 // chunk_kb: K-blocks whose hi*hi products share one TMEM chunk buffer before
 // it is drained into the fp32 registers.
-template <int BN, int BK, int STAGES, int EPI_W, bool SEP>
-__global__ void __launch_bounds__(Shape<BN, BK, STAGES, EPI_W, SEP>::THREADS, 1)
+template <int BN, int BK, int STAGES, int EPI_W, int ACC, int CG>
+__global__ void __launch_bounds__(Shape<BN, BK, STAGES, EPI_W, ACC, CG>::THREADS, 1)
 gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
                    const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
                    int M, int N, int K, int chunk_kb, GemmEpi epi, int *err, float *ws, int *flags, int sk)
 {
-    using S = Shape<BN, BK, STAGES, EPI_W, SEP>;
+    using S = Shape<BN, BK, STAGES, EPI_W, ACC, CG>;
+    constexpr bool SEP = ACC == ACC_SEP, WIDE = ACC == ACC_WIDE;
+    constexpr uint32_t CW = S::CW;
     constexpr int SWB = BK * 4;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *tiles = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -479,12 +565,14 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
     uint32_t *tmem_slot = (uint32_t *)(bars + S::NBAR);
     volatile int *abort = (volatile int *)(tmem_slot + 1);
 
+    const uint32_t rank = CG == 2 ? cta_rank_in_cluster() : 0;
+    const bool leader = rank == 0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_tiles = (N + BN - 1) / BN;
-    const int num_tiles = ((M + BM - 1) / BM) * n_tiles;
+    const int num_tiles = ((M + CG * BM - 1) / (CG * BM)) * n_tiles;
     const int num_kb = (K + BK - 1) / BK;
     const int n_chunks = (num_kb + chunk_kb - 1) / chunk_kb;
-    const bool skm = !SEP && sk && ws && flags;    // stream-K needs per-chunk partials: fold mode only
+    const bool skm = !SEP && sk && ws && flags;    // stream-K needs per-chunk partials: not ACC_SEP
     const uint32_t full0 = su32(bars), empty0 = su32(bars + STAGES);
     constexpr int NBUF = S::NBUF;
     const uint32_t cfull0 = su32(bars + 2 * STAGES), cempty0 = cfull0 + 8 * NBUF;
@@ -497,25 +585,33 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
         }
         for (int b = 0; b < NBUF; b++) {
             bar_init(cfull0 + 8 * b, 1);
-            bar_init(cempty0 + 8 * b, EPI_W);
+            bar_init(cempty0 + 8 * b, CG * EPI_W);        // the epilogue warps of every CTA of the group
         }
         for (int b = 0; b < 2; b++) {
             bar_init(sfull0 + 8 * b, 1);
-            bar_init(sempty0 + 8 * b, EPI_W);
+            bar_init(sempty0 + 8 * b, CG * EPI_W);
         }
         bar_init(drain, 1);
         *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                     ::"r"(su32(tmem_slot)), "r"(S::TMEM_COLS) : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        if constexpr (CG == 2) {
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                         ::"r"(su32(tmem_slot)), "r"(S::TMEM_COLS) : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                         ::"r"(su32(tmem_slot)), "r"(S::TMEM_COLS) : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        }
     }
     fence_before();
-    __syncthreads();
+    if constexpr (CG == 2) cluster_sync();      // barriers initialised and TMEM allocated in both CTAs
+    else __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
+    const int P = gridDim.x / CG, p = blockIdx.x / CG;   // tile groups (CTA pairs) and this one
 
     if (warp == 0) {
         if (lane == 0) {
@@ -527,40 +623,56 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
             uint32_t phase = 0;
             long issued = 0;
             bool ok = true;
-            Sched sc(num_tiles, n_chunks, skm);
+            Sched sc(num_tiles, n_chunks, skm, P, p);
             Seg sg;
             while (ok && sc.next(sg)) {
-                const int m0 = (sg.tile / n_tiles) * BM, n0 = (sg.tile % n_tiles) * BN;
+                const int m0 = (sg.tile / n_tiles) * CG * BM + (int)rank * BM;
+                const int nb = (sg.tile % n_tiles) * BN + (int)rank * (BN / CG);
                 const int kb_end = min(sg.c1 * chunk_kb, num_kb);
                 for (int kb = sg.c0 * chunk_kb; kb < kb_end; kb++) {
                     if (!bar_wait(empty0 + 8 * stage, phase ^ 1, abort, err, 1)) { ok = false; break; }
-                    const uint32_t fb = full0 + 8 * stage;
                     const uint32_t base = su32(tiles + (size_t)stage * S::STAGE_BYTES);
-                    bar_expect_tx(fb, S::STAGE_BYTES);
-                    tma_load(base, &a_hi, fb, kb * BK, m0);
-                    tma_load(base + S::A_BYTES, &a_lo, fb, kb * BK, m0);
-                    tma_load(base + 2 * S::A_BYTES, &b_hi, fb, kb * BK, n0);
-                    tma_load(base + 2 * S::A_BYTES + S::B_BYTES, &b_lo, fb, kb * BK, n0);
+                    if constexpr (CG == 2) {
+                        // both CTAs' copies complete on the leader's barrier
+                        const uint32_t fb = peer_addr(full0 + 8 * stage, 0);
+                        if (leader) bar_expect_tx(full0 + 8 * stage, 2 * S::STAGE_BYTES);
+                        tma_load_pair(base, &a_hi, fb, kb * BK, m0);
+                        tma_load_pair(base + S::A_BYTES, &a_lo, fb, kb * BK, m0);
+                        tma_load_pair(base + 2 * S::A_BYTES, &b_hi, fb, kb * BK, nb);
+                        tma_load_pair(base + 2 * S::A_BYTES + S::B_BYTES, &b_lo, fb, kb * BK, nb);
+                    } else {
+                        const uint32_t fb = full0 + 8 * stage;
+                        bar_expect_tx(fb, S::STAGE_BYTES);
+                        tma_load(base, &a_hi, fb, kb * BK, m0);
+                        tma_load(base + S::A_BYTES, &a_lo, fb, kb * BK, m0);
+                        tma_load(base + 2 * S::A_BYTES, &b_hi, fb, kb * BK, nb);
+                        tma_load(base + 2 * S::A_BYTES + S::B_BYTES, &b_lo, fb, kb * BK, nb);
+                    }
                     issued++;
                     if (++stage == STAGES) { stage = 0; phase ^= 1; }
                 }
             }
-            // Let the last fill of every stage land before the CTA exits.
-            for (int i = 1; i <= STAGES && i <= issued; i++) {
-                int s = stage - i;
-                uint32_t ph = phase;
-                if (s < 0) { s += STAGES; ph ^= 1; }
-                bar_wait(full0 + 8 * s, ph, abort, err, 2, false);
-            }
+            // Let the last fill of every stage land before the CTA exits (in a
+            // pair, the follower's copies complete on the leader's barrier).
+            if (leader)
+                for (int i = 1; i <= STAGES && i <= issued; i++) {
+                    int s = stage - i;
+                    uint32_t ph = phase;
+                    if (s < 0) { s += STAGES; ph ^= 1; }
+                    bar_wait(full0 + 8 * s, ph, abort, err, 2, false);
+                }
         }
         __syncwarp();
     } else if (warp == 1) {
-        if (lane == 0) {
-            const uint32_t id = idesc_tf32<BN>();
+        if (leader && lane == 0) {
+            const uint32_t id = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                ((uint32_t)((CG * BM) >> 4) << 24);
+            const uint32_t id_wide = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)((2 * BN) >> 3) << 17) |
+                                     ((uint32_t)((CG * BM) >> 4) << 24);
             int stage = 0;
             uint32_t phase = 0, chunk = 0;
             bool ok = true;
-            Sched sc(num_tiles, n_chunks, skm);
+            Sched sc(num_tiles, n_chunks, skm, P, p);
             Seg sg;
             for (int local = 0; ok && sc.next(sg); local++) {
                 const uint32_t ts = local & 1;
@@ -570,8 +682,8 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                     const uint32_t b = chunk % NBUF;
                     if (!bar_wait(cempty0 + 8 * b, ((chunk / NBUF) & 1) ^ 1, abort, err, 3)) { ok = false; break; }
                     fence_after();
-                    const uint32_t db = tmem + b * (uint32_t)BN;
-                    const uint32_t ds = SEP ? tmem + (NBUF + ts) * (uint32_t)BN : db;
+                    const uint32_t db = tmem + b * CW;
+                    const uint32_t ds = SEP ? tmem + (NBUF + ts) * CW : db;
                     const int kb0 = c * chunk_kb, kb1 = min(kb0 + chunk_kb, num_kb);
                     const int ks0 = SEP ? 0 : kb0;          // first K-block of the small-term accumulator
                     for (int kb = kb0; kb < kb1; kb++) {
@@ -585,30 +697,53 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                             const unsigned long long al = sdesc<SWB>(base + S::A_BYTES + off);
                             const unsigned long long bh = sdesc<SWB>(base + 2 * S::A_BYTES + off);
                             const unsigned long long bl = sdesc<SWB>(base + 2 * S::A_BYTES + S::B_BYTES + off);
-                            mma_tf32(db, ah, bh, id, (kb > kb0 || k > 0) ? 1u : 0u);
-                            mma_tf32(ds, al, bh, id, (!SEP || kb > ks0 || k > 0) ? 1u : 0u);
-                            mma_tf32(ds, ah, bl, id, 1u);
+                            const uint32_t acc0 = (kb > kb0 || k > 0) ? 1u : 0u;
+                            const uint32_t acc1 = (!SEP || kb > ks0 || k > 0) ? 1u : 0u;
+                            if constexpr (WIDE) {
+                                mma_tf32(db, ah, bh, id_wide, acc0);      // [hi*hi | hi*lo]
+                                mma_tf32(db, al, bh, id, 1u);             // + lo*hi
+                            } else if constexpr (CG == 2) {
+                                mma_tf32_pair(db, ah, bh, id, acc0);
+                                mma_tf32_pair(ds, al, bh, id, acc1);
+                                mma_tf32_pair(ds, ah, bl, id, 1u);
+                            } else {
+                                mma_tf32(db, ah, bh, id, acc0);
+                                mma_tf32(ds, al, bh, id, acc1);
+                                mma_tf32(ds, ah, bl, id, 1u);
+                            }
                         }
-                        mma_commit(empty0 + 8 * stage);
+                        if constexpr (CG == 2) mma_commit_pair(empty0 + 8 * stage);
+                        else mma_commit(empty0 + 8 * stage);
                         if (++stage == STAGES) { stage = 0; phase ^= 1; }
                     }
-                    if (ok) mma_commit(cfull0 + 8 * b);
+                    if (ok) {
+                        if constexpr (CG == 2) mma_commit_pair(cfull0 + 8 * b);
+                        else mma_commit(cfull0 + 8 * b);
+                    }
                 }
-                if (SEP && ok) mma_commit(sfull0 + 8 * ts);
+                if (SEP && ok) {
+                    if constexpr (CG == 2) mma_commit_pair(sfull0 + 8 * ts);
+                    else mma_commit(sfull0 + 8 * ts);
+                }
             }
             // Every MMA issued above has retired once this barrier flips.
-            mma_commit(drain);
+            if constexpr (CG == 2) mma_commit_pair_local(drain);
+            else mma_commit(drain);
             bar_wait(drain, 0, abort, err, 5, false);
         }
         __syncwarp();
     } else {
         const int q = warp & 3;                    // TMEM lanes 32q .. 32q+31 = tile rows
-        const int h = (warp - 2) >> 2;             // column half of the tile
+        const int h = (warp - 2) >> 2;             // column group of the tile
         const uint32_t lane_cols = ((uint32_t)(q * 32) << 16) + (uint32_t)(h * S::HALF);
         const int ew = warp - 2;                   // epilogue warp index: its stream-K flag and slot part
+        const int me = blockIdx.x;                 // this CTA's stream-K slot
+        // chunk and tile buffers are released on the leader's barriers
+        const uint32_t cempty_r = CG == 2 ? peer_addr(cempty0, 0) : cempty0;
+        const uint32_t sempty_r = CG == 2 ? peer_addr(sempty0, 0) : sempty0;
         uint32_t chunk = 0;
         bool ok = true;
-        Sched sc(num_tiles, n_chunks, skm);
+        Sched sc(num_tiles, n_chunks, skm, P, p);
         Seg sg;
         for (int local = 0; ok && sc.next(sg); local++) {
             float acc[S::HALF];
@@ -618,43 +753,51 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                 const uint32_t b = chunk % NBUF;
                 if (!bar_wait(cfull0 + 8 * b, (chunk / NBUF) & 1, abort, err, 6)) { ok = false; break; }
                 fence_after();
-                drain_add<S::HALF, S::LDW>(tmem + lane_cols + b * (uint32_t)BN, acc);
+                if constexpr (WIDE) drain_add2<S::HALF>(tmem + lane_cols + b * CW, tmem + lane_cols + b * CW + BN, acc);
+                else drain_add<S::HALF, S::LDW>(tmem + lane_cols + b * CW, acc);
                 fence_before();
                 __syncwarp();
-                if (lane == 0) bar_arrive(cempty0 + 8 * b);
+                if (lane == 0) {
+                    if constexpr (CG == 2) bar_arrive_cluster(cempty_r + 8 * b);
+                    else bar_arrive(cempty_r + 8 * b);
+                }
             }
             if (!ok) break;
             if (SEP) {
                 const uint32_t ts = local & 1;
                 if (!bar_wait(sfull0 + 8 * ts, (local >> 1) & 1, abort, err, 7)) break;
                 fence_after();
-                drain_add<S::HALF, S::LDW>(tmem + lane_cols + (NBUF + ts) * (uint32_t)BN, acc);
+                drain_add<S::HALF, S::LDW>(tmem + lane_cols + (NBUF + ts) * CW, acc);
                 fence_before();
                 __syncwarp();
-                if (lane == 0) bar_arrive(sempty0 + 8 * ts);
+                if (lane == 0) {
+                    if constexpr (CG == 2) bar_arrive_cluster(sempty_r + 8 * ts);
+                    else bar_arrive(sempty_r + 8 * ts);
+                }
             }
-
             if (skm && sg.c0 > 0) {
                 // contributor: this warp's 32 x HALF partial sums to its part of
                 // the CTA's slot (column-major, so each column is one 128-byte
                 // line), then the flag the owner's matching warp waits on
-                float *slot = ws + ((size_t)blockIdx.x * EPI_W + ew) * 32 * S::HALF;
+                float *slot = ws + ((size_t)me * EPI_W + ew) * 32 * S::HALF;
 #pragma unroll
                 for (int j = 0; j < S::HALF; j++) slot[j * 32 + lane] = acc[j];
                 __threadfence();
                 __syncwarp();
-                if (lane == 0) st_release(flags + blockIdx.x * EPI_W + ew, 1);
+                if (lane == 0) st_release(flags + me * EPI_W + ew, 1);
                 continue;
             }
             if (skm && sg.c1 < n_chunks) {
-                // owner: add the contributors' partial sums in chunk order, then
-                // clear their flags for the next launch
+                // owner: add the contributors' partial sums in chunk order (the
+                // same-rank CTA of each contributing group), then clear their
+                // flags for the next launch
                 const long long end = (long long)(sg.tile - sc.R * sc.P + 1) * n_chunks;
-                for (int qq = blockIdx.x + 1; ok && qq < sc.P && sc.first(qq) < end; qq++) {
-                    if (sc.first(qq + 1) == sc.first(qq)) continue;          // a CTA with no units
-                    int *f = flags + qq * EPI_W + ew;
+                for (int qq = p + 1; ok && qq < sc.P && sc.first(qq) < end; qq++) {
+                    if (sc.first(qq + 1) == sc.first(qq)) continue;          // a group with no units
+                    const int other = qq * CG + (int)rank;
+                    int *f = flags + other * EPI_W + ew;
                     if (!flag_wait(f, abort, err, 8)) { ok = false; break; }
-                    const float *slot = ws + ((size_t)qq * EPI_W + ew) * 32 * S::HALF;
+                    const float *slot = ws + ((size_t)other * EPI_W + ew) * 32 * S::HALF;
 #pragma unroll
                     for (int j = 0; j < S::HALF; j++) acc[j] = __fadd_rn(acc[j], slot[j * 32 + lane]);
                     __syncwarp();
@@ -662,7 +805,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                 }
                 if (!ok) break;
             }
-            const int m0 = (sg.tile / n_tiles) * BM, n0 = (sg.tile % n_tiles) * BN;
+            const int m0 = (sg.tile / n_tiles) * CG * BM + (int)rank * BM, n0 = (sg.tile % n_tiles) * BN;
             epi_store_tile<S::HALF>(epi, acc, epi_stage + ew * (S::EPI_STAGE_BYTES / 4), m0 + q * 32,
                                     n0 + h * S::HALF, M, N);
         }
@@ -670,267 +813,13 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
 
     fence_before();
     __syncthreads();
+    if constexpr (CG == 2) cluster_sync();      // the leader's MMAs into this CTA's TMEM are done
     if (warp == 1) {
         fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(S::TMEM_COLS) : "memory");
-    }
-}
-
-// ------------------------------------------------------- CTA-pair variant
-// The same GEMM on pairs of CTAs (a cluster of 2, tcgen05 cta_group::2):
-// one 256 x 128 tile per pair, CTA r owning rows 128r..128r+127 of it. Each
-// CTA loads its own 128 rows of A and half of B (64 of the 128 columns), so a
-// stage is 48 KB instead of 64 KB and the ring is 4 deep. The even CTA is the
-// leader: its producer arms the stage barrier with the bytes of both CTAs,
-// both CTAs' TMA loads complete on that barrier, and one lane of the leader
-// issues the M=256 MMAs, committing to both CTAs' barriers at once. Each CTA
-// drains its own 128 TMEM lanes; the drains are acknowledged to the leader.
-
-__device__ __forceinline__ uint32_t cta_rank_in_cluster()
-{
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-// address of the same shared-memory offset in CTA `rank` of the cluster
-__device__ __forceinline__ uint32_t peer_addr(uint32_t addr, uint32_t rank)
-{
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-    return r;
-}
-__device__ __forceinline__ void bar_arrive_cluster(uint32_t cluster_addr)
-{
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-__device__ __forceinline__ void cluster_sync()
-{
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// TMA load into this CTA's shared memory whose bytes complete on the
-// leader's barrier (cluster address).
-__device__ __forceinline__ void tma_load_pair(uint32_t dst, const CUtensorMap *map, uint32_t bar_cluster, int x, int y)
-{
-    asm volatile("cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-                 " [%0], [%1, {%2, %3}], [%4];"
-                 ::"r"(dst), "l"((unsigned long long)map), "r"(x), "r"(y), "r"(bar_cluster) : "memory");
-}
-__device__ __forceinline__ void mma_tf32_pair(uint32_t d, unsigned long long a, unsigned long long b, uint32_t id, uint32_t acc)
-{
-    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                 "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
-                 ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc));
-}
-// commit the leader's MMAs to the barrier at this offset in both CTAs
-__device__ __forceinline__ void mma_commit_pair(uint32_t bar)
-{
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
-                 ::"r"(bar), "h"((unsigned short)3) : "memory");
-}
-// commit the leader's MMAs to one of its own barriers
-__device__ __forceinline__ void mma_commit_pair_local(uint32_t bar)
-{
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-
-template <int STAGES>
-struct PairShape {
-    static constexpr int BN = 128;                        // tile columns (both CTAs)
-    static constexpr uint32_t A_BYTES = BM * 32 * 4;      // this CTA's 128 rows, BK = 32
-    static constexpr uint32_t B_BYTES = (BN / 2) * 32 * 4; // this CTA's 64 columns
-    static constexpr uint32_t STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
-    static constexpr uint32_t TMEM_COLS = 512;
-    static constexpr int HALF = BN / 2;
-    static constexpr int NBAR = 2 * STAGES + 8 + 1;
-    static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 8 * NBAR + 16;
-};
-
-template <int STAGES>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
-gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
-                        const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
-                        int M, int N, int K, int chunk_kb, GemmEpi epi, int *err)
-{
-    using S = PairShape<STAGES>;
-    constexpr int BN = S::BN, BK = 32, SWB = 128;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *tiles = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t *bars = (uint64_t *)(tiles + (size_t)STAGES * S::STAGE_BYTES);
-    uint32_t *tmem_slot = (uint32_t *)(bars + S::NBAR);
-    volatile int *abort = (volatile int *)(tmem_slot + 1);
-
-    const uint32_t rank = cta_rank_in_cluster();
-    const bool leader = rank == 0;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-    const int n_tiles = (N + BN - 1) / BN;
-    const int num_tiles = ((M + 2 * BM - 1) / (2 * BM)) * n_tiles;
-    const int num_kb = (K + BK - 1) / BK;
-    const int n_chunks = (num_kb + chunk_kb - 1) / chunk_kb;
-    const uint32_t full0 = su32(bars), empty0 = su32(bars + STAGES);
-    const uint32_t cfull0 = su32(bars + 2 * STAGES), cempty0 = cfull0 + 16;
-    const uint32_t sfull0 = cempty0 + 16, sempty0 = sfull0 + 16, drain = sempty0 + 16;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; s++) {
-            bar_init(full0 + 8 * s, 1);
-            bar_init(empty0 + 8 * s, 1);
-        }
-        for (int b = 0; b < 2; b++) {
-            bar_init(cfull0 + 8 * b, 1);
-            bar_init(cempty0 + 8 * b, 2 * EPI_WARPS);    // epilogue warps of both CTAs
-            bar_init(sfull0 + 8 * b, 1);
-            bar_init(sempty0 + 8 * b, 2 * EPI_WARPS);
-        }
-        bar_init(drain, 1);
-        *abort = 0;
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
-                     ::"r"(su32(tmem_slot)), "r"(S::TMEM_COLS) : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-    }
-    fence_before();
-    cluster_sync();          // barriers initialised and TMEM allocated in both CTAs
-    fence_after();
-    const uint32_t tmem = *tmem_slot;
-
-    if (warp == 0) {
-        if (lane == 0) {
-            asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&a_hi) : "memory");
-            asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&a_lo) : "memory");
-            asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&b_hi) : "memory");
-            asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&b_lo) : "memory");
-            int stage = 0;
-            uint32_t phase = 0;
-            long issued = 0;
-            bool ok = true;
-            for (int t = pair; ok && t < num_tiles; t += npairs) {
-                const int m0 = (t / n_tiles) * 2 * BM + (int)rank * BM;
-                const int nb = (t % n_tiles) * BN + (int)rank * (BN / 2);
-                for (int kb = 0; kb < num_kb; kb++) {
-                    if (!bar_wait(empty0 + 8 * stage, phase ^ 1, abort, err, 1)) { ok = false; break; }
-                    const uint32_t fb = peer_addr(full0 + 8 * stage, 0);
-                    const uint32_t base = su32(tiles + (size_t)stage * S::STAGE_BYTES);
-                    if (leader) bar_expect_tx(full0 + 8 * stage, 2 * S::STAGE_BYTES);
-                    tma_load_pair(base, &a_hi, fb, kb * BK, m0);
-                    tma_load_pair(base + S::A_BYTES, &a_lo, fb, kb * BK, m0);
-                    tma_load_pair(base + 2 * S::A_BYTES, &b_hi, fb, kb * BK, nb);
-                    tma_load_pair(base + 2 * S::A_BYTES + S::B_BYTES, &b_lo, fb, kb * BK, nb);
-                    issued++;
-                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
-                }
-            }
-            // The leader lets the last fill of every stage land before exiting;
-            // the follower's copies complete on that same barrier.
-            if (leader)
-                for (int i = 1; i <= STAGES && i <= issued; i++) {
-                    int s = stage - i;
-                    uint32_t ph = phase;
-                    if (s < 0) { s += STAGES; ph ^= 1; }
-                    bar_wait(full0 + 8 * s, ph, abort, err, 2, false);
-                }
-        }
-        __syncwarp();
-    } else if (warp == 1) {
-        if (leader && lane == 0) {
-            const uint32_t id = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                                ((uint32_t)((2 * BM) >> 4) << 24);
-            int stage = 0;
-            uint32_t phase = 0, chunk = 0;
-            bool ok = true;
-            int local = 0;
-            for (int t = pair; ok && t < num_tiles; t += npairs, local++) {
-                const uint32_t ts = local & 1;
-                if (!bar_wait(sempty0 + 8 * ts, ((local >> 1) & 1) ^ 1, abort, err, 3)) break;
-                fence_after();
-                const uint32_t ds = tmem + (2 + ts) * (uint32_t)BN;
-                for (int c = 0; ok && c < n_chunks; c++, chunk++) {
-                    const uint32_t b = chunk & 1;
-                    if (!bar_wait(cempty0 + 8 * b, ((chunk >> 1) & 1) ^ 1, abort, err, 3)) { ok = false; break; }
-                    fence_after();
-                    const uint32_t db = tmem + b * (uint32_t)BN;
-                    const int kb0 = c * chunk_kb, kb1 = min(kb0 + chunk_kb, num_kb);
-                    for (int kb = kb0; kb < kb1; kb++) {
-                        if (!bar_wait(full0 + 8 * stage, phase, abort, err, 4)) { ok = false; break; }
-                        fence_after();
-                        const uint32_t base = su32(tiles + (size_t)stage * S::STAGE_BYTES);
-#pragma unroll
-                        for (int k = 0; k < BK / 8; k++) {
-                            const uint32_t off = (uint32_t)k * 32u;
-                            const unsigned long long ah = sdesc<SWB>(base + off);
-                            const unsigned long long al = sdesc<SWB>(base + S::A_BYTES + off);
-                            const unsigned long long bh = sdesc<SWB>(base + 2 * S::A_BYTES + off);
-                            const unsigned long long bl = sdesc<SWB>(base + 2 * S::A_BYTES + S::B_BYTES + off);
-                            mma_tf32_pair(db, ah, bh, id, (kb > kb0 || k > 0) ? 1u : 0u);
-                            mma_tf32_pair(ds, al, bh, id, (kb > 0 || k > 0) ? 1u : 0u);
-                            mma_tf32_pair(ds, ah, bl, id, 1u);
-                        }
-                        mma_commit_pair(empty0 + 8 * stage);
-                        if (++stage == STAGES) { stage = 0; phase ^= 1; }
-                    }
-                    if (ok) mma_commit_pair(cfull0 + 8 * b);
-                }
-                if (ok) mma_commit_pair(sfull0 + 8 * ts);
-            }
-            // Every MMA issued above has retired once this barrier flips.
-            mma_commit_pair_local(drain);
-            bar_wait(drain, 0, abort, err, 5, false);
-        }
-        __syncwarp();
-    } else {
-        const int q = warp & 3;
-        const int h = (warp - 2) >> 2;
-        const uint32_t lane_cols = ((uint32_t)(q * 32) << 16) + (uint32_t)(h * S::HALF);
-        const uint32_t cempty_l = peer_addr(cempty0, 0), sempty_l = peer_addr(sempty0, 0);
-        uint32_t chunk = 0;
-        bool ok = true;
-        int local = 0;
-        for (int t = pair; ok && t < num_tiles; t += npairs, local++) {
-            float acc[S::HALF];
-#pragma unroll
-            for (int j = 0; j < S::HALF; j++) acc[j] = 0.0f;
-            for (int c = 0; c < n_chunks; c++, chunk++) {
-                const uint32_t b = chunk & 1;
-                if (!bar_wait(cfull0 + 8 * b, (chunk >> 1) & 1, abort, err, 6)) { ok = false; break; }
-                fence_after();
-                drain_add<S::HALF>(tmem + lane_cols + b * (uint32_t)BN, acc);
-                fence_before();
-                __syncwarp();
-                if (lane == 0) bar_arrive_cluster(cempty_l + 8 * b);
-            }
-            if (!ok) break;
-            const uint32_t ts = local & 1;
-            if (!bar_wait(sfull0 + 8 * ts, (local >> 1) & 1, abort, err, 7)) break;
-            fence_after();
-            drain_add<S::HALF>(tmem + lane_cols + (2 + ts) * (uint32_t)BN, acc);
-            fence_before();
-            __syncwarp();
-            if (lane == 0) bar_arrive_cluster(sempty_l + 8 * ts);
-
-            const int m0 = (t / n_tiles) * 2 * BM + (int)rank * BM, n0 = (t % n_tiles) * BN;
-            const int r = m0 + q * 32 + lane;
-            if (r < M) {
-                const int src_row = r % epi.rgroup + epi.roff;
-                const size_t dst_row = (size_t)(r / epi.rgroup) * epi.rstride + epi.roff + r % epi.rgroup;
-                const int nb = n0 + h * S::HALF;
-#pragma unroll
-                for (int j = 0; j < S::HALF; j += 4) {
-                    const int n = nb + j;
-                    if (n < N)
-                        epi_store4(epi, src_row, dst_row, n, min(4, N - n), acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
-                }
-            }
-        }
-    }
-
-    fence_before();
-    __syncthreads();
-    cluster_sync();          // the leader's MMAs into this CTA's TMEM are done
-    if (warp == 1) {
-        fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(S::TMEM_COLS) : "memory");
+        if constexpr (CG == 2)
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(S::TMEM_COLS) : "memory");
+        else
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(S::TMEM_COLS) : "memory");
     }
 }
 
@@ -979,22 +868,23 @@ struct Cfg {
     int bn, bk, stages;
     size_t smem;
     const void *fn;
-    bool pair;          // CTA-pair kernel: 256-row tiles, B boxes of bn/2 rows
+    int cg;             // CTAs per tile: 2 = a CTA pair (256-row tiles, B boxes of bn/2 rows)
     int threads;
     bool sep;           // separate small-term accumulators (no stream-K)
     int epi_warps;
 };
 
-#define TCG_CFG(BN, BK, ST, EW, SEP)                                                            \
-    { BN, BK, ST, Shape<BN, BK, ST, EW, SEP>::SMEM, (const void *)gemm_tf32x3_kernel<BN, BK, ST, EW, SEP>, \
-      false, Shape<BN, BK, ST, EW, SEP>::THREADS, SEP, EW }
+#define TCG_CFG(BN, BK, ST, EW, ACC, CG)                                                                   \
+    { BN, BK, ST, Shape<BN, BK, ST, EW, ACC, CG>::SMEM, (const void *)gemm_tf32x3_kernel<BN, BK, ST, EW, ACC, CG>, \
+      CG, Shape<BN, BK, ST, EW, ACC, CG>::THREADS, ACC == ACC_SEP, EW }
 const Cfg CFGS[] = {
-    TCG_CFG(128, 32, 3, 8, true), TCG_CFG(64, 32, 4, 8, true), TCG_CFG(128, 16, 6, 8, true),
-    TCG_CFG(64, 16, 8, 8, true), TCG_CFG(96, 32, 3, 8, true), TCG_CFG(96, 16, 7, 8, true),
-    { 128, 32, 4, PairShape<4>::SMEM, (const void *)gemm_tf32x3_pair_kernel<4>, true, NUM_THREADS, true, EPI_WARPS },
-    // 128 x 256 tiles: the small terms fold into the chunk buffers
-    TCG_CFG(256, 16, 4, 16, false), TCG_CFG(256, 32, 2, 16, false),
-    TCG_CFG(128, 32, 3, 8, false), TCG_CFG(128, 32, 3, 16, true), TCG_CFG(128, 32, 3, 16, false),
+    TCG_CFG(128, 32, 3, 8, ACC_SEP, 1), TCG_CFG(64, 32, 4, 8, ACC_SEP, 1), TCG_CFG(128, 16, 6, 8, ACC_SEP, 1),
+    TCG_CFG(64, 16, 8, 8, ACC_SEP, 1), TCG_CFG(96, 32, 3, 8, ACC_SEP, 1), TCG_CFG(96, 16, 7, 8, ACC_SEP, 1),
+    TCG_CFG(128, 32, 4, 16, ACC_FOLD, 2),                               // CTA pair, folded
+    TCG_CFG(256, 16, 4, 16, ACC_FOLD, 1), TCG_CFG(256, 32, 2, 16, ACC_FOLD, 1),
+    TCG_CFG(128, 32, 3, 8, ACC_FOLD, 1), TCG_CFG(128, 32, 3, 16, ACC_SEP, 1), TCG_CFG(128, 32, 3, 16, ACC_FOLD, 1),
+    TCG_CFG(128, 32, 4, 16, ACC_SEP, 2),                                // CTA pair, separate small terms
+    TCG_CFG(128, 32, 3, 16, ACC_WIDE, 1), TCG_CFG(128, 32, 3, 8, ACC_WIDE, 1),
 };
 #undef TCG_CFG
 constexpr int NCFG = sizeof(CFGS) / sizeof(CFGS[0]);
@@ -1016,18 +906,14 @@ int choose_cfg(int M, int N)
 
 int gemm_throughput_cfg()
 {
-    // The small terms folded into four TMEM chunk buffers, which lets the last
-    // partial wave of tiles be split by stream-K: the fastest shape on every
-    // ViT GEMM (three truncating tensor-core adds per K-step in a chunk instead
-    // of one: ~1e-6 of max|C| at K = 3072). BN=64 or 96 tiles, the CTA pair
-    // and 128 x 256 tiles measured slower.
+    // ACC_WIDE 128 x 128 tiles, 16 epilogue warps: two MMA instructions per
+    // K-step (an N = 256 one for hi*hi | hi*lo, an N = 128 one for lo*hi), and
+    // stream-K capable. 10-15% faster than the three N = 128 MMAs of the other
+    // modes on every ViT GEMM, ~1e-6 of max|C| at K = 3072. BN = 64 or 96
+    // tiles, CTA pairs and 128 x 256 tiles measured slower.
     if (g_force_cfg >= 0 && g_force_cfg < NCFG) return g_force_cfg;
-    return 11;
+    return 13;
 }
-
-namespace {
-
-}  // namespace
 
 // K-elements accumulated in TMEM between two drains into fp32 registers.
 int g_chunk_k = 256;
@@ -1075,7 +961,7 @@ bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b
     const int cfg = force_cfg >= 0 ? force_cfg : choose_cfg(M, N);
     if (cfg >= NCFG) return fail("gemm_plan: no configuration %d", cfg);
     const Cfg &c = CFGS[cfg];
-    const int b_rows = c.pair ? c.bn / 2 : c.bn;         // B box: this CTA's share of the tile columns
+    const int b_rows = c.bn / c.cg;                     // B box: this CTA's share of the tile columns
     if (!encode_kmajor(&p.a_hi, a_hi, M, K, BM, c.bk) || !encode_kmajor(&p.a_lo, a_lo, M, K, BM, c.bk) ||
         !encode_kmajor(&p.b_hi, b_hi, N, K, b_rows, c.bk) || !encode_kmajor(&p.b_lo, b_lo, N, K, b_rows, c.bk))
         return false;
@@ -1091,7 +977,8 @@ bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b
                     !(epi.rowadd && epi.residual);
     }
     const int sms = ctx().sms > 0 ? ctx().sms : 148;
-    if (c.pair) {           // one cluster of two CTAs per 256-row tile, as many as fit at once
+    int groups = sms;        // tile groups resident at once: CTAs, or CTA pairs
+    if (c.cg == 2) {
         static int max_clusters[64];
         const int dev = ctx().device & 63;
         if (!max_clusters[dev]) {
@@ -1101,7 +988,7 @@ bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b
             at.id = cudaLaunchAttributeClusterDimension;
             at.val.clusterDim.x = 2; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
             lc.gridDim = dim3(2);
-            lc.blockDim = dim3(NUM_THREADS);
+            lc.blockDim = dim3(c.threads);
             lc.dynamicSmemBytes = c.smem;
             lc.attrs = &at;
             lc.numAttrs = 1;
@@ -1112,27 +999,25 @@ bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b
             }
             max_clusters[dev] = n < sms / 2 ? n : sms / 2;
         }
-        const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + c.bn - 1) / c.bn);
-        p.grid = 2 * (tiles < max_clusters[dev] ? tiles : max_clusters[dev]);
-    } else {
-        const int tiles = ((M + BM - 1) / BM) * ((N + c.bn - 1) / c.bn);
-        p.grid = tiles < sms ? tiles : sms;
-        // stream-K for a partial last wave; the grid then has room for every
-        // chunk unit when there is less than one wave of tiles
-        // Worth it when the last wave leaves at least half the SMs idle, or
-        // when a tile has many chunks (fine units); with 2-5 chunks and a
-        // fuller last wave the partial-sum hand-over costs what it saves.
-        const int chunks = (K + g_chunk_k - 1) / g_chunk_k;
-        const int last = tiles % sms;
-        const bool pays = last <= sms / 2 || chunks >= 6;
-        if (g_streamk && work && work->ws && work->flags && !c.sep && last != 0 && chunks > 1 && pays) {
-            const long units = (long)tiles * chunks;
-            const int grid = tiles >= sms ? sms : (int)(units < sms ? units : sms);
-            if (grid <= work->ctas) {
-                p.grid = grid;
-                p.sk = 1;
-                p.work = *work;
-            }
+        groups = max_clusters[dev];
+    }
+    const int tiles = ((M + c.cg * BM - 1) / (c.cg * BM)) * ((N + c.bn - 1) / c.bn);
+    p.grid = c.cg * (tiles < groups ? tiles : groups);
+    // Stream-K for a partial last wave; the grid then has room for every chunk
+    // unit when there is less than one wave of tiles. Worth it when the last
+    // wave leaves at least half the SMs idle, or when a tile has many chunks
+    // (fine units); with 2-5 chunks and a fuller last wave the partial-sum
+    // hand-over costs what it saves.
+    const int chunks = (K + g_chunk_k - 1) / g_chunk_k;
+    const int last = tiles % groups;
+    const bool pays = last <= groups / 2 || chunks >= 6;
+    if (g_streamk && work && work->ws && work->flags && !c.sep && last != 0 && chunks > 1 && pays) {
+        const long units = (long)tiles * chunks;
+        const int g = tiles >= groups ? groups : (int)(units < groups ? units : groups);
+        if (c.cg * g <= work->ctas) {
+            p.grid = c.cg * g;
+            p.sk = 1;
+            p.work = *work;
         }
     }
     return true;
@@ -1156,7 +1041,21 @@ bool gemm_run(const GemmPlan &p, cudaStream_t s, int *err)
     void *args[] = { (void *)&p.a_hi, (void *)&p.a_lo, (void *)&p.b_hi, (void *)&p.b_lo,
                      (void *)&p.M, (void *)&p.N, (void *)&p.K, (void *)&chunk_kb, (void *)&p.epi, (void *)&err,
                      (void *)&ws, (void *)&flags, (void *)&sk };
-    TCG_CUDA(cudaLaunchKernel(c.fn, dim3(p.grid), dim3(c.threads), args, c.smem, s));
+    if (c.cg == 2) {
+        cudaLaunchConfig_t lc = {};
+        cudaLaunchAttribute at;
+        at.id = cudaLaunchAttributeClusterDimension;
+        at.val.clusterDim.x = 2; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
+        lc.gridDim = dim3(p.grid);
+        lc.blockDim = dim3(c.threads);
+        lc.dynamicSmemBytes = c.smem;
+        lc.stream = s;
+        lc.attrs = &at;
+        lc.numAttrs = 1;
+        TCG_CUDA(cudaLaunchKernelExC(&lc, c.fn, args));
+    } else {
+        TCG_CUDA(cudaLaunchKernel(c.fn, dim3(p.grid), dim3(c.threads), args, c.smem, s));
+    }
     return true;
 }
 

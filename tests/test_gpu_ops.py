@@ -128,7 +128,7 @@ def test_mha_vs_oracle(dev, T, H, HD):
 SHAPES = [(1, 64, 4), (127, 100, 12), (129, 200, 588), (300, 768, 768), (50, 2304, 768), (261, 130, 3072)]
 
 
-@pytest.mark.parametrize("cfg", [0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, -2])
+@pytest.mark.parametrize("cfg", [0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, -2])
 @pytest.mark.parametrize("M,N,K", SHAPES)
 def test_linear_every_config(dev, cfg, M, N, K):
     L = tcg.lib()
