@@ -202,15 +202,17 @@ matvec_kq_kernel(const uint8_t *__restrict__ W, const float *__restrict__ x, flo
 
 // ----------------------------------------------------- streaming matvec
 // Persistent CTAs of 16 warps, one per SM. x stays in shared memory for the
-// whole launch (for Q4_K also the sum of every 8 consecutive x, for the min
-// term). Every warp streams its weight segments (a quarter row of Q4_K, a
-// whole row of Q6_K) through a two-slot cp.async ring and computes one slot
-// while the next lands. A superblock is handled by a half-warp, 16 weights
-// per lane: the quant bytes are turned into floats 2^23 + q with byte
-// permutes, shifted back exactly with packed f32x2 adds, and dotted with x
-// by packed f32x2 FMAs:
-//   Q4_K  sum (a q - c) x  =  a * sum(q x) - c * sum(x)   per 8 weights
-//   Q6_K  sum (d sc) q x   =  (d sc) * sum(q x)
+// whole launch, its float4 units XOR-swizzled so that the x loads of a warp
+// spread over all eight 16-byte bank groups (for Q4_K also the sum of every 16
+// consecutive x, for the min term). Every warp streams its weight segments (a
+// part of a row of Q4_K, a whole row of Q6_K) through a two-slot cp.async ring
+// and computes one slot while the next lands. Eight lanes share a superblock,
+// 32 weights per lane, and a warp works on four consecutive superblocks at a
+// time. The quant bytes are turned into floats 2^23 + q with byte permutes,
+// shifted back exactly with packed f32x2 adds, and dotted with x by packed
+// f32x2 FMAs:
+//   Q4_K  sum (a q - c) x  =  a * sum(q x) - c * sum(x)   per 16 weights
+//   Q6_K  sum (d sc) q x   =  (d sc) * sum(q x)           per 8 weights
 constexpr int MV_WARPS = 16;
 typedef unsigned long long u64;
 
@@ -266,11 +268,42 @@ __device__ __forceinline__ uint2 lds8_unaligned(const uint8_t *p)
     return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
 }
 
-__device__ __forceinline__ float sb_dot_q4k(const uint8_t *blk, int l16, const float *xs, const float *x8, int k0)
+// x is stored by float4 unit u at u ^ swz(u): Q4_K lanes differ in u's bits
+// 2 (half of a 32-weight group), 4-5 (group) and 6-7 (superblock); Q6_K lanes
+// in bits 1-2, 5 and 6-7. XOR-ing the bank-group bits 0-2 with bits 4-6 (Q4_K)
+// or 5-7 (Q6_K) leaves at most four distinct units per bank group in a warp's
+// float4 load, the minimum for 512 bytes.
+template <int TYPE>
+__device__ __forceinline__ int xswz(int u)
 {
-    const int g = l16 >> 2, p = (l16 & 3) * 8;
+    return TYPE == GGML_TYPE_Q4_K ? u ^ ((u >> 4) & 7) : u ^ ((u >> 5) & 7);
+}
+template <int TYPE>
+__device__ __forceinline__ ulonglong2 ldx(const float *xs, int k)
+{
+    return reinterpret_cast<const ulonglong2 *>(xs)[xswz<TYPE>(k >> 2)];
+}
+
+// sum_i (v_i - off) x_i over the 8 bytes v of (w0, w1) with x[0..8) in xa, xb;
+// neg_off2 holds -(2^23 + off) twice.
+__device__ __forceinline__ float dot8x(uint32_t w0, uint32_t w1, u64 neg_off2, ulonglong2 xa, ulonglong2 xb)
+{
+    u64 acc = 0ull;
+    acc = fma2(add2(magic2(w0, 0), neg_off2), xa.x, acc);
+    acc = fma2(add2(magic2(w0, 2), neg_off2), xa.y, acc);
+    acc = fma2(add2(magic2(w1, 0), neg_off2), xb.x, acc);
+    acc = fma2(add2(magic2(w1, 2), neg_off2), xb.y, acc);
+    return __uint_as_float((uint32_t)acc) + __uint_as_float((uint32_t)(acc >> 32));
+}
+
+// Lane j (0..7) of a Q4_K superblock at k0: the 16 bytes 32g + 16hh of its
+// quants (g = j / 2, hh = j % 2) hold weights 64g + 16hh + i of sub-block 2g
+// (low nibbles) and 64g + 32 + 16hh + i of sub-block 2g + 1 (high nibbles).
+__device__ __forceinline__ float lane_dot_q4k(const uint8_t *blk, int j, const float *xs, const float *x16, int k0)
+{
+    const int g = j >> 1, hh = j & 1;
     const uint4 hd = *reinterpret_cast<const uint4 *>(blk);
-    const uint2 q = *reinterpret_cast<const uint2 *>(blk + 16 + 32 * g + p);
+    const uint4 q = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * g + 16 * hh);
     const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFFu)));
     const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
     // 6-bit scale / min of sub-blocks 2g (lo nibbles) and 2g+1 (hi nibbles)
@@ -286,33 +319,47 @@ __device__ __forceinline__ float sb_dot_q4k(const uint8_t *blk, int l16, const f
         c[u] = dmin * (float)mn;
     }
     const u64 neg = 0xCB000000CB000000ull;          // (-2^23, -2^23)
-    const int xo = k0 + 64 * g + p;
-    const float dl = dot8(q.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, neg, xs + xo);
-    const float dh = dot8((q.x >> 4) & 0x0F0F0F0Fu, (q.y >> 4) & 0x0F0F0F0Fu, neg, xs + xo + 32);
-    float r = a[0] * dl;
-    r = fmaf(-c[0], x8[xo >> 3], r);
-    r = fmaf(a[1], dh, r);
-    return fmaf(-c[1], x8[(xo + 32) >> 3], r);
+    const int xo = k0 + 64 * g + 16 * hh;
+    const uint32_t w[4] = { q.x, q.y, q.z, q.w };
+    float sl = 0.0f, sh = 0.0f;
+#pragma unroll
+    for (int m = 0; m < 4; m += 2) {
+        const uint32_t l0 = w[m] & 0x0F0F0F0Fu, l1 = w[m + 1] & 0x0F0F0F0Fu;
+        const uint32_t h0 = (w[m] >> 4) & 0x0F0F0F0Fu, h1 = (w[m + 1] >> 4) & 0x0F0F0F0Fu;
+        sl += dot8x(l0, l1, neg, ldx<GGML_TYPE_Q4_K>(xs, xo + 4 * m), ldx<GGML_TYPE_Q4_K>(xs, xo + 4 * m + 4));
+        sh += dot8x(h0, h1, neg, ldx<GGML_TYPE_Q4_K>(xs, xo + 32 + 4 * m), ldx<GGML_TYPE_Q4_K>(xs, xo + 36 + 4 * m));
+    }
+    float r = a[0] * sl;
+    r = fmaf(-c[0], x16[xo >> 4], r);
+    r = fmaf(a[1], sh, r);
+    return fmaf(-c[1], x16[(xo + 32) >> 4], r);
 }
 
-__device__ __forceinline__ float sb_dot_q6k(const uint8_t *blk, int l16, const float *xs, int k0)
+// Lane j (0..7) of a Q6_K superblock at k0: half h = j / 4 of the superblock,
+// l0 = 8 (j % 4); its 8 bytes ql[64h + l0], ql[64h + 32 + l0] and
+// qh[32h + l0] give the weights 128h + l0 + 32c + i (c = 0..3, i < 8), each
+// group of 8 in one sub-block of 16.
+__device__ __forceinline__ float lane_dot_q6k(const uint8_t *blk, int j, const float *xs, int k0)
 {
-    const int h = l16 >> 3, rr = (l16 >> 2) & 1, l0 = (l16 & 3) * 8;
-    const uint2 ql = lds8_unaligned(blk + 64 * h + 32 * rr + l0);
+    const int h = j >> 2, l0 = (j & 3) * 8;
+    const uint2 q0 = lds8_unaligned(blk + 64 * h + l0);
+    const uint2 q1 = lds8_unaligned(blk + 64 * h + 32 + l0);
     const uint2 qh = lds8_unaligned(blk + 128 + 32 * h + l0);
     const float d = __half2float(__ushort_as_half((unsigned short)(blk[208] | (blk[209] << 8))));
-    const float sa = d * (float)(int8_t)blk[192 + 8 * h + 2 * rr + (l0 >> 4)];
-    const float sb = d * (float)(int8_t)blk[192 + 8 * h + 2 * (rr + 2) + (l0 >> 4)];
+    const int sb = 192 + 8 * h + (l0 >> 4);
     const u64 neg = 0xCB000020CB000020ull;          // (-(2^23 + 32), twice)
-    const uint32_t s0 = 2 * rr, s1 = 2 * rr + 4;
-    const uint32_t a0 = (ql.x & 0x0F0F0F0Fu) | (((qh.x >> s0) & 0x03030303u) << 4);
-    const uint32_t a1 = (ql.y & 0x0F0F0F0Fu) | (((qh.y >> s0) & 0x03030303u) << 4);
-    const uint32_t b0 = ((ql.x >> 4) & 0x0F0F0F0Fu) | (((qh.x >> s1) & 0x03030303u) << 4);
-    const uint32_t b1 = ((ql.y >> 4) & 0x0F0F0F0Fu) | (((qh.y >> s1) & 0x03030303u) << 4);
-    const int xo = k0 + 128 * h + 32 * rr + l0;
-    const float da = dot8(a0, a1, neg, xs + xo);
-    const float db = dot8(b0, b1, neg, xs + xo + 64);
-    return fmaf(sb, db, sa * da);
+    const int xo = k0 + 128 * h + l0;
+    float r = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        const uint2 lo = (c & 1) ? q1 : q0;
+        const int ls = (c >> 1) * 4, hs = 2 * c;
+        const uint32_t a0 = ((lo.x >> ls) & 0x0F0F0F0Fu) | (((qh.x >> hs) & 0x03030303u) << 4);
+        const uint32_t a1 = ((lo.y >> ls) & 0x0F0F0F0Fu) | (((qh.y >> hs) & 0x03030303u) << 4);
+        const float dd = d * (float)(int8_t)blk[sb + 2 * c];
+        r = fmaf(dd, dot8x(a0, a1, neg, ldx<GGML_TYPE_Q6_K>(xs, xo + 32 * c), ldx<GGML_TYPE_Q6_K>(xs, xo + 32 * c + 4)), r);
+    }
+    return r;
 }
 
 template <int TYPE, int SEGS>
@@ -324,13 +371,13 @@ matvec_stream_kernel(const uint8_t *__restrict__ W, const float *__restrict__ x,
     constexpr int RPI = MV_WARPS / SEGS;                 // rows per CTA iteration
     extern __shared__ uint4 sm4[];
     float *xs = reinterpret_cast<float *>(sm4);
-    float *x8 = xs + K;
+    float *x16 = xs + K;
     const int bpr = K / QK, bps = bpr / SEGS;            // superblocks per row / segment
     const int seg_bytes = bps * BB;
-    uint8_t *ring = reinterpret_cast<uint8_t *>(x8 + ((K / 8 + 3) & ~3));
+    uint8_t *ring = reinterpret_cast<uint8_t *>(x16 + ((K / 16 + 3) & ~3));
     __shared__ float part[MV_WARPS];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int half = lane >> 4, l16 = lane & 15;
+    const int sbi = lane >> 3, j8 = lane & 7;           // superblock of the four, lane within it
     const int seg = wid % SEGS, rloc = wid / SEGS;
     uint8_t *slot[2] = { ring + (size_t)wid * 2 * seg_bytes, ring + (size_t)wid * 2 * seg_bytes + seg_bytes };
 
@@ -346,17 +393,33 @@ matvec_stream_kernel(const uint8_t *__restrict__ W, const float *__restrict__ x,
 
     int it = blockIdx.x;
     prefetch(it, slot[0]);
-    for (int i = threadIdx.x; i < K / 4; i += blockDim.x)
-        reinterpret_cast<float4 *>(xs)[i] = __ldg(reinterpret_cast<const float4 *>(x) + i);
+    // x into shared memory: every load of a thread issued before its stores
+    for (int i0 = threadIdx.x; i0 < K / 4; i0 += 8 * blockDim.x) {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int i = i0 + u * blockDim.x;
+            if (i < K / 4) v[u] = __ldg(reinterpret_cast<const float4 *>(x) + i);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int i = i0 + u * blockDim.x;
+            if (i < K / 4) reinterpret_cast<float4 *>(xs)[xswz<TYPE>(i)] = v[u];
+        }
+    }
     __syncthreads();
-    if (TYPE == GGML_TYPE_Q4_K)
-        for (int i = threadIdx.x; i < K / 8; i += blockDim.x) {
+    if (TYPE == GGML_TYPE_Q4_K) {
+        for (int i = threadIdx.x; i < K / 16; i += blockDim.x) {
             float s = 0.0f;
 #pragma unroll
-            for (int j = 0; j < 8; j++) s += xs[8 * i + j];
-            x8[i] = s;
+            for (int u = 0; u < 4; u++) {
+                const float4 v = reinterpret_cast<const float4 *>(xs)[xswz<TYPE>(4 * i + u)];
+                s += v.x; s += v.y; s += v.z; s += v.w;
+            }
+            x16[i] = s;
         }
-    __syncthreads();
+        __syncthreads();
+    }
 
     for (int n = 0; it * RPI < N; it += gridDim.x, n++) {
         const int nxt = it + gridDim.x;
@@ -367,12 +430,10 @@ matvec_stream_kernel(const uint8_t *__restrict__ W, const float *__restrict__ x,
         const int row = it * RPI + rloc;
         float acc = 0.0f;
         if (row < N) {
-            for (int b = half; b < bps + half; b += 2) {
-                if (b < bps) {
-                    const int k0 = (seg * bps + b) * QK;
-                    if (TYPE == GGML_TYPE_Q4_K) acc += sb_dot_q4k(buf + (size_t)b * BB, l16, xs, x8, k0);
-                    else acc += sb_dot_q6k(buf + (size_t)b * BB, l16, xs, k0);
-                }
+            for (int b = sbi; b < bps; b += 4) {
+                const int k0 = (seg * bps + b) * QK;
+                if (TYPE == GGML_TYPE_Q4_K) acc += lane_dot_q4k(buf + (size_t)b * BB, j8, xs, x16, k0);
+                else acc += lane_dot_q6k(buf + (size_t)b * BB, j8, xs, k0);
             }
         }
         __syncwarp();
@@ -401,7 +462,7 @@ static bool try_matvec_stream(float *y, const void *W, const float *x, int N, in
     const int bpr = K / QK;
     if (bpr % SEGS || ((size_t)(bpr / SEGS) * BB) % 16 || ((uintptr_t)W & 15)) return false;
     const size_t ring = (size_t)MV_WARPS * 2 * (bpr / SEGS) * BB;
-    const size_t smem = (size_t)K * 4 + (size_t)((K / 8 + 3) & ~3) * 4 + ring;
+    const size_t smem = (size_t)K * 4 + (size_t)((K / 16 + 3) & ~3) * 4 + ring;
     if (smem > 200 * 1024) return false;
     static unsigned done[64];
     const int dev = ctx().device & 63;

@@ -20,6 +20,19 @@ __device__ __forceinline__ void put(const OutSpec &o, size_t row, int col, float
     }
 }
 
+__device__ __forceinline__ void put4(const OutSpec &o, size_t row, int col, const float (&v)[4])
+{
+    const size_t i = row * (size_t)o.ld + col;
+    if (o.plain) *reinterpret_cast<float4 *>(o.plain + i) = make_float4(v[0], v[1], v[2], v[3]);
+    if (o.hi) {
+        float h[4], l[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) split_tf32(v[j], h[j], l[j]);
+        *reinterpret_cast<float4 *>(o.hi + i) = make_float4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<float4 *>(o.lo + i) = make_float4(l[0], l[1], l[2], l[3]);
+    }
+}
+
 // ---------------------------------------------------------------- LayerNorm
 // One warp per row. Pass 1: double sum -> mean. Pass 2: double sum of
 // squared deviations -> biased variance. inv = (float)(1/sqrt(var+eps)) in
@@ -49,11 +62,78 @@ __global__ void layernorm_kernel(const float *x, int ld_in, const float *__restr
     }
 }
 
+// The same LayerNorm with the row held in registers: lane l owns the float4s
+// l, l + 32, ... (VPL of them, cols = 128 * VPL), read once and written once
+// as float4 (plain or tf32 hi/lo). Same arithmetic as layernorm_kernel; the
+// double sums run in another order.
+template <int VPL>
+__global__ void __launch_bounds__(256, 4)
+layernorm_vec_kernel(const float *x, int ld_in, const float *__restrict__ g, const float *__restrict__ b, int rows,
+                     float eps, OutSpec out)
+{
+    constexpr int cols = 128 * VPL;
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const float4 *in = reinterpret_cast<const float4 *>(x + (size_t)row * ld_in);
+    float4 v[VPL];
+#pragma unroll
+    for (int i = 0; i < VPL; i++) v[i] = in[lane + 32 * i];
+    double s = 0.0;
+#pragma unroll
+    for (int i = 0; i < VPL; i++) s += ((double)v[i].x + (double)v[i].y) + ((double)v[i].z + (double)v[i].w);
+    const double mean = warp_sum(s) / (double)cols;
+    double ss = 0.0;
+#pragma unroll
+    for (int i = 0; i < VPL; i++) {
+        const double a = __dsub_rn((double)v[i].x, mean), bb = __dsub_rn((double)v[i].y, mean);
+        const double c = __dsub_rn((double)v[i].z, mean), d = __dsub_rn((double)v[i].w, mean);
+        ss = __dadd_rn(ss, __dadd_rn(__dadd_rn(__dmul_rn(a, a), __dmul_rn(bb, bb)),
+                                     __dadd_rn(__dmul_rn(c, c), __dmul_rn(d, d))));
+    }
+    const double var = warp_sum(ss) / (double)cols;
+    const float inv = (float)(1.0 / sqrt(var + (double)eps));
+#pragma unroll
+    for (int i = 0; i < VPL; i++) {
+        const int c = 4 * (lane + 32 * i);
+        float o[4] = { __fmul_rn((float)((double)v[i].x - mean), inv), __fmul_rn((float)((double)v[i].y - mean), inv),
+                       __fmul_rn((float)((double)v[i].z - mean), inv), __fmul_rn((float)((double)v[i].w - mean), inv) };
+        if (g) {
+            const float4 gg = *reinterpret_cast<const float4 *>(g + c);
+            o[0] = __fmul_rn(o[0], gg.x); o[1] = __fmul_rn(o[1], gg.y);
+            o[2] = __fmul_rn(o[2], gg.z); o[3] = __fmul_rn(o[3], gg.w);
+        }
+        if (b) {
+            const float4 bv = *reinterpret_cast<const float4 *>(b + c);
+            o[0] = __fadd_rn(o[0], bv.x); o[1] = __fadd_rn(o[1], bv.y);
+            o[2] = __fadd_rn(o[2], bv.z); o[3] = __fadd_rn(o[3], bv.w);
+        }
+        put4(out, row, c, o);
+    }
+}
+
 bool launch_layernorm(const float *x, int ld_in, const float *g, const float *b, int rows, int cols,
                       float eps, const OutSpec &out, cudaStream_t s)
 {
     if (rows <= 0) return true;
-    layernorm_kernel<<<ceil_div(rows, 8), 256, 0, s>>>(x, ld_in, g, b, rows, cols, eps, out);
+    const auto a16 = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
+    const bool vec = cols % 128 == 0 && cols <= 1024 && !(ld_in & 3) && !(out.ld & 3) && a16(x) && a16(g) &&
+                     a16(b) && a16(out.plain) && a16(out.hi) && a16(out.lo);
+    const unsigned grid = ceil_div(rows, 8);
+    if (vec) {
+        switch (cols / 128) {
+        case 1: layernorm_vec_kernel<1><<<grid, 256, 0, s>>>(x, ld_in, g, b, rows, eps, out); break;
+        case 2: layernorm_vec_kernel<2><<<grid, 256, 0, s>>>(x, ld_in, g, b, rows, eps, out); break;
+        case 3: layernorm_vec_kernel<3><<<grid, 256, 0, s>>>(x, ld_in, g, b, rows, eps, out); break;
+        case 4: layernorm_vec_kernel<4><<<grid, 256, 0, s>>>(x, ld_in, g, b, rows, eps, out); break;
+        case 5: layernorm_vec_kernel<5><<<grid, 256, 0, s>>>(x, ld_in, g, b, rows, eps, out); break;
+        case 6: layernorm_vec_kernel<6><<<grid, 256, 0, s>>>(x, ld_in, g, b, rows, eps, out); break;
+        case 7: layernorm_vec_kernel<7><<<grid, 256, 0, s>>>(x, ld_in, g, b, rows, eps, out); break;
+        default: layernorm_vec_kernel<8><<<grid, 256, 0, s>>>(x, ld_in, g, b, rows, eps, out); break;
+        }
+    } else {
+        layernorm_kernel<<<grid, 256, 0, s>>>(x, ld_in, g, b, rows, cols, eps, out);
+    }
     TCG_LAUNCHED();
     return true;
 }
@@ -140,19 +220,6 @@ __global__ void mha_kernel(const float *__restrict__ q, const float *__restrict_
 // Softmax is exact two-pass per row as in src/ops.c:129-139 (max, expf, double
 // sum, one reciprocal); the weighted sum runs over keys in order.
 constexpr int MHA_BQ = 64;
-
-__device__ __forceinline__ void put4(const OutSpec &o, size_t row, int col, const float (&v)[4])
-{
-    const size_t i = row * (size_t)o.ld + col;
-    if (o.plain) *reinterpret_cast<float4 *>(o.plain + i) = make_float4(v[0], v[1], v[2], v[3]);
-    if (o.hi) {
-        float h[4], l[4];
-#pragma unroll
-        for (int j = 0; j < 4; j++) split_tf32(v[j], h[j], l[j]);
-        *reinterpret_cast<float4 *>(o.hi + i) = make_float4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<float4 *>(o.lo + i) = make_float4(l[0], l[1], l[2], l[3]);
-    }
-}
 
 __global__ void __launch_bounds__(256)
 mha64_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
@@ -252,6 +319,129 @@ mha64_kernel(const float *__restrict__ q, const float *__restrict__ k, const flo
         if (4 * ty + i < nq) put4(out, base + q0 + 4 * ty + i, col + 4 * tx, o[i]);
 }
 
+// head_dim 64 and T <= 64 (ViT-B/32: 50 tokens): one CTA of 16 x 16 threads
+// per (head, image). Q and K are stored d-major (t contiguous), so the 4 x 4
+// score tile of thread (ty, tx) -- rows 4ty.., keys 4tx.. -- costs two float4
+// shared loads per d (the Q one a broadcast within the half-warp). The
+// softmax runs on those registers: a row's 64 scores live in the 16 lanes of
+// one half-warp, reduced by shuffles, with the steps of src/ops.c:129-139
+// (max, expf of the difference, double sum, one reciprocal, multiply). P then
+// overwrites Q's shared array row-major and the thread's 4 x 4 output tile --
+// rows 4ty.., dims 4tx.. -- accumulates p * v over keys in order, with float4
+// loads of P (broadcast) and V. 48 KB per CTA.
+constexpr int MHAS_T = 64;
+
+__global__ void __launch_bounds__(256)
+mha64s_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v, int ldi,
+              int T, OutSpec out)
+{
+    __shared__ __align__(16) float Qt[64 * MHAS_T];    // [d][t], then P [t][s]
+    __shared__ __align__(16) float Kt[64 * MHAS_T];    // [d][t]
+    __shared__ __align__(16) float Vs[MHAS_T * 64];    // [t][d]
+    const int col = blockIdx.x * 64;
+    const size_t base = (size_t)blockIdx.y * T;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+
+    // Q, K transposed: a warp task is (matrix, 4 dims, 32 rows); lane = row,
+    // so the shared stores are consecutive; the neighbouring tasks of a warp
+    // read the other half of each 32-byte sector.
+    for (int task = wid; task < 2 * 16 * 2; task += 8) {
+        const int mat = task >> 5, d4 = (task >> 1) & 15, t = (task & 1) * 32 + lane;
+        const float *src = mat ? k : q;
+        float4 x = zero;
+        if (t < T) x = __ldg(reinterpret_cast<const float4 *>(src + (base + t) * (size_t)ldi + col + 4 * d4));
+        float *dst = (mat ? Kt : Qt) + 4 * d4 * MHAS_T + t;
+        dst[0] = x.x;
+        dst[MHAS_T] = x.y;
+        dst[2 * MHAS_T] = x.z;
+        dst[3 * MHAS_T] = x.w;
+    }
+    for (int i = threadIdx.x; i < MHAS_T * 16; i += 256) {
+        const int t = i >> 4, d = (i & 15) * 4;
+        float4 x = zero;
+        if (t < T) x = __ldg(reinterpret_cast<const float4 *>(v + (base + t) * (size_t)ldi + col + d));
+        *reinterpret_cast<float4 *>(Vs + t * 64 + d) = x;
+    }
+    __syncthreads();
+
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const bool active = 4 * ty < T && 4 * tx < T;       // a half-warp shares ty: uniform per row group
+    float sc[4][4] = {};
+    if (4 * ty < T) {
+#pragma unroll 8
+        for (int d = 0; d < 64; d++) {
+            const float4 a = *reinterpret_cast<const float4 *>(Qt + d * MHAS_T + 4 * ty);
+            const float4 kk = *reinterpret_cast<const float4 *>(Kt + d * MHAS_T + 4 * tx);
+            const float av[4] = { a.x, a.y, a.z, a.w };
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                sc[i][0] = fmaf(av[i], kk.x, sc[i][0]);
+                sc[i][1] = fmaf(av[i], kk.y, sc[i][1]);
+                sc[i][2] = fmaf(av[i], kk.z, sc[i][2]);
+                sc[i][3] = fmaf(av[i], kk.w, sc[i][3]);
+            }
+        }
+    }
+    (void)active;
+    const float scale = 1.0f / sqrtf(64.0f);
+    float p[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            sc[i][j] = __fmul_rn(sc[i][j], scale);
+            if (4 * tx + j < T) mx = fmaxf(mx, sc[i][j]);
+        }
+#pragma unroll
+        for (int o = 8; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        double sum = 0.0;
+        float e[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            e[j] = 4 * tx + j < T ? expf(__fsub_rn(sc[i][j], mx)) : 0.0f;
+            sum += (double)e[j];
+        }
+#pragma unroll
+        for (int o = 8; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        const float inv = (float)(1.0 / sum);
+#pragma unroll
+        for (int j = 0; j < 4; j++) p[i][j] = __fmul_rn(e[j], inv);
+    }
+    __syncthreads();                                    // every thread is done with Qt
+    float *Ps = Qt;                                     // [t][s]
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+        *reinterpret_cast<float4 *>(Ps + (4 * ty + i) * MHAS_T + 4 * tx) = make_float4(p[i][0], p[i][1], p[i][2], p[i][3]);
+    __syncthreads();
+
+    if (4 * ty >= T) return;
+    float o[4][4] = {};
+    const int T4 = (T + 3) & ~3;
+    for (int s0 = 0; s0 < T4; s0 += 4) {
+        float4 pr[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) pr[i] = *reinterpret_cast<const float4 *>(Ps + (4 * ty + i) * MHAS_T + s0);
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            if (s0 + u >= T) break;
+            const float4 vv = *reinterpret_cast<const float4 *>(Vs + (s0 + u) * 64 + 4 * tx);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float pv = u == 0 ? pr[i].x : u == 1 ? pr[i].y : u == 2 ? pr[i].z : pr[i].w;
+                o[i][0] = fmaf(pv, vv.x, o[i][0]);
+                o[i][1] = fmaf(pv, vv.y, o[i][1]);
+                o[i][2] = fmaf(pv, vv.z, o[i][2]);
+                o[i][3] = fmaf(pv, vv.w, o[i][3]);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+        if (4 * ty + i < T) put4(out, base + 4 * ty + i, col + 4 * tx, o[i]);
+}
+
 static size_t mha64_smem(int T)
 {
     const size_t T4 = (size_t)((T + 3) & ~3);
@@ -265,6 +455,12 @@ bool launch_mha(const float *q, const float *k, const float *v, int ldi, int T, 
     if (hd <= 0 || hd > 128) return fail("attention: head_dim %d outside 1..128", hd);
     const bool aligned = !(((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) & 15) && !(ldi & 3) &&
                          !(out.ld & 3) && !(((uintptr_t)out.plain | (uintptr_t)out.hi | (uintptr_t)out.lo) & 15);
+    if (hd == 64 && aligned && T <= MHAS_T) {
+        dim3 grid(n_head, n_img);
+        mha64s_kernel<<<grid, 256, 0, s>>>(q, k, v, ldi, T, out);
+        TCG_LAUNCHED();
+        return true;
+    }
     if (hd == 64 && aligned && mha64_smem(T) <= 227 * 1024) {
         static unsigned done64[64];
         const int dev = ctx().device & 63;

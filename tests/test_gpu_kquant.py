@@ -114,12 +114,22 @@ def test_dequant_view_from_gguf(gpu, tmp_path):
     L.arena_destroy(C.byref(a))
 
 
-def dev_matvec(raw, x, N, K, qt):
+def dev_matvec(raw, x, N, K, qt, repeat=1):
+    """y of the device matvec; with repeat > 1 every launch must give the
+    same bits (the K-segment reduction resets its counters itself)."""
     L = tcg.lib()
     with tcg.DeviceBuffer.from_array(raw) as w, tcg.DeviceBuffer.from_array(x) as xb, \
             tcg.DeviceBuffer(N * 4) as y:
-        tcg.check(L.tcg_matvec_q(y.ptr, w.ptr, xb.ptr, N, K, qt), "tcg_matvec_q")
-        return y.download(N)
+        first = None
+        for _ in range(repeat):
+            tcg.check(L.tcg_matvec_q(y.ptr, w.ptr, xb.ptr, N, K, qt), "tcg_matvec_q")
+            got = y.download(N)
+            if first is None:
+                first = got
+            else:
+                assert np.array_equal(got, first)
+        assert L.tcg_device_error() == 0
+        return first
 
 
 @pytest.mark.parametrize("qt,N,K,seed", [
@@ -131,7 +141,7 @@ def dev_matvec(raw, x, N, K, qt):
 def test_matvec_vs_dequant_then_linear(gpu, qt, N, K, seed):
     raw = G.make_kquant(qt, N, K, seed=seed)
     x = np.random.default_rng(seed + 100).standard_normal(K).astype(np.float32)
-    got = dev_matvec(raw, x, N, K, qt)
+    got = dev_matvec(raw, x, N, K, qt, repeat=3)
     want = oracle.matvec_q(raw, x, N, K, qt)
     err = np.abs(got.astype(np.float64) - want).max() / np.abs(want).max()
     assert err <= MATVEC_TOL, err
