@@ -45,9 +45,12 @@ CACHE = os.environ.get("TCG_BENCH_CACHE", "/tmp/roofline_b200_bench")
 PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
-# DRAM bytes per launch of the dominant kernel from an ncu capture (see the
-# profiles/ summary of the same workload); None until captured.
-NCU_GEMM_TRAFFIC_PER_LAUNCH = None
+# DRAM bytes (read + write) per launch of the dominant kernel, the 3xTF32
+# GEMM, averaged over the 50 GEMM launches of one ViT-B/32 forward at batch
+# 256: one-pass ncu capture of dram__bytes_read.sum + dram__bytes_write.sum
+# (profiles/gemm_vit_b32_dram_traffic.md). It applies to that workload only.
+NCU_GEMM_TRAFFIC_PER_LAUNCH = 289.5e6
+NCU_GEMM_TRAFFIC_WORKLOAD = ("vit-b32", 256)
 
 
 def peaks():
@@ -376,7 +379,8 @@ def run_ours(args, dist):
         gemm_launches = kcount[0] / args.steps
         tf_peak = pk["bf16_tflops_sustained"] / 2.0 / 3.0
         achieved = gf * per / (gemm_ms * 1e-3) / 1e12           # per rank, slowest rank's time
-        traffic = NCU_GEMM_TRAFFIC_PER_LAUNCH
+        # the captured figure belongs to one per-GPU workload; other shards move other bytes
+        traffic = NCU_GEMM_TRAFFIC_PER_LAUNCH if (args.model, per) == NCU_GEMM_TRAFFIC_WORKLOAD else None
         result = {
             "metric": "ViT-B/32 images/sec",
             "value": round(args.batch / (ms_max * 1e-3), 2),
@@ -391,7 +395,9 @@ def run_ours(args, dist):
                        "seq_len": cfg["n_token"], "parallelism": f"dp{dist.world} (image shards; weights "
                        "broadcast once by NCCL)",
                        "l2": "inputs larger than L2: 703 MB of tf32 hi/lo weights + activations per step",
-                       "gemm": "3xTF32 on tcgen05 (3 tf32 MMAs per product, fp32 TMEM accumulator)"},
+                       "gemm": "3xTF32 on tcgen05: hi*hi, hi*lo, lo*hi tf32 products per fp32 product (an "
+                               "N=256 MMA for hi*hi|hi*lo and an N=128 one for lo*hi), fp32 TMEM chunk "
+                               "accumulators drained every 256 K into fp32 registers; stream-K tail"},
             "roofline": {"kernel": "gemm_tf32x3 (tcgen05, TMA-fed)", "bound": "tensor",
                          "achieved": round(achieved, 1), "peak": round(tf_peak, 1), "unit": "TFLOP/s",
                          "frac": round(achieved / tf_peak, 3),
