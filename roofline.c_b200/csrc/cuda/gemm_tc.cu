@@ -37,150 +37,18 @@
 // down, in-flight copies and MMAs are drained, and TMEM is freed.
 #include "gemm.cuh"
 #include "numerics.cuh"
+#include "tc05.cuh"
 
 namespace tcg {
 namespace {
 
 constexpr int BM = 128;
-constexpr unsigned long long WAIT_NS = 4000000000ull;   // 4 s per wait
-
-__device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void bar_init(uint32_t b, uint32_t count)
-{
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(b), "r"(count) : "memory");
-}
-__device__ __forceinline__ void bar_expect_tx(uint32_t b, uint32_t bytes)
-{
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(b), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void bar_arrive(uint32_t b)
-{
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(b) : "memory");
-}
-__device__ __forceinline__ bool bar_test(uint32_t b, uint32_t parity)
-{
-    uint32_t ok;
-    asm volatile("{\n\t.reg .pred p;\n\t"
-                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-                 "selp.u32 %0, 1, 0, p;\n\t}"
-                 : "=r"(ok) : "r"(b), "r"(parity) : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ unsigned long long now_ns()
-{
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-// Wait for the phase of parity `parity` to complete. Gives up (false) when
-// `abort` is raised by another role or after WAIT_NS, in which case it
-// raises `abort` and records `code` in the device error word.
-__device__ bool bar_wait(uint32_t b, uint32_t parity, volatile int *abort, int *err, int code, bool heed_abort = true)
-{
-    if (bar_test(b, parity)) return true;
-    const unsigned long long t0 = now_ns();
-    for (uint32_t it = 1;; ++it) {
-        if (bar_test(b, parity)) return true;
-        if ((it & 127) == 0) {
-            if (heed_abort && *abort) return false;
-            if (now_ns() - t0 > WAIT_NS) {
-                *abort = 1;
-                atomicExch(err, code);
-                return false;
-            }
-        }
-    }
-}
-
-__device__ __forceinline__ void tma_load(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y)
-{
-    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-                 " [%0], [%1, {%2, %3}], [%4];"
-                 ::"r"(dst), "l"((unsigned long long)map), "r"(x), "r"(y), "r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// UMMA shared-memory descriptor, K-major, swizzled rows of SWB bytes:
-// start>>4 @0, LBO (unused for swizzled K-major) = 1 @16, SBO = 8 rows @32,
-// version 1 @46, layout @61 (2 = 128B, 4 = 64B, 6 = 32B swizzle).
-template <int SWB>
-__device__ __forceinline__ unsigned long long sdesc(uint32_t addr)
-{
-    constexpr unsigned long long layout = SWB == 128 ? 2ull : (SWB == 64 ? 4ull : 6ull);
-    return (unsigned long long)((addr & 0x3FFFFu) >> 4) | (1ull << 16) |
-           ((unsigned long long)((8 * SWB) >> 4) << 32) | (1ull << 46) | (layout << 61);
-}
-
 // Instruction descriptor of kind::tf32, fp32 accumulator, both operands
 // K-major, M = 128, N = BN.
 template <int BN>
 __device__ __forceinline__ uint32_t idesc_tf32()
 {
     return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_tf32(uint32_t d, unsigned long long a, unsigned long long b, uint32_t id, uint32_t acc)
-{
-    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                 "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
-                 ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc));
-}
-
-__device__ __forceinline__ void mma_commit(uint32_t bar)
-{
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-
-// 32 consecutive accumulator columns of this thread's TMEM lane; the wait
-// sits in the same asm block so no use of the registers can precede it.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
-{
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32"
-                 " {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                 "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
-                 "tcgen05.wait::ld.sync.aligned;"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-                   "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-                   "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-                 : "r"(taddr)
-                 : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16])
-{
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32"
-                 " {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
-                 "tcgen05.wait::ld.sync.aligned;"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-                 : "r"(taddr)
-                 : "memory");
-}
-
-// 64 columns in one load, one wait.
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64])
-{
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x64.b32"
-                 " {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                 "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
-                 "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
-                 "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
-                 "tcgen05.wait::ld.sync.aligned;"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-                   "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-                   "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
-                   "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
-                   "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
-                   "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
-                   "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
-                 : "r"(taddr)
-                 : "memory");
 }
 
 __device__ __forceinline__ float epi_value(const GemmEpi &e, float x, int src_row, int n)
