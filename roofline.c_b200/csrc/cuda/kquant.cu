@@ -203,16 +203,16 @@ matvec_kq_kernel(const uint8_t *__restrict__ W, const float *__restrict__ x, flo
 // ----------------------------------------------------- streaming matvec
 // Persistent CTAs of 16 warps, one per SM. x stays in shared memory for the
 // whole launch, its float4 units XOR-swizzled so that the x loads of a warp
-// spread over all eight 16-byte bank groups (for Q4_K also the sum of every 16
+// spread over all eight 16-byte bank groups (for Q4_K also the sum of every 32
 // consecutive x, for the min term). Every warp streams its weight segments (a
-// part of a row of Q4_K, a whole row of Q6_K) through a two-slot cp.async ring
-// and computes one slot while the next lands. Eight lanes share a superblock,
-// 32 weights per lane, and a warp works on four consecutive superblocks at a
-// time. The quant bytes are turned into floats 2^23 + q with byte permutes,
+// part of a row of Q4_K, a whole row of Q6_K) through a cp.async ring of two to four slots
+// and computes one slot while the next lands. Four lanes share a superblock,
+// 64 weights per lane (its scales decoded once), and a warp works on eight
+// consecutive superblocks at a time. The quant bytes are turned into floats 2^23 + q with byte permutes,
 // shifted back exactly with packed f32x2 adds, and dotted with x by packed
 // f32x2 FMAs:
-//   Q4_K  sum (a q - c) x  =  a * sum(q x) - c * sum(x)   per 16 weights
-//   Q6_K  sum (d sc) q x   =  (d sc) * sum(q x)           per 8 weights
+//   Q4_K  sum (a q - c) x  =  a * sum(q x) - c * sum(x)   per sub-block of 32
+//   Q6_K  sum (d sc) q x   =  (d sc) * sum(q x)           per sub-block of 16
 constexpr int MV_WARPS = 16;
 typedef unsigned long long u64;
 
@@ -221,7 +221,6 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src)
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 __device__ __forceinline__ void cp_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ u64 fma2(u64 a, u64 b, u64 c)
@@ -258,15 +257,6 @@ __device__ __forceinline__ float dot8(uint32_t w0, uint32_t w1, u64 neg_off2, co
     return __uint_as_float((uint32_t)acc) + __uint_as_float((uint32_t)(acc >> 32));
 }
 
-// 8 bytes at a 2-byte-aligned shared-memory address.
-__device__ __forceinline__ uint2 lds8_unaligned(const uint8_t *p)
-{
-    const uintptr_t a = (uintptr_t)p;
-    const uint32_t *w = reinterpret_cast<const uint32_t *>(a & ~(uintptr_t)3);
-    const uint32_t sh = (uint32_t)(a & 3) * 8u;
-    const uint32_t w0 = w[0], w1 = w[1], w2 = w[2];
-    return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
-}
 
 // x is stored by float4 unit u at u ^ swz(u): Q4_K lanes differ in u's bits
 // 2 (half of a 32-weight group), 4-5 (group) and 6-7 (superblock); Q6_K lanes
@@ -278,35 +268,38 @@ __device__ __forceinline__ int xswz(int u)
 {
     return TYPE == GGML_TYPE_Q4_K ? u ^ ((u >> 4) & 7) : u ^ ((u >> 5) & 7);
 }
-template <int TYPE>
-__device__ __forceinline__ ulonglong2 ldx(const float *xs, int k)
-{
-    return reinterpret_cast<const ulonglong2 *>(xs)[xswz<TYPE>(k >> 2)];
-}
 
-// sum_i (v_i - off) x_i over the 8 bytes v of (w0, w1) with x[0..8) in xa, xb;
-// neg_off2 holds -(2^23 + off) twice.
-__device__ __forceinline__ float dot8x(uint32_t w0, uint32_t w1, u64 neg_off2, ulonglong2 xa, ulonglong2 xb)
+// acc += sum over the 8 bytes v of (w0, w1) of (v - off) * x, x in xa, xb
+// (four f32x2 pairs); neg_off2 holds -(2^23 + off) twice.
+__device__ __forceinline__ u64 dot8acc(uint32_t w0, uint32_t w1, u64 neg_off2, ulonglong2 xa, ulonglong2 xb, u64 acc)
 {
-    u64 acc = 0ull;
     acc = fma2(add2(magic2(w0, 0), neg_off2), xa.x, acc);
     acc = fma2(add2(magic2(w0, 2), neg_off2), xa.y, acc);
     acc = fma2(add2(magic2(w1, 0), neg_off2), xb.x, acc);
     acc = fma2(add2(magic2(w1, 2), neg_off2), xb.y, acc);
-    return __uint_as_float((uint32_t)acc) + __uint_as_float((uint32_t)(acc >> 32));
+    return acc;
+}
+__device__ __forceinline__ float pair_sum(u64 a)
+{
+    return __uint_as_float((uint32_t)a) + __uint_as_float((uint32_t)(a >> 32));
+}
+// the float4 unit at physical index u of the swizzled x
+__device__ __forceinline__ ulonglong2 ldxu(const float *xs, int u)
+{
+    return reinterpret_cast<const ulonglong2 *>(xs)[u];
 }
 
-// Lane j (0..7) of a Q4_K superblock at k0: the 16 bytes 32g + 16hh of its
-// quants (g = j / 2, hh = j % 2) hold weights 64g + 16hh + i of sub-block 2g
-// (low nibbles) and 64g + 32 + 16hh + i of sub-block 2g + 1 (high nibbles).
-__device__ __forceinline__ float lane_dot_q4k(const uint8_t *blk, int j, const float *xs, const float *x16, int k0)
+// Lane g (0..3) of a Q4_K superblock b: its 32 quant bytes 32g .. 32g + 31
+// hold weights 64g + i of sub-block 2g (low nibbles) and 64g + 32 + i of
+// sub-block 2g + 1 (high nibbles), i < 32. x unit 64b + 16g + m (+ 8 for the
+// high half) sits at physical unit (64b + 16g + 8 hi) + (m ^ f), f = (4b + g) & 7.
+__device__ __forceinline__ float lane_dot_q4k(const uint8_t *blk, int g, const float *xs, const float *x32, int b)
 {
-    const int g = j >> 1, hh = j & 1;
     const uint4 hd = *reinterpret_cast<const uint4 *>(blk);
-    const uint4 q = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * g + 16 * hh);
+    const uint4 qa = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * g);
+    const uint4 qb = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * g);
     const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFFu)));
     const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
-    // 6-bit scale / min of sub-blocks 2g (lo nibbles) and 2g+1 (hi nibbles)
     const int k = 2 * (g & 1);
     float a[2], c[2];
 #pragma unroll
@@ -319,50 +312,70 @@ __device__ __forceinline__ float lane_dot_q4k(const uint8_t *blk, int j, const f
         c[u] = dmin * (float)mn;
     }
     const u64 neg = 0xCB000000CB000000ull;          // (-2^23, -2^23)
-    const int xo = k0 + 64 * g + 16 * hh;
-    const uint32_t w[4] = { q.x, q.y, q.z, q.w };
-    float sl = 0.0f, sh = 0.0f;
+    const int base = 64 * b + 16 * g, f = (4 * b + g) & 7;
+    const uint32_t w[8] = { qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w };
+    u64 al = 0ull, ah = 0ull;
 #pragma unroll
-    for (int m = 0; m < 4; m += 2) {
-        const uint32_t l0 = w[m] & 0x0F0F0F0Fu, l1 = w[m + 1] & 0x0F0F0F0Fu;
-        const uint32_t h0 = (w[m] >> 4) & 0x0F0F0F0Fu, h1 = (w[m + 1] >> 4) & 0x0F0F0F0Fu;
-        sl += dot8x(l0, l1, neg, ldx<GGML_TYPE_Q4_K>(xs, xo + 4 * m), ldx<GGML_TYPE_Q4_K>(xs, xo + 4 * m + 4));
-        sh += dot8x(h0, h1, neg, ldx<GGML_TYPE_Q4_K>(xs, xo + 32 + 4 * m), ldx<GGML_TYPE_Q4_K>(xs, xo + 36 + 4 * m));
+    for (int m = 0; m < 8; m += 2) {
+        const ulonglong2 l0 = ldxu(xs, base + (m ^ f)), l1 = ldxu(xs, base + ((m + 1) ^ f));
+        const ulonglong2 h0 = ldxu(xs, base + 8 + (m ^ f)), h1 = ldxu(xs, base + 8 + ((m + 1) ^ f));
+        al = dot8acc(w[m] & 0x0F0F0F0Fu, w[m + 1] & 0x0F0F0F0Fu, neg, l0, l1, al);
+        ah = dot8acc((w[m] >> 4) & 0x0F0F0F0Fu, (w[m + 1] >> 4) & 0x0F0F0F0Fu, neg, h0, h1, ah);
     }
-    float r = a[0] * sl;
-    r = fmaf(-c[0], x16[xo >> 4], r);
-    r = fmaf(a[1], sh, r);
-    return fmaf(-c[1], x16[(xo + 32) >> 4], r);
+    float r = a[0] * pair_sum(al);
+    r = fmaf(-c[0], x32[8 * b + 2 * g], r);
+    r = fmaf(a[1], pair_sum(ah), r);
+    return fmaf(-c[1], x32[8 * b + 2 * g + 1], r);
 }
 
-// Lane j (0..7) of a Q6_K superblock at k0: half h = j / 4 of the superblock,
-// l0 = 8 (j % 4); its 8 bytes ql[64h + l0], ql[64h + 32 + l0] and
-// qh[32h + l0] give the weights 128h + l0 + 32c + i (c = 0..3, i < 8), each
-// group of 8 in one sub-block of 16.
-__device__ __forceinline__ float lane_dot_q6k(const uint8_t *blk, int j, const float *xs, int k0)
+// 16 bytes at a 2-byte-aligned shared-memory address.
+__device__ __forceinline__ uint4 lds16_unaligned(const uint8_t *p)
 {
-    const int h = j >> 2, l0 = (j & 3) * 8;
-    const uint2 q0 = lds8_unaligned(blk + 64 * h + l0);
-    const uint2 q1 = lds8_unaligned(blk + 64 * h + 32 + l0);
-    const uint2 qh = lds8_unaligned(blk + 128 + 32 * h + l0);
-    const float d = __half2float(__ushort_as_half((unsigned short)(blk[208] | (blk[209] << 8))));
-    const int sb = 192 + 8 * h + (l0 >> 4);
+    const uintptr_t a = (uintptr_t)p;
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(a & ~(uintptr_t)3);
+    const uint32_t sh = (uint32_t)(a & 3) * 8u;
+    const uint32_t w0 = w[0], w1 = w[1], w2 = w[2], w3 = w[3], w4 = w[4];
+    return make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh), __funnelshift_r(w2, w3, sh),
+                      __funnelshift_r(w3, w4, sh));
+}
+
+// Lane g (0..3) of a Q6_K superblock b: half h = g / 2, l0 = 16 (g % 2); its
+// 16 bytes ql[64h + l0 ..], ql[64h + 32 + l0 ..] and qh[32h + l0 ..] give the
+// weights 128h + 32c + l0 + i (c = 0..3, i < 16), each group of 16 one
+// sub-block. x unit 64b + 32h + 8c + 4(g % 2) + j sits at physical
+// (64b + 32h + 8c) + ((4(g % 2) + j) ^ f), f = (2b + h) & 7.
+__device__ __forceinline__ float lane_dot_q6k(const uint8_t *blk, int g, const float *xs, int b)
+{
+    const int h = g >> 1, e = g & 1, l0 = 16 * e;
+    const uint4 q0 = lds16_unaligned(blk + 64 * h + l0);
+    const uint4 q1 = lds16_unaligned(blk + 64 * h + 32 + l0);
+    const uint4 qh = lds16_unaligned(blk + 128 + 32 * h + l0);
+    const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(blk + 208)));
+    const int sb = 192 + 8 * h + e;
     const u64 neg = 0xCB000020CB000020ull;          // (-(2^23 + 32), twice)
-    const int xo = k0 + 128 * h + l0;
+    const int base = 64 * b + 32 * h, f = (2 * b + h) & 7;
+    const uint32_t lw0[4] = { q0.x, q0.y, q0.z, q0.w }, lw1[4] = { q1.x, q1.y, q1.z, q1.w };
+    const uint32_t hw[4] = { qh.x, qh.y, qh.z, qh.w };
     float r = 0.0f;
 #pragma unroll
     for (int c = 0; c < 4; c++) {
-        const uint2 lo = (c & 1) ? q1 : q0;
+        const uint32_t *lo = (c & 1) ? lw1 : lw0;
         const int ls = (c >> 1) * 4, hs = 2 * c;
-        const uint32_t a0 = ((lo.x >> ls) & 0x0F0F0F0Fu) | (((qh.x >> hs) & 0x03030303u) << 4);
-        const uint32_t a1 = ((lo.y >> ls) & 0x0F0F0F0Fu) | (((qh.y >> hs) & 0x03030303u) << 4);
-        const float dd = d * (float)(int8_t)blk[sb + 2 * c];
-        r = fmaf(dd, dot8x(a0, a1, neg, ldx<GGML_TYPE_Q6_K>(xs, xo + 32 * c), ldx<GGML_TYPE_Q6_K>(xs, xo + 32 * c + 4)), r);
+        u64 acc = 0ull;
+#pragma unroll
+        for (int m = 0; m < 4; m += 2) {
+            const uint32_t v0 = ((lo[m] >> ls) & 0x0F0F0F0Fu) | (((hw[m] >> hs) & 0x03030303u) << 4);
+            const uint32_t v1 = ((lo[m + 1] >> ls) & 0x0F0F0F0Fu) | (((hw[m + 1] >> hs) & 0x03030303u) << 4);
+            const ulonglong2 xa = ldxu(xs, base + 8 * c + ((4 * e + m) ^ f));
+            const ulonglong2 xb = ldxu(xs, base + 8 * c + ((4 * e + m + 1) ^ f));
+            acc = dot8acc(v0, v1, neg, xa, xb, acc);
+        }
+        r = fmaf(d * (float)(int8_t)blk[sb + 2 * c], pair_sum(acc), r);
     }
     return r;
 }
 
-template <int TYPE, int SEGS>
+template <int TYPE, int SEGS, int NSLOT>
 __global__ void __launch_bounds__(MV_WARPS * 32, 1)
 matvec_stream_kernel(const uint8_t *__restrict__ W, const float *__restrict__ x, float *__restrict__ y,
                      int N, int K)
@@ -371,15 +384,15 @@ matvec_stream_kernel(const uint8_t *__restrict__ W, const float *__restrict__ x,
     constexpr int RPI = MV_WARPS / SEGS;                 // rows per CTA iteration
     extern __shared__ uint4 sm4[];
     float *xs = reinterpret_cast<float *>(sm4);
-    float *x16 = xs + K;
+    float *x32 = xs + K;
     const int bpr = K / QK, bps = bpr / SEGS;            // superblocks per row / segment
     const int seg_bytes = bps * BB;
-    uint8_t *ring = reinterpret_cast<uint8_t *>(x16 + ((K / 16 + 3) & ~3));
+    uint8_t *ring = reinterpret_cast<uint8_t *>(x32 + ((K / 32 + 3) & ~3));
     __shared__ float part[MV_WARPS];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int sbi = lane >> 3, j8 = lane & 7;           // superblock of the four, lane within it
+    const int sbi = lane >> 2, g4 = lane & 3;           // superblock of the eight, lane within it
     const int seg = wid % SEGS, rloc = wid / SEGS;
-    uint8_t *slot[2] = { ring + (size_t)wid * 2 * seg_bytes, ring + (size_t)wid * 2 * seg_bytes + seg_bytes };
+    uint8_t *slots = ring + (size_t)wid * NSLOT * seg_bytes;   // this warp's NSLOT-deep ring
 
     auto prefetch = [&](int it, uint8_t *dst) {
         const int row = it * RPI + rloc;
@@ -392,7 +405,8 @@ matvec_stream_kernel(const uint8_t *__restrict__ W, const float *__restrict__ x,
     };
 
     int it = blockIdx.x;
-    prefetch(it, slot[0]);
+#pragma unroll
+    for (int i = 0; i < NSLOT - 1; i++) prefetch(it + i * (int)gridDim.x, slots + (size_t)i * seg_bytes);
     // x into shared memory: every load of a thread issued before its stores
     for (int i0 = threadIdx.x; i0 < K / 4; i0 += 8 * blockDim.x) {
         float4 v[8];
@@ -409,31 +423,31 @@ matvec_stream_kernel(const uint8_t *__restrict__ W, const float *__restrict__ x,
     }
     __syncthreads();
     if (TYPE == GGML_TYPE_Q4_K) {
-        for (int i = threadIdx.x; i < K / 16; i += blockDim.x) {
+        for (int i = threadIdx.x; i < K / 32; i += blockDim.x) {
             float s = 0.0f;
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const float4 v = reinterpret_cast<const float4 *>(xs)[xswz<TYPE>(4 * i + u)];
+            for (int u = 0; u < 8; u++) {
+                const float4 v = reinterpret_cast<const float4 *>(xs)[xswz<TYPE>(8 * i + u)];
                 s += v.x; s += v.y; s += v.z; s += v.w;
             }
-            x16[i] = s;
+            x32[i] = s;
         }
         __syncthreads();
     }
 
     for (int n = 0; it * RPI < N; it += gridDim.x, n++) {
-        const int nxt = it + gridDim.x;
-        prefetch(nxt, slot[(n + 1) & 1]);           // empty group past the end
-        cp_wait1();
+        // NSLOT - 1 iterations ahead, into the slot the previous iteration read
+        prefetch(it + (NSLOT - 1) * (int)gridDim.x, slots + (size_t)((n + NSLOT - 1) % NSLOT) * seg_bytes);
+        asm volatile("cp.async.wait_group %0;" ::"n"(NSLOT - 1) : "memory");
         __syncwarp();
-        const uint8_t *buf = slot[n & 1];
+        const uint8_t *buf = slots + (size_t)(n % NSLOT) * seg_bytes;
         const int row = it * RPI + rloc;
         float acc = 0.0f;
         if (row < N) {
-            for (int b = sbi; b < bps; b += 4) {
-                const int k0 = (seg * bps + b) * QK;
-                if (TYPE == GGML_TYPE_Q4_K) acc += lane_dot_q4k(buf + (size_t)b * BB, j8, xs, x16, k0);
-                else acc += lane_dot_q6k(buf + (size_t)b * BB, j8, xs, k0);
+            for (int b = sbi; b < bps; b += 8) {
+                const int bg = seg * bps + b;               // superblock index within the row
+                if (TYPE == GGML_TYPE_Q4_K) acc += lane_dot_q4k(buf + (size_t)b * BB, g4, xs, x32, bg);
+                else acc += lane_dot_q6k(buf + (size_t)b * BB, g4, xs, bg);
             }
         }
         __syncwarp();
@@ -455,19 +469,13 @@ matvec_stream_kernel(const uint8_t *__restrict__ W, const float *__restrict__ x,
     cp_wait0();
 }
 
-template <int TYPE, int SEGS>
-static bool try_matvec_stream(float *y, const void *W, const float *x, int N, int K)
+template <int TYPE, int SEGS, int NSLOT>
+static bool launch_matvec_stream(float *y, const void *W, const float *x, int N, int K, size_t smem)
 {
-    constexpr int BB = KQ<TYPE>::BYTES;
-    const int bpr = K / QK;
-    if (bpr % SEGS || ((size_t)(bpr / SEGS) * BB) % 16 || ((uintptr_t)W & 15)) return false;
-    const size_t ring = (size_t)MV_WARPS * 2 * (bpr / SEGS) * BB;
-    const size_t smem = (size_t)K * 4 + (size_t)((K / 16 + 3) & ~3) * 4 + ring;
-    if (smem > 200 * 1024) return false;
     static unsigned done[64];
     const int dev = ctx().device & 63;
     if (!done[dev]) {
-        if (cudaFuncSetAttribute(matvec_stream_kernel<TYPE, SEGS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(matvec_stream_kernel<TYPE, SEGS, NSLOT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  200 * 1024) != cudaSuccess) {
             cudaGetLastError();
             return false;
@@ -477,8 +485,24 @@ static bool try_matvec_stream(float *y, const void *W, const float *x, int N, in
     constexpr int RPI = MV_WARPS / SEGS;
     const long iters = ((long)N + RPI - 1) / RPI;
     const int grid = (int)(iters < ctx().sms ? iters : ctx().sms);
-    matvec_stream_kernel<TYPE, SEGS><<<grid, MV_WARPS * 32, smem, ctx().cur>>>((const uint8_t *)W, x, y, N, K);
+    matvec_stream_kernel<TYPE, SEGS, NSLOT><<<grid, MV_WARPS * 32, smem, ctx().cur>>>((const uint8_t *)W, x, y, N, K);
     return cudaGetLastError() == cudaSuccess || fail("matvec launch failed");
+}
+
+// The deepest ring (4, 3 or 2 segments per warp) whose shared memory fits.
+template <int TYPE, int SEGS>
+static bool try_matvec_stream(float *y, const void *W, const float *x, int N, int K)
+{
+    constexpr int BB = KQ<TYPE>::BYTES;
+    const int bpr = K / QK;
+    if (bpr % SEGS || ((size_t)(bpr / SEGS) * BB) % 16 || ((uintptr_t)W & 15)) return false;
+    const size_t base = (size_t)K * 4 + (size_t)((K / 32 + 3) & ~3) * 4;
+    const size_t seg = (size_t)MV_WARPS * (bpr / SEGS) * BB;
+    const size_t cap = 200 * 1024;
+    if (base + 4 * seg <= cap) return launch_matvec_stream<TYPE, SEGS, 4>(y, W, x, N, K, base + 4 * seg);
+    if (base + 3 * seg <= cap) return launch_matvec_stream<TYPE, SEGS, 3>(y, W, x, N, K, base + 3 * seg);
+    if (base + 2 * seg <= cap) return launch_matvec_stream<TYPE, SEGS, 2>(y, W, x, N, K, base + 2 * seg);
+    return false;
 }
 
 static unsigned grid_for(size_t warps_needed)
