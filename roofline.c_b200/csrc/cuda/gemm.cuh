@@ -26,6 +26,9 @@ struct GemmEpi {
     // set by gemm_plan: N, every leading dimension a multiple of 4 and every
     // pointer 16-byte aligned, so the epilogue may move float4s
     bool vec = false;
+    // set by gemm_plan: vec, no row remapping and no rowadd; the outputs are
+    // written by bulk tensor stores (GemmPlan's output maps)
+    bool tma = false;
 };
 
 // Device memory for the stream-K split of a GEMM's last, partial wave of
@@ -47,6 +50,7 @@ bool gemm_work_reset(const GemmWork &w, cudaStream_t s);   // zero the flags aft
 // hi/lo pairs, row-major with row stride K. Tensor maps are encoded once.
 struct GemmPlan {
     CUtensorMap a_hi, a_lo, b_hi, b_lo;
+    CUtensorMap o_plain, o_hi, o_lo;     // output maps, 32 x 8 boxes (epi.tma)
     int M = 0, N = 0, K = 0;
     int cfg = -1;        // kernel configuration index
     int grid = 0;

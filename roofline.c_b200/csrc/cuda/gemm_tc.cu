@@ -211,12 +211,12 @@ template <int HALF>
 __device__ __forceinline__ void drain_add2(uint32_t ta, uint32_t tb, float (&acc)[HALF])
 {
 #pragma unroll
-    for (int j = 0; j < HALF; j += 16) {
-        uint32_t x[16], y[16];
-        tmem_ld16(ta + (uint32_t)j, x);
-        tmem_ld16(tb + (uint32_t)j, y);
+    for (int j = 0; j < HALF; j += 8) {
+        uint32_t x[8], y[8];
+        tmem_ld8(ta + (uint32_t)j, x);
+        tmem_ld8(tb + (uint32_t)j, y);
 #pragma unroll
-        for (int i = 0; i < 16; i++)
+        for (int i = 0; i < 8; i++)
             acc[j + i] = __fadd_rn(acc[j + i], __fadd_rn(__uint_as_float(x[i]), __uint_as_float(y[i])));
     }
 }
@@ -239,18 +239,20 @@ __device__ __forceinline__ void epi_store_tile(const GemmEpi &e, const float (&a
     const int lane = threadIdx.x & 31;
     const int c = lane & 3;
     const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-    int src_row[4];
-    size_t dst_row[4];
-    bool row_ok[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int r = row0 + i * 8 + (lane >> 2);
-        row_ok[i] = r < M;
-        src_row[i] = r % e.rgroup + e.roff;
-        dst_row[i] = (size_t)(r / e.rgroup) * e.rstride + e.roff + r % e.rgroup;
-    }
 #pragma unroll
     for (int s = 0; s < NS; s++) {
+        // row indices are recomputed per slice: holding them across slices
+        // costs registers that the accumulators need
+        int src_row[4];
+        size_t dst_row[4];
+        bool row_ok[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int r = row0 + i * 8 + (lane >> 2);
+            row_ok[i] = r < M;
+            src_row[i] = r % e.rgroup + e.roff;
+            dst_row[i] = (size_t)(r / e.rgroup) * e.rstride + e.roff + r % e.rgroup;
+        }
         const int j = 16 * s;
 #pragma unroll
         for (int k = 0; k < 4; k++) {
@@ -306,6 +308,106 @@ __device__ __forceinline__ void epi_store_tile(const GemmEpi &e, const float (&a
                 *reinterpret_cast<float4 *>(e.out.lo + o) = make_float4(l[0], l[1], l[2], l[3]);
             }
         }
+    }
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem()
+{
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// One bulk tensor store of a shared-memory box to (x, y) of map, as its own
+// bulk group.
+__device__ __forceinline__ void tma_store(const CUtensorMap *map, uint32_t src, int x, int y)
+{
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+                 ::"l"((unsigned long long)map), "r"(x), "r"(y), "r"(src) : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until at most PENDING of this thread's bulk groups still read shared memory.
+template <int PENDING>
+__device__ __forceinline__ void bulk_wait_read()
+{
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(PENDING) : "memory");
+}
+
+// The epilogue of a tile whose rows map one to one onto output rows (no
+// rowadd): lane = row, as the accumulators come out of TMEM, so nothing is
+// transposed. Units of 8 columns of one output array go through two
+// alternating 32 x 8 shared buffers in the 32-byte swizzle (16-byte chunk c of
+// row r at c ^ ((r >> 2) & 1): conflict-free for row-per-lane float4 writes),
+// each sent by one bulk tensor store that clips rows >= M and columns >= N.
+// The bias comes from one register per 32 columns (breg, loaded when the
+// tile started) by shuffles; the lane's residual row segment of the next unit
+// is loaded while the current unit is finished.
+template <int HALF>
+__device__ __forceinline__ void epi_store_tile_tma(const GemmEpi &e, const float (&acc)[HALF], float *stage,
+                                                   const CUtensorMap *mp, const CUtensorMap *mh,
+                                                   const CUtensorMap *ml, int row0, int n0, int M, int N,
+                                                   const float (&breg)[(HALF + 31) / 32])
+{
+    constexpr int NU = HALF / 8;
+    static_assert(HALF % 8 == 0, "8-column store units");
+    if (row0 >= M) return;                         // all 32 rows below the matrix: nothing to store
+    const int lane = threadIdx.x & 31;
+    const int r = row0 + lane;
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float *res = e.residual && r < M ? e.residual + (size_t)(e.roff + r) * e.out.ld + n0 : nullptr;
+    float4 rc0 = zero, rc1 = zero;
+    if (res) {
+        if (n0 < N) rc0 = ld4(res);
+        if (n0 + 4 < N) rc1 = ld4(res + 4);
+    }
+    const int sw = (lane >> 2) & 1;
+    int buf = 0;
+#pragma unroll
+    for (int u = 0; u < NU; u++) {
+        const int n = n0 + 8 * u;
+        if (n >= N) break;
+        float4 rn0 = zero, rn1 = zero;
+        if (res && u + 1 < NU) {
+            if (n + 8 < N) rn0 = ld4(res + 8 * (u + 1));
+            if (n + 12 < N) rn1 = ld4(res + 8 * (u + 1) + 4);
+        }
+        const float rv[8] = { rc0.x, rc0.y, rc0.z, rc0.w, rc1.x, rc1.y, rc1.z, rc1.w };
+        float x[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int c = 8 * u + j;
+            float v = acc[c];
+            if (e.bias) v = __fadd_rn(v, __shfl_sync(0xffffffffu, breg[c / 32], c % 32));
+            if (e.act == 1) v = gelu_exact(v);
+            else if (e.act == 2) v = gelu_quick(v);
+            if (e.residual) v = __fadd_rn(rv[j], v);
+            x[j] = v;
+        }
+#pragma unroll
+        for (int o = 0; o < 3; o++) {
+            const CUtensorMap *m = o == 0 ? (e.out.plain ? mp : nullptr) : o == 1 ? (e.out.hi ? mh : nullptr)
+                                                                                  : (e.out.lo ? ml : nullptr);
+            if (!m) continue;
+            float y[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                if (o == 0) {
+                    y[j] = x[j];
+                } else {
+                    float h, l;
+                    split_tf32(x[j], h, l);
+                    y[j] = o == 1 ? h : l;
+                }
+            }
+            if (lane == 0) bulk_wait_read<1>();     // the store that used this buffer last has read it
+            __syncwarp();
+            float *b = stage + buf * 256;
+            *reinterpret_cast<float4 *>(b + lane * 8 + 4 * sw) = make_float4(y[0], y[1], y[2], y[3]);
+            *reinterpret_cast<float4 *>(b + lane * 8 + 4 * (sw ^ 1)) = make_float4(y[4], y[5], y[6], y[7]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) tma_store(m, su32(b), n, row0);
+            buf ^= 1;
+        }
+        rc0 = rn0;
+        rc1 = rn1;
     }
 }
 
@@ -420,6 +522,8 @@ template <int BN, int BK, int STAGES, int EPI_W, int ACC, int CG>
 __global__ void __launch_bounds__(Shape<BN, BK, STAGES, EPI_W, ACC, CG>::THREADS, 1)
 gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
                    const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
+                   const __grid_constant__ CUtensorMap o_plain, const __grid_constant__ CUtensorMap o_hi,
+                   const __grid_constant__ CUtensorMap o_lo,
                    int M, int N, int K, int chunk_kb, GemmEpi epi, int *err, float *ws, int *flags, int sk)
 {
     using S = Shape<BN, BK, STAGES, EPI_W, ACC, CG>;
@@ -480,6 +584,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
     fence_after();
     const uint32_t tmem = *tmem_slot;
     const int P = gridDim.x / CG, p = blockIdx.x / CG;   // tile groups (CTA pairs) and this one
+    pdl_wait();                  // no global access above this line
 
     if (warp == 0) {
         if (lane == 0) {
@@ -487,6 +592,11 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
             asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&a_lo) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&b_hi) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&b_lo) : "memory");
+            if (epi.tma) {
+                asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&o_plain) : "memory");
+                asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&o_hi) : "memory");
+                asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&o_lo) : "memory");
+            }
             int stage = 0;
             uint32_t phase = 0;
             long issued = 0;
@@ -617,6 +727,14 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
             float acc[S::HALF];
 #pragma unroll
             for (int j = 0; j < S::HALF; j++) acc[j] = 0.0f;
+            // bias of this warp's columns for the bulk-store epilogue, loaded
+            // now so that its latency hides behind the tile's MMAs
+            float breg[(S::HALF + 31) / 32];
+#pragma unroll
+            for (int i = 0; i < (S::HALF + 31) / 32; i++) {
+                const int cc = 32 * i + lane, nn = (sg.tile % n_tiles) * BN + h * S::HALF + cc;
+                breg[i] = epi.tma && epi.bias && cc < S::HALF && nn < N ? epi.bias[nn] : 0.0f;
+            }
             for (int c = sg.c0; c < sg.c1; c++, chunk++) {
                 const uint32_t b = chunk % NBUF;
                 if (!bar_wait(cfull0 + 8 * b, (chunk / NBUF) & 1, abort, err, 6)) { ok = false; break; }
@@ -674,9 +792,14 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                 if (!ok) break;
             }
             const int m0 = (sg.tile / n_tiles) * CG * BM + (int)rank * BM, n0 = (sg.tile % n_tiles) * BN;
-            epi_store_tile<S::HALF>(epi, acc, epi_stage + ew * (S::EPI_STAGE_BYTES / 4), m0 + q * 32,
-                                    n0 + h * S::HALF, M, N);
+            if (epi.tma)
+                epi_store_tile_tma<S::HALF>(epi, acc, epi_stage + ew * (S::EPI_STAGE_BYTES / 4), &o_plain, &o_hi,
+                                            &o_lo, m0 + q * 32, n0 + h * S::HALF, M, N, breg);
+            else
+                epi_store_tile<S::HALF>(epi, acc, epi_stage + ew * (S::EPI_STAGE_BYTES / 4), m0 + q * 32,
+                                        n0 + h * S::HALF, M, N);
         }
+        if (lane == 0) bulk_wait_read<0>();          // shared memory stays until the stores have read it
     }
 
     fence_before();
@@ -730,6 +853,22 @@ bool encode_kmajor(CUtensorMap *m, const float *ptr, int rows, int K, int box_ro
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail("cuTensorMapEncodeTiled failed (%d) for [%d x %d]", (int)r, rows, K);
     return true;
+}
+
+// Output map for the bulk-store epilogue: rows x cols fp32 with row stride
+// ld, boxes of 32 rows x 8 columns in the 32-byte swizzle.
+bool encode_out(CUtensorMap *m, const float *ptr, int rows, int cols, int ld)
+{
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail("cuTensorMapEncodeTiled is not available from the driver");
+    cuuint64_t dims[2] = { (cuuint64_t)cols, (cuuint64_t)rows };
+    cuuint64_t strides[1] = { (cuuint64_t)ld * 4u };
+    cuuint32_t box[2] = { 8, 32 };
+    cuuint32_t estr[2] = { 1, 1 };
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)ptr, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
 }
 
 struct Cfg {
@@ -821,6 +960,8 @@ bool gemm_work_reset(const GemmWork &w, cudaStream_t s)
 }
 
 int g_streamk = 1;        // tuning hook: 0 computes every tile whole
+int g_tma_store = 1;      // tuning hook: 0 keeps every epilogue on plain stores
+static thread_local int g_last_plan[4];   // grid, stream-K, configuration, bulk-store epilogue of the latest plan
 
 bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo,
                int M, int N, int K, const GemmEpi &epi, int force_cfg, const GemmWork *work)
@@ -843,6 +984,14 @@ bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b
         p.epi.vec = N % 4 == 0 && epi.out.ld % 4 == 0 && a16(epi.bias) && a16(epi.residual) && a16(epi.out.plain) &&
                     a16(epi.out.hi) && a16(epi.out.lo) && a16(epi.rowadd) && (!epi.rowadd || epi.ld_rowadd % 4 == 0) &&
                     !(epi.rowadd && epi.residual);
+        // bulk tensor stores need one output row per GEMM row (no remap)
+        p.epi.tma = false;
+        if (g_tma_store && p.epi.vec && !epi.rowadd && epi.rgroup >= M && epi.roff >= 0) {
+            const size_t off = (size_t)epi.roff * epi.out.ld;
+            p.epi.tma = (!epi.out.plain || encode_out(&p.o_plain, epi.out.plain + off, M, N, epi.out.ld)) &&
+                        (!epi.out.hi || encode_out(&p.o_hi, epi.out.hi + off, M, N, epi.out.ld)) &&
+                        (!epi.out.lo || encode_out(&p.o_lo, epi.out.lo + off, M, N, epi.out.ld));
+        }
     }
     const int sms = ctx().sms > 0 ? ctx().sms : 148;
     int groups = sms;        // tile groups resident at once: CTAs, or CTA pairs
@@ -878,7 +1027,7 @@ bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b
     // hand-over costs what it saves.
     const int chunks = (K + g_chunk_k - 1) / g_chunk_k;
     const int last = tiles % groups;
-    const bool pays = last <= groups / 2 || chunks >= 6;
+    const bool pays = g_streamk == 2 || last <= groups / 2 || chunks >= 6;
     if (g_streamk && work && work->ws && work->flags && !c.sep && last != 0 && chunks > 1 && pays) {
         const long units = (long)tiles * chunks;
         const int g = tiles >= groups ? groups : (int)(units < groups ? units : groups);
@@ -888,6 +1037,10 @@ bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b
             p.work = *work;
         }
     }
+    g_last_plan[0] = p.grid;
+    g_last_plan[1] = p.sk;
+    g_last_plan[2] = cfg;
+    g_last_plan[3] = p.epi.tma ? 1 : 0;
     return true;
 }
 
@@ -907,23 +1060,22 @@ bool gemm_run(const GemmPlan &p, cudaStream_t s, int *err)
     int *flags = p.work.flags;
     int sk = p.sk;
     void *args[] = { (void *)&p.a_hi, (void *)&p.a_lo, (void *)&p.b_hi, (void *)&p.b_lo,
-                     (void *)&p.M, (void *)&p.N, (void *)&p.K, (void *)&chunk_kb, (void *)&p.epi, (void *)&err,
+                     (void *)&p.o_plain, (void *)&p.o_hi, (void *)&p.o_lo, (void *)&p.M, (void *)&p.N, (void *)&p.K, (void *)&chunk_kb, (void *)&p.epi, (void *)&err,
                      (void *)&ws, (void *)&flags, (void *)&sk };
+    cudaLaunchAttribute at[2];
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(p.grid);
+    lc.blockDim = dim3(c.threads);
+    lc.dynamicSmemBytes = c.smem;
+    lc.stream = s;
+    lc.attrs = at;
+    lc.numAttrs = pdl_attr(at);
     if (c.cg == 2) {
-        cudaLaunchConfig_t lc = {};
-        cudaLaunchAttribute at;
-        at.id = cudaLaunchAttributeClusterDimension;
-        at.val.clusterDim.x = 2; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
-        lc.gridDim = dim3(p.grid);
-        lc.blockDim = dim3(c.threads);
-        lc.dynamicSmemBytes = c.smem;
-        lc.stream = s;
-        lc.attrs = &at;
-        lc.numAttrs = 1;
-        TCG_CUDA(cudaLaunchKernelExC(&lc, c.fn, args));
-    } else {
-        TCG_CUDA(cudaLaunchKernel(c.fn, dim3(p.grid), dim3(c.threads), args, c.smem, s));
+        cudaLaunchAttribute &cl = at[lc.numAttrs++];
+        cl.id = cudaLaunchAttributeClusterDimension;
+        cl.val.clusterDim.x = 2; cl.val.clusterDim.y = 1; cl.val.clusterDim.z = 1;
     }
+    TCG_CUDA(cudaLaunchKernelExC(&lc, c.fn, args));
     return true;
 }
 
@@ -1008,13 +1160,31 @@ bool tcg_linear_cfg(float *y, const float *x, const float *W, const float *bias,
 
 int tcg_gemm_num_cfgs(void) { return gemm_num_cfgs(); }
 
+// Tuning and test hook: 0 keeps every GEMM epilogue on plain stores, 1
+// (default) uses bulk tensor stores where the output rows allow. Applies to
+// GEMMs planned afterwards. Returns the previous setting.
+int tcg_gemm_set_tma_store(int on)
+{
+    const int old = g_tma_store;
+    g_tma_store = on ? 1 : 0;
+    return old;
+}
+
+// Test hook: the grid size, stream-K flag, configuration and bulk-store
+// epilogue flag of the latest GEMM plan made on this thread.
+void tcg_gemm_last_plan(int out[4])
+{
+    for (int i = 0; i < 4; i++) out[i] = g_last_plan[i];
+}
+
 // Tuning and test hook: 0 turns the stream-K split of a GEMM's last, partial
-// wave off (every tile computed whole, results independent of M), 1 on.
+// wave off (every tile computed whole, results independent of M), 1 splits it
+// where the heuristic expects a gain, 2 whenever there is a partial wave.
 // Applies to GEMMs planned afterwards. Returns the previous setting.
-int tcg_gemm_set_streamk(int on)
+int tcg_gemm_set_streamk(int mode)
 {
     const int old = g_streamk;
-    g_streamk = on ? 1 : 0;
+    g_streamk = mode < 0 ? 0 : (mode > 2 ? 2 : mode);
     return old;
 }
 

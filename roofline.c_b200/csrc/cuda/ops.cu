@@ -40,6 +40,7 @@ __device__ __forceinline__ void put4(const OutSpec &o, size_t row, int col, cons
 __global__ void layernorm_kernel(const float *x, int ld_in, const float *__restrict__ g,
                                  const float *__restrict__ b, int rows, int cols, float eps, OutSpec out)
 {
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= rows) return;
@@ -65,20 +66,30 @@ __global__ void layernorm_kernel(const float *x, int ld_in, const float *__restr
 // The same LayerNorm with the row held in registers: lane l owns the float4s
 // l, l + 32, ... (VPL of them, cols = 128 * VPL), read once and written once
 // as float4 (plain or tf32 hi/lo). Same arithmetic as layernorm_kernel; the
-// double sums run in another order.
+// double sums run in another order. Gamma and beta are staged in shared
+// memory once per CTA, so the output loop waits on no global load.
 template <int VPL>
-__global__ void __launch_bounds__(256, 4)
+__global__ void __launch_bounds__(256, 2)
 layernorm_vec_kernel(const float *x, int ld_in, const float *__restrict__ g, const float *__restrict__ b, int rows,
                      float eps, OutSpec out)
 {
+    pdl_wait();
     constexpr int cols = 128 * VPL;
+    __shared__ float4 gs[32 * VPL], bs[32 * VPL];       // gamma, beta: shared by the CTA's eight rows
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (row >= rows) return;
-    const float4 *in = reinterpret_cast<const float4 *>(x + (size_t)row * ld_in);
     float4 v[VPL];
+    if (row < rows) {
+        const float4 *in = reinterpret_cast<const float4 *>(x + (size_t)row * ld_in);
 #pragma unroll
-    for (int i = 0; i < VPL; i++) v[i] = in[lane + 32 * i];
+        for (int i = 0; i < VPL; i++) v[i] = in[lane + 32 * i];
+    }
+    for (int i = threadIdx.x; i < 32 * VPL; i += blockDim.x) {
+        if (g) gs[i] = reinterpret_cast<const float4 *>(g)[i];
+        if (b) bs[i] = reinterpret_cast<const float4 *>(b)[i];
+    }
+    __syncthreads();
+    if (row >= rows) return;
     double s = 0.0;
 #pragma unroll
     for (int i = 0; i < VPL; i++) s += ((double)v[i].x + (double)v[i].y) + ((double)v[i].z + (double)v[i].w);
@@ -99,12 +110,12 @@ layernorm_vec_kernel(const float *x, int ld_in, const float *__restrict__ g, con
         float o[4] = { __fmul_rn((float)((double)v[i].x - mean), inv), __fmul_rn((float)((double)v[i].y - mean), inv),
                        __fmul_rn((float)((double)v[i].z - mean), inv), __fmul_rn((float)((double)v[i].w - mean), inv) };
         if (g) {
-            const float4 gg = *reinterpret_cast<const float4 *>(g + c);
+            const float4 gg = gs[lane + 32 * i];
             o[0] = __fmul_rn(o[0], gg.x); o[1] = __fmul_rn(o[1], gg.y);
             o[2] = __fmul_rn(o[2], gg.z); o[3] = __fmul_rn(o[3], gg.w);
         }
         if (b) {
-            const float4 bv = *reinterpret_cast<const float4 *>(b + c);
+            const float4 bv = bs[lane + 32 * i];
             o[0] = __fadd_rn(o[0], bv.x); o[1] = __fadd_rn(o[1], bv.y);
             o[2] = __fadd_rn(o[2], bv.z); o[3] = __fadd_rn(o[3], bv.w);
         }
@@ -122,17 +133,17 @@ bool launch_layernorm(const float *x, int ld_in, const float *g, const float *b,
     const unsigned grid = ceil_div(rows, 8);
     if (vec) {
         switch (cols / 128) {
-        case 1: layernorm_vec_kernel<1><<<grid, 256, 0, s>>>(x, ld_in, g, b, rows, eps, out); break;
-        case 2: layernorm_vec_kernel<2><<<grid, 256, 0, s>>>(x, ld_in, g, b, rows, eps, out); break;
-        case 3: layernorm_vec_kernel<3><<<grid, 256, 0, s>>>(x, ld_in, g, b, rows, eps, out); break;
-        case 4: layernorm_vec_kernel<4><<<grid, 256, 0, s>>>(x, ld_in, g, b, rows, eps, out); break;
-        case 5: layernorm_vec_kernel<5><<<grid, 256, 0, s>>>(x, ld_in, g, b, rows, eps, out); break;
-        case 6: layernorm_vec_kernel<6><<<grid, 256, 0, s>>>(x, ld_in, g, b, rows, eps, out); break;
-        case 7: layernorm_vec_kernel<7><<<grid, 256, 0, s>>>(x, ld_in, g, b, rows, eps, out); break;
-        default: layernorm_vec_kernel<8><<<grid, 256, 0, s>>>(x, ld_in, g, b, rows, eps, out); break;
+        case 1: TCG_CUDA(launch_pdl(layernorm_vec_kernel<1>, grid, 256, 0, s, x, ld_in, g, b, rows, eps, out)); break;
+        case 2: TCG_CUDA(launch_pdl(layernorm_vec_kernel<2>, grid, 256, 0, s, x, ld_in, g, b, rows, eps, out)); break;
+        case 3: TCG_CUDA(launch_pdl(layernorm_vec_kernel<3>, grid, 256, 0, s, x, ld_in, g, b, rows, eps, out)); break;
+        case 4: TCG_CUDA(launch_pdl(layernorm_vec_kernel<4>, grid, 256, 0, s, x, ld_in, g, b, rows, eps, out)); break;
+        case 5: TCG_CUDA(launch_pdl(layernorm_vec_kernel<5>, grid, 256, 0, s, x, ld_in, g, b, rows, eps, out)); break;
+        case 6: TCG_CUDA(launch_pdl(layernorm_vec_kernel<6>, grid, 256, 0, s, x, ld_in, g, b, rows, eps, out)); break;
+        case 7: TCG_CUDA(launch_pdl(layernorm_vec_kernel<7>, grid, 256, 0, s, x, ld_in, g, b, rows, eps, out)); break;
+        default: TCG_CUDA(launch_pdl(layernorm_vec_kernel<8>, grid, 256, 0, s, x, ld_in, g, b, rows, eps, out)); break;
         }
     } else {
-        layernorm_kernel<<<grid, 256, 0, s>>>(x, ld_in, g, b, rows, cols, eps, out);
+        TCG_CUDA(launch_pdl(layernorm_kernel, grid, 256, 0, s, x, ld_in, g, b, rows, cols, eps, out));
     }
     TCG_LAUNCHED();
     return true;
@@ -148,6 +159,7 @@ template <int DPL>   // head dims per lane: hd <= 32*DPL
 __global__ void mha_kernel(const float *__restrict__ q, const float *__restrict__ k,
                            const float *__restrict__ v, int ldi, int T, int hd, OutSpec out)
 {
+    pdl_wait();
     extern __shared__ float sm[];
     const int h = blockIdx.x, img = blockIdx.y;
     const int nw = blockDim.x >> 5, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -225,6 +237,7 @@ __global__ void __launch_bounds__(256)
 mha64_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
              int ldi, int T, OutSpec out)
 {
+    pdl_wait();
     extern __shared__ float4 sm4[];
     float *sm = reinterpret_cast<float *>(sm4);
     const int T4 = (T + 3) & ~3;
@@ -331,10 +344,11 @@ mha64_kernel(const float *__restrict__ q, const float *__restrict__ k, const flo
 // loads of P (broadcast) and V. 48 KB per CTA.
 constexpr int MHAS_T = 64;
 
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 4)
 mha64s_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v, int ldi,
               int T, OutSpec out)
 {
+    pdl_wait();
     __shared__ __align__(16) float Qt[64 * MHAS_T];    // [d][t], then P [t][s]
     __shared__ __align__(16) float Kt[64 * MHAS_T];    // [d][t]
     __shared__ __align__(16) float Vs[MHAS_T * 64];    // [t][d]
@@ -345,23 +359,37 @@ mha64s_kernel(const float *__restrict__ q, const float *__restrict__ k, const fl
 
     // Q, K transposed: a warp task is (matrix, 4 dims, 32 rows); lane = row,
     // so the shared stores are consecutive; the neighbouring tasks of a warp
-    // read the other half of each 32-byte sector.
-    for (int task = wid; task < 2 * 16 * 2; task += 8) {
+    // read the other half of each 32-byte sector. All twelve loads of a thread
+    // (eight Q/K tasks, four V float4s) are issued before the first store: one
+    // memory round trip instead of twelve.
+    float4 xqk[8], xv[4];
+#pragma unroll
+    for (int it = 0; it < 8; it++) {
+        const int task = wid + 8 * it;
         const int mat = task >> 5, d4 = (task >> 1) & 15, t = (task & 1) * 32 + lane;
         const float *src = mat ? k : q;
-        float4 x = zero;
-        if (t < T) x = __ldg(reinterpret_cast<const float4 *>(src + (base + t) * (size_t)ldi + col + 4 * d4));
-        float *dst = (mat ? Kt : Qt) + 4 * d4 * MHAS_T + t;
-        dst[0] = x.x;
-        dst[MHAS_T] = x.y;
-        dst[2 * MHAS_T] = x.z;
-        dst[3 * MHAS_T] = x.w;
+        xqk[it] = t < T ? __ldg(reinterpret_cast<const float4 *>(src + (base + t) * (size_t)ldi + col + 4 * d4)) : zero;
     }
-    for (int i = threadIdx.x; i < MHAS_T * 16; i += 256) {
+#pragma unroll
+    for (int it = 0; it < 4; it++) {
+        const int i = threadIdx.x + 256 * it;
         const int t = i >> 4, d = (i & 15) * 4;
-        float4 x = zero;
-        if (t < T) x = __ldg(reinterpret_cast<const float4 *>(v + (base + t) * (size_t)ldi + col + d));
-        *reinterpret_cast<float4 *>(Vs + t * 64 + d) = x;
+        xv[it] = t < T ? __ldg(reinterpret_cast<const float4 *>(v + (base + t) * (size_t)ldi + col + d)) : zero;
+    }
+#pragma unroll
+    for (int it = 0; it < 8; it++) {
+        const int task = wid + 8 * it;
+        const int mat = task >> 5, d4 = (task >> 1) & 15, t = (task & 1) * 32 + lane;
+        float *dst = (mat ? Kt : Qt) + 4 * d4 * MHAS_T + t;
+        dst[0] = xqk[it].x;
+        dst[MHAS_T] = xqk[it].y;
+        dst[2 * MHAS_T] = xqk[it].z;
+        dst[3 * MHAS_T] = xqk[it].w;
+    }
+#pragma unroll
+    for (int it = 0; it < 4; it++) {
+        const int i = threadIdx.x + 256 * it;
+        *reinterpret_cast<float4 *>(Vs + (i >> 4) * 64 + (i & 15) * 4) = xv[it];
     }
     __syncthreads();
 
@@ -457,7 +485,7 @@ bool launch_mha(const float *q, const float *k, const float *v, int ldi, int T, 
                          !(out.ld & 3) && !(((uintptr_t)out.plain | (uintptr_t)out.hi | (uintptr_t)out.lo) & 15);
     if (hd == 64 && aligned && T <= MHAS_T) {
         dim3 grid(n_head, n_img);
-        mha64s_kernel<<<grid, 256, 0, s>>>(q, k, v, ldi, T, out);
+        TCG_CUDA(launch_pdl(mha64s_kernel, grid, 256, 0, s, q, k, v, ldi, T, out));
         TCG_LAUNCHED();
         return true;
     }
@@ -469,7 +497,7 @@ bool launch_mha(const float *q, const float *k, const float *v, int ldi, int T, 
             done64[dev] = 1;
         }
         dim3 grid(n_head, n_img, (T + MHA_BQ - 1) / MHA_BQ);
-        mha64_kernel<<<grid, 256, mha64_smem(T), s>>>(q, k, v, ldi, T, out);
+        TCG_CUDA(launch_pdl(mha64_kernel, grid, 256, mha64_smem(T), s, q, k, v, ldi, T, out));
         TCG_LAUNCHED();
         return true;
     }
@@ -487,9 +515,9 @@ bool launch_mha(const float *q, const float *k, const float *v, int ldi, int T, 
         TCG_CUDA(cudaFuncSetAttribute(mha_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, maxsm));
         attr_done[dev] = 1;
     }
-    if (hd <= 32) mha_kernel<1><<<grid, nw * 32, smem, s>>>(q, k, v, ldi, T, hd, out);
-    else if (hd <= 64) mha_kernel<2><<<grid, nw * 32, smem, s>>>(q, k, v, ldi, T, hd, out);
-    else mha_kernel<4><<<grid, nw * 32, smem, s>>>(q, k, v, ldi, T, hd, out);
+    if (hd <= 32) TCG_CUDA(launch_pdl(mha_kernel<1>, grid, nw * 32, smem, s, q, k, v, ldi, T, hd, out));
+    else if (hd <= 64) TCG_CUDA(launch_pdl(mha_kernel<2>, grid, nw * 32, smem, s, q, k, v, ldi, T, hd, out));
+    else TCG_CUDA(launch_pdl(mha_kernel<4>, grid, nw * 32, smem, s, q, k, v, ldi, T, hd, out));
     TCG_LAUNCHED();
     return true;
 }
@@ -593,6 +621,7 @@ template <int VEC>
 __global__ void patches_kernel(const float *__restrict__ px, int n_img, int S, int P,
                                float *__restrict__ hi, float *__restrict__ lo)
 {
+    pdl_wait();
     typedef typename std::conditional<VEC == 4, float4, typename std::conditional<VEC == 2, float2, float>::type>::type V;
     const int G = S / P, PV = P / VEC, KPV = 3 * P * PV;          // vectors per patch row
     const size_t total = (size_t)n_img * G * G * KPV;
@@ -619,9 +648,9 @@ bool launch_patches(const float *px, int n_img, int S, int P, float *hi, float *
     if (total == 0) return true;
     const bool a16 = !(((uintptr_t)px | (uintptr_t)hi | (uintptr_t)lo) & 15) && !(S & 3);
     const bool a8 = !(((uintptr_t)px | (uintptr_t)hi | (uintptr_t)lo) & 7) && !(S & 1);
-    if (P % 4 == 0 && a16) patches_kernel<4><<<grid1d(total / 4), 256, 0, s>>>(px, n_img, S, P, hi, lo);
-    else if (P % 2 == 0 && a8) patches_kernel<2><<<grid1d(total / 2), 256, 0, s>>>(px, n_img, S, P, hi, lo);
-    else patches_kernel<1><<<grid1d(total), 256, 0, s>>>(px, n_img, S, P, hi, lo);
+    if (P % 4 == 0 && a16) TCG_CUDA(launch_pdl(patches_kernel<4>, grid1d(total / 4), 256, 0, s, px, n_img, S, P, hi, lo));
+    else if (P % 2 == 0 && a8) TCG_CUDA(launch_pdl(patches_kernel<2>, grid1d(total / 2), 256, 0, s, px, n_img, S, P, hi, lo));
+    else TCG_CUDA(launch_pdl(patches_kernel<1>, grid1d(total), 256, 0, s, px, n_img, S, P, hi, lo));
     TCG_LAUNCHED();
     return true;
 }
@@ -659,6 +688,7 @@ bool launch_transpose_split(const float *src, int R, int C, float *hi, float *lo
 __global__ void cls_rows_kernel(float *__restrict__ x, const float *__restrict__ cls,
                                 const float *__restrict__ pos, int n_img, int T, int D)
 {
+    pdl_wait();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_img * D; i += gridDim.x * blockDim.x) {
         const int img = i / D, d = i % D;
         x[(size_t)img * T * D + d] = __fadd_rn(cls[d], pos[d]);
@@ -668,7 +698,7 @@ __global__ void cls_rows_kernel(float *__restrict__ x, const float *__restrict__
 bool launch_cls_rows(float *x, const float *cls, const float *pos, int n_img, int T, int D, cudaStream_t s)
 {
     if (n_img <= 0) return true;
-    cls_rows_kernel<<<grid1d((size_t)n_img * D), 256, 0, s>>>(x, cls, pos, n_img, T, D);
+    TCG_CUDA(launch_pdl(cls_rows_kernel, grid1d((size_t)n_img * D), 256, 0, s, x, cls, pos, n_img, T, D));
     TCG_LAUNCHED();
     return true;
 }

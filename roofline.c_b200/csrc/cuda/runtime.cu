@@ -12,6 +12,7 @@ namespace tcg {
 
 static thread_local Ctx g_ctx;
 static thread_local char g_err[256];
+int g_pdl = 1;
 
 Ctx &ctx() { return g_ctx; }
 
@@ -96,6 +97,16 @@ int tcg_device_count(void)
 }
 
 int tcg_sm_count(void) { return ctx().ready ? ctx().sms : 0; }
+
+// Tuning hook: 0 launches every kernel in plain stream order, 1 (default)
+// with programmatic dependent launch. Applies to launches (and forward
+// graphs captured) afterwards. Returns the previous setting.
+extern "C" int tcg_set_pdl(int on)
+{
+    const int old = tcg::g_pdl;
+    tcg::g_pdl = on ? 1 : 0;
+    return old;
+}
 
 bool tcg_sync(void)
 {

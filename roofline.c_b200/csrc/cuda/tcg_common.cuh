@@ -36,6 +36,42 @@ void *scratch(size_t bytes);                        // ctx scratch, grown on dem
 
 inline unsigned ceil_div(size_t a, size_t b) { return (unsigned)((a + b - 1) / b); }
 
+// Programmatic dependent launch. A kernel launched with launch_pdl() is
+// scheduled as the CTAs of the kernel before it on the stream retire, instead
+// of after that kernel's completion has been processed; it does its local
+// prologue (shared-memory barriers, TMEM allocation), then pdl_wait(), which
+// returns once every earlier kernel of the stream has completed with its
+// writes visible, before its first global load or store. No kernel signals
+// its dependents early (griddepcontrol.launch_dependents): dependents that
+// start during a tail crowd onto the few idle SMs and then run unbalanced.
+// Without the launch attribute pdl_wait() does nothing.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+extern int g_pdl;   // 1: launch_pdl() sets the attribute (default); 0: plain stream order
+
+// Fills attrs[0] with the PDL attribute when enabled; returns the count used.
+inline unsigned pdl_attr(cudaLaunchAttribute *attrs)
+{
+    if (!g_pdl) return 0;
+    attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[0].val.programmaticStreamSerializationAllowed = 1;
+    return 1;
+}
+
+template <typename... P, typename... A>
+inline cudaError_t launch_pdl(void (*fn)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A &&...args)
+{
+    cudaLaunchAttribute attrs[1];
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = grid;
+    lc.blockDim = block;
+    lc.dynamicSmemBytes = smem;
+    lc.stream = s;
+    lc.attrs = attrs;
+    lc.numAttrs = pdl_attr(attrs);
+    return cudaLaunchKernelEx(&lc, fn, static_cast<A &&>(args)...);
+}
+
 }  // namespace tcg
 
 #define TCG_CUDA(call)                                                        \

@@ -12,6 +12,7 @@ Each case runs `--warmup` untimed launches, then `--reps` timed ones with a
 256 MB memset between them (L2 flush), and prints one JSON line.
 """
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -76,14 +77,18 @@ class SplitOperands:
 
 def case_gemm(a):
     old_sk = tcg.lib().tcg_gemm_set_streamk(a.streamk)
+    old_tma = tcg.lib().tcg_gemm_set_tma_store(a.tma_store)
     ops = SplitOperands(a.M, a.N, a.K)
     with tcg.DeviceBuffer(256 << 20) as flush:
         ms, _ = timed(lambda: ops.run(a.cfg), a.warmup, a.reps, flush)
+    plan = (ctypes.c_int * 4)()
+    tcg.lib().tcg_gemm_last_plan(plan)
     ops.close()
     tcg.lib().tcg_gemm_set_streamk(old_sk)
+    tcg.lib().tcg_gemm_set_tma_store(old_tma)
     flops = 2.0 * a.M * a.N * a.K
     return {"case": "gemm", "M": a.M, "N": a.N, "K": a.K, "cfg": a.cfg, "streamk": a.streamk, "ms": round(ms, 4),
-            "tflops": round(flops / ms / 1e9, 1)}
+            "tflops": round(flops / ms / 1e9, 1), "grid": plan[0], "split": plan[1], "tma_store": plan[3]}
 
 
 def case_gemmsweep(a):
@@ -151,6 +156,8 @@ def case_vit(a):
     path, cfg = G.cached_vit_gguf(cache, a.model, 0, **over)
     # the GEMM plans of a batch size are made at its first forward
     old_cfg, old_sk = L.tcg_gemm_force_cfg(a.cfg), L.tcg_gemm_set_streamk(a.streamk)
+    old_pdl = L.tcg_set_pdl(a.pdl)
+    old_tma = L.tcg_gemm_set_tma_store(a.tma_store)
     m = tcg.VitModel(path)
     m.upload(a.batch)
     px = G.make_pixels(a.batch, cfg["image"], 1)
@@ -160,8 +167,10 @@ def case_vit(a):
     m.close()
     L.tcg_gemm_force_cfg(old_cfg)
     L.tcg_gemm_set_streamk(old_sk)
+    L.tcg_set_pdl(old_pdl)
+    L.tcg_gemm_set_tma_store(old_tma)
     return {"case": "vit", "model": a.model, "layers": cfg["n_layer"], "batch": a.batch, "cfg": a.cfg,
-            "streamk": a.streamk, "ms": round(ms, 4),
+            "streamk": a.streamk, "pdl": a.pdl, "tma_store": a.tma_store, "ms": round(ms, 4),
             "images/s": round(a.batch / ms * 1e3, 1)}
 
 
@@ -174,6 +183,7 @@ def main():
     g.add_argument("--K", type=int, default=768)
     g.add_argument("--cfg", type=int, default=-1)
     g.add_argument("--streamk", type=int, default=1)
+    g.add_argument("--tma-store", type=int, default=1)
     gs = sub.add_parser("gemmsweep")
     gs.add_argument("--chunks", default="32,64,128,256,4096")
     gs.add_argument("--cfgs", default="all")
@@ -192,6 +202,8 @@ def main():
     v.add_argument("--steps", type=int, default=3)
     v.add_argument("--cfg", type=int, default=-1, help="GEMM configuration for every linear (-1: automatic)")
     v.add_argument("--streamk", type=int, default=1, help="0: every GEMM tile computed whole")
+    v.add_argument("--pdl", type=int, default=1, help="0: no programmatic dependent launch")
+    v.add_argument("--tma-store", type=int, default=1, help="0: GEMM epilogues on plain stores")
     for p in (g, gs, mv, dq, v):
         p.add_argument("--warmup", type=int, default=3)
         p.add_argument("--reps", type=int, default=5)

@@ -155,6 +155,39 @@ def test_gemm_untransposed_and_odd_k(dev):
     assert np.abs(y.download((9, 7)) - want).max() <= 1e-5 * np.abs(want).max()
 
 
+@pytest.mark.parametrize("cfg", [-1, 13, 14, 1, 6])
+@pytest.mark.parametrize("M,N,K", [(1, 64, 4), (127, 100, 12), (300, 768, 768), (261, 130, 3072), (1600, 2304, 768)])
+def test_bulk_store_epilogue(dev, cfg, M, N, K):
+    """Bulk tensor stores (N a multiple of 4) and plain stores give the same
+    bits; partial 8-column units and row tiles past M are clipped."""
+    import ctypes
+    L = tcg.lib()
+    rng = np.random.default_rng(M + 3 * N + K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    W = (rng.standard_normal((N, K)) * 0.05).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    xp, wp, bp = dev.put(x), dev.put(W), dev.put(b)
+    got = {}
+    for t in (0, 1):
+        y = dev.empty(M * N + 64)
+        tcg.check(L.tcg_memset(y.ptr, 0x7f, (M * N + 64) * 4))
+        old = L.tcg_gemm_set_tma_store(t)
+        try:
+            tcg.check(L.tcg_linear_cfg(y.ptr, xp, wp, bp, M, N, K, cfg), f"cfg {cfg} tma {t}")
+        finally:
+            L.tcg_gemm_set_tma_store(old)
+        plan = (ctypes.c_int * 4)()
+        L.tcg_gemm_last_plan(plan)
+        assert plan[3] == (1 if t and N % 4 == 0 else 0)
+        full = y.download((M * N + 64,))
+        assert np.all(full[M * N:].view(np.uint32) == 0x7f7f7f7f)      # nothing written past the matrix
+        got[t] = full[:M * N].reshape(M, N)
+    assert np.array_equal(got[0], got[1])
+    want = oracle.linear(x, W, b, M, N, K)
+    assert np.abs(got[1].astype(np.float64) - want).max() <= GEMM_TOL * np.abs(want).max()
+    assert L.tcg_device_error() == 0
+
+
 @pytest.mark.parametrize("M,N,K", [(700, 512, 768), (2000, 2304, 768), (1600, 768, 3072)])
 def test_streamk_split(dev, M, N, K):
     L = tcg.lib()

@@ -141,6 +141,28 @@ def test_streamk_forward(gpu, cache_dir):
     assert L.tcg_device_error() == 0
 
 
+def test_bulk_store_epilogue_matches_plain_stores(gpu, cache_dir):
+    """The GEMM epilogue that writes through bulk tensor stores (rows one to
+    one, lane = row) does the same round-to-nearest operations, in the same
+    order, as the plain-store one: the embeddings are identical, bit for bit.
+    Batch 9 leaves the last row tile partly and wholly below the matrix."""
+    L = tcg.lib()
+    path, cfg = model(cache_dir, "vit-b32", n_layer=3)
+    px = G.make_pixels(9, cfg["image"], 11)
+    outs = {}
+    for t in (0, 1):
+        old = L.tcg_gemm_set_tma_store(t)
+        m = tcg.VitModel(path)
+        try:
+            m.upload(9)
+            outs[t], _ = m.encode(px)
+        finally:
+            m.close()
+            L.tcg_gemm_set_tma_store(old)
+    assert np.array_equal(outs[0], outs[1])
+    assert L.tcg_device_error() == 0
+
+
 def test_async_submit_matches_blocking(gpu, cache_dir):
     import ctypes
     L = tcg.lib()
