@@ -3,9 +3,10 @@
 // dequant-matvec.
 //
 // Layout of one warp's work: a group of 8 superblocks (1152 B of Q4_K or
-// 1680 B of Q6_K, both multiples of 16 B) is copied global -> shared with
-// 128-bit loads, then every lane decodes 8 consecutive weights of each
-// superblock (lane l owns weights 8l..8l+7) and writes them as two float4.
+// 1680 B of Q6_K) is loaded with 128-bit loads while the previous group is
+// decoded, then copied to shared memory, and every lane decodes 8 consecutive
+// weights of each superblock (lane l owns weights 8l..8l+7) and writes them as
+// two float4.
 // Arithmetic is the rounding sequence of the C restatement with no
 // contraction: Q4_K w = (d*sc)*q - (dmin*m), Q6_K w = (d*sc)*q.
 #include "tcg_common.cuh"
@@ -23,6 +24,29 @@ constexpr int WARPS = 8;          // warps per CTA
 template <int TYPE> struct KQ;
 template <> struct KQ<GGML_TYPE_Q4_K> { static constexpr int BYTES = 144; };
 template <> struct KQ<GGML_TYPE_Q6_K> { static constexpr int BYTES = 210; };
+
+// Packed fp32 pairs (low word = first element), each half rounded to nearest
+// like the scalar instruction.
+typedef unsigned long long u64;
+__device__ __forceinline__ u64 fma2(u64 a, u64 b, u64 c)
+{
+    u64 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ u64 add2(u64 a, u64 b)
+{
+    u64 d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// bytes j and j+1 of w as the float pair (2^23 + byte_j, 2^23 + byte_j+1)
+__device__ __forceinline__ u64 magic2(uint32_t w, int j)
+{
+    const uint32_t a = __byte_perm(w, 0x4B000000u, 0x7440u | (unsigned)j);
+    const uint32_t b = __byte_perm(w, 0x4B000000u, 0x7440u | (unsigned)(j + 1));
+    return (u64)a | ((u64)b << 32);
+}
 
 // Exact binary16 -> binary32 by bit manipulation (tc_f16_to_f32,
 // src/dequant.c:5-38): subnormals renormalised, NaN payloads kept.
@@ -114,27 +138,59 @@ __device__ __forceinline__ void decode8<GGML_TYPE_Q6_K>(const uint8_t *blk, int 
     }
 }
 
+// Warps stride over chunks of GROUP superblocks (chunk c to warp c mod
+// warps, so the grid sweeps one contiguous window of the tensor). The
+// 16-byte-aligned span covering a warp's next chunk is loaded into registers
+// while the current one is decoded from its shared buffer (an aligned 16-byte
+// word that holds a byte of the tensor lies in the same page as that byte, so
+// the span's edges cannot fault); each lane writes its 8 weights of every
+// superblock as two float4.
 template <int TYPE>
 __global__ void __launch_bounds__(WARPS * 32)
 dequant_kq_kernel(const uint8_t *__restrict__ src, float *__restrict__ dst, size_t nblocks)
 {
     constexpr int BB = KQ<TYPE>::BYTES;
-    __shared__ __align__(16) uint8_t buf[WARPS][GROUP * BB];
+    constexpr int C = GROUP;
+    constexpr int SPAN = (C * BB + 30) / 16 * 16;            // bytes of the widest aligned span
+    constexpr int LPL = (SPAN / 16 + 31) / 32;               // 16-byte loads per lane
+    __shared__ __align__(16) uint8_t buf[WARPS][SPAN];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const size_t ngroups = (nblocks + GROUP - 1) / GROUP;
-    for (size_t grp = (size_t)blockIdx.x * WARPS + wid; grp < ngroups; grp += (size_t)gridDim.x * WARPS) {
-        const size_t b0 = grp * GROUP;
-        const int nb = (int)min((size_t)GROUP, nblocks - b0);
-        stage(buf[wid], src + b0 * BB, nb * BB, lane);
+    const size_t nw = (size_t)gridDim.x * WARPS;
+    const size_t nchunks = (nblocks + C - 1) / C;
+    const uintptr_t base = (uintptr_t)src;
+    uint4 r[LPL];
+    auto span = [&](size_t c, uintptr_t &a0, size_t &b0, int &nb) {
+        b0 = c * C;
+        nb = (int)min((size_t)C, nblocks - b0);
+        a0 = (base + b0 * BB) & ~(uintptr_t)15;
+        return (int)((((base + (b0 + nb) * BB + 15) & ~(uintptr_t)15) - a0) / 16);
+    };
+    auto load = [&](size_t c) {
+        uintptr_t a0; size_t b0; int nb;
+        const int n16 = span(c, a0, b0, nb);
+#pragma unroll
+        for (int u = 0; u < LPL; u++)
+            if (lane + 32 * u < n16) r[u] = __ldg(reinterpret_cast<const uint4 *>(a0) + lane + 32 * u);
+    };
+    size_t c = (size_t)blockIdx.x * WARPS + wid;
+    if (c < nchunks) load(c);
+    for (; c < nchunks; c += nw) {
+        uintptr_t a0; size_t b0; int nb;
+        const int n16 = span(c, a0, b0, nb);
+        const int off = (int)((base + b0 * BB) - a0);
+        __syncwarp();                                        // the previous chunk is decoded
+#pragma unroll
+        for (int u = 0; u < LPL; u++)
+            if (lane + 32 * u < n16) reinterpret_cast<uint4 *>(buf[wid])[lane + 32 * u] = r[u];
         __syncwarp();
+        if (c + nw < nchunks) load(c + nw);                  // in flight during the decode below
         for (int b = 0; b < nb; b++) {
             float w[8];
-            decode8<TYPE>(buf[wid] + b * BB, lane, w);
+            decode8<TYPE>(buf[wid] + off + b * BB, lane, w);
             float4 *o = reinterpret_cast<float4 *>(dst + (b0 + b) * QK + 8 * lane);
             o[0] = make_float4(w[0], w[1], w[2], w[3]);
             o[1] = make_float4(w[4], w[5], w[6], w[7]);
         }
-        __syncwarp();
     }
 }
 
@@ -214,7 +270,6 @@ matvec_kq_kernel(const uint8_t *__restrict__ W, const float *__restrict__ x, flo
 //   Q4_K  sum (a q - c) x  =  a * sum(q x) - c * sum(x)   per sub-block of 32
 //   Q6_K  sum (d sc) q x   =  (d sc) * sum(q x)           per sub-block of 16
 constexpr int MV_WARPS = 16;
-typedef unsigned long long u64;
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src)
 {
@@ -223,25 +278,6 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src)
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-__device__ __forceinline__ u64 fma2(u64 a, u64 b, u64 c)
-{
-    u64 d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ u64 add2(u64 a, u64 b)
-{
-    u64 d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-// bytes j and j+1 of w as the float pair (2^23 + byte_j, 2^23 + byte_j+1)
-__device__ __forceinline__ u64 magic2(uint32_t w, int j)
-{
-    const uint32_t a = __byte_perm(w, 0x4B000000u, 0x7440u | (unsigned)j);
-    const uint32_t b = __byte_perm(w, 0x4B000000u, 0x7440u | (unsigned)(j + 1));
-    return (u64)a | ((u64)b << 32);
-}
 
 // sum_i (v_i - off) x_i over the 8 bytes v of (w0, w1); x 16-byte aligned in
 // shared memory; neg_off2 holds -(2^23 + off) twice.
