@@ -332,6 +332,170 @@ mha64_kernel(const float *__restrict__ q, const float *__restrict__ k, const flo
         if (4 * ty + i < nq) put4(out, base + q0 + 4 * ty + i, col + 4 * tx, o[i]);
 }
 
+// head_dim 64, any T whose scores fit (ViT-L/14: 257 tokens): one CTA per
+// (head, image, block of BQ queries), BQ/4 x 16 threads. The block's scores
+// against all T keys stay in shared memory (the two-pass softmax of
+// src/ops.c:129-139), while K and V stream through a double-buffered window
+// of 64 keys, copied by cp.async in their row-major layout.
+//   scores: thread (ty, tx) takes keys 4ty.., queries 4tx.. of the window; per
+//           four dims, four float4 of K rows and four float4 of Q^T (Q stored
+//           d-major once per CTA); sums run over d in order.
+//   output: thread (qy, dx) takes queries 4qy.., dims 4dx..; per four keys,
+//           four float4 of P and four of V; sums run over keys in order.
+// The arithmetic is that of mha64_kernel, operation for operation.
+constexpr int MHB_W = 64;            // keys per K/V window
+
+__device__ __forceinline__ void mhb_cp16(float *dst, const float *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src) : "memory");
+}
+
+__host__ __device__ __forceinline__ int mhb_stride(int T)
+{
+    const int T4 = (T + 3) & ~3;
+    return (T4 / 4) & 1 ? T4 : T4 + 4;        // an odd number of float4 per score row
+}
+
+template <int BQ>
+static size_t mhb_smem(int T)
+{
+    return ((size_t)64 * BQ + (size_t)BQ * mhb_stride(T) + 2 * MHB_W * 64) * sizeof(float);
+}
+
+template <int BQ>
+__global__ void __launch_bounds__(BQ * 4)
+mha64b_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v, int ldi,
+              int T, OutSpec out)
+{
+    constexpr int NT = BQ * 4, QG = BQ / 4;
+    pdl_wait();
+    extern __shared__ float4 sm4[];
+    const int TS = mhb_stride(T);
+    float *Qt = reinterpret_cast<float *>(sm4);            // [64 d][BQ]
+    float *Ss = Qt + 64 * BQ;                              // [BQ][TS]
+    float *KV = Ss + (size_t)BQ * TS;                      // [2][MHB_W keys][64 d]
+    const int col = blockIdx.x * 64;
+    const size_t base = (size_t)blockIdx.y * T;
+    const int q0 = blockIdx.z * BQ, nq = min(BQ, T - q0);
+    const int tid = threadIdx.x;
+    const int nwin = (T + MHB_W - 1) / MHB_W;
+
+    // rows t0 .. t0 + 63 of K or V into window buffer w (rows past T left as they are)
+    auto fetch = [&](const float *src, int win) {
+        float *dst = KV + (win & 1) * MHB_W * 64;
+        const int t0 = win * MHB_W;
+        for (int i = tid; i < MHB_W * 16; i += NT) {
+            const int r = i >> 4, c = (i & 15) * 4;
+            if (t0 + r < T) mhb_cp16(dst + r * 64 + c, src + (base + t0 + r) * (size_t)ldi + col + c);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    fetch(k, 0);
+    // Q^T, d-major: a warp's lanes take consecutive queries of one float4 of dims
+    for (int i = tid; i < BQ * 16; i += NT) {
+        const int qq = i % BQ, d4 = i / BQ;
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (qq < nq) x = __ldg(reinterpret_cast<const float4 *>(q + (base + q0 + qq) * (size_t)ldi + col + 4 * d4));
+        Qt[(4 * d4 + 0) * BQ + qq] = x.x;
+        Qt[(4 * d4 + 1) * BQ + qq] = x.y;
+        Qt[(4 * d4 + 2) * BQ + qq] = x.z;
+        Qt[(4 * d4 + 3) * BQ + qq] = x.w;
+    }
+
+    const float scale = 1.0f / sqrtf(64.0f);
+    {
+        const int ty = tid / QG, tx = tid % QG;            // keys 4ty.., queries 4tx..
+        for (int w = 0; w < nwin; w++) {
+            if (w + 1 < nwin) fetch(k, w + 1);
+            else asm volatile("cp.async.commit_group;" ::: "memory");
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+            __syncthreads();
+            const float *Kb = KV + (w & 1) * MHB_W * 64;
+            const int kc = w * MHB_W + 4 * ty;
+            if (kc < T) {
+                float acc[4][4] = {};                      // [key j][query i]
+#pragma unroll 4
+                for (int d = 0; d < 64; d += 4) {
+                    float4 kr[4], qc[4];
+#pragma unroll
+                    for (int j = 0; j < 4; j++) kr[j] = *reinterpret_cast<const float4 *>(Kb + (4 * ty + j) * 64 + d);
+#pragma unroll
+                    for (int c = 0; c < 4; c++) qc[c] = *reinterpret_cast<const float4 *>(Qt + (d + c) * BQ + 4 * tx);
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        const float qv[4] = { qc[c].x, qc[c].y, qc[c].z, qc[c].w };
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const float kv = c == 0 ? kr[j].x : c == 1 ? kr[j].y : c == 2 ? kr[j].z : kr[j].w;
+#pragma unroll
+                            for (int i = 0; i < 4; i++) acc[j][i] = fmaf(qv[i], kv, acc[j][i]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    *reinterpret_cast<float4 *>(Ss + (4 * tx + i) * TS + kc) =
+                        make_float4(__fmul_rn(acc[0][i], scale), __fmul_rn(acc[1][i], scale),
+                                    __fmul_rn(acc[2][i], scale), __fmul_rn(acc[3][i], scale));
+            }
+            __syncthreads();                               // window w is read; w + 2 may overwrite it
+        }
+    }
+    fetch(v, 0);                                           // V's first window loads during the softmax
+
+    const int lane = tid & 31, wid = tid >> 5;
+    for (int r = wid; r < nq; r += NT / 32) {
+        float *row = Ss + r * TS;
+        float mx = -INFINITY;
+        for (int s = lane; s < T; s += 32) mx = fmaxf(mx, row[s]);
+        mx = warp_max(mx);
+        double sum = 0.0;
+        for (int s = lane; s < T; s += 32) {
+            const float e = expf(__fsub_rn(row[s], mx));
+            row[s] = e;
+            sum += (double)e;
+        }
+        const float inv = (float)(1.0 / warp_sum(sum));
+        for (int s = lane; s < T; s += 32) row[s] = __fmul_rn(row[s], inv);
+    }
+
+    const int qy = tid >> 4, dx = tid & 15;                // queries 4qy.., dims 4dx..
+    float o[4][4] = {};
+    for (int w = 0; w < nwin; w++) {
+        if (w + 1 < nwin) fetch(v, w + 1);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        __syncthreads();                                   // also: the softmax is done (first window)
+        const float *Vb = KV + (w & 1) * MHB_W * 64;
+        const int t0 = w * MHB_W, n = min(MHB_W, T - t0);
+        if (4 * qy < nq) {
+            for (int s0 = 0; s0 < n; s0 += 4) {
+                float4 pr[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) pr[i] = *reinterpret_cast<const float4 *>(Ss + (4 * qy + i) * TS + t0 + s0);
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    if (s0 + u >= n) break;
+                    const float4 vv = *reinterpret_cast<const float4 *>(Vb + (s0 + u) * 64 + 4 * dx);
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float pv = u == 0 ? pr[i].x : u == 1 ? pr[i].y : u == 2 ? pr[i].z : pr[i].w;
+                        o[i][0] = fmaf(pv, vv.x, o[i][0]);
+                        o[i][1] = fmaf(pv, vv.y, o[i][1]);
+                        o[i][2] = fmaf(pv, vv.z, o[i][2]);
+                        o[i][3] = fmaf(pv, vv.w, o[i][3]);
+                    }
+                }
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+        if (4 * qy + i < nq) put4(out, base + q0 + 4 * qy + i, col + 4 * dx, o[i]);
+}
+
 // head_dim 64 and T <= 64 (ViT-B/32: 50 tokens): one CTA of 16 x 16 threads
 // per (head, image). Q and K are stored d-major (t contiguous), so the 4 x 4
 // score tile of thread (ty, tx) -- rows 4ty.., keys 4tx.. -- costs two float4
@@ -476,6 +640,8 @@ static size_t mha64_smem(int T)
     return (MHA_BQ * 64 + 3 * 64 * T4) * sizeof(float);
 }
 
+int g_mha_variant = 1;      // T > 64: 0 whole-K/V kernel, 1 / 2 streaming kernel with 64 / 48-query blocks
+
 bool launch_mha(const float *q, const float *k, const float *v, int ldi, int T, int n_head, int hd,
                 int n_img, const OutSpec &out, cudaStream_t s)
 {
@@ -488,6 +654,25 @@ bool launch_mha(const float *q, const float *k, const float *v, int ldi, int T, 
         TCG_CUDA(launch_pdl(mha64s_kernel, grid, 256, 0, s, q, k, v, ldi, T, out));
         TCG_LAUNCHED();
         return true;
+    }
+    if (hd == 64 && aligned && g_mha_variant != 0) {
+        const bool q48 = g_mha_variant == 2;
+        const size_t sm = q48 ? mhb_smem<48>(T) : mhb_smem<64>(T);
+        if (sm <= 227 * 1024) {
+            static unsigned doneb[64];
+            const int dev = ctx().device & 63, bit = q48 ? 2 : 1;
+            if (!(doneb[dev] & bit)) {
+                TCG_CUDA(cudaFuncSetAttribute(q48 ? mha64b_kernel<48> : mha64b_kernel<64>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+                doneb[dev] |= bit;
+            }
+            const int bq = q48 ? 48 : 64;
+            dim3 grid(n_head, n_img, (T + bq - 1) / bq);
+            if (q48) TCG_CUDA(launch_pdl(mha64b_kernel<48>, grid, 192, sm, s, q, k, v, ldi, T, out));
+            else TCG_CUDA(launch_pdl(mha64b_kernel<64>, grid, 256, sm, s, q, k, v, ldi, T, out));
+            TCG_LAUNCHED();
+            return true;
+        }
     }
     if (hd == 64 && aligned && mha64_smem(T) <= 227 * 1024) {
         static unsigned done64[64];
@@ -812,3 +997,13 @@ bool tcg_scale(float *out, const float *x, float s, size_t n)
 }
 
 }  // extern "C"
+
+// Tuning and test hook: the attention kernel for head_dim 64 and T > 64
+// (0: whole K/V in shared memory, 1 / 2: streamed K/V with 64 / 48-query
+// blocks; identical results). Returns the previous setting.
+extern "C" int tcg_set_attention_variant(int variant)
+{
+    const int old = tcg::g_mha_variant;
+    tcg::g_mha_variant = variant < 0 ? 0 : (variant > 2 ? 2 : variant);
+    return old;
+}

@@ -125,6 +125,34 @@ def test_mha_vs_oracle(dev, T, H, HD):
     assert np.abs(got - want).max() <= 1e-5 * np.abs(want).max()
 
 
+@pytest.mark.parametrize("T,H", [(65, 2), (100, 3), (257, 2), (300, 1), (577, 2)])
+def test_mha_long_sequence_kernels_agree(dev, T, H):
+    """For head_dim 64 and T > 64 the streamed-K/V kernel (64- or 48-query
+    blocks) performs the whole-K/V kernel's operations in the same order:
+    identical bits where both apply, and within the oracle's bound. T = 577
+    fits only the streamed kernel (the others would need 318 KB of shared
+    memory and the call is refused)."""
+    L = tcg.lib()
+    rng = np.random.default_rng(T + 100 * H)
+    q, k, v = (rng.standard_normal((T, H * 64)).astype(np.float32) for _ in range(3))
+    qp, kp, vp = dev.put(q), dev.put(k), dev.put(v)
+    got = {}
+    for variant in ((0, 1, 2) if T <= 300 else (1, 2)):
+        y = dev.empty(T * H * 64)
+        old = L.tcg_set_attention_variant(variant)
+        try:
+            tcg.check(L.tcg_mha(y.ptr, qp, kp, vp, T, H, 64), f"variant {variant}")
+        finally:
+            L.tcg_set_attention_variant(old)
+        got[variant] = y.download((T, H * 64))
+    if T <= 300:
+        assert np.array_equal(got[0], got[1]) and np.array_equal(got[0], got[2])
+    assert np.array_equal(got[1], got[2])
+    want = oracle.mha(q, k, v, T, H, 64)
+    assert np.abs(got[1] - want).max() <= 1e-5 * np.abs(want).max()
+    assert L.tcg_device_error() == 0
+
+
 SHAPES = [(1, 64, 4), (127, 100, 12), (129, 200, 588), (300, 768, 768), (50, 2304, 768), (261, 130, 3072)]
 
 
