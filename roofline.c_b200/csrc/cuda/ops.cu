@@ -66,30 +66,22 @@ __global__ void layernorm_kernel(const float *x, int ld_in, const float *__restr
 // The same LayerNorm with the row held in registers: lane l owns the float4s
 // l, l + 32, ... (VPL of them, cols = 128 * VPL), read once and written once
 // as float4 (plain or tf32 hi/lo). Same arithmetic as layernorm_kernel; the
-// double sums run in another order. Gamma and beta are staged in shared
-// memory once per CTA, so the output loop waits on no global load.
+// double sums run in another order. (Staging gamma/beta in shared memory
+// needed 111 registers, two CTAs per SM, and ran 15% slower.)
 template <int VPL>
-__global__ void __launch_bounds__(256, 2)
+__global__ void __launch_bounds__(256, 4)
 layernorm_vec_kernel(const float *x, int ld_in, const float *__restrict__ g, const float *__restrict__ b, int rows,
                      float eps, OutSpec out)
 {
     pdl_wait();
     constexpr int cols = 128 * VPL;
-    __shared__ float4 gs[32 * VPL], bs[32 * VPL];       // gamma, beta: shared by the CTA's eight rows
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    float4 v[VPL];
-    if (row < rows) {
-        const float4 *in = reinterpret_cast<const float4 *>(x + (size_t)row * ld_in);
-#pragma unroll
-        for (int i = 0; i < VPL; i++) v[i] = in[lane + 32 * i];
-    }
-    for (int i = threadIdx.x; i < 32 * VPL; i += blockDim.x) {
-        if (g) gs[i] = reinterpret_cast<const float4 *>(g)[i];
-        if (b) bs[i] = reinterpret_cast<const float4 *>(b)[i];
-    }
-    __syncthreads();
     if (row >= rows) return;
+    const float4 *in = reinterpret_cast<const float4 *>(x + (size_t)row * ld_in);
+    float4 v[VPL];
+#pragma unroll
+    for (int i = 0; i < VPL; i++) v[i] = in[lane + 32 * i];
     double s = 0.0;
 #pragma unroll
     for (int i = 0; i < VPL; i++) s += ((double)v[i].x + (double)v[i].y) + ((double)v[i].z + (double)v[i].w);
@@ -110,12 +102,12 @@ layernorm_vec_kernel(const float *x, int ld_in, const float *__restrict__ g, con
         float o[4] = { __fmul_rn((float)((double)v[i].x - mean), inv), __fmul_rn((float)((double)v[i].y - mean), inv),
                        __fmul_rn((float)((double)v[i].z - mean), inv), __fmul_rn((float)((double)v[i].w - mean), inv) };
         if (g) {
-            const float4 gg = gs[lane + 32 * i];
+            const float4 gg = *reinterpret_cast<const float4 *>(g + c);
             o[0] = __fmul_rn(o[0], gg.x); o[1] = __fmul_rn(o[1], gg.y);
             o[2] = __fmul_rn(o[2], gg.z); o[3] = __fmul_rn(o[3], gg.w);
         }
         if (b) {
-            const float4 bv = bs[lane + 32 * i];
+            const float4 bv = *reinterpret_cast<const float4 *>(b + c);
             o[0] = __fadd_rn(o[0], bv.x); o[1] = __fadd_rn(o[1], bv.y);
             o[2] = __fadd_rn(o[2], bv.z); o[3] = __fadd_rn(o[3], bv.w);
         }
