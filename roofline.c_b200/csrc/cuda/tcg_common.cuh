@@ -49,6 +49,7 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 
 extern int g_pdl;   // 1: launch_pdl() sets the attribute (default); 0: plain stream order
 
+
 // Fills attrs[0] with the PDL attribute when enabled; returns the count used.
 inline unsigned pdl_attr(cudaLaunchAttribute *attrs)
 {

@@ -131,9 +131,10 @@ def case_matvec(a):
     with tcg.DeviceBuffer.from_array(raw) as w, tcg.DeviceBuffer.from_array(x) as xb, \
             tcg.DeviceBuffer(a.N * 4) as y, tcg.DeviceBuffer(256 << 20) as flush:
         ms, _ = timed(lambda: tcg.check(L.tcg_matvec_q(y.ptr, w.ptr, xb.ptr, a.N, a.K, qt)), a.warmup, a.reps, flush)
+    kern = L.tcg_matvec_last_kernel()
     nbytes = a.N * a.K // 256 * bb + 4 * (a.N + a.K)
-    return {"case": "matvec", "type": a.type, "N": a.N, "K": a.K, "ms": round(ms, 5), "bytes": nbytes,
-            "GB/s": round(nbytes / ms / 1e6, 1)}
+    return {"case": "matvec", "type": a.type, "N": a.N, "K": a.K, "kernel": kern, "ms": round(ms, 5),
+            "bytes": nbytes, "GB/s": round(nbytes / ms / 1e6, 1)}
 
 
 def case_dequant(a):
