@@ -647,6 +647,8 @@ bool launch_mha(const float *q, const float *k, const float *v, int ldi, int T, 
         TCG_LAUNCHED();
         return true;
     }
+    if (hd == 64 && aligned && g_mha_variant == 3 && launch_mha64_tc_long(q, k, v, ldi, T, n_head, n_img, out, s))
+        return true;
     if (hd == 64 && aligned && g_mha_variant != 0) {
         const bool q48 = g_mha_variant == 2;
         const size_t sm = q48 ? mhb_smem<48>(T) : mhb_smem<64>(T);
@@ -992,10 +994,11 @@ bool tcg_scale(float *out, const float *x, float s, size_t n)
 
 // Tuning and test hook: the attention kernel for head_dim 64 and T > 64
 // (0: whole K/V in shared memory, 1 / 2: streamed K/V with 64 / 48-query
-// blocks; identical results). Returns the previous setting.
+// blocks, identical results; 3: tensor cores where 128 <= T <= 1024).
+// Returns the previous setting.
 extern "C" int tcg_set_attention_variant(int variant)
 {
     const int old = tcg::g_mha_variant;
-    tcg::g_mha_variant = variant < 0 ? 0 : (variant > 2 ? 2 : variant);
+    tcg::g_mha_variant = variant < 0 ? 0 : (variant > 3 ? 3 : variant);
     return old;
 }

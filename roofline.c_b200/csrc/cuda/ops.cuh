@@ -21,6 +21,10 @@ bool launch_layernorm(const float *x, int ld_in, const float *g, const float *b,
 
 // Attention over n_img images of T tokens (src/ops.c:112-151). Image i,
 // token t, head h reads q at q + (i*T + t)*ldi + h*hd (same for k, v).
+// head_dim 64, 128 <= T <= 1024 on the tensor cores (attn_tc.cu); false when the shape does not fit.
+bool launch_mha64_tc_long(const float *q, const float *k, const float *v, int ldi, int T, int n_head, int n_img,
+                          const OutSpec &out, cudaStream_t s);
+
 bool launch_mha(const float *q, const float *k, const float *v, int ldi, int T, int n_head, int hd,
                 int n_img, const OutSpec &out, cudaStream_t s);
 

@@ -153,6 +153,25 @@ def test_mha_long_sequence_kernels_agree(dev, T, H):
     assert L.tcg_device_error() == 0
 
 
+@pytest.mark.parametrize("T,H", [(128, 2), (129, 3), (200, 2), (257, 4), (300, 1), (577, 2)])
+def test_mha_tensor_core_long(dev, T, H):
+    """head_dim 64, 128 <= T: whole blocks of 128 queries on tcgen05 (3xTF32,
+    running-maximum softmax), the remaining rows one warp per row; within the
+    oracle's bound."""
+    L = tcg.lib()
+    rng = np.random.default_rng(T + 7 * H)
+    q, k, v = (rng.standard_normal((T, H * 64)).astype(np.float32) for _ in range(3))
+    y = dev.empty(T * H * 64)
+    old = L.tcg_set_attention_variant(3)
+    try:
+        tcg.check(L.tcg_mha(y.ptr, dev.put(q), dev.put(k), dev.put(v), T, H, 64), "tensor-core attention")
+    finally:
+        L.tcg_set_attention_variant(old)
+    got, want = y.download((T, H * 64)), oracle.mha(q, k, v, T, H, 64)
+    assert np.abs(got - want).max() <= 1e-5 * np.abs(want).max()
+    assert L.tcg_device_error() == 0
+
+
 SHAPES = [(1, 64, 4), (127, 100, 12), (129, 200, 588), (300, 768, 768), (50, 2304, 768), (261, 130, 3072)]
 
 

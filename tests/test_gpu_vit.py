@@ -94,6 +94,28 @@ def test_l14_two_layers_vs_oracle(gpu, cache_dir):
         m.close()
 
 
+def test_l14_tensor_core_attention_vs_oracle(gpu, cache_dir):
+    """ViT-L/14 (T = 257) with attention on the tensor cores, two images."""
+    L = tcg.lib()
+    path, cfg = model(cache_dir, "vit-l14", n_layer=2)
+    w = G.make_vit_weights(cfg, 0)
+    px = G.make_pixels(2, cfg["image"], 4)
+    old = L.tcg_set_attention_variant(3)
+    m = tcg.VitModel(path)
+    try:
+        m.upload(2)
+        out, taps = m.encode(px, taps=True)
+        for i in (0, 1):
+            ref = oracle.PortVit(cfg, w).forward(px[i])
+            assert rel_inf(out[i], ref["embedding"]) <= TOL
+            for k in TAPS:
+                assert rel_inf(taps[k][i], ref[k]) <= TOL, (i, k)
+        assert L.tcg_device_error() == 0
+    finally:
+        m.close()
+        L.tcg_set_attention_variant(old)
+
+
 def test_batch_invariance_and_graph_replay(gpu, cache_dir):
     L = tcg.lib()
     path, cfg = model(cache_dir, "vit-b32", n_layer=3)
