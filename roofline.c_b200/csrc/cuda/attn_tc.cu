@@ -2,17 +2,20 @@
 // head_dim 64 and long sequences (ViT-L/14: T = 257) on the 5th-generation
 // tensor cores, fp32-accurate through 3xTF32.
 //
-// One CTA of 128 threads takes 128 consecutive queries of one (image, head);
-// thread r owns query row r = TMEM lane r. Keys go in blocks of 64:
+// One CTA of 256 threads takes 128 consecutive queries of one (image, head);
+// threads r and r + 128 share query row r = TMEM lane r, each with 32 of a
+// block's keys and 32 of the output dims. Keys go in blocks of 64, each
+// block's K and V loaded into registers while the previous block computes:
 //   S = Q K^T    128 x 64 in TMEM columns 0-63: 8 K-steps of 8 dims x 3 tf32
 //                products (lo*hi, hi*lo, hi*hi), 24 kind::tf32 MMAs;
-//   softmax      thread r scales its row, keeps a running maximum m, rescales
-//                by a = expf(m_old - m), takes p = expf(s - m), and adds the
-//                p to a double row sum;
+//   softmax      the row's two threads scale their scores and exchange their
+//                block maxima through shared memory; each keeps the running
+//                maximum m, rescales by a = expf(m_old - m), takes p =
+//                expf(s - m) and adds its p to its half of a double row sum;
 //   O += P V     P goes back to shared memory as tf32 pairs and 24 MMAs give
-//                P V (128 x 64) in TMEM columns 64-127; thread r folds its
-//                row into 64 fp32 registers: o = o * a + pv.
-// At the end o / sum is written. The result is the reference's softmax up to
+//                P V (128 x 64) in TMEM columns 64-127; each thread folds its
+//                32 dims into fp32 registers: o = o * a + pv.
+// At the end o / (sum of the two halves) is written. The result is the reference's softmax up to
 // the rounding of the running maximum's rescaling (a few ulp).
 // Operands live in shared memory in the K-major, 128-byte-swizzled layout the
 // UMMA descriptor reads: a [R x 32 fp32] tile has row r at r * 128 bytes and
@@ -23,7 +26,7 @@
 // issuing MMAs, waits (bounded) for the last commit it issued and frees TMEM.
 //
 // Query rows past the last whole block of 128 (one row at T = 257) take the
-// warp-per-row kernel below, the reference's two passes on the CUDA cores.
+// CTA-per-row kernel below, the reference's two passes on the CUDA cores.
 #include "ops.cuh"
 #include "numerics.cuh"
 #include "tc05.cuh"
@@ -31,7 +34,7 @@
 namespace tcg {
 namespace {
 
-constexpr int AL_THREADS = 128;
+constexpr int AL_THREADS = 256;
 constexpr int AL_KB = 64;                                 // keys per block
 constexpr uint32_t T128 = 128 * 128;                      // [128 x 32] fp32 tile, 16 KB
 constexpr uint32_t T64 = 64 * 128;                        // [64 x 32] fp32 tile, 8 KB
@@ -41,7 +44,7 @@ constexpr uint32_t OFF_KH = 4 * T128, OFF_KL = OFF_KH + 2 * T64;      // K block
 constexpr uint32_t OFF_VH = OFF_KL + 2 * T64, OFF_VL = OFF_VH + 2 * T64;   // V^T block [64 d x 64 keys]
 constexpr uint32_t OFF_PH = OFF_VL + 2 * T64, OFF_PL = OFF_PH + 2 * T128;  // P block [128 q x 64 keys]
 constexpr uint32_t AL_TILES = OFF_PL + 2 * T128;          // 192 KB
-constexpr size_t AL_SMEM = 1024 + AL_TILES + 64;
+constexpr size_t AL_SMEM = 1024 + AL_TILES + 32 + 256 * 4 + 256 * 8;
 constexpr uint32_t AL_TMEM_COLS = 128;                    // S: 0-63, P V: 64-127
 constexpr unsigned long long AL_WAIT_NS = 4000000000ull;
 
@@ -99,7 +102,10 @@ mha64_tc_long_kernel(const float *__restrict__ q, const float *__restrict__ k, c
     uint64_t *bars = (uint64_t *)(tiles + AL_TILES);
     uint32_t *tmem_slot = (uint32_t *)(bars + 2);
     volatile int *abort = (volatile int *)(tmem_slot + 1);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float *xmax = (float *)(tiles + AL_TILES + 32);              // [256] block maxima of the two halves
+    double *xsum = (double *)(tiles + AL_TILES + 32 + 256 * 4);  // [256] row sums of the two halves
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int r = tid & 127, h = tid >> 7;                       // query row, half (keys / dims 32h .. 32h + 31)
     const uint32_t bar_s = su32(bars), bar_o = su32(bars + 1);
     const int col = blockIdx.x * 64;
     const size_t base = (size_t)blockIdx.y * T;
@@ -119,56 +125,68 @@ mha64_tc_long_kernel(const float *__restrict__ q, const float *__restrict__ k, c
     }
     // Q: 128 rows x 16 float4; consecutive threads take consecutive float4 of a row
     for (int i = tid; i < 128 * 16; i += AL_THREADS) {
-        const int r = i >> 4, d4 = i & 15;
-        const float4 x = __ldg(reinterpret_cast<const float4 *>(q + (base + q0 + r) * (size_t)ldi + col + 4 * d4));
-        st_pair4(tiles, OFF_QH, OFF_QL, (uint32_t)(d4 >> 3) * T128 + swz(r, 4 * (d4 & 7)), x);
+        const int qr = i >> 4, d4 = i & 15;
+        const float4 x = __ldg(reinterpret_cast<const float4 *>(q + (base + q0 + qr) * (size_t)ldi + col + 4 * d4));
+        st_pair4(tiles, OFF_QH, OFF_QL, (uint32_t)(d4 >> 3) * T128 + swz(qr, 4 * (d4 & 7)), x);
     }
+    // A block's K and V in registers: K element i = tid + 256 u -> key i >> 4, float4 i & 15;
+    // V: thread -> key tid & 63, dims 16 (tid >> 6) .. + 15
+    float4 kreg[4], vreg[4];
+    auto load_kv = [&](int t0, int nk) {
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int i = tid + AL_THREADS * u, key = i >> 4, d4 = i & 15;
+            kreg[u] = key < nk ? __ldg(reinterpret_cast<const float4 *>(k + (base + t0 + key) * (size_t)ldi + col + 4 * d4))
+                               : zero;
+        }
+        const int key = tid & 63, dq = tid >> 6;
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+            vreg[u] = key < nk ? __ldg(reinterpret_cast<const float4 *>(v + (base + t0 + key) * (size_t)ldi + col + 16 * dq + 4 * u))
+                               : zero;
+    };
+    auto store_kv = [&]() {
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int i = tid + AL_THREADS * u, key = i >> 4, d4 = i & 15;
+            st_pair4(tiles, OFF_KH, OFF_KL, (uint32_t)(d4 >> 3) * T64 + swz(key, 4 * (d4 & 7)), kreg[u]);
+        }
+        const int key = tid & 63, dq = tid >> 6;
+        const uint32_t kt = (uint32_t)(key >> 5) * T64;
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const float xv[4] = { vreg[u].x, vreg[u].y, vreg[u].z, vreg[u].w };
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                float hi, lo;
+                split_tf32(xv[j], hi, lo);
+                const uint32_t off = kt + swz(16 * dq + 4 * u + j, key & 31);
+                *reinterpret_cast<float *>(tiles + OFF_VH + off) = hi;
+                *reinterpret_cast<float *>(tiles + OFF_VL + off) = lo;
+            }
+        }
+    };
+    load_kv(0, min(AL_KB, T));
     fence_before();
     __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
     const uint32_t tbase = su32(tiles);
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
 
     const float scale = 1.0f / sqrtf(64.0f);
-    float o[64];
+    float o[32];
 #pragma unroll
-    for (int j = 0; j < 64; j++) o[j] = 0.0f;
+    for (int j = 0; j < 32; j++) o[j] = 0.0f;
     float m = -INFINITY;
-    double sum = 0.0;
+    double sum = 0.0;                                            // this half's share of the row sum
     bool ok = true;
     int issued = 0;                  // thread 0's last commit: 1 S, 2 P V (of block last_kb)
     int last_kb = 0;
     const int nblk = (T + AL_KB - 1) / AL_KB;
     for (int kb = 0; kb < nblk; kb++) {
         const int t0 = kb * AL_KB, nk = min(AL_KB, T - t0);
-        // K block: 64 keys x 16 float4 (keys past T zero)
-        for (int i = tid; i < AL_KB * 16; i += AL_THREADS) {
-            const int r = i >> 4, d4 = i & 15;
-            const float4 x = r < nk ? __ldg(reinterpret_cast<const float4 *>(k + (base + t0 + r) * (size_t)ldi + col + 4 * d4))
-                                    : zero;
-            st_pair4(tiles, OFF_KH, OFF_KL, (uint32_t)(d4 >> 3) * T64 + swz(r, 4 * (d4 & 7)), x);
-        }
-        // V block transposed: thread -> key tid & 63, dims 32 (tid >> 6) .. + 31
-        {
-            const int key = tid & 63, dh = tid >> 6;
-            const bool in = key < nk;
-            const float *src = v + (base + t0 + key) * (size_t)ldi + col + 32 * dh;
-            const uint32_t kt = (uint32_t)(key >> 5) * T64;
-#pragma unroll 2
-            for (int d4 = 0; d4 < 8; d4++) {
-                const float4 x = in ? __ldg(reinterpret_cast<const float4 *>(src + 4 * d4)) : zero;
-                const float xv[4] = { x.x, x.y, x.z, x.w };
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    float h, l;
-                    split_tf32(xv[j], h, l);
-                    const uint32_t off = kt + swz(32 * dh + 4 * d4 + j, key & 31);
-                    *reinterpret_cast<float *>(tiles + OFF_VH + off) = h;
-                    *reinterpret_cast<float *>(tiles + OFF_VL + off) = l;
-                }
-            }
-        }
+        store_kv();                                              // this block's K and V, loaded one block ahead
         fence_async_smem();
         fence_before();
         __syncthreads();
@@ -180,39 +198,40 @@ mha64_tc_long_kernel(const float *__restrict__ q, const float *__restrict__ k, c
             last_kb = kb;
         }
         __syncwarp();
+        if (kb + 1 < nblk) load_kv(t0 + AL_KB, min(AL_KB, T - t0 - AL_KB));   // in flight during this block
         if (ok) ok = bar_wait(bar_s, (uint32_t)(kb & 1), abort, err, 13);
         fence_after();
-        // softmax step of row tid over this block's nk keys
-        float p[64];
-        float a;
+        // softmax step: this thread's 32 keys of row r
+        float p[32];
         {
-            uint32_t sv[64];
-            tmem_ld64(lane_base, sv);
+            uint32_t sv[32];
+            tmem_ld32(lane_base + 32 * h, sv);
             float mb = -INFINITY;
 #pragma unroll
-            for (int j = 0; j < 64; j++) {
+            for (int j = 0; j < 32; j++) {
                 p[j] = __fmul_rn(__uint_as_float(sv[j]), scale);
-                if (j < nk) mb = fmaxf(mb, p[j]);
+                if (32 * h + j < nk) mb = fmaxf(mb, p[j]);
             }
-            const float mn = fmaxf(m, mb);
-            a = expf(__fsub_rn(m, mn));              // 0 on the first block (m = -inf)
+            xmax[tid] = mb;
+        }
+        fence_before();
+        __syncthreads();                 // both halves' maxima posted; every row's S is read; the last P V is folded
+        const float mn = fmaxf(m, fmaxf(xmax[r], xmax[r + 128]));
+        const float a = expf(__fsub_rn(m, mn));                  // 0 on the first block (m = -inf)
+        {
             double bs = 0.0;
 #pragma unroll
-            for (int j = 0; j < 64; j++) {
-                p[j] = j < nk ? expf(__fsub_rn(p[j], mn)) : 0.0f;
+            for (int j = 0; j < 32; j++) {
+                p[j] = 32 * h + j < nk ? expf(__fsub_rn(p[j], mn)) : 0.0f;
                 bs += (double)p[j];
             }
             sum = sum * (double)a + bs;
             m = mn;
         }
-        fence_before();
-        __syncthreads();                         // every row's S is read; the last P V is folded
 #pragma unroll
-        for (int c4 = 0; c4 < 16; c4++) {
-            const int key = 4 * c4;
-            st_pair4(tiles, OFF_PH, OFF_PL, (uint32_t)(key >> 5) * T128 + swz(tid, key & 31),
-                     make_float4(p[key], p[key + 1], p[key + 2], p[key + 3]));
-        }
+        for (int c4 = 0; c4 < 8; c4++)
+            st_pair4(tiles, OFF_PH, OFF_PL, (uint32_t)h * T128 + swz(r, 4 * c4),
+                     make_float4(p[4 * c4], p[4 * c4 + 1], p[4 * c4 + 2], p[4 * c4 + 3]));
         fence_async_smem();
         fence_before();
         __syncthreads();
@@ -227,30 +246,32 @@ mha64_tc_long_kernel(const float *__restrict__ q, const float *__restrict__ k, c
         if (ok) ok = bar_wait(bar_o, (uint32_t)(kb & 1), abort, err, 14);
         fence_after();
         {
-            uint32_t pv[64];
-            tmem_ld64(lane_base + 64, pv);
+            uint32_t pv[32];
+            tmem_ld32(lane_base + 64 + 32 * h, pv);
 #pragma unroll
-            for (int j = 0; j < 64; j++) o[j] = fmaf(o[j], a, __uint_as_float(pv[j]));
+            for (int j = 0; j < 32; j++) o[j] = fmaf(o[j], a, __uint_as_float(pv[j]));
         }
         fence_before();
-        __syncthreads();                         // P V is read; the next block may overwrite K, V, P
+        __syncthreads();                 // P V is read; the next block may overwrite K, V, P and the maxima
         fence_after();
     }
+    xsum[tid] = sum;
+    __syncthreads();
     if (ok) {
-        const float inv = (float)(1.0 / sum);
-        const size_t row = base + q0 + tid;
+        const float inv = (float)(1.0 / (xsum[r] + xsum[r + 128]));
+        const size_t row = base + q0 + r;
 #pragma unroll
-        for (int d = 0; d < 64; d += 4) {
+        for (int d = 0; d < 32; d += 4) {
             const float o4[4] = { __fmul_rn(o[d], inv), __fmul_rn(o[d + 1], inv), __fmul_rn(o[d + 2], inv),
                                   __fmul_rn(o[d + 3], inv) };
-            const size_t i = row * (size_t)out.ld + col + d;
+            const size_t i = row * (size_t)out.ld + col + 32 * h + d;
             if (out.plain) *reinterpret_cast<float4 *>(out.plain + i) = make_float4(o4[0], o4[1], o4[2], o4[3]);
             if (out.hi) {
-                float h[4], l[4];
+                float hi4[4], lo4[4];
 #pragma unroll
-                for (int u = 0; u < 4; u++) split_tf32(o4[u], h[u], l[u]);
-                *reinterpret_cast<float4 *>(out.hi + i) = make_float4(h[0], h[1], h[2], h[3]);
-                *reinterpret_cast<float4 *>(out.lo + i) = make_float4(l[0], l[1], l[2], l[3]);
+                for (int u = 0; u < 4; u++) split_tf32(o4[u], hi4[u], lo4[u]);
+                *reinterpret_cast<float4 *>(out.hi + i) = make_float4(hi4[0], hi4[1], hi4[2], hi4[3]);
+                *reinterpret_cast<float4 *>(out.lo + i) = make_float4(lo4[0], lo4[1], lo4[2], lo4[3]);
             }
         }
     }
@@ -270,109 +291,102 @@ mha64_tc_long_kernel(const float *__restrict__ q, const float *__restrict__ k, c
     }
 }
 
-// One warp per query row (rows row0 .. T - 1): the reference's two passes.
-// Lane l scores keys l, l + 32, ... against the whole query row; the maximum,
-// expf of the differences, the double sum and its reciprocal as in
-// src/ops.c:129-139; lane l then accumulates output dims 2l, 2l + 1 over the
-// keys in order, taking each probability from its lane by a shuffle.
-constexpr int AR_KEYS = 32;                               // keys per lane (T <= 1024)
-
-__global__ void __launch_bounds__(128)
-mha64_rows_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v, int ldi,
-                  int T, int row0, OutSpec out)
+// One CTA of 256 threads per query row (rows row0 .. T - 1): the reference's
+// two passes (src/ops.c:129-139). Thread t scores keys t, t + 256, ... against
+// the row (dims in order); the block's maximum, expf of the differences, a
+// double sum over the warps in order and its reciprocal; then thread t sums
+// dim t & 63 over one quarter of the keys (in order, V rows read coalesced,
+// eight in flight), and the quarters are added in order.
+__global__ void __launch_bounds__(256)
+mha64_row_cta_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v, int ldi,
+                     int T, int row0, OutSpec out)
 {
     pdl_wait();
-    const int lane = threadIdx.x & 31;
-    const int row = row0 + blockIdx.z * 4 + (threadIdx.x >> 5);
-    if (row >= T) return;
+    __shared__ __align__(16) float qs[64];
+    __shared__ float ps[1024];
+    __shared__ float wmax[8];
+    __shared__ double wsum[8];
+    __shared__ float part[4][64];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int row = row0 + blockIdx.z;
     const int col = blockIdx.x * 64;
     const size_t base = (size_t)blockIdx.y * T;
-    float qr[64];
-#pragma unroll
-    for (int d4 = 0; d4 < 16; d4++) {
-        const float4 x = __ldg(reinterpret_cast<const float4 *>(q + (base + row) * (size_t)ldi + col + 4 * d4));
-        qr[4 * d4] = x.x; qr[4 * d4 + 1] = x.y; qr[4 * d4 + 2] = x.z; qr[4 * d4 + 3] = x.w;
-    }
+    if (tid < 16)
+        reinterpret_cast<float4 *>(qs)[tid] =
+            __ldg(reinterpret_cast<const float4 *>(q + (base + row) * (size_t)ldi + col + 4 * tid));
+    __syncthreads();
     const float scale = 1.0f / sqrtf(64.0f);
-    float e[AR_KEYS];
     float mx = -INFINITY;
+    for (int s = tid; s < T; s += 256) {
+        const float4 *kr = reinterpret_cast<const float4 *>(k + (base + s) * (size_t)ldi + col);
+        float4 x[16];
 #pragma unroll
-    for (int i = 0; i < AR_KEYS; i++) {
-        const int s = lane + 32 * i;
-        e[i] = -INFINITY;
-        if (s < T) {
-            const float *kr = k + (base + s) * (size_t)ldi + col;
-            float acc = 0.0f;
+        for (int d4 = 0; d4 < 16; d4++) x[d4] = __ldg(kr + d4);
+        float acc = 0.0f;
 #pragma unroll
-            for (int d4 = 0; d4 < 16; d4++) {
-                const float4 x = __ldg(reinterpret_cast<const float4 *>(kr + 4 * d4));
-                acc = fmaf(qr[4 * d4], x.x, acc);
-                acc = fmaf(qr[4 * d4 + 1], x.y, acc);
-                acc = fmaf(qr[4 * d4 + 2], x.z, acc);
-                acc = fmaf(qr[4 * d4 + 3], x.w, acc);
-            }
-            e[i] = __fmul_rn(acc, scale);
-            mx = fmaxf(mx, e[i]);
+        for (int d4 = 0; d4 < 16; d4++) {
+            acc = fmaf(qs[4 * d4], x[d4].x, acc);
+            acc = fmaf(qs[4 * d4 + 1], x[d4].y, acc);
+            acc = fmaf(qs[4 * d4 + 2], x[d4].z, acc);
+            acc = fmaf(qs[4 * d4 + 3], x[d4].w, acc);
         }
+        ps[s] = __fmul_rn(acc, scale);
+        mx = fmaxf(mx, ps[s]);
     }
     mx = warp_max(mx);
+    if (lane == 0) wmax[warp] = mx;
+    __syncthreads();
+    mx = wmax[0];
+#pragma unroll
+    for (int w = 1; w < 8; w++) mx = fmaxf(mx, wmax[w]);
     double sum = 0.0;
-#pragma unroll
-    for (int i = 0; i < AR_KEYS; i++) {
-        const int s = lane + 32 * i;
-        e[i] = s < T ? expf(__fsub_rn(e[i], mx)) : 0.0f;
-        sum += (double)e[i];
+    for (int s = tid; s < T; s += 256) {
+        const float e = expf(__fsub_rn(ps[s], mx));
+        ps[s] = e;
+        sum += (double)e;
     }
-    const float inv = (float)(1.0 / warp_sum(sum));
-    float o0 = 0.0f, o1 = 0.0f;
+    sum = warp_sum(sum);
+    if (lane == 0) wsum[warp] = sum;
+    __syncthreads();
+    double tot = wsum[0];
 #pragma unroll
-    for (int i = 0; i < AR_KEYS; i++) {
-        if (32 * i >= T) break;
-        const float ps = __fmul_rn(e[i], inv);
-        for (int s8 = 0; s8 < 32; s8 += 8) {                // eight V rows in flight, then their sums in order
-            if (32 * i + s8 >= T) break;
-            float2 x[8];
+    for (int w = 1; w < 8; w++) tot += wsum[w];
+    const float inv = (float)(1.0 / tot);
+    const int d = tid & 63, qq = tid >> 6, per = (T + 3) / 4;
+    const int s0 = qq * per, s1 = min(T, s0 + per);
+    float o = 0.0f;
+    for (int s = s0; s < s1; s += 8) {
+        float x[8];
 #pragma unroll
-            for (int u = 0; u < 8; u++) {
-                const int s = 32 * i + s8 + u;
-                x[u] = s < T ? __ldg(reinterpret_cast<const float2 *>(v + (base + s) * (size_t)ldi + col + 2 * lane))
-                             : make_float2(0.f, 0.f);
-            }
+        for (int u = 0; u < 8; u++) x[u] = s + u < s1 ? __ldg(v + (base + s + u) * (size_t)ldi + col + d) : 0.0f;
 #pragma unroll
-            for (int u = 0; u < 8; u++) {
-                const float p = __shfl_sync(0xffffffffu, ps, s8 + u);
-                if (32 * i + s8 + u < T) {
-                    o0 = fmaf(p, x[u].x, o0);
-                    o1 = fmaf(p, x[u].y, o1);
-                }
-            }
+        for (int u = 0; u < 8; u++)
+            if (s + u < s1) o = fmaf(__fmul_rn(ps[s + u], inv), x[u], o);
+    }
+    part[qq][d] = o;
+    __syncthreads();
+    if (tid < 64) {
+        const float r = __fadd_rn(__fadd_rn(__fadd_rn(part[0][tid], part[1][tid]), part[2][tid]), part[3][tid]);
+        const size_t i = (base + row) * (size_t)out.ld + col + tid;
+        if (out.plain) out.plain[i] = r;
+        if (out.hi) {
+            float hi, lo;
+            split_tf32(r, hi, lo);
+            out.hi[i] = hi;
+            out.lo[i] = lo;
         }
-    }
-    const size_t i = (base + row) * (size_t)out.ld + col + 2 * lane;
-    if (out.plain) {
-        out.plain[i] = o0;
-        out.plain[i + 1] = o1;
-    }
-    if (out.hi) {
-        float h, l;
-        split_tf32(o0, h, l);
-        out.hi[i] = h;
-        out.lo[i] = l;
-        split_tf32(o1, h, l);
-        out.hi[i + 1] = h;
-        out.lo[i + 1] = l;
     }
 }
 
 }  // namespace
 
 // head_dim 64, 128 <= T <= 1024: whole blocks of 128 queries on the tensor
-// cores, the rest one warp per row. False (nothing launched) when the shape
+// cores, the rest one CTA per row. False (nothing launched) when the shape
 // does not fit; the caller then takes a CUDA-core kernel.
 bool launch_mha64_tc_long(const float *q, const float *k, const float *v, int ldi, int T, int n_head, int n_img,
                           const OutSpec &out, cudaStream_t s)
 {
-    if (T < 128 || T > 32 * AR_KEYS) return false;
+    if (T < 128 || T > 1024) return false;
     static unsigned done[64];
     const int dev = ctx().device & 63;
     if (!done[dev]) {
@@ -383,7 +397,7 @@ bool launch_mha64_tc_long(const float *q, const float *k, const float *v, int ld
     TCG_CUDA(launch_pdl(mha64_tc_long_kernel, dim3(n_head, n_img, nfull), dim3(AL_THREADS), AL_SMEM, s, q, k, v, ldi, T,
                         out, ctx().d_err));
     if (rest > 0)
-        TCG_CUDA(launch_pdl(mha64_rows_kernel, dim3(n_head, n_img, (rest + 3) / 4), dim3(128), 0, s, q, k, v, ldi, T,
+        TCG_CUDA(launch_pdl(mha64_row_cta_kernel, dim3(n_head, n_img, rest), dim3(256), 0, s, q, k, v, ldi, T,
                             128 * nfull, out));
     TCG_LAUNCHED();
     return true;

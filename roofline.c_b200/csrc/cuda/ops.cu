@@ -632,7 +632,9 @@ static size_t mha64_smem(int T)
     return (MHA_BQ * 64 + 3 * 64 * T4) * sizeof(float);
 }
 
-int g_mha_variant = 1;      // T > 64: 0 whole-K/V kernel, 1 / 2 streaming kernel with 64 / 48-query blocks
+// T > 64: 1 (default) tensor cores where 128 <= T <= 1024, else the streaming kernel with 64-query blocks;
+// 0 whole-K/V kernel; 2 streaming kernel with 48-query blocks; 3 tensor cores where they apply
+int g_mha_variant = 1;
 
 bool launch_mha(const float *q, const float *k, const float *v, int ldi, int T, int n_head, int hd,
                 int n_img, const OutSpec &out, cudaStream_t s)
@@ -647,10 +649,12 @@ bool launch_mha(const float *q, const float *k, const float *v, int ldi, int T, 
         TCG_LAUNCHED();
         return true;
     }
-    if (hd == 64 && aligned && g_mha_variant == 3 && launch_mha64_tc_long(q, k, v, ldi, T, n_head, n_img, out, s))
+    if (hd == 64 && aligned && (g_mha_variant == 3 || g_mha_variant == 1) &&
+        launch_mha64_tc_long(q, k, v, ldi, T, n_head, n_img, out, s))
         return true;
     if (hd == 64 && aligned && g_mha_variant != 0) {
         const bool q48 = g_mha_variant == 2;
+        // variant 1 here: T < 128 or T > 1024; variant 3 here: the tensor-core kernel did not apply
         const size_t sm = q48 ? mhb_smem<48>(T) : mhb_smem<64>(T);
         if (sm <= 227 * 1024) {
             static unsigned doneb[64];
@@ -993,9 +997,9 @@ bool tcg_scale(float *out, const float *x, float s, size_t n)
 }  // extern "C"
 
 // Tuning and test hook: the attention kernel for head_dim 64 and T > 64
-// (0: whole K/V in shared memory, 1 / 2: streamed K/V with 64 / 48-query
-// blocks, identical results; 3: tensor cores where 128 <= T <= 1024).
-// Returns the previous setting.
+// (1, the default: tensor cores where 128 <= T <= 1024, else streamed K/V with
+// 64-query blocks; 0: whole K/V in shared memory; 2: streamed K/V with
+// 48-query blocks; 3: tensor cores only). Returns the previous setting.
 extern "C" int tcg_set_attention_variant(int variant)
 {
     const int old = tcg::g_mha_variant;

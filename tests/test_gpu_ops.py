@@ -127,11 +127,12 @@ def test_mha_vs_oracle(dev, T, H, HD):
 
 @pytest.mark.parametrize("T,H", [(65, 2), (100, 3), (257, 2), (300, 1), (577, 2)])
 def test_mha_long_sequence_kernels_agree(dev, T, H):
-    """For head_dim 64 and T > 64 the streamed-K/V kernel (64- or 48-query
-    blocks) performs the whole-K/V kernel's operations in the same order:
-    identical bits where both apply, and within the oracle's bound. T = 577
-    fits only the streamed kernel (the others would need 318 KB of shared
-    memory and the call is refused)."""
+    """head_dim 64, T > 64. The streamed-K/V kernel (64- or 48-query blocks)
+    performs the whole-K/V kernel's operations in the same order: identical
+    bits where both apply (T = 577 fits only the streamed one; the others
+    would need 318 KB of shared memory and the call is refused). The default
+    (variant 1) is that kernel below T = 128 and the tensor cores from 128 on;
+    every variant within the oracle's bound."""
     L = tcg.lib()
     rng = np.random.default_rng(T + 100 * H)
     q, k, v = (rng.standard_normal((T, H * 64)).astype(np.float32) for _ in range(3))
@@ -146,10 +147,12 @@ def test_mha_long_sequence_kernels_agree(dev, T, H):
             L.tcg_set_attention_variant(old)
         got[variant] = y.download((T, H * 64))
     if T <= 300:
-        assert np.array_equal(got[0], got[1]) and np.array_equal(got[0], got[2])
-    assert np.array_equal(got[1], got[2])
+        assert np.array_equal(got[0], got[2])
+    if T < 128:
+        assert np.array_equal(got[1], got[2])
     want = oracle.mha(q, k, v, T, H, 64)
-    assert np.abs(got[1] - want).max() <= 1e-5 * np.abs(want).max()
+    for variant, g in got.items():
+        assert np.abs(g - want).max() <= 1e-5 * np.abs(want).max(), variant
     assert L.tcg_device_error() == 0
 
 
