@@ -45,7 +45,7 @@ constexpr uint32_t OFF_VH = OFF_KL + 2 * T64, OFF_VL = OFF_VH + 2 * T64;   // V^
 constexpr uint32_t OFF_PH = OFF_VL + 2 * T64, OFF_PL = OFF_PH + 2 * T128;  // P block [128 q x 64 keys]
 constexpr uint32_t AL_TILES = OFF_PL + 2 * T128;          // 192 KB
 constexpr size_t AL_SMEM = 1024 + AL_TILES + 32 + 256 * 4 + 256 * 8;
-constexpr uint32_t AL_TMEM_COLS = 128;                    // S: 0-63, P V: 64-127
+constexpr uint32_t AL_TMEM_COLS = 256;                    // S: two buffers at 0 and 64, P V: at 128 and 192
 constexpr unsigned long long AL_WAIT_NS = 4000000000ull;
 
 // byte offset of element (r, c) of a [R x 32] swizzled fp32 tile
@@ -132,25 +132,33 @@ mha64_tc_long_kernel(const float *__restrict__ q, const float *__restrict__ k, c
     // A block's K and V in registers: K element i = tid + 256 u -> key i >> 4, float4 i & 15;
     // V: thread -> key tid & 63, dims 16 (tid >> 6) .. + 15
     float4 kreg[4], vreg[4];
-    auto load_kv = [&](int t0, int nk) {
+    auto load_k = [&](int t0, int nk) {
 #pragma unroll
         for (int u = 0; u < 4; u++) {
             const int i = tid + AL_THREADS * u, key = i >> 4, d4 = i & 15;
             kreg[u] = key < nk ? __ldg(reinterpret_cast<const float4 *>(k + (base + t0 + key) * (size_t)ldi + col + 4 * d4))
                                : zero;
         }
+    };
+    auto load_v = [&](int t0, int nk) {
         const int key = tid & 63, dq = tid >> 6;
 #pragma unroll
         for (int u = 0; u < 4; u++)
             vreg[u] = key < nk ? __ldg(reinterpret_cast<const float4 *>(v + (base + t0 + key) * (size_t)ldi + col + 16 * dq + 4 * u))
                                : zero;
     };
-    auto store_kv = [&]() {
+    auto load_kv = [&](int t0, int nk) {
+        load_k(t0, nk);
+        load_v(t0, nk);
+    };
+    auto store_k = [&]() {
 #pragma unroll
         for (int u = 0; u < 4; u++) {
             const int i = tid + AL_THREADS * u, key = i >> 4, d4 = i & 15;
             st_pair4(tiles, OFF_KH, OFF_KL, (uint32_t)(d4 >> 3) * T64 + swz(key, 4 * (d4 & 7)), kreg[u]);
         }
+    };
+    auto store_v = [&]() {
         const int key = tid & 63, dq = tid >> 6;
         const uint32_t kt = (uint32_t)(key >> 5) * T64;
 #pragma unroll
@@ -166,46 +174,45 @@ mha64_tc_long_kernel(const float *__restrict__ q, const float *__restrict__ k, c
             }
         }
     };
+    const int nblk = (T + AL_KB - 1) / AL_KB;
     load_kv(0, min(AL_KB, T));
+    store_k();                                                   // K of block 0; its V stays in registers
+    fence_async_smem();
     fence_before();
     __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
     const uint32_t tbase = su32(tiles);
     const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+    bool ok = true;
+    int last_s = -1, last_o = -1;    // blocks of thread 0's latest S and P V commits
+    if (tid == 0) {
+        mma_3x(tmem, tbase + OFF_QH, tbase + OFF_QL, tbase + OFF_KH, tbase + OFF_KL);
+        mma_commit(bar_s);
+        last_s = 0;
+    }
+    __syncwarp();
+    if (nblk > 1) load_k(AL_KB, min(AL_KB, T - AL_KB));         // K of block 1
 
     const float scale = 1.0f / sqrtf(64.0f);
     float o[32];
 #pragma unroll
     for (int j = 0; j < 32; j++) o[j] = 0.0f;
-    float m = -INFINITY;
+    float m = -INFINITY, a_prev = 0.0f;
     double sum = 0.0;                                            // this half's share of the row sum
-    bool ok = true;
-    int issued = 0;                  // thread 0's last commit: 1 S, 2 P V (of block last_kb)
-    int last_kb = 0;
-    const int nblk = (T + AL_KB - 1) / AL_KB;
+    // Block kb: S(kb) was issued a block earlier into S buffer kb & 1; after it
+    // lands, K(kb + 1) replaces K(kb) and S(kb + 1) goes to the other buffer
+    // while this block's softmax runs; P V(kb - 1), issued a block earlier, is
+    // folded late (with its rescale factor a_prev); then P(kb) and V(kb)
+    // replace P(kb - 1) and V(kb - 1) and P V(kb) goes to P V buffer kb & 1.
     for (int kb = 0; kb < nblk; kb++) {
         const int t0 = kb * AL_KB, nk = min(AL_KB, T - t0);
-        store_kv();                                              // this block's K and V, loaded one block ahead
-        fence_async_smem();
-        fence_before();
-        __syncthreads();
-        fence_after();
-        if (tid == 0 && ok) {
-            mma_3x(tmem, tbase + OFF_QH, tbase + OFF_QL, tbase + OFF_KH, tbase + OFF_KL);
-            mma_commit(bar_s);
-            issued = 1;
-            last_kb = kb;
-        }
-        __syncwarp();
-        if (kb + 1 < nblk) load_kv(t0 + AL_KB, min(AL_KB, T - t0 - AL_KB));   // in flight during this block
         if (ok) ok = bar_wait(bar_s, (uint32_t)(kb & 1), abort, err, 13);
         fence_after();
-        // softmax step: this thread's 32 keys of row r
         float p[32];
         {
             uint32_t sv[32];
-            tmem_ld32(lane_base + 32 * h, sv);
+            tmem_ld32(lane_base + 64 * (kb & 1) + 32 * h, sv);
             float mb = -INFINITY;
 #pragma unroll
             for (int j = 0; j < 32; j++) {
@@ -214,8 +221,18 @@ mha64_tc_long_kernel(const float *__restrict__ q, const float *__restrict__ k, c
             }
             xmax[tid] = mb;
         }
+        if (kb + 1 < nblk) store_k();                            // S(kb) is done with K(kb)
+        fence_async_smem();
         fence_before();
-        __syncthreads();                 // both halves' maxima posted; every row's S is read; the last P V is folded
+        __syncthreads();                 // both halves' maxima posted; K(kb + 1) in place
+        fence_after();
+        if (tid == 0 && ok && kb + 1 < nblk) {
+            mma_3x(tmem + 64 * ((kb + 1) & 1), tbase + OFF_QH, tbase + OFF_QL, tbase + OFF_KH, tbase + OFF_KL);
+            mma_commit(bar_s);
+            last_s = kb + 1;
+        }
+        __syncwarp();
+        if (kb + 2 < nblk) load_k(t0 + 2 * AL_KB, min(AL_KB, T - t0 - 2 * AL_KB));
         const float mn = fmaxf(m, fmaxf(xmax[r], xmax[r + 128]));
         const float a = expf(__fsub_rn(m, mn));                  // 0 on the first block (m = -inf)
         {
@@ -228,32 +245,39 @@ mha64_tc_long_kernel(const float *__restrict__ q, const float *__restrict__ k, c
             sum = sum * (double)a + bs;
             m = mn;
         }
+        if (kb > 0) {                                            // fold P V(kb - 1)
+            if (ok) ok = bar_wait(bar_o, (uint32_t)((kb - 1) & 1), abort, err, 14);
+            fence_after();
+            uint32_t pv[32];
+            tmem_ld32(lane_base + 128 + 64 * ((kb - 1) & 1) + 32 * h, pv);
+#pragma unroll
+            for (int j = 0; j < 32; j++) o[j] = fmaf(o[j], a_prev, __uint_as_float(pv[j]));
+        }
 #pragma unroll
         for (int c4 = 0; c4 < 8; c4++)
             st_pair4(tiles, OFF_PH, OFF_PL, (uint32_t)h * T128 + swz(r, 4 * c4),
                      make_float4(p[4 * c4], p[4 * c4 + 1], p[4 * c4 + 2], p[4 * c4 + 3]));
+        store_v();                                               // V(kb), loaded a block earlier
         fence_async_smem();
         fence_before();
-        __syncthreads();
+        __syncthreads();                 // P(kb), V(kb) in place; P V(kb - 1) and the maxima read
         fence_after();
         if (tid == 0 && ok) {
-            mma_3x(tmem + 64, tbase + OFF_PH, tbase + OFF_PL, tbase + OFF_VH, tbase + OFF_VL);
+            mma_3x(tmem + 128 + 64 * (kb & 1), tbase + OFF_PH, tbase + OFF_PL, tbase + OFF_VH, tbase + OFF_VL);
             mma_commit(bar_o);
-            issued = 2;
-            last_kb = kb;
+            last_o = kb;
         }
         __syncwarp();
-        if (ok) ok = bar_wait(bar_o, (uint32_t)(kb & 1), abort, err, 14);
-        fence_after();
-        {
-            uint32_t pv[32];
-            tmem_ld32(lane_base + 64 + 32 * h, pv);
+        if (kb + 1 < nblk) load_v(t0 + AL_KB, min(AL_KB, T - t0 - AL_KB));
+        a_prev = a;
+    }
+    if (ok) ok = bar_wait(bar_o, (uint32_t)((nblk - 1) & 1), abort, err, 14);
+    fence_after();
+    {
+        uint32_t pv[32];
+        tmem_ld32(lane_base + 128 + 64 * ((nblk - 1) & 1) + 32 * h, pv);
 #pragma unroll
-            for (int j = 0; j < 32; j++) o[j] = fmaf(o[j], a, __uint_as_float(pv[j]));
-        }
-        fence_before();
-        __syncthreads();                 // P V is read; the next block may overwrite K, V, P and the maxima
-        fence_after();
+        for (int j = 0; j < 32; j++) o[j] = fmaf(o[j], a_prev, __uint_as_float(pv[j]));
     }
     xsum[tid] = sum;
     __syncthreads();
@@ -277,11 +301,12 @@ mha64_tc_long_kernel(const float *__restrict__ q, const float *__restrict__ k, c
     }
     // MMAs that may still run (a wait gave up) must finish before TMEM is freed:
     // thread 0 waits, bounded, for the last commit it issued.
-    if (!ok && tid == 0 && issued) {
-        const uint32_t last = issued == 2 ? bar_o : bar_s;
-        const uint32_t parity = (uint32_t)(last_kb & 1);
+    if (!ok && tid == 0) {
         const unsigned long long t0 = now_ns();
-        while (!bar_test(last, parity) && now_ns() - t0 < AL_WAIT_NS) {}
+        if (last_s >= 0)
+            while (!bar_test(bar_s, (uint32_t)(last_s & 1)) && now_ns() - t0 < AL_WAIT_NS) {}
+        if (last_o >= 0)
+            while (!bar_test(bar_o, (uint32_t)(last_o & 1)) && now_ns() - t0 < AL_WAIT_NS) {}
     }
     fence_before();
     __syncthreads();
