@@ -524,7 +524,7 @@ matvec_stream_kernel(const uint8_t *__restrict__ W, const float *__restrict__ x,
     cp_wait0();
 }
 
-int g_mv_last = 0;         // kernel of the latest matvec: 2 segment stream, 3 staged
+int g_mv_last = 0;         // kernel of the latest matvec: 2 segment stream, 3 staged, 4 tensor cores
 
 template <int TYPE, int SEGS, int NSLOT>
 static bool launch_matvec_stream(float *y, const void *W, const float *x, int N, int K, size_t smem)
@@ -583,9 +583,21 @@ static bool launch_matvec(float *y, const void *W, const float *x, int N, int K)
     return true;
 }
 
+bool launch_matvec_tc_q4k(float *y, const void *W, const float *x, int N, int K, bool *used);   // mv_tc.cu
+
 template <int TYPE>
 static bool matvec_dispatch(float *y, const void *W, const float *x, int N, int K)
 {
+    // Q4_K on the tensor cores when enabled (tcg_matvec_set_tc) and the
+    // matrix is 16-byte aligned
+    if (TYPE == GGML_TYPE_Q4_K) {
+        bool used = false;
+        if (!launch_matvec_tc_q4k(y, W, x, N, K, &used)) return false;
+        if (used) {
+            g_mv_last = 4;
+            return true;
+        }
+    }
     // The streaming kernel whenever its segments tile the rows in 16-byte
     // units and x fits on chip; rows split in 4 when there are few of them.
     const long rows_per_sm = (long)N / (ctx().sms > 0 ? ctx().sms : 148);
@@ -715,5 +727,6 @@ const float *tcg_dequant_view(const gguf_tensor_t *t, tcg_arena_t *a, bool *conv
 }  // extern "C"
 
 // Test hook: the kernel of the latest K-quant matvec (2: row segments
-// streamed through a cp.async ring, 3: staged groups; 0: none yet).
+// streamed through a cp.async ring, 3: staged groups, 4: Q4_K on the tensor
+// cores; 0: none yet).
 extern "C" int tcg_matvec_last_kernel(void) { return tcg::g_mv_last; }

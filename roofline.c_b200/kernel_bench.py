@@ -128,10 +128,12 @@ def case_matvec(a):
     qt, bb = QTYPES[a.type]
     raw = G.make_kquant(qt, a.N, a.K, seed=3)
     x = np.random.default_rng(4).standard_normal(a.K).astype(np.float32)
+    old_tc = L.tcg_matvec_set_tc(a.tc)
     with tcg.DeviceBuffer.from_array(raw) as w, tcg.DeviceBuffer.from_array(x) as xb, \
             tcg.DeviceBuffer(a.N * 4) as y, tcg.DeviceBuffer(256 << 20) as flush:
         ms, _ = timed(lambda: tcg.check(L.tcg_matvec_q(y.ptr, w.ptr, xb.ptr, a.N, a.K, qt)), a.warmup, a.reps, flush)
     kern = L.tcg_matvec_last_kernel()
+    L.tcg_matvec_set_tc(old_tc)
     nbytes = a.N * a.K // 256 * bb + 4 * (a.N + a.K)
     return {"case": "matvec", "type": a.type, "N": a.N, "K": a.K, "kernel": kern, "ms": round(ms, 5),
             "bytes": nbytes, "GB/s": round(nbytes / ms / 1e6, 1)}
@@ -192,6 +194,7 @@ def main():
     mv.add_argument("--type", choices=sorted(QTYPES), default="q4k")
     mv.add_argument("--N", type=int, default=4096)
     mv.add_argument("--K", type=int, default=14336)
+    mv.add_argument("--tc", type=int, default=0, help="1: Q4_K on the tensor cores (opt-in kernel)")
     dq = sub.add_parser("dequant")
     dq.add_argument("--type", choices=sorted(QTYPES), default="q4k")
     dq.add_argument("--rows", type=int, default=14336)

@@ -150,6 +150,49 @@ def test_matvec_vs_dequant_then_linear(gpu, qt, N, K, seed):
     assert err <= MATVEC_TOL, err
 
 
+def _x_cases(K, seed):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal(K).astype(np.float32)
+    wide = x * np.float32(2.0) ** rng.integers(-30, 30, K).astype(np.float32)   # 60 binades within sub-blocks
+    zeros = x.copy()
+    zeros[32:96] = 0.0                                                          # whole zero sub-blocks
+    zeros[300:301] = 0.0
+    tiny = (x * np.float32(1e-30)).astype(np.float32)
+    return {"normal": x, "wide": wide.astype(np.float32), "zeros": zeros, "tiny": tiny}
+
+
+@pytest.mark.parametrize("N,K", [
+    (4096, 14336),      # the decode matvec: ~12 units per CTA, tiles shared by several CTAs
+    (100, 2304),        # one ragged tile split over 9 CTAs
+    (129, 256),         # two tiles, one row in the second
+    (37888, 256),       # 296 tiles of one superblock, two per CTA, written directly
+    (1, 256), (70, 4096), (300, 768),
+])
+def test_matvec_q4k_tensor_cores(gpu, N, K):
+    """The opt-in Q4_K matvec on tcgen05 (int8 nibbles x int8 pieces of x,
+    exact integer sums per sub-block) against the oracle and against the
+    CUDA-core kernel, on x with wide dynamic range, zero sub-blocks and tiny
+    values; repeated launches give the same bits (tile counters reset
+    themselves)."""
+    L = tcg.lib()
+    raw = G.make_kquant(G.Q4_K, N, K, seed=N + K)
+    for name, x in _x_cases(K, N * 7 + K).items():
+        old = L.tcg_matvec_set_tc(1)
+        try:
+            got = dev_matvec(raw, x, N, K, G.Q4_K, repeat=3)
+            assert L.tcg_matvec_last_kernel() == 4
+        finally:
+            L.tcg_matvec_set_tc(old)
+        want = oracle.matvec_q(raw, x, N, K, G.Q4_K).astype(np.float64)
+        scale = np.abs(want).max()
+        assert scale > 0, name
+        err = np.abs(got.astype(np.float64) - want).max() / scale
+        assert err <= MATVEC_TOL, (name, err)
+        cuda_cores = dev_matvec(raw, x, N, K, G.Q4_K)
+        assert L.tcg_matvec_last_kernel() in (2, 3)
+        assert np.abs(cuda_cores.astype(np.float64) - want).max() / scale <= MATVEC_TOL, name
+
+
 def test_matvec_rejections(gpu):
     L = tcg.lib()
     assert not L.tcg_matvec_q(None, None, None, 4, 300, G.Q4_K)
