@@ -235,6 +235,62 @@ def test_quick_gelu_model(gpu, tmp_path):
         m.close()
 
 
+def _kquant_like(qt, rows, cols, seed, d_std):
+    """Random K-quant blocks of a [rows, cols] matrix whose weights have a
+    trained model's scale: the fp16 super-scales d (and dmin) ~ |N(0, d_std)|,
+    many of them fp16 subnormals."""
+    nb = rows * cols // 256
+    blk = (G.make_q4k_blocks if qt == G.Q4_K else G.make_q6k_blocks)(nb, seed)
+    rng = np.random.default_rng(seed + 1)
+    half = lambda: np.abs(rng.normal(0.0, d_std, nb)).astype(np.float16).view(np.uint8).reshape(nb, 2)  # noqa: E731
+    if qt == G.Q4_K:
+        blk[:, 0:2] = half()
+        blk[:, 2:4] = half()
+    else:
+        blk[:, 208:210] = half()
+    return blk.reshape(-1)
+
+
+def test_kquant_weights_model(gpu, tmp_path):
+    """A ViT-B/32 (two layers) whose linear weights are K-quant tensors: Q4_K
+    qkv and up projections, Q6_K out, down and the output projection.
+    tc_vit_load materialises them through the dequant seam (src/vit.c:17-37,
+    tc_dequant_view with the Q4_K / Q6_K arms), so the forward must equal the
+    fp32 model of the dequantised weights."""
+    cfg = G.vit_config("vit-b32", n_layer=2)
+    w = G.make_vit_weights(cfg, 5)
+    quant = {"attn_qkv.weight": (G.Q4_K, 4e-5), "ffn_up.weight": (G.Q4_K, 4e-5),
+             "attn_out.weight": (G.Q6_K, 3e-6), "ffn_down.weight": (G.Q6_K, 3e-6), "v.proj": (G.Q6_K, 3e-6)}
+    tensors = []
+    for k, (name, arr) in enumerate(list(w.items())):
+        key = name if name == "v.proj" else ".".join(name.split(".")[-2:])
+        if key in quant:
+            qt, d_std = quant[key]
+            rows, cols = arr.shape
+            raw = _kquant_like(qt, rows, cols, 100 + k, d_std)
+            w[name] = oracle.dequant(raw, rows * cols, qt).reshape(rows, cols)
+            tensors.append((name, raw, qt, arr.shape))
+        else:
+            tensors.append((name, arr, G.F32, arr.shape))
+    assert sum(t[2] != G.F32 for t in tensors) == 4 * cfg["n_layer"] + 1
+    path = str(tmp_path / "kq.gguf")
+    G.write_gguf(path, G.vit_metadata(cfg), tensors)
+    px = G.make_pixels(2, cfg["image"], 6)
+    port = oracle.PortVit(cfg, w)
+    m = tcg.VitModel(path)
+    try:
+        m.upload(2)
+        out, taps = m.encode(px, taps=True)
+        for i in range(2):
+            ref = port.forward(px[i])
+            assert rel_inf(out[i], ref["embedding"]) <= TOL, i
+            assert cosine(out[i], ref["embedding"]) >= 0.9999
+            for k in TAPS:
+                assert rel_inf(taps[k][i], ref[k]) <= TOL, (i, k)
+    finally:
+        m.close()
+
+
 def test_device_entry_and_limits(gpu, cache_dir):
     L = tcg.lib()
     path, cfg = model(cache_dir, "vit-b32", n_layer=1)
