@@ -35,11 +35,9 @@
 // bounded; on a timeout the kernel raises the device error word and still
 // completes the tile arrivals so the counters stay consistent.
 #include "tcg_common.cuh"
-#include "tcg_internal.h"
 #include "tc05.cuh"
 
 #include <cuda.h>
-#include <string.h>
 
 namespace tcg {
 
