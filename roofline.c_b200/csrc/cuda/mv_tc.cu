@@ -430,8 +430,11 @@ EncodeFn mq_encode_fn()
     return fn;
 }
 
-// Per-device working memory: tile counters (zero between calls), partial
-// sums, B tiles and x factors. Grown (and zeroed) on demand.
+// Working memory of this host thread's calls on a device (the library
+// context is per thread too): tile counters (zero between calls), partial
+// sums, B tiles and x factors. Grown (and zeroed) on demand. Calls of one
+// thread must be stream-ordered: two in flight at once on different streams
+// would share the counters.
 struct MqBuf {
     uint8_t *p = nullptr;
     size_t bytes = 0;
@@ -440,7 +443,7 @@ struct MqBuf {
     int map_n = 0, map_k = 0;
     CUtensorMap map;
 };
-MqBuf g_mq[64];
+thread_local MqBuf g_mq[64];
 
 }  // namespace
 
