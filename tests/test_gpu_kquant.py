@@ -137,14 +137,19 @@ def dev_matvec(raw, x, N, K, qt, repeat=1):
     (G.Q6_K, 128256, 4096, 5),     # the output head
     (G.Q4_K, 1, 256, 7), (G.Q6_K, 3, 768, 8), (G.Q4_K, 100, 2304, 9),
     (G.Q6_K, 5000, 512, 10), (G.Q4_K, 70, 4096, 11),
+    (G.Q4_K, 4095, 14336, 12),     # odd row count, a partial last CTA iteration
+    (G.Q4_K, 9473, 14336, 13),     # long rows, many of them: row pairs, the last pair one row
+    (G.Q6_K, 9473, 14336, 14),     # 210-byte superblocks: no 16-byte segment split, the staged kernel
 ])
 def test_matvec_vs_dequant_then_linear(gpu, qt, N, K, seed):
     raw = G.make_kquant(qt, N, K, seed=seed)
     x = np.random.default_rng(seed + 100).standard_normal(K).astype(np.float32)
     got = dev_matvec(raw, x, N, K, qt, repeat=3)
     kernel = tcg.lib().tcg_matvec_last_kernel()
-    # the two benchmark shapes run the streaming kernel; every shape one of the two
-    assert kernel == 2 if (N, K) in ((4096, 14336), (128256, 4096)) else kernel in (2, 3), kernel
+    # the benchmark shapes (and every Q4_K one with long rows) run the
+    # streaming kernel; every shape one of the two
+    stream = (qt == G.Q4_K and K in (14336, 4096)) or (N, K) == (128256, 4096)
+    assert kernel == 2 if stream else kernel in (2, 3), kernel
     want = oracle.matvec_q(raw, x, N, K, qt)
     err = np.abs(got.astype(np.float64) - want).max() / np.abs(want).max()
     assert err <= MATVEC_TOL, err
@@ -191,6 +196,22 @@ def test_matvec_q4k_tensor_cores(gpu, N, K):
         cuda_cores = dev_matvec(raw, x, N, K, G.Q4_K)
         assert L.tcg_matvec_last_kernel() in (2, 3)
         assert np.abs(cuda_cores.astype(np.float64) - want).max() / scale <= MATVEC_TOL, name
+
+
+@pytest.mark.parametrize("case", ["normal", "wide", "zeros", "tiny"])
+def test_matvec_q4k_row_pairs_x_cases(gpu, case):
+    """Q4_K rows are taken in pairs that share every x load; an odd row
+    count leaves the last pair one row (they run where the rows are too long
+    for the one-row rings). x with 60 binades, zero sub-blocks and 1e-30
+    values."""
+    N, K = 9473, 14336
+    raw = G.make_kquant(G.Q4_K, N, K, seed=21)
+    x = _x_cases(K, 22)[case]
+    got = dev_matvec(raw, x, N, K, G.Q4_K, repeat=2)
+    assert tcg.lib().tcg_matvec_last_kernel() == 2
+    want = oracle.matvec_q(raw, x, N, K, G.Q4_K).astype(np.float64)
+    err = np.abs(got.astype(np.float64) - want).max() / np.abs(want).max()
+    assert err <= MATVEC_TOL, err
 
 
 def test_matvec_rejections(gpu):
