@@ -224,8 +224,14 @@ def host_threads():
 # ------------------------------------------------------------ K-quant rows
 
 def kquant_aux(tcg, hbm_peak):
-    """GB/s of dequant (14336x4096) and fused matvec; each launch timed alone
-    with events, L2 flushed (a 256 MB memset) between launches."""
+    """GB/s of dequant (14336x4096) and fused matvec, two ways:
+    - isolated: each launch timed alone with events, L2 flushed (a 256 MB
+      memset) before it; the flush's dirty lines are written back while the
+      timed kernel runs, and the event pair adds ~2.6 us;
+    - b2b: launches back to back, the total over the launches; each launch
+      touches more than the 126 MB L2 holds (dequant 268 MB, Q6_K matvec
+      431 MB; the 33 MB Q4_K matrix rotates over 10 copies, 331 MB), as in a
+      decode pass over successive layers."""
     L = tcg.lib()
     flush = tcg.DeviceBuffer(256 << 20)
     out = {}
@@ -239,26 +245,38 @@ def kquant_aux(tcg, hbm_peak):
             ts.append(tcg.time_ms(fn, 2, 3))
         return statistics.median(ts)
 
+    def b2b(fns, reps=10):
+        for f in fns[:2]:
+            f()
+        return statistics.median(tcg.time_ms(lambda: [f() for f in fns], 2, 3) / len(fns) for _ in range(reps))
+
+    def row(nbytes, ms, ms_b2b, launches):
+        gbs, gbs2 = nbytes / ms / 1e6, nbytes / ms_b2b / 1e6
+        return {"GB/s": round(gbs, 1), "us": round(ms * 1e3, 2), "bytes": nbytes, "frac": round(gbs / hbm_peak, 3),
+                "b2b": {"GB/s": round(gbs2, 1), "us": round(ms_b2b * 1e3, 2), "frac": round(gbs2 / hbm_peak, 3),
+                        "launches": launches}}
+
     for name, qt, bb in (("q4k", G.Q4_K, 144), ("q6k", G.Q6_K, 210)):
         rows, cols = 14336, 4096
         raw = G.make_kquant(qt, rows, cols, seed=2)
         n = rows * cols
         with tcg.DeviceBuffer.from_array(raw) as src, tcg.DeviceBuffer(n * 4) as dst:
-            ms = timed(lambda: tcg.check(L.tcg_dequant(dst.ptr, src.ptr, n, qt)))
-        nbytes = n // 256 * bb + n * 4
-        gbs = nbytes / ms / 1e6
-        out[f"dequant_{name}_{rows}x{cols}"] = {"GB/s": round(gbs, 1), "us": round(ms * 1e3, 2),
-                                               "bytes": nbytes, "frac": round(gbs / hbm_peak, 3)}
-    for name, qt, bb, N, K, seed in (("q4k", G.Q4_K, 144, 4096, 14336, 3), ("q6k", G.Q6_K, 210, 128256, 4096, 5)):
+            run = lambda: tcg.check(L.tcg_dequant(dst.ptr, src.ptr, n, qt))
+            ms = timed(run)
+            ms2 = b2b([run] * 8)
+        out[f"dequant_{name}_{rows}x{cols}"] = row(n // 256 * bb + n * 4, ms, ms2, 8)
+    for name, qt, bb, N, K, seed, copies in (("q4k", G.Q4_K, 144, 4096, 14336, 3, 10),
+                                             ("q6k", G.Q6_K, 210, 128256, 4096, 5, 1)):
         raw = G.make_kquant(qt, N, K, seed=seed)
         x = np.random.default_rng(seed + 1).standard_normal(K).astype(np.float32)
-        with tcg.DeviceBuffer.from_array(raw) as w, tcg.DeviceBuffer.from_array(x) as xb, \
-                tcg.DeviceBuffer(N * 4) as y:
-            ms = timed(lambda: tcg.check(L.tcg_matvec_q(y.ptr, w.ptr, xb.ptr, N, K, qt)))
-        nbytes = N * K // 256 * bb + K * 4 + N * 4
-        gbs = nbytes / ms / 1e6
-        out[f"matvec_{name}_{N}x{K}"] = {"GB/s": round(gbs, 1), "us": round(ms * 1e3, 2),
-                                        "bytes": nbytes, "frac": round(gbs / hbm_peak, 3)}
+        ws = [tcg.DeviceBuffer.from_array(raw) for _ in range(copies)]
+        with tcg.DeviceBuffer.from_array(x) as xb, tcg.DeviceBuffer(N * 4) as y:
+            mv = [lambda w=w: tcg.check(L.tcg_matvec_q(y.ptr, w.ptr, xb.ptr, N, K, qt)) for w in ws]
+            ms = timed(mv[0])
+            ms2 = b2b(mv * (10 // copies))
+        for w in ws:
+            w.close()
+        out[f"matvec_{name}_{N}x{K}"] = row(N * K // 256 * bb + K * 4 + N * 4, ms, ms2, 10)
     flush.close()
     return out
 
