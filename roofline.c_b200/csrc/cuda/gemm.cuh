@@ -67,6 +67,8 @@ bool gemm_run(const GemmPlan &p, cudaStream_t s, int *err);
 // The configuration for throughput (the ViT forward): folded small terms,
 // stream-K capable; the automatic choice (force_cfg -1) is the accurate one.
 int gemm_throughput_cfg();
+// the configuration of one ViT GEMM of M x N x K (gemm_tc.cu)
+int gemm_vit_cfg(int M, int N, int K);
 
 // Tile widths available (index = cfg); for tests and tuning.
 int gemm_num_cfgs();

@@ -926,6 +926,28 @@ int gemm_throughput_cfg()
 int g_chunk_k = 256;
 
 int gemm_num_cfgs() { return NCFG; }
+
+// The configuration of one ViT GEMM: the ACC_WIDE 128 x 128 shape of
+// gemm_throughput_cfg(), except where its tiles make exactly one whole wave
+// plus a remainder of at most 1/16 of the SMs. There every SM runs one whole
+// tile with no successor to overlap its pipeline fill and drain, which
+// measured ~100 us per 128 x 128 x 3072 tile against ~63 us per wave when
+// several waves follow one another. In that case a long K (at least 6 TMEM
+// chunks) takes the 128 x 256 folded shape (7) and a short one the
+// separate-accumulator 128 x 128 shape (10). Measured at M = 3200, N = 768
+// (the ViT-B/32 shard of 64 images): 94 vs 111 us at K = 3072, 43 vs 49 us at
+// K = 768. Both stay within ~1.6e-6 of max|C| of a float64 product.
+int gemm_vit_cfg(int M, int N, int K)
+{
+    const int tp = gemm_throughput_cfg();
+    if (g_force_cfg >= 0 && g_force_cfg < NCFG) return tp;
+    const int sms = ctx().sms > 0 ? ctx().sms : 148;
+    const long tiles = (long)((M + BM - 1) / BM) * ((N + CFGS[tp].bn - 1) / CFGS[tp].bn);
+    const long last = tiles - sms;
+    if (last <= 0 || last > sms / 16) return tp;
+    return (K + g_chunk_k - 1) / g_chunk_k >= 6 ? 7 : 10;
+}
+
 int gemm_cfg_bn(int cfg) { return cfg >= 0 && cfg < NCFG ? CFGS[cfg].bn : 0; }
 
 size_t gemm_work_ws_floats(int ctas) { return (size_t)ctas * BM * 256; }

@@ -252,7 +252,8 @@ static tcg_vit::Plans *plans_for(tcg_vit *v, int n)
     e.out.ld = D;
     const GemmWork *w = &v->work;
     const int tp = gemm_throughput_cfg();
-    if (!gemm_plan(p->patch, v->p_hi, v->p_lo, v->patch_h, v->patch_l, n * G2, D, K0, e, tp, w)) return nullptr;
+    if (!gemm_plan(p->patch, v->p_hi, v->p_lo, v->patch_h, v->patch_l, n * G2, D, K0, e, gemm_vit_cfg(n * G2, D, K0), w))
+        return nullptr;
 
     GemmEpi pe;                                   // embedding = pooled x proj, into v->out
     pe.out.plain = v->out;
@@ -283,10 +284,10 @@ static tcg_vit::Plans *plans_for(tcg_vit *v, int n)
         d.residual = v->x;
         d.out.plain = v->x;
         d.out.ld = D;
-        if (!gemm_plan(p->qkv[i], v->h_hi, v->h_lo, y.qkv_h, y.qkv_l, M, 3 * D, D, q, tp, w) ||
-            !gemm_plan(p->out[i], v->h_hi, v->h_lo, y.out_h, y.out_l, M, D, D, o, tp, w) ||   // a aliases h
-            !gemm_plan(p->up[i], v->h_hi, v->h_lo, y.up_h, y.up_l, M, F, D, u, tp, w) ||
-            !gemm_plan(p->down[i], v->f_hi, v->f_lo, y.down_h, y.down_l, M, D, F, d, tp, w))
+        if (!gemm_plan(p->qkv[i], v->h_hi, v->h_lo, y.qkv_h, y.qkv_l, M, 3 * D, D, q, gemm_vit_cfg(M, 3 * D, D), w) ||
+            !gemm_plan(p->out[i], v->h_hi, v->h_lo, y.out_h, y.out_l, M, D, D, o, gemm_vit_cfg(M, D, D), w) ||   // a aliases h
+            !gemm_plan(p->up[i], v->h_hi, v->h_lo, y.up_h, y.up_l, M, F, D, u, gemm_vit_cfg(M, F, D), w) ||
+            !gemm_plan(p->down[i], v->f_hi, v->f_lo, y.down_h, y.down_l, M, D, F, d, gemm_vit_cfg(M, D, F), w))
             return nullptr;
     }
     tcg_vit::Plans *raw = p.get();

@@ -9,6 +9,8 @@ of embedding cosine >= 0.9999 (tests/test_vit.c:197).
 * the full-depth ViT-B/32 over a batch, per image, against the oracle;
 * batch invariance, graph replay == eager, and the argument checks.
 """
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -76,6 +78,48 @@ def test_b32_full_depth_batch_vs_oracle(gpu, cache_dir):
                 assert rel_inf(taps[k][i], ref[k]) <= TOL, (i, k, rel_inf(taps[k][i], ref[k]))
     finally:
         m.close()
+
+
+def test_b32_one_wave_shapes_vs_oracle(gpu, cache_dir):
+    """64 images, the shard of a 4-GPU run: the patch, out and down GEMMs
+    make one wave of 128 x 128 tiles plus two, so they run the 128 x 256 and
+    separate-accumulator shapes. First and last image against the oracle;
+    the whole batch against the forward with every GEMM on the 128 x 128
+    shape."""
+    L = tcg.lib()
+    path, cfg = model(cache_dir, "vit-b32", n_layer=2)
+    w = G.make_vit_weights(cfg, 0)
+    px = G.make_pixels(64, cfg["image"], 3)
+    m = tcg.VitModel(path)
+    try:
+        m.upload(64)
+        out, taps = m.encode(px, taps=True)
+        plan = (ctypes.c_int * 4)()
+        L.tcg_gemm_last_plan(plan)              # the last plan made: the last layer's down projection
+        assert plan[2] == 7, list(plan)
+        again, _ = m.encode(px)                 # graph replay
+        assert np.array_equal(out, again)
+    finally:
+        m.close()
+    port = oracle.PortVit(cfg, w)
+    for i in (0, 63):
+        ref = port.forward(px[i])
+        assert rel_inf(out[i], ref["embedding"]) <= TOL
+        for k in TAPS:
+            assert rel_inf(taps[k][i], ref[k]) <= TOL, (i, k)
+    old = L.tcg_gemm_force_cfg(13)
+    try:
+        m = tcg.VitModel(path)
+        try:
+            m.upload(64)
+            wide, _ = m.encode(px)
+        finally:
+            m.close()
+    finally:
+        L.tcg_gemm_force_cfg(old)
+    for i in range(64):
+        assert rel_inf(out[i], wide[i]) <= TOL, i
+    assert L.tcg_device_error() == 0
 
 
 def test_l14_two_layers_vs_oracle(gpu, cache_dir):
