@@ -478,6 +478,15 @@ __device__ __forceinline__ void stage_x(const float *__restrict__ x, float *xs, 
     }
 }
 
+// Barrier of the SEGS warps of one row group (named barrier 1 + rloc; 0 is
+// the CTA-wide one): the other row groups of the CTA run on.
+template <int SEGS>
+__device__ __forceinline__ void group_sync(int rloc)
+{
+    static_assert(MV_WARPS / SEGS < 16, "one named barrier per row group");
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + rloc), "n"(SEGS * 32) : "memory");
+}
+
 template <int TYPE, int SEGS, int NSLOT, int ROWS>
 __global__ void __launch_bounds__(MV_WARPS * 32, 1)
 matvec_stream_kernel(const uint8_t *__restrict__ W, const float *__restrict__ x, float *__restrict__ y,
@@ -542,7 +551,7 @@ matvec_stream_kernel(const uint8_t *__restrict__ W, const float *__restrict__ x,
         for (int r = 0; r < ROWS; r++)
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xFFFFFFFFu, acc[r], o);
-        if (SEGS == 1) {
+        if constexpr (SEGS == 1) {
 #pragma unroll
             for (int r = 0; r < ROWS; r++)
                 if (lane == 0 && row0 + r < N) y[row0 + r] = acc[r];
@@ -551,7 +560,7 @@ matvec_stream_kernel(const uint8_t *__restrict__ W, const float *__restrict__ x,
 #pragma unroll
                 for (int r = 0; r < ROWS; r++) part[wid * ROWS + r] = acc[r];
             }
-            __syncthreads();
+            group_sync<SEGS>(rloc);
             if (seg == 0 && lane == 0) {
 #pragma unroll
                 for (int r = 0; r < ROWS; r++) {
@@ -562,7 +571,7 @@ matvec_stream_kernel(const uint8_t *__restrict__ W, const float *__restrict__ x,
                     }
                 }
             }
-            __syncthreads();
+            group_sync<SEGS>(rloc);
         }
     }
     cp_wait0();
