@@ -26,6 +26,8 @@ N(0, 0.02) (LayerNorm gamma 1 + N(0, 0.02)), seed 0; pixels U[-1, 1), seed 1.
 --impl reference times the reference's CPU implementation alone (rank 0).
 """
 import argparse
+import contextlib
+import ctypes
 import json
 import os
 import statistics
@@ -283,6 +285,22 @@ def kquant_aux(tcg, hbm_peak):
 
 # ------------------------------------------------------------ our arm
 
+@contextlib.contextmanager
+def stdout_to_stderr():
+    """Send what C code prints to stdout (NCCL's version banner at
+    communicator set-up) to stderr, so that rank 0's stdout stays the one
+    JSON line; C stdio is flushed before fd 1 is put back."""
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        yield
+    finally:
+        ctypes.CDLL(None).fflush(None)
+        os.dup2(saved, 1)
+        os.close(saved)
+
+
 def run_ours(args, dist):
     import tcg
     pk, pk_kind = peaks()
@@ -305,7 +323,8 @@ def run_ours(args, dist):
             tcg.check(L.tcg_nccl_unique_id(buf), "tcg_nccl_unique_id")
             uid = buf.raw
         uid = dist.bcast_bytes(uid)
-        model.upload_bcast(per, dist.rank, dist.world, uid)
+        with stdout_to_stderr():
+            model.upload_bcast(per, dist.rank, dist.world, uid)
     else:
         model.upload(per)
 
@@ -441,7 +460,8 @@ def run_ours(args, dist):
             "model_flop_per_image": gf + af + pf,
             "device_error": derr, "outputs_finite": emb_ok,
         }
-    model.close()
+    with stdout_to_stderr():
+        model.close()
     dpx.close()
     dout.close()
     for b in (hpx, hout, hpx2, hout2):
