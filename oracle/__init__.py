@@ -32,11 +32,14 @@ def _ptr(a):
     return a.ctypes.data_as(C.c_void_p) if a is not None else None
 
 
-def build(with_ref: bool = True) -> None:
+def build(with_ref: bool = True, ref_dir: str | None = None) -> None:
+    """Build the C restatement and, when `with_ref` and a reference source
+    tree is named (`ref_dir`, else the TC_REFERENCE environment variable),
+    the reference's own library."""
     subprocess.run(["make", "-s", "-C", HERE, "port"], check=True)
-    if with_ref and os.path.isdir(os.environ.get("TC_REFERENCE", "/root/reference") + "/src"):
-        subprocess.run(["make", "-s", "-C", HERE, "ref",
-                        "REF=" + os.environ.get("TC_REFERENCE", "/root/reference")], check=True)
+    ref = ref_dir or os.environ.get("TC_REFERENCE")
+    if with_ref and ref and os.path.isdir(os.path.join(ref, "src")):
+        subprocess.run(["make", "-s", "-C", HERE, "ref", "REF=" + ref], check=True)
 
 
 _port = None

@@ -499,15 +499,22 @@ __device__ __forceinline__ int ld_acquire(const int *f)
     return v;
 }
 
+// Test hook (tcg_test_gemm_withhold_flags): the stream-K flag wait's limit,
+// and whether contributors raise their flags at all (1: they never do, so
+// every owner's wait runs out, which is how the failure path gets tested
+// without a fault).
+__device__ unsigned long long g_flag_wait_ns = WAIT_NS;
+__device__ int g_flag_withhold = 0;
+
 // Wait (bounded, like bar_wait) until a contributor has raised flag f.
 __device__ bool flag_wait(const int *f, volatile int *abort, int *err, int code)
 {
-    const unsigned long long t0 = now_ns();
+    const unsigned long long t0 = now_ns(), limit = g_flag_wait_ns;
     for (uint32_t it = 1;; ++it) {
         if (ld_acquire(f) != 0) return true;
         if ((it & 63) == 0) {
             if (*abort) return false;
-            if (now_ns() - t0 > WAIT_NS) {
+            if (now_ns() - t0 > limit) {
                 *abort = 1;
                 atomicExch(err, code);
                 return false;
@@ -770,7 +777,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                 for (int j = 0; j < S::HALF; j++) slot[j * 32 + lane] = acc[j];
                 __threadfence();
                 __syncwarp();
-                if (lane == 0) st_release(flags + me * EPI_W + ew, 1);
+                if (lane == 0 && !g_flag_withhold) st_release(flags + me * EPI_W + ew, 1);
                 continue;
             }
             if (skm && sg.c1 < n_chunks) {
@@ -1218,6 +1225,39 @@ int tcg_gemm_force_cfg(int cfg)
     const int old = g_force_cfg;
     g_force_cfg = cfg >= 0 && cfg < gemm_num_cfgs() ? cfg : -1;
     return old;
+}
+
+// Test hook for the failure path of the stream-K hand-over: with on != 0,
+// contributors stop raising their flags and an owner gives up waiting after
+// wait_ms (then the kernel winds down, the device error word reads 8 and
+// tcg_clear_device_error() makes the GEMMs usable again); on = 0 restores
+// normal operation and the 4 s limit. Synchronous. The stream-K flags of a
+// plan are only used by the throughput configuration (tcg_gemm_throughput_cfg).
+bool tcg_test_gemm_withhold_flags(int on, double wait_ms)
+{
+    if (!need_ctx()) return false;
+    const int w = on ? 1 : 0;
+    const unsigned long long ns = on && wait_ms > 0 ? (unsigned long long)(wait_ms * 1e6) : WAIT_NS;
+    TCG_CUDA(cudaStreamSynchronize(ctx().cur));
+    TCG_CUDA(cudaMemcpyToSymbol(g_flag_withhold, &w, sizeof w));
+    TCG_CUDA(cudaMemcpyToSymbol(g_flag_wait_ns, &ns, sizeof ns));
+    return true;
+}
+
+int tcg_gemm_throughput_cfg(void) { return gemm_throughput_cfg(); }
+
+// Test hook: bytes the op API has allocated on this thread's device for its
+// grow-on-demand operand scratch and its stream-K workspace (0 until a call
+// needs them).
+size_t tcg_op_scratch_bytes(void)
+{
+    if (!ctx().ready) return 0;
+    size_t b = ctx().scratch_bytes;
+    if (ctx().gemm_work) {
+        const GemmWork *w = (const GemmWork *)ctx().gemm_work;
+        b += gemm_work_ws_floats(w->ctas) * sizeof(float) + gemm_work_flag_count(w->ctas) * sizeof(int);
+    }
+    return b;
 }
 
 // Test hook: K-elements per TMEM chunk (a multiple of 32; larger is faster

@@ -19,6 +19,8 @@
 // later reads.
 #include "gemm.cuh"
 
+#include <mutex>
+
 namespace {
 
 constexpr size_t SCRATCH_FLOATS = (size_t)TCG_NOALLOC_SCRATCH_BYTES / sizeof(float);
@@ -32,8 +34,12 @@ static __device__ __align__(256) float g_scratch[SCRATCH_FLOATS];
 // names a host-side stand-in, never a device address, so the address comes
 // from cudaGetSymbolAddress with the device current (the first call on each
 // device does this, which is why that first call belongs outside any stream
-// capture).
+// capture). Host threads with their own contexts on one device may make
+// that first call together: std::call_once lets exactly one of them look the
+// address up and publishes it to the others.
 float *g_scratch_dev[64];
+cudaError_t g_scratch_err[64];
+std::once_flag g_scratch_once[64];
 
 }  // namespace
 
@@ -55,15 +61,15 @@ extern "C" bool tcg_linear_noalloc(float *y, const float *x, const float *W, con
 
     const int dev = ctx().device;
     if (dev < 0 || dev >= 64) return fail("tcg_linear_noalloc: device index %d out of range", dev);
-    if (!g_scratch_dev[dev]) {
+    std::call_once(g_scratch_once[dev], [dev] {
         void *p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
-        if (e != cudaSuccess || !p) {
-            cudaGetLastError();
-            return fail("tcg_linear_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-        }
-        g_scratch_dev[dev] = static_cast<float *>(p);
-    }
+        g_scratch_err[dev] = cudaGetSymbolAddress(&p, g_scratch);
+        if (g_scratch_err[dev] == cudaSuccess && !p) g_scratch_err[dev] = cudaErrorInvalidSymbol;
+        if (g_scratch_err[dev] != cudaSuccess) cudaGetLastError();
+        else g_scratch_dev[dev] = static_cast<float *>(p);
+    });
+    if (g_scratch_err[dev] != cudaSuccess)
+        return fail("tcg_linear_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(g_scratch_err[dev]));
     float *xh = g_scratch_dev[dev], *xl = xh + xa, *wh = xl + xa, *wl = wh + wa;
 
     cudaStream_t s = ctx().cur;

@@ -34,7 +34,7 @@ import oracle  # noqa: E402
 import tcg_gguf as G  # noqa: E402
 
 OUT = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("TC_REFERENCE", "/root/reference")
+REF = os.environ.get("TC_REFERENCE", "")
 OPS_SHA256 = "56160063ceb733fe6ad2f8022bb8c2f75b64181511109fb657cc3b040537279a"
 
 
@@ -118,7 +118,9 @@ def vit_fixture():
 
 
 if __name__ == "__main__":
-    oracle.build(with_ref=True)
+    if not REF or not os.path.isdir(os.path.join(REF, "src")):
+        sys.exit("set TC_REFERENCE to the roofline.c source tree (the directory holding src/ and tests/)")
+    oracle.build(with_ref=True, ref_dir=REF)
     ops_fixture()
     kquant_fixture()
     vit_fixture()
