@@ -116,6 +116,14 @@ class Dist:
         self.td.all_reduce(t, op=self.td.ReduceOp.MAX)
         return float(t.item())
 
+    def sum(self, x: float) -> float:
+        if self.world == 1:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64)
+        self.td.all_reduce(t, op=self.td.ReduceOp.SUM)
+        return float(t.item())
+
     def bcast_bytes(self, b: bytes) -> bytes:
         if self.world == 1:
             return b
@@ -126,6 +134,33 @@ class Dist:
     def close(self):
         if self.world > 1:
             self.td.destroy_process_group()
+
+
+# ------------------------------------------------------------ parity
+
+GOLDEN = os.path.join(ROOT, "tests", "golden", "vit_bench_golden.npz")
+
+
+def shard_parity(model, batch, lo, emb):
+    """Compare this rank's embeddings (images lo .. lo + len(emb) of the
+    batch) with the reference tc_vit_encode's, frozen for the benchmark's
+    model and batch: (max |err| / max |ref| over the images checked, the
+    smallest cosine, how many images). None when no frozen outputs match."""
+    try:
+        g = np.load(GOLDEN)
+    except OSError:
+        return None
+    if f"{model}.index" not in g.files or int(g[f"{model}.batch"]) != batch:
+        return None
+    worst, cmin, n = 0.0, 1.0, 0
+    for j, i in enumerate(g[f"{model}.index"]):
+        if lo <= i < lo + len(emb):
+            got = emb[i - lo].astype(np.float64)
+            ref = g[f"{model}.embedding"][j].astype(np.float64)
+            worst = max(worst, float(np.abs(got - ref).max() / np.abs(ref).max()))
+            cmin = min(cmin, float(got @ ref / np.linalg.norm(got) / np.linalg.norm(ref)))
+            n += 1
+    return worst, cmin, n
 
 
 # ------------------------------------------------------------ clock sampler
@@ -393,6 +428,8 @@ def run_ours(args, dist):
     dist.barrier()
     clk = clocks.stop()
     emb_ok = bool(np.isfinite(hout.array).all() and np.array_equal(hout.array, hout2.array))
+    # this rank's embeddings (from the timed serving loop) against the reference's
+    par = shard_parity(args.model, args.batch, lo, hout.array)
 
     # per-kernel-class device time: the same forward, eagerly, with events
     L.tcg_vit_profile_begin()
@@ -404,6 +441,9 @@ def run_ours(args, dist):
     launches = L.tcg_vit_launches_per_forward(model.dev)
     derr = L.tcg_device_error()
 
+    par_checked = dist.sum(par[2] if par else 0)
+    par_rel = dist.max(par[0] if par and par[2] else 0.0)
+    par_cos = -dist.max(-(par[1] if par and par[2] else 1.0))
     ms_max = dist.max(ms)
     e2e_max = dist.max(e2e_ms)
     e2e_block_max = dist.max(e2e_block_ms)
@@ -465,6 +505,12 @@ def run_ours(args, dist):
             "clocks": clk,
             "model_flop_per_image": gf + af + pf,
             "device_error": derr, "outputs_finite": emb_ok,
+            "parity_max_rel": round(par_rel, 9) if par_checked else None,
+            "parity": {"images_checked": int(par_checked), "max_rel": par_rel if par_checked else None,
+                       "min_cosine": par_cos if par_checked else None, "bar": "max|err| <= 1e-4 max|ref|, "
+                       "cosine >= 0.9999", "vs": "embeddings of the reference's tc_vit_encode at full depth "
+                       "(first and last image of every 1/2/4/8-GPU shard and one middle image), frozen in "
+                       "tests/golden/vit_bench_golden.npz; checked on every rank, max over ranks"},
         }
     with stdout_to_stderr():
         model.close()

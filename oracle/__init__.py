@@ -9,6 +9,9 @@ Two libraries live here:
   * _ref/libtcref.so    -- roofline.c's own src/*.c compiled unmodified by
     `make -C oracle ref` (only where the reference tree is present; the .so
     then travels with the repository snapshot).
+and, from `make -C oracle droptests`, the reference's own test programs
+(_ref/test_{arena,gguf,ops}_tcg) compiled against include/ and linked with
+the product library libtcg.so -- the drop-in check, run by tests/.
 """
 from __future__ import annotations
 
@@ -40,6 +43,10 @@ def build(with_ref: bool = True, ref_dir: str | None = None) -> None:
     ref = ref_dir or os.environ.get("TC_REFERENCE")
     if with_ref and ref and os.path.isdir(os.path.join(ref, "src")):
         subprocess.run(["make", "-s", "-C", HERE, "ref", "REF=" + ref], check=True)
+        # the reference's own test programs linked against libtcg.so (the
+        # drop-in check), once the library is built
+        if os.path.exists(os.path.join(os.path.dirname(HERE), "roofline.c_b200", "lib", "libtcg.so")):
+            subprocess.run(["make", "-s", "-C", HERE, "droptests", "REF=" + ref], check=True)
 
 
 _port = None

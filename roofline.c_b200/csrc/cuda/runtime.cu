@@ -57,6 +57,26 @@ void *scratch(size_t bytes)
     return c.scratch;
 }
 
+void *stage_buffer(size_t bytes)
+{
+    Ctx &c = g_ctx;
+    if (bytes <= c.stage_bytes) return c.stage;
+    if (c.stage) {
+        cudaStreamSynchronize(c.cur);
+        cudaFree(c.stage);
+        c.stage = nullptr;
+        c.stage_bytes = 0;
+    }
+    const size_t want = bytes < (16u << 20) ? (16u << 20) : bytes;
+    if (cudaMalloc(&c.stage, want) != cudaSuccess) {
+        cudaGetLastError();
+        fail("device staging of %zu bytes: out of memory", want);
+        return nullptr;
+    }
+    c.stage_bytes = want;
+    return c.stage;
+}
+
 }  // namespace tcg
 
 using tcg::ctx;

@@ -26,6 +26,8 @@ struct Ctx {
     void *scratch = nullptr;      // grow-only device scratch for the op API
     size_t scratch_bytes = 0;
     void *gemm_work = nullptr;    // the op API's GemmWork (gemm_tc.cu)
+    void *stage = nullptr;        // grow-only device copies of host-buffer op calls (ops_api.cu)
+    size_t stage_bytes = 0;
 };
 
 Ctx &ctx();
@@ -33,6 +35,7 @@ bool need_ctx();                                    // false + message if no dev
 bool fail(const char *fmt, ...) __attribute__((format(printf, 1, 2)));
 bool cuda_fail(cudaError_t e, const char *what, const char *file, int line);
 void *scratch(size_t bytes);                        // ctx scratch, grown on demand
+void *stage_buffer(size_t bytes);                   // ctx staging for host-buffer ops, grown on demand
 
 inline unsigned ceil_div(size_t a, size_t b) { return (unsigned)((a + b - 1) / b); }
 

@@ -74,6 +74,10 @@ def vit_golden():
     return dict(np.load(os.path.join(GOLDEN, "vit_golden.npz")))
 
 
+def vit_bench_golden():
+    return dict(np.load(os.path.join(GOLDEN, "vit_bench_golden.npz")))
+
+
 def check_close(got, want, atol, rtol, what=""):
     """The reference's op-test rule (tests/test_ops.c:53): fail only when
     BOTH the worst absolute and the worst relative error are exceeded."""

@@ -18,6 +18,10 @@ repository, so the GPU tests never need either.
                      (oracle/_ref/libtcref.so, built from the reference
                      sources) on seeded synthetic models: embedding, CLS row
                      and per-tap float64 sums for two shapes.
+  vit_bench_golden.npz  the same tc_vit_encode at full depth on the
+                     benchmark's own models and batches (ViT-B/32 batch 256,
+                     ViT-L/14 batch 128): embeddings of the first and last
+                     image of every 1/2/4/8-GPU shard and one middle image.
 
     python tests/golden/make_golden.py
 """
@@ -117,6 +121,65 @@ def vit_fixture():
     np.savez_compressed(os.path.join(OUT, "vit_golden.npz"), **out)
 
 
+# Images of the benchmark's batches whose full-depth embeddings are frozen:
+# the first and last image of every shard of a 1/2/4/8-GPU run (the shard
+# edges), plus one from the middle of the batch.
+BENCH_CASES = (
+    # (model, batch, pixel seed)
+    ("vit-b32", 256, 1),
+    ("vit-l14", 128, 1),
+)
+
+
+def bench_indices(batch: int) -> list:
+    idx = {batch // 2 + 5}
+    for world in (1, 2, 4, 8):
+        per = batch // world
+        for r in range(world):
+            idx.update((r * per, r * per + per - 1))
+    return sorted(idx)
+
+
+def vit_bench_fixture(threads: int = 0):
+    """Full-depth embeddings of the benchmark's own models (weights seed 0)
+    and batches, from the reference's tc_vit_encode, one image per host
+    thread at a time."""
+    import tempfile
+    import threading
+    threads = threads or os.cpu_count() or 1
+    out = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        for name, batch, pseed in BENCH_CASES:
+            path, cfg = G.cached_vit_gguf(tmp, name, 0)
+            px = G.make_pixels(batch, cfg["image"], pseed)
+            idx = bench_indices(batch)
+            emb = np.zeros((len(idx), cfg["d_out"]), np.float32)
+            models = [oracle.RefVit(path) for _ in range(min(threads, len(idx)))]
+            todo = list(enumerate(idx))
+            lock = threading.Lock()
+
+            def work(m):
+                while True:
+                    with lock:
+                        if not todo:
+                            return
+                        j, i = todo.pop()
+                    emb[j] = m.encode(px[i], cfg["d_out"])["embedding"]
+
+            ts = [threading.Thread(target=work, args=(m,)) for m in models]
+            for t in ts:
+                t.start()
+            for t in ts:
+                t.join()
+            for m in models:
+                m.close()
+            out[f"{name}.index"] = np.array(idx, np.int32)
+            out[f"{name}.embedding"] = emb
+            out[f"{name}.batch"] = np.array(batch, np.int32)
+            print(f"{name}: {len(idx)} images of a batch of {batch}", flush=True)
+    np.savez_compressed(os.path.join(OUT, "vit_bench_golden.npz"), **out)
+
+
 if __name__ == "__main__":
     if not REF or not os.path.isdir(os.path.join(REF, "src")):
         sys.exit("set TC_REFERENCE to the roofline.c source tree (the directory holding src/ and tests/)")
@@ -124,4 +187,5 @@ if __name__ == "__main__":
     ops_fixture()
     kquant_fixture()
     vit_fixture()
+    vit_bench_fixture()
     print("golden fixtures written to", OUT)
