@@ -639,6 +639,7 @@ static bool launch_matvec(float *y, const void *W, const float *x, int N, int K)
 }
 
 bool launch_matvec_tc_q4k(float *y, const void *W, const float *x, int N, int K, bool *used);   // mv_tc.cu
+bool launch_matvec_mma_q4k(float *y, const void *W, const float *x, int N, int K, bool *used);  // mv_mma.cu
 
 template <int TYPE>
 static bool matvec_dispatch(float *y, const void *W, const float *x, int N, int K)
@@ -650,6 +651,12 @@ static bool matvec_dispatch(float *y, const void *W, const float *x, int N, int 
         if (!launch_matvec_tc_q4k(y, W, x, N, K, &used)) return false;
         if (used) {
             g_mv_last = 4;
+            return true;
+        }
+        // the integer mma.sync kernel (default) wherever it applies
+        if (!launch_matvec_mma_q4k(y, W, x, N, K, &used)) return false;
+        if (used) {
+            g_mv_last = 5;
             return true;
         }
     }
@@ -792,6 +799,6 @@ const float *tcg_dequant_view(const gguf_tensor_t *t, tcg_arena_t *a, bool *conv
 }  // extern "C"
 
 // Test hook: the kernel of the latest K-quant matvec (2: row segments
-// streamed through a cp.async ring, 3: staged groups, 4: Q4_K on the tensor
-// cores; 0: none yet).
+// streamed through a cp.async ring, 3: staged groups, 4: Q4_K on tcgen05,
+// 5: Q4_K on the integer mma.sync kernel; 0: none yet).
 extern "C" int tcg_matvec_last_kernel(void) { return tcg::g_mv_last; }

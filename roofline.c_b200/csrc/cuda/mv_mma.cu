@@ -1,0 +1,600 @@
+// mv_mma.cu -- the fused Q4_K dequant-matvec y = W x on the warp-level
+// integer tensor path (mma.sync m16n8k32, u8 x s8 -> s32).
+//
+// The Q4_K arm of the dequant seam (roofline.c src/dequant.c:40-63 with
+// ggml's Q4_K block: fp16 d and dmin, twelve bytes of 6-bit scales and mins,
+// 128 bytes of nibbles) gives weight k of 32-weight sub-block j the value
+// (d*sc_j)*q_k - (dmin*m_j), so a row's dot product regroups as
+//     y_r = sum_sb d * sum_j sc_j * sum_{k in j} q_k x_k  -  dmin * sum_j m_j * X_j,
+// X_j the sum of x over sub-block j. The sums over q run as exact integer
+// MMAs; everything per weight is one mask:
+//   - A (16 rows x 32 weights of one sub-block): the quant bytes as loaded,
+//     masked to the low nibbles (sub-block 2c of 32-byte chunk c) or to the
+//     high nibbles kept in place, i.e. 16 q (sub-block 2c+1);
+//   - B (32 weights x 8 columns): each superblock of x is scaled by a power
+//     of two to |v| < 64 and split into four int8 pieces
+//     v = p0 + p1/2^7 + p2/2^14 + p3/2^21 (the rest is below 2^-26 of the
+//     superblock's largest |x|), pieces in columns 0-3, zeros in 4-7. The
+//     pieces of the superblocks a CTA needs are built in shared memory when
+//     it starts;
+//   - C: per thread, rows g and g+8 of the tile times columns 2t, 2t+1:
+//     lane quad t = 0 holds the p0/p1 sums, t = 1 the p2/p3 sums. They are
+//     multiplied by the row's 6-bit sub-block scale and summed over the
+//     superblock in 32-bit integers (exact: below 2^28), then converted once
+//     per superblock, scaled by d and the power of two, and accumulated in
+//     fp32. The min term is spread over the four lanes of a quad (two
+//     sub-blocks each) and the quad's partial sums meet by two shuffles.
+// Results differ from the dequantise-then-dot order by rounding only.
+//
+// Work: units of (16-row tile, K segment of spb superblocks), segment-major,
+// split into one contiguous range per CTA (one persistent CTA per SM). The
+// weights are fed by the tensor memory accelerator: one producer lane copies
+// each unit's 16 row segments (spb * 144 contiguous bytes each) into a ring of
+// shared-memory slots, as many units ahead as the slots hold, from the
+// kernel's first instructions on, so that most of an SM's share of the
+// matrix is in flight at once while x is being prepared: one 3-D tensor copy
+// per unit (36 words x spb superblocks x 16 rows; rows past N arrive as
+// zeros). The slot's rows are spb * 144 bytes apart, and MMA row g reads slot
+// row sigma(g), a permutation chosen per spb so that the quant loads of a
+// half-warp hit distinct shared-memory banks. Sixteen consumer
+// warps take the CTA's units in turn. A tile split into S > 1 segments is
+// summed by the last warp to finish one of its segments, in segment order (a
+// per-tile arrival counter that this warp resets), so every call gives the
+// same bits. Slot waits are bounded; one that gives up raises the device
+// error word, and the unit still arrives (with a zero partial sum) so the
+// counters stay consistent. No thread waits on another CTA.
+#include "tcg_common.cuh"
+#include "tc05.cuh"
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <mutex>
+
+namespace tcg {
+
+namespace {
+
+constexpr int MM_WARPS = 16;
+constexpr int MM_BB = 144;                  // Q4_K bytes per superblock
+constexpr int MM_XSB = 1024 + 32 + 16;      // shared bytes per superblock of x: pieces, 8 sums, scale (+pad)
+
+// D = A B over one sub-block: A u8 16 x 32 (a0: row g, k 4t..4t+3; a1: row
+// g+8; a2, a3: k 16+4t..), B s8 32 x 8 (b0: k 4t..4t+3 of column g, b1: k
+// 16+4t..), D rows g, g+8 x columns 2t, 2t+1.
+__device__ __forceinline__ void mma_u8s8(int d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+                 "{%8, %9}, {%10, %10, %10, %10};"
+                 : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+__device__ __forceinline__ uint32_t byte_of(uint32_t w, int b) { return __byte_perm(w, 0u, 0x4440u | (unsigned)b); }
+
+// four int8 from four integer-valued floats in [-128, 127]
+__device__ __forceinline__ uint32_t pack4(float a, float b, float c, float d)
+{
+    const uint32_t lo = __byte_perm((uint32_t)__float2int_rn(a), (uint32_t)__float2int_rn(b), 0x0040u);
+    const uint32_t hi = __byte_perm((uint32_t)__float2int_rn(c), (uint32_t)__float2int_rn(d), 0x0040u);
+    return __byte_perm(lo, hi, 0x5410u);
+}
+
+// One superblock of a unit in flight: headers (d, dmin, scales) of rows g and
+// g+8, and this lane's 8 quant bytes of each 32-byte chunk of both rows.
+struct Sb {
+    uint4 h0, h1;
+    uint2 q0[4], q1[4];
+};
+
+// The 6-bit scales (sc) and mins (mn) of sub-blocks 0-3 and 4-7, one per byte.
+__device__ __forceinline__ void scales_of(const uint4 &h, uint32_t &sc_lo, uint32_t &sc_hi, uint32_t &mn_lo,
+                                          uint32_t &mn_hi)
+{
+    sc_lo = h.y & 0x3F3F3F3Fu;
+    mn_lo = h.z & 0x3F3F3F3Fu;
+    sc_hi = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+    mn_hi = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+}
+
+__device__ __forceinline__ float f16lo(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu))); }
+__device__ __forceinline__ float f16hi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
+// a small non-negative integer (< 2^23) as a float, exactly
+__device__ __forceinline__ float small_int_float(uint32_t v) { return __uint_as_float(0x4B000000u | v) - 8388608.0f; }
+
+// Accumulate superblock s (x pieces at xsb) of rows g, g+8 into acc0 / acc1
+// (this lane's share: the p-pair sums for t < 2, the min terms of sub-blocks
+// 2t, 2t+1 for every t).
+__device__ __forceinline__ void sb_dot(const Sb &s, const uint8_t *xsb, int g, int t, float &acc0, float &acc1)
+{
+    uint32_t sc0l, sc0h, mn0l, mn0h, sc1l, sc1h, mn1l, mn1h;
+    scales_of(s.h0, sc0l, sc0h, mn0l, mn0h);
+    scales_of(s.h1, sc1l, sc1h, mn1l, mn1h);
+    int lo[4] = { 0, 0, 0, 0 }, hi[4] = { 0, 0, 0, 0 };
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        const uint32_t w0 = c < 2 ? sc0l : sc0h, w1 = c < 2 ? sc1l : sc1h;
+        const int bl = 2 * (c & 1);
+        const int sA0 = (int)byte_of(w0, bl), sA1 = (int)byte_of(w1, bl);           // sub-block 2c
+        const int sB0 = (int)byte_of(w0, bl + 1), sB1 = (int)byte_of(w1, bl + 1);   // sub-block 2c + 1
+        uint32_t b0 = 0, b1 = 0, e0 = 0, e1 = 0;
+        if (g < 4) {
+            const uint2 bl2 = *reinterpret_cast<const uint2 *>(xsb + (2 * c) * 128 + g * 32 + 8 * t);
+            const uint2 bh2 = *reinterpret_cast<const uint2 *>(xsb + (2 * c + 1) * 128 + g * 32 + 8 * t);
+            b0 = bl2.x; b1 = bl2.y; e0 = bh2.x; e1 = bh2.y;
+        }
+        int d[4];
+        mma_u8s8(d, s.q0[c].x & 0x0F0F0F0Fu, s.q1[c].x & 0x0F0F0F0Fu, s.q0[c].y & 0x0F0F0F0Fu,
+                 s.q1[c].y & 0x0F0F0F0Fu, b0, b1);
+        lo[0] += d[0] * sA0; lo[1] += d[1] * sA0; lo[2] += d[2] * sA1; lo[3] += d[3] * sA1;
+        mma_u8s8(d, s.q0[c].x & 0xF0F0F0F0u, s.q1[c].x & 0xF0F0F0F0u, s.q0[c].y & 0xF0F0F0F0u,
+                 s.q1[c].y & 0xF0F0F0F0u, e0, e1);
+        hi[0] += d[0] * sB0; hi[1] += d[1] * sB0; hi[2] += d[2] * sB1; hi[3] += d[3] * sB1;
+    }
+    // 16 * (sum over the superblock); |.| < 2^28
+    const float v0 = (float)(lo[0] * 16 + hi[0]), v1 = (float)(lo[1] * 16 + hi[1]);
+    const float v2 = (float)(lo[2] * 16 + hi[2]), v3 = (float)(lo[3] * 16 + hi[3]);
+    // piece pair of this lane: (p0, p1) for t = 0, (p2, p3) for t = 1 (t > 1: zero sums)
+    const float xe = *reinterpret_cast<const float *>(xsb + 1024 + 32);      // 2^(e - 13)
+    const float k = t == 1 ? 3.814697265625e-06f : 0.0625f;                   // 2^-18 : 2^-4 (the 16 above)
+    const float f0 = fmaf(v0, 128.0f, v1), f1 = fmaf(v2, 128.0f, v3);
+    const float d0 = f16lo(s.h0.x), d1 = f16lo(s.h1.x);
+    // (f xe) (d k): both factors stay normal floats for every d and exponent
+    acc0 = fmaf(f0 * xe, d0 * k, acc0);
+    acc1 = fmaf(f1 * xe, d1 * k, acc1);
+    // min terms of sub-blocks 2t, 2t+1
+    const float2 X = *reinterpret_cast<const float2 *>(xsb + 1024 + 8 * t);
+    const uint32_t m0 = t < 2 ? mn0l : mn0h, m1 = t < 2 ? mn1l : mn1h;
+    const int bm = (2 * t) & 3;
+    const float dm0 = f16hi(s.h0.x), dm1 = f16hi(s.h1.x);
+    acc0 = fmaf(-dm0, fmaf(small_int_float(byte_of(m0, bm)), X.x, small_int_float(byte_of(m0, bm + 1)) * X.y), acc0);
+    acc1 = fmaf(-dm1, fmaf(small_int_float(byte_of(m1, bm)), X.x, small_int_float(byte_of(m1, bm + 1)) * X.y), acc1);
+}
+
+constexpr int MM_THREADS = MM_WARPS * 32 + 32;   // sixteen consumer warps and the producer warp
+
+// fetch-and-add with release (the warp's partial sums, ordered before it by
+// __syncwarp) and acquire (the other segments' sums, for the last to arrive)
+__device__ __forceinline__ int atom_add_acq_rel(int *p, int v)
+{
+    int old;
+    asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+__device__ __forceinline__ void tma_load3(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y, int z)
+{
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%2, %3, %4}], [%5];"
+                 ::"r"(dst), "l"((unsigned long long)map), "r"(x), "r"(y), "r"(z), "r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void load_sb_smem(Sb &s, const uint8_t *r0, const uint8_t *r1, int t)
+{
+    s.h0 = *reinterpret_cast<const uint4 *>(r0);
+    s.h1 = *reinterpret_cast<const uint4 *>(r1);
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        s.q0[c] = *reinterpret_cast<const uint2 *>(r0 + 16 + 32 * c + 8 * t);
+        s.q1[c] = *reinterpret_cast<const uint2 *>(r1 + 16 + 32 * c + 8 * t);
+    }
+}
+
+// Shared memory: x pieces (nsl superblocks), nslot unit slots of 16 rows x rs
+// bytes, then the slots' full and empty barriers and the abort flag.
+__global__ void __launch_bounds__(MM_THREADS, 1)
+mv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restrict__ x, float *__restrict__ y,
+                  int N, int nsb, int spb, int S, int tiles, long long U, float *ws, int *cnt, int nslot, int nwork,
+                  uint32_t sigma, int x_bytes, int early, int *err)
+{
+    extern __shared__ __align__(128) uint8_t smx[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const long long u0 = U * blockIdx.x / gridDim.x, u1 = U * (blockIdx.x + 1) / gridDim.x;
+    const int nunits = (int)(u1 - u0);
+    const int seg_lo = (int)(u0 / tiles);
+    const int sb0 = seg_lo * spb;                                   // first superblock of x this CTA holds
+    const int nsl = min((int)((u1 - 1) / tiles + 1) * spb, nsb) - sb0;   // superblocks of x it holds
+    const int rs = spb * MM_BB;                                     // slot row stride
+    uint8_t *slots = smx + x_bytes;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(slots + (size_t)nslot * 16 * rs);
+    const uint32_t full0 = su32(bars), empty0 = su32(bars + nslot);
+    volatile int *abort = reinterpret_cast<volatile int *>(bars + 2 * nslot);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < nslot; s++) {
+            bar_init(full0 + 8 * s, 1);
+            bar_init(empty0 + 8 * s, 1);
+        }
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (warp == MM_WARPS) {
+        // producer: unit k of the CTA into slot k % nslot once its previous
+        // unit has been consumed
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&wmap) : "memory");
+            auto fill = [&](int k) {
+                const long long u = u0 + k;
+                const int seg = (int)(u / tiles), tile = (int)(u % tiles);
+                const uint32_t fb = full0 + 8 * (k % nslot);
+                bar_expect_tx(fb, (uint32_t)(16 * rs));
+                tma_load3(su32(slots + (size_t)(k % nslot) * 16 * rs), &wmap, fb, 0, seg * spb, tile * 16);
+            };
+            int k = 0;
+            // With early set, the caller guarantees that no kernel before this
+            // one on the stream writes W: the first slots fill while that
+            // kernel finishes.
+            if (early)
+                for (; k < nslot && k < nunits; k++) fill(k);
+            pdl_wait();
+            for (; k < nunits; k++) {
+                const int slot = k % nslot;
+                if (k >= nslot && !bar_wait(empty0 + 8 * slot, (uint32_t)((k / nslot - 1) & 1), abort, err, 0x4D4D01))
+                    break;
+                fill(k);
+            }
+            // the copies in flight land before the CTA exits
+            for (int j = k - 1; j >= 0 && j >= k - nslot; j--)
+                bar_wait(full0 + 8 * (j % nslot), (uint32_t)((j / nslot) & 1), abort, err, 0x4D4D02, false);
+        }
+        return;
+    }
+    pdl_wait();
+
+    // x pieces of the CTA's superblocks: warp per superblock, lane l holds
+    // x 8l .. 8l+7 (sub-block l/4, positions 8(l%4) ..)
+    for (int i = warp; i < nsl; i += MM_WARPS) {
+        const float4 *xv = reinterpret_cast<const float4 *>(x + (size_t)(sb0 + i) * 256 + 8 * lane);
+        const float4 va = __ldg(xv), vb = __ldg(xv + 1);
+        float v[8] = { va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w };
+        float mx = 0.0f, sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            mx = fmaxf(mx, fabsf(v[k]));
+            sum += v[k];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+        sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+        sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
+        int e = 0;
+        if (mx > 0.0f) frexpf(mx, &e);                              // max|x| < 2^e
+        e = max(e, -110);                                           // keeps 2^(e-13) and 2^(6-e) normal floats
+        const float sc = __uint_as_float((uint32_t)(127 + 6 - e) << 23);   // 2^(6-e): |v sc| < 64
+        uint8_t *xsb = smx + (size_t)i * MM_XSB;
+        uint32_t pw[4][2];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            float r[4], p[4][4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) r[k] = v[4 * h + k] * sc;   // exact
+#pragma unroll
+            for (int piece = 0; piece < 4; piece++)
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    p[piece][k] = rintf(r[k]);
+                    r[k] = (r[k] - p[piece][k]) * 128.0f;           // exact; |r| <= 64
+                }
+#pragma unroll
+            for (int piece = 0; piece < 4; piece++) pw[piece][h] = pack4(p[piece][0], p[piece][1], p[piece][2], p[piece][3]);
+        }
+        const int j = lane >> 2, pos = 8 * (lane & 3);
+#pragma unroll
+        for (int piece = 0; piece < 4; piece++)
+            *reinterpret_cast<uint2 *>(xsb + j * 128 + piece * 32 + pos) = make_uint2(pw[piece][0], pw[piece][1]);
+        if ((lane & 3) == 0) reinterpret_cast<float *>(xsb + 1024)[j] = sum;
+        if (lane == 0) *reinterpret_cast<float *>(xsb + 1024 + 32) = __uint_as_float((uint32_t)(127 + e - 13) << 23);
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(MM_WARPS * 32) : "memory");    // the consumers only
+
+    // Consumer w takes units w, w + nwork, ...: nslot is a multiple of nwork
+    // (or no slot is reused), so every slot is read by one warp only, in
+    // unit order, and a warp never tests a slot's barrier while an earlier
+    // fill of that slot is still pending (which its parity test would read
+    // as complete).
+    for (int k = warp; warp < nwork && k < nunits; k += nwork) {
+        const long long u = u0 + k;
+        const int seg = (int)(u / tiles), tile = (int)(u % tiles);
+        const int slot = k % nslot;
+        const bool ok = bar_wait(full0 + 8 * slot, (uint32_t)((k / nslot) & 1), abort, err, 0x4D4D03);
+        float acc0 = 0.0f, acc1 = 0.0f;
+        const int sg = (int)((sigma >> (3 * g)) & 7u);               // this lane's slot row (and row + 8)
+        if (ok) {
+            const uint8_t *r0 = slots + (size_t)slot * 16 * rs + (size_t)sg * rs;
+            const uint8_t *r1 = r0 + (size_t)8 * rs;
+            const uint8_t *xs = smx + (size_t)(seg * spb - sb0) * MM_XSB;
+            const int steps = min(spb, nsb - seg * spb);            // the last segment of a row may be short
+            for (int i = 0; i < steps; i++) {
+                Sb sb;
+                load_sb_smem(sb, r0 + i * MM_BB, r1 + i * MM_BB, t);
+                sb_dot(sb, xs + (size_t)i * MM_XSB, g, t, acc0, acc1);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) bar_arrive(empty0 + 8 * slot);               // the slot's bytes are read
+        // the quad's four shares of rows g and g+8
+        acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 1);
+        acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 1);
+        acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 2);
+        acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 2);
+        const int r0 = tile * 16 + sg, r1 = r0 + 8;
+        if (S == 1) {
+            if (t == 0) {
+                if (r0 < N) y[r0] = acc0;
+                if (r1 < N) y[r1] = acc1;
+            }
+            continue;
+        }
+        if (t == 0) {
+            if (r0 < N) ws[(size_t)seg * N + r0] = acc0;
+            if (r1 < N) ws[(size_t)seg * N + r1] = acc1;
+        }
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = atom_add_acq_rel(cnt + tile, 1) == S - 1;
+        last = __shfl_sync(0xFFFFFFFFu, last, 0);
+        if (last) {
+            __syncwarp();
+            const int r = tile * 16 + lane;
+            if (lane < 16 && r < N) {
+                float v = 0.0f;
+                for (int s = 0; s < S; s++) v += __ldcg(ws + (size_t)s * N + r);
+                y[r] = v;
+            }
+            if (lane == 0) cnt[tile] = 0;                           // ready for the next call
+        }
+    }
+}
+
+// Working memory of this host thread's calls on a device: per-tile arrival
+// counters (zero between calls) and the segments' partial sums. Grown on
+// demand; calls of one thread are stream-ordered, so they never share it.
+struct MmBuf {
+    uint8_t *p = nullptr;
+    size_t bytes = 0;
+    int cnt_cap = 0;
+};
+thread_local MmBuf g_mm[64];
+
+}  // namespace
+
+int g_mv_mma = 1;          // 1 (default): Q4_K matvec on this kernel where it applies
+int g_mv_mma_segs = 0;     // tuning hook: K segments per tile (0: chosen per shape)
+int g_mv_early = 0;        // 1: the caller's weights are never written by the kernel before a matvec
+int g_mv_slots = 0;        // tuning hook: most unit slots per CTA (0: as many as shared memory holds)
+
+// Superblocks per unit (the last segment of a row may be shorter): a row of
+// at most 8 superblocks is one unit; otherwise 5-8 superblocks, the fewest
+// padding columns in the last segment, then closest to 7 (measured, back to
+// back on B200: 16 x 7-superblock units give 12.3 us for 4096 x 14336
+// against 13.3 us with 8 superblocks and 15.0 us with 4; 14336 x 4096 runs
+// 12.8 us with 8 superblocks, 13.6 with 16 and 14.7 with 4; units of one or
+// two superblocks are several times slower).
+static int mm_unit_superblocks(int nsb)
+{
+    if (nsb <= 8) return nsb;
+    int best = 7, best_pad = 1 << 30;
+    for (int spb : { 7, 8, 6, 5 }) {
+        const int pad = (nsb + spb - 1) / spb * spb - nsb;
+        if (pad < best_pad) {
+            best_pad = pad;
+            best = spb;
+        }
+    }
+    return best;
+}
+
+typedef CUresult (*EncodeFn3)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                              const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeFn3 mm_encode_fn()
+{
+    static EncodeFn3 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeFn3)p;
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+// The order in which MMA rows g = 0..7 read the slot's rows (and rows + 8),
+// three bits each: a half-warp's lanes (rows g = 0..3, then 4..7, quad lanes
+// t = 0..3) load 8 bytes at word (rs/4) * sigma(g) + 2t (+ a common offset),
+// which fall in distinct banks when the four rows' word offsets mod 32 are 8
+// apart. The permutation with the fewest bank conflicts, identity first.
+static uint32_t mm_sigma_search(int w)
+{
+    int perm[8] = { 0, 1, 2, 3, 4, 5, 6, 7 }, best[8] = { 0, 1, 2, 3, 4, 5, 6, 7 };
+    int best_cost = 1 << 30;
+    do {
+        int cost = 0;
+        for (int h = 0; h < 2; h++) {
+            int banks[32] = {};
+            for (int gq = 0; gq < 4; gq++)
+                for (int tq = 0; tq < 4; tq++)
+                    for (int b = 0; b < 2; b++) banks[(w * perm[4 * h + gq] + 2 * tq + b) % 32]++;
+            int worst = 0;
+            for (int b = 0; b < 32; b++) worst = banks[b] > worst ? banks[b] : worst;
+            cost += worst;
+        }
+        if (cost < best_cost) {
+            best_cost = cost;
+            for (int i = 0; i < 8; i++) best[i] = perm[i];
+        }
+    } while (best_cost > 2 && std::next_permutation(perm, perm + 8));
+    uint32_t s = 0;
+    for (int i = 0; i < 8; i++) s |= (uint32_t)best[i] << (3 * i);
+    return s;
+}
+
+// mm_sigma_search for the stride rs, computed once per word offset mod 32.
+static uint32_t mm_sigma(int rs)
+{
+    static std::once_flag once[32];
+    static uint32_t table[32];
+    const int w = (rs / 4) % 32;
+    std::call_once(once[w], [w] { table[w] = mm_sigma_search(w); });
+    return table[w];
+}
+
+// This host thread's tensor map of the latest matrix (and its shape).
+struct MmMap {
+    const void *w = nullptr;
+    int n = 0, k = 0, spb = 0;
+    CUtensorMap map;
+};
+thread_local MmMap g_mm_map[64];
+
+bool launch_matvec_mma_q4k(float *y, const void *W, const float *x, int N, int K, bool *used)
+{
+    *used = false;
+    if (!g_mv_mma || ((uintptr_t)W & 15) || N <= 0 || K <= 0 || K % 256) return true;
+    const int nsb = K / 256, tiles = (N + 15) / 16, sms = ctx().sms > 0 ? ctx().sms : 148;
+    // spb superblocks per unit, S segments per row (the last one may be short)
+    const int spb = g_mv_mma_segs > 0 ? (nsb + g_mv_mma_segs - 1) / g_mv_mma_segs : mm_unit_superblocks(nsb);
+    const int S = (nsb + spb - 1) / spb;
+    if (spb > 256) return true;                                  // a box holds at most 256 superblocks
+    const long long U = (long long)tiles * S;
+    const int G = (int)(U < sms ? U : sms);
+    // the most superblocks of x, and units, one CTA holds
+    int nsl_max = 0, units_max = 0;
+    for (int c = 0; c < G; c++) {
+        const long long u0 = U * c / G, u1 = U * (c + 1) / G;
+        const int first = (int)(u0 / tiles) * spb, last = (int)((u1 - 1) / tiles + 1) * spb;
+        const int n = (last < nsb ? last : nsb) - first;
+        nsl_max = n > nsl_max ? n : nsl_max;
+        units_max = (int)(u1 - u0) > units_max ? (int)(u1 - u0) : units_max;
+    }
+    const int rs = spb * MM_BB;
+    const size_t cap = 232448;                                   // the most dynamic shared memory of a CTA
+    const size_t x_bytes = ((size_t)nsl_max * MM_XSB + 127) & ~(size_t)127;
+    const size_t slot = (size_t)16 * rs;
+    if (x_bytes + 2 * (slot + 16) + 16 > cap) return true;        // not two slots: the CUDA-core kernels
+    int nslot = (int)((cap - x_bytes - 16) / (slot + 16));
+    if (g_mv_slots >= 2 && nslot > g_mv_slots) nslot = g_mv_slots;
+    // Consumers: nwork warps taking units in turn. A reused slot must belong
+    // to one warp, so then nslot is a multiple of nwork.
+    int nwork;
+    if (nslot >= units_max) {
+        nslot = units_max;                                       // every unit its own slot
+        nwork = nslot < MM_WARPS ? nslot : MM_WARPS;
+    } else if (nslot >= MM_WARPS) {
+        nslot -= nslot % MM_WARPS;
+        nwork = MM_WARPS;
+    } else {
+        nwork = nslot;
+    }
+    const size_t smem = x_bytes + (size_t)nslot * slot + (size_t)nslot * 16 + 16;
+    float *ws = nullptr;
+    int *cnt = nullptr;
+    if (S > 1) {
+        MmBuf &b = g_mm[ctx().device & 63];
+        const int cnt_cap = tiles > b.cnt_cap ? tiles : b.cnt_cap;
+        const size_t cnt_bytes = ((size_t)cnt_cap * 4 + 255) & ~(size_t)255;
+        const size_t need = cnt_bytes + (size_t)S * N * 4;
+        if (need > b.bytes || cnt_cap > b.cnt_cap) {
+            if (b.p) {
+                TCG_CUDA(cudaStreamSynchronize(ctx().cur));
+                cudaFree(b.p);
+                b.p = nullptr;
+                b.bytes = 0;
+            }
+            const size_t want = need + need / 4;
+            if (cudaMalloc(&b.p, want) != cudaSuccess) {
+                cudaGetLastError();
+                return fail("matvec working memory of %zu bytes: out of memory", want);
+            }
+            TCG_CUDA(cudaMemsetAsync(b.p, 0, want, ctx().cur));
+            b.bytes = want;
+            b.cnt_cap = cnt_cap;
+        }
+        cnt = (int *)b.p;
+        ws = (float *)(b.p + (((size_t)b.cnt_cap * 4 + 255) & ~(size_t)255));
+    }
+    const int dev = ctx().device & 63;
+    MmMap &mp = g_mm_map[dev];
+    if (mp.w != W || mp.n != N || mp.k != K || mp.spb != spb) {
+        EncodeFn3 fn = mm_encode_fn();
+        if (!fn) return fail("cuTensorMapEncodeTiled is not available from the driver");
+        // 32-bit words: 36 per superblock, nsb superblocks per row, N rows
+        cuuint64_t dims[3] = { (cuuint64_t)(MM_BB / 4), (cuuint64_t)nsb, (cuuint64_t)N };
+        cuuint64_t strides[2] = { (cuuint64_t)MM_BB, (cuuint64_t)nsb * MM_BB };
+        cuuint32_t box[3] = { (cuuint32_t)(MM_BB / 4), (cuuint32_t)spb, 16 };
+        cuuint32_t estr[3] = { 1, 1, 1 };
+        const CUresult r = fn(&mp.map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, (void *)W, dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            mp.w = nullptr;
+            return fail("cuTensorMapEncodeTiled failed (%d) for the Q4_K matrix [%d x %d]", (int)r, N, K);
+        }
+        mp.w = W;
+        mp.n = N;
+        mp.k = K;
+        mp.spb = spb;
+    }
+    static unsigned done[64];
+    if (!done[dev]) {
+        TCG_CUDA(cudaFuncSetAttribute(mv_q4k_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cap));
+        done[dev] = 1;
+    }
+    TCG_CUDA(launch_pdl(mv_q4k_mma_kernel, dim3(G), dim3(MM_THREADS), smem, ctx().cur, mp.map, x, y, N, nsb, spb, S,
+                        tiles, U, ws, cnt, nslot, nwork, mm_sigma(rs), (int)x_bytes, g_mv_early, ctx().d_err));
+    *used = true;
+    return true;
+}
+
+}  // namespace tcg
+
+// Tuning and test hook: 1 (default) runs the Q4_K matvec on the integer
+// mma.sync kernel where it applies, 0 on the CUDA-core kernels. Returns the
+// previous setting.
+extern "C" int tcg_matvec_set_mma(int on)
+{
+    const int old = tcg::g_mv_mma;
+    tcg::g_mv_mma = on ? 1 : 0;
+    return old;
+}
+
+// Tuning hook: K segments per 16-row tile of the integer mma.sync matvec
+// (units of ceil(superblocks per row / segs) superblocks; 0 restores the
+// choice per shape). Returns the previous setting.
+extern "C" int tcg_matvec_mma_segments(int segs)
+{
+    const int old = tcg::g_mv_mma_segs;
+    tcg::g_mv_mma_segs = segs > 0 ? segs : 0;
+    return old;
+}
+
+// Q4_K matvec promise (default 0): with 1, the caller guarantees that the
+// kernel queued just before a matvec on the same stream never writes that
+// matvec's weight matrix (true of a decode pass whose weights are uploaded
+// once), and the matvec starts fetching its weights while that kernel is
+// still finishing. x may still be produced by it. Returns the previous value.
+extern "C" int tcg_matvec_set_static_weights(int on)
+{
+    const int old = tcg::g_mv_early;
+    tcg::g_mv_early = on ? 1 : 0;
+    return old;
+}
+
+// Tuning hook: at most this many unit slots (units in flight) per CTA of the
+// Q4_K mma.sync matvec; 0 restores as many as shared memory holds. Returns
+// the previous setting.
+extern "C" int tcg_matvec_mma_slots(int n)
+{
+    const int old = tcg::g_mv_slots;
+    tcg::g_mv_slots = n >= 2 ? n : 0;
+    return old;
+}

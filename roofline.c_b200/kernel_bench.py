@@ -128,15 +128,31 @@ def case_matvec(a):
     qt, bb = QTYPES[a.type]
     raw = G.make_kquant(qt, a.N, a.K, seed=3)
     x = np.random.default_rng(4).standard_normal(a.K).astype(np.float32)
-    old_tc = L.tcg_matvec_set_tc(a.tc)
-    with tcg.DeviceBuffer.from_array(raw) as w, tcg.DeviceBuffer.from_array(x) as xb, \
-            tcg.DeviceBuffer(a.N * 4) as y, tcg.DeviceBuffer(256 << 20) as flush:
-        ms, _ = timed(lambda: tcg.check(L.tcg_matvec_q(y.ptr, w.ptr, xb.ptr, a.N, a.K, qt)), a.warmup, a.reps, flush)
+    old_tc, old_mma = L.tcg_matvec_set_tc(a.tc), L.tcg_matvec_set_mma(a.mma)
+    old_segs = L.tcg_matvec_mma_segments(a.segs)
+    old_static = L.tcg_matvec_set_static_weights(a.static_weights)
+    # back to back: the matrix rotates over enough copies that each launch
+    # reads from HBM, not L2 (as in a decode pass over successive layers)
+    copies = max(1, min(10, -(-(300 << 20) // raw.nbytes)))
+    ws = [tcg.DeviceBuffer.from_array(raw) for _ in range(copies)]
+    with tcg.DeviceBuffer.from_array(x) as xb, tcg.DeviceBuffer(a.N * 4) as y, \
+            tcg.DeviceBuffer(256 << 20) as flush:
+        mv = [lambda w=w: tcg.check(L.tcg_matvec_q(y.ptr, w.ptr, xb.ptr, a.N, a.K, qt)) for w in ws]
+        ms, _ = timed(mv[0], a.warmup, a.reps, flush)
+        launches = max(10, copies)
+        b2b, _ = timed(lambda: [mv[i % copies]() for i in range(launches)], a.warmup, a.reps)
+        b2b /= launches
+    for w in ws:
+        w.close()
     kern = L.tcg_matvec_last_kernel()
     L.tcg_matvec_set_tc(old_tc)
+    L.tcg_matvec_set_mma(old_mma)
+    L.tcg_matvec_mma_segments(old_segs)
+    L.tcg_matvec_set_static_weights(old_static)
     nbytes = a.N * a.K // 256 * bb + 4 * (a.N + a.K)
     return {"case": "matvec", "type": a.type, "N": a.N, "K": a.K, "kernel": kern, "ms": round(ms, 5),
-            "bytes": nbytes, "GB/s": round(nbytes / ms / 1e6, 1)}
+            "bytes": nbytes, "GB/s": round(nbytes / ms / 1e6, 1), "b2b_ms": round(b2b, 5),
+            "b2b_GB/s": round(nbytes / b2b / 1e6, 1), "copies": copies}
 
 
 def case_dequant(a):
@@ -195,6 +211,10 @@ def main():
     mv.add_argument("--N", type=int, default=4096)
     mv.add_argument("--K", type=int, default=14336)
     mv.add_argument("--tc", type=int, default=0, help="1: Q4_K on the tensor cores (opt-in kernel)")
+    mv.add_argument("--mma", type=int, default=1, help="0: Q4_K on the CUDA-core kernels")
+    mv.add_argument("--segs", type=int, default=0, help="K segments per tile of the mma kernel (0: automatic)")
+    mv.add_argument("--static-weights", type=int, default=0,
+                    help="1: promise that no earlier kernel writes W (weights fetched before the previous ends)")
     dq = sub.add_parser("dequant")
     dq.add_argument("--type", choices=sorted(QTYPES), default="q4k")
     dq.add_argument("--rows", type=int, default=14336)

@@ -146,10 +146,12 @@ def test_matvec_vs_dequant_then_linear(gpu, qt, N, K, seed):
     x = np.random.default_rng(seed + 100).standard_normal(K).astype(np.float32)
     got = dev_matvec(raw, x, N, K, qt, repeat=3)
     kernel = tcg.lib().tcg_matvec_last_kernel()
-    # the benchmark shapes (and every Q4_K one with long rows) run the
-    # streaming kernel; every shape one of the two
-    stream = (qt == G.Q4_K and K in (14336, 4096)) or (N, K) == (128256, 4096)
-    assert kernel == 2 if stream else kernel in (2, 3), kernel
+    # Q4_K runs the integer mma.sync kernel; Q6_K the streaming kernel at the
+    # benchmark shape, else the streaming or the staged one
+    if qt == G.Q4_K:
+        assert kernel == 5, kernel
+    else:
+        assert kernel == 2 if (N, K) == (128256, 4096) else kernel in (2, 3), kernel
     want = oracle.matvec_q(raw, x, N, K, qt)
     err = np.abs(got.astype(np.float64) - want).max() / np.abs(want).max()
     assert err <= MATVEC_TOL, err
@@ -193,8 +195,12 @@ def test_matvec_q4k_tensor_cores(gpu, N, K):
         assert scale > 0, name
         err = np.abs(got.astype(np.float64) - want).max() / scale
         assert err <= MATVEC_TOL, (name, err)
-        cuda_cores = dev_matvec(raw, x, N, K, G.Q4_K)
-        assert L.tcg_matvec_last_kernel() in (2, 3)
+        old = L.tcg_matvec_set_mma(0)
+        try:
+            cuda_cores = dev_matvec(raw, x, N, K, G.Q4_K)
+            assert L.tcg_matvec_last_kernel() in (2, 3)
+        finally:
+            L.tcg_matvec_set_mma(old)
         assert np.abs(cuda_cores.astype(np.float64) - want).max() / scale <= MATVEC_TOL, name
 
 
@@ -207,11 +213,69 @@ def test_matvec_q4k_row_pairs_x_cases(gpu, case):
     N, K = 9473, 14336
     raw = G.make_kquant(G.Q4_K, N, K, seed=21)
     x = _x_cases(K, 22)[case]
-    got = dev_matvec(raw, x, N, K, G.Q4_K, repeat=2)
-    assert tcg.lib().tcg_matvec_last_kernel() == 2
+    L = tcg.lib()
+    old = L.tcg_matvec_set_mma(0)
+    try:
+        got = dev_matvec(raw, x, N, K, G.Q4_K, repeat=2)
+        assert L.tcg_matvec_last_kernel() == 2
+    finally:
+        L.tcg_matvec_set_mma(old)
     want = oracle.matvec_q(raw, x, N, K, G.Q4_K).astype(np.float64)
     err = np.abs(got.astype(np.float64) - want).max() / np.abs(want).max()
     assert err <= MATVEC_TOL, err
+
+
+@pytest.mark.parametrize("N,K", [
+    (4096, 14336),      # the decode matvec: 16-row tiles split in 8 K segments, summed by the last warp
+    (14336, 4096),      # many tiles, split in 16
+    (4095, 14336),      # a ragged last tile
+    (9473, 14336),      # long rows, many of them
+    (100, 2304), (129, 256), (1, 256), (17, 512), (70, 4096), (37888, 256), (300, 768),
+    (4096, 11008), (300, 11008),   # 43 superblocks a row: the last segment of a row is short
+])
+def test_matvec_q4k_mma(gpu, N, K):
+    """The default Q4_K matvec: integer mma.sync over the raw nibbles and
+    exact int8 pieces of x, against the oracle (dequantise, then the
+    reference's linear) and the CUDA-core kernel, on x with wide dynamic
+    range, zero sub-blocks and tiny values; repeated launches give the same
+    bits (the per-tile counters reset themselves)."""
+    L = tcg.lib()
+    raw = G.make_kquant(G.Q4_K, N, K, seed=N + 3 * K)
+    for name, x in _x_cases(K, N * 5 + K).items():
+        got = dev_matvec(raw, x, N, K, G.Q4_K, repeat=3)
+        assert L.tcg_matvec_last_kernel() == 5
+        want = oracle.matvec_q(raw, x, N, K, G.Q4_K).astype(np.float64)
+        scale = np.abs(want).max()
+        assert scale > 0, name
+        err = np.abs(got.astype(np.float64) - want).max() / scale
+        assert err <= MATVEC_TOL, (name, err)
+        old = L.tcg_matvec_set_mma(0)
+        try:
+            cuda_cores = dev_matvec(raw, x, N, K, G.Q4_K)
+        finally:
+            L.tcg_matvec_set_mma(old)
+        assert np.abs(cuda_cores.astype(np.float64) - got).max() / scale <= 2 * MATVEC_TOL, name
+
+
+@pytest.mark.parametrize("segs", [2, 4, 5, 7, 8, 9, 14])
+def test_matvec_q4k_mma_segments(gpu, segs):
+    """K splits of the 4096 x 14336 decode matvec: units of 16 rows x
+    ceil(56/segs) superblocks (5 and 9 segments leave a short last one) stream through a ring of shared-memory slots that is
+    refilled (more units per CTA than slots for the long units), and split
+    tiles are summed by the last segment to arrive; each against the oracle,
+    three calls giving the same bits."""
+    N, K = 4096, 14336
+    L = tcg.lib()
+    raw = G.make_kquant(G.Q4_K, N, K, seed=31)
+    x = _x_cases(K, 32)["wide"]
+    old = L.tcg_matvec_mma_segments(segs)
+    try:
+        got = dev_matvec(raw, x, N, K, G.Q4_K, repeat=3)
+        assert L.tcg_matvec_last_kernel() == 5
+    finally:
+        L.tcg_matvec_mma_segments(old)
+    want = oracle.matvec_q(raw, x, N, K, G.Q4_K).astype(np.float64)
+    assert np.abs(got.astype(np.float64) - want).max() / np.abs(want).max() <= MATVEC_TOL
 
 
 def test_matvec_rejections(gpu):
