@@ -349,7 +349,9 @@ def run_ours(args, dist):
 
     tcg.init(dist.local)
     L = tcg.lib()
+    t_load = time.perf_counter()
     model = tcg.VitModel(path)
+    load_ms = (time.perf_counter() - t_load) * 1e3
     if dist.world > 1:
         import ctypes
         uid = None
@@ -362,6 +364,9 @@ def run_ours(args, dist):
             model.upload_bcast(per, dist.rank, dist.world, uid)
     else:
         model.upload(per)
+    # the host-to-device part of the weight upload (rank 0's, where broadcast)
+    upload_ms = L.tcg_vit_last_upload_ms()
+    weight_bytes = os.path.getsize(path)
 
     pixels = G.make_pixels(args.batch, cfg["image"], 1)
     shard = np.ascontiguousarray(pixels[lo:hi])
@@ -505,6 +510,12 @@ def run_ours(args, dist):
             "clocks": clk,
             "model_flop_per_image": gf + af + pf,
             "device_error": derr, "outputs_finite": emb_ok,
+            "upload": {"tc_vit_load_ms": round(load_ms, 3), "h2d_ms": round(upload_ms, 2),
+                       "weight_bytes": weight_bytes, "GB/s": round(weight_bytes / upload_ms / 1e6, 2)
+                       if upload_ms > 0 else None,
+                       "how": "zero-copy GGUF mapping read by host threads into two page-locked chunks while "
+                              "the copy engine moves the other (first upload of the process, chunks "
+                              "allocated inside)"},
             "parity_max_rel": round(par_rel, 9) if par_checked else None,
             "parity": {"images_checked": int(par_checked), "max_rel": par_rel if par_checked else None,
                        "min_cosine": par_cos if par_checked else None, "bar": "max|err| <= 1e-4 max|ref|, "

@@ -164,6 +164,16 @@ int        tcg_vit_max_batch(const tcg_vit_t *v);
 size_t     tcg_vit_device_bytes(const tcg_vit_t *v);
 /* Record the layer loop as a CUDA graph per batch size (default on). */
 void       tcg_vit_use_graphs(tcg_vit_t *v, bool on);
+/* How later uploads move the weights from the GGUF mapping (pageable memory,
+ * src/gguf.h:3-10) to the device: 0 one copy per tensor from the mapping,
+ * 1 (default) through two page-locked chunks that host threads fill while
+ * the copy engine drains the other, 2 the mapping page-locked in place
+ * (cudaHostRegister, read-only; where the system refuses that, the staged
+ * copy of mode 1). Returns the previous mode. */
+int        tcg_vit_set_upload_mode(int mode);
+/* Wall time of this thread's latest weight upload (the host-to-device part
+ * of tcg_vit_upload, or of rank 0's tcg_vit_upload_bcast), milliseconds. */
+double     tcg_vit_last_upload_ms(void);
 
 /* HOST buffers: pixels [n, 3, image, image] (already normalised), out
  * [n, d_out]. Copies in, runs, copies out, and returns after the result is
@@ -194,6 +204,36 @@ bool tcg_vit_wait(tcg_vit_t *v, int ticket);
 int  tcg_vit_launches_per_forward(const tcg_vit_t *v);
 void tcg_vit_profile_begin(void);
 bool tcg_vit_profile_end(float ms[4], int count[4]);
+
+/* ------------------------------------------- image preprocessing (new)
+ * open_clip's eval transform, which the reference leaves to the caller
+ * (src/vit.h:75-78) and whose parameters its GGUF records
+ * (clip-vit.preprocess.*): resize the shorter side to `image` with Pillow's
+ * resampling (the 8-bit result bit-identical to Pillow's Image.resize),
+ * centre crop, x / 255, minus mean, divided by std. DEVICE buffers: rgb
+ * [n, height, width, 3] uint8 interleaved, pixels [n, 3, image, image] fp32,
+ * ready for tcg_vit_encode_device. interpolation 0 bicubic, 1 bilinear.
+ * Asynchronous; uses the library's device scratch. */
+bool tcg_preprocess_rgb8(float *pixels, const uint8_t *rgb, int n, int height, int width, int image,
+                         const float mean[3], const float std[3], int interpolation);
+/* The same with the model's image size, mean and std (tc_vit_load) and its
+ * clip-vit.preprocess.interpolation / resize_mode keys (bicubic when absent;
+ * any other filter or resize rule is refused). */
+bool tcg_vit_preprocess(const tc_vit_t *m, float *pixels, const uint8_t *rgb, int n, int height, int width);
+
+/* ------------------------------------------------ roofline (new)
+ * The B200 roofline of a GGUF model, in place of the fixed 68 GB/s ceiling
+ * of the reference's tc-inspect (tools/tc_inspect.c:201-223): weights read
+ * once per unit of work (a token; an image at batch 1 for clip-vit), so the
+ * memory ceiling is hbm_gbs / weight bytes; the compute ceiling is
+ * tensor_tflops / FLOPs per unit (clip-vit: from its metadata; otherwise 2
+ * per weight); ridge_batch is where they meet. Host only, no GPU. */
+typedef struct {
+    double weight_bytes, hbm_gbs, tensor_tflops;
+    double flops_per_unit, mem_units_per_s, compute_units_per_s, ridge_batch;
+    bool encoder;
+} tc_roofline_t;
+bool tc_roofline_b200(const gguf_t *g, double hbm_gbs, double tensor_tflops, tc_roofline_t *out);
 
 /* ------------------------------------------------ multi-GPU (NCCL)
  * One process per GPU. Rank 0 creates the id and hands it to the others by

@@ -18,9 +18,14 @@
 #include "gemm.cuh"
 #include "tcg_internal.h"
 
+#include <algorithm>
+#include <chrono>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <string.h>
+#include <string>
+#include <thread>
 #include <vector>
 
 struct tcg_vit {
@@ -436,9 +441,200 @@ static int launches_per_forward(const tcg_vit *v) { return 2 + 4 + 7 * v->L; }
 
 }  // namespace tcg
 
+// ------------------------------------------------------------ weight upload
+//
+// The weights are zero-copy views into the GGUF mapping (src/gguf.h:3-10):
+// pageable memory, which the copy engine cannot read directly. Three ways to
+// move them into the device slab (tcg_vit_set_upload_mode):
+//   0  one cudaMemcpyAsync per tensor from the mapping (the driver stages
+//      pageable memory through its own pinned buffer, one chunk at a time);
+//   1  staged (default): the mapping is read into two page-locked chunks in
+//      turn by a few host threads while the copy engine moves the other chunk
+//      to the device, so reading the mapping and the PCIe transfer overlap;
+//   2  registered: the mapped data section is page-locked in place
+//      (cudaHostRegister, read-only) and copied tensor by tensor.
+int g_upload_mode = 1;
+static thread_local double g_upload_ms = 0.0;
+static thread_local std::string g_upload_fallback;    // why mode 2 fell back to the staged copy
+
 using namespace tcg;
 
+namespace {
+
+constexpr size_t UP_CHUNK = 32u << 20;       // bytes per page-locked chunk
+constexpr int UP_THREADS = 8;                // host threads filling a chunk
+
+// The two page-locked chunks of a device, allocated by its first staged
+// upload and kept for the life of the process (page-locking 64 MB costs tens
+// of milliseconds, as much as the copy of a ViT-B/32); uploads to one device
+// take turns on them.
+struct UpStage {
+    std::mutex mu;
+    unsigned char *chunk[2] = { nullptr, nullptr };
+    cudaEvent_t done[2] = { nullptr, nullptr };
+};
+UpStage g_up_stage[64];
+
+// A piece of a tensor placed in a chunk: its device destination, its offset
+// in the chunk, its host source and length.
+struct UpPiece {
+    float *dst;
+    size_t at;
+    const unsigned char *src;
+    size_t bytes;
+};
+
+void fill_chunk(unsigned char *chunk, const std::vector<UpPiece> &pieces)
+{
+    // split the chunk's bytes evenly over the threads, piece boundaries aside
+    size_t total = 0;
+    for (const UpPiece &p : pieces) total += p.bytes;
+    const size_t share = (total + UP_THREADS - 1) / UP_THREADS;
+    auto work = [&](int t) {
+        const size_t lo = share * t, hi = std::min(total, lo + share);
+        size_t base = 0;
+        for (const UpPiece &p : pieces) {
+            const size_t a = std::max(lo, base), b = std::min(hi, base + p.bytes);
+            if (a < b) memcpy(chunk + p.at + (a - base), p.src + (a - base), b - a);
+            base += p.bytes;
+        }
+    };
+    std::vector<std::thread> ts;
+    for (int t = 1; t < UP_THREADS; t++) ts.emplace_back(work, t);
+    work(0);
+    for (std::thread &t : ts) t.join();
+}
+
+bool upload_staged(const std::vector<WEntry> &table, const std::vector<size_t> &off, float *slab, cudaStream_t s)
+{
+    UpStage &st = g_up_stage[ctx().device & 63];
+    std::lock_guard<std::mutex> lock(st.mu);
+    unsigned char **chunk = st.chunk;
+    cudaEvent_t *done = st.done;
+    bool ok = true;
+    for (int b = 0; b < 2 && ok; b++) {
+        if (!chunk[b] && cudaHostAlloc((void **)&chunk[b], UP_CHUNK, cudaHostAllocDefault) != cudaSuccess) {
+            chunk[b] = nullptr;
+            ok = false;
+        }
+        if (ok && !done[b] && cudaEventCreateWithFlags(&done[b], cudaEventDisableTiming) != cudaSuccess) {
+            done[b] = nullptr;
+            ok = false;
+        }
+    }
+    if (!ok) fail("weight upload: cannot allocate %zu MB of page-locked staging", 2 * UP_CHUNK >> 20);
+    size_t ti = 0, toff = 0;                 // next tensor, bytes of it already placed
+    for (int b = 0; ok && ti < table.size(); b ^= 1) {
+        std::vector<UpPiece> pieces;
+        size_t used = 0;
+        while (ti < table.size() && used < UP_CHUNK) {
+            const size_t bytes = table[ti].n * sizeof(float);
+            const size_t take = std::min(bytes - toff, UP_CHUNK - used);
+            pieces.push_back({ slab + off[ti] + toff / sizeof(float), used,
+                               reinterpret_cast<const unsigned char *>(table[ti].host) + toff, take });
+            used += (take + 15) & ~(size_t)15;
+            toff += take;
+            if (toff == bytes) { ti++; toff = 0; }
+        }
+        // the chunk's previous copies have left it before it is refilled
+        if (cudaEventSynchronize(done[b]) != cudaSuccess) { ok = false; break; }
+        fill_chunk(chunk[b], pieces);
+        for (const UpPiece &p : pieces)
+            if (cudaMemcpyAsync(p.dst, chunk[b] + p.at, p.bytes, cudaMemcpyHostToDevice, s) != cudaSuccess) ok = false;
+        if (ok && cudaEventRecord(done[b], s) != cudaSuccess) ok = false;
+    }
+    if (cudaStreamSynchronize(s) != cudaSuccess) ok = false;
+    if (!ok) {
+        cudaGetLastError();
+        if (!tcg_last_error()[0]) fail("weight upload: staged copy failed");
+    }
+    return ok;
+}
+
+bool upload_registered(const tc_vit_t *m, const std::vector<WEntry> &table, const std::vector<size_t> &off,
+                       float *slab, cudaStream_t s)
+{
+    // the page-aligned span of the mapping that holds the tensor data
+    const size_t page = 4096;
+    const uintptr_t a0 = (uintptr_t)m->gguf.data & ~(uintptr_t)(page - 1);
+    const uintptr_t a1 = ((uintptr_t)m->gguf.data + m->gguf.data_size + page - 1) & ~(uintptr_t)(page - 1);
+    const uintptr_t m0 = (uintptr_t)m->gguf.map, m1 = m0 + m->gguf.map_size;
+    if (!m->gguf.data || a0 < m0 || a1 > ((m1 + page - 1) & ~(uintptr_t)(page - 1)))
+        return fail("weight upload: tensor data outside the mapping");
+    const cudaError_t re = cudaHostRegister((void *)a0, a1 - a0, cudaHostRegisterReadOnly);
+    if (re != cudaSuccess) {
+        cudaGetLastError();
+        return fail("weight upload: cudaHostRegister of %zu MB failed: %s", (size_t)(a1 - a0) >> 20,
+                    cudaGetErrorString(re));
+    }
+    bool ok = true;
+    for (size_t i = 0; ok && i < table.size(); i++)
+        ok = cudaMemcpyAsync(slab + off[i], table[i].host, table[i].n * sizeof(float), cudaMemcpyHostToDevice, s) ==
+             cudaSuccess;
+    if (cudaStreamSynchronize(s) != cudaSuccess) ok = false;
+    cudaHostUnregister((void *)a0);
+    if (!ok) {
+        cudaGetLastError();
+        return fail("weight upload: registered copy failed");
+    }
+    return true;
+}
+
+// The host weights of table into the slab, by the current mode; returns
+// with the copies complete.
+bool upload_tensors(const tc_vit_t *m, const std::vector<WEntry> &table, const std::vector<size_t> &off, float *slab,
+                    cudaStream_t s)
+{
+    for (size_t i = 0; i < table.size(); i++)
+        if (!table[i].host) return fail("weight upload: weight %zu unresolved", i);
+    const auto t0 = std::chrono::steady_clock::now();
+    g_upload_fallback.clear();
+    bool ok;
+    if (g_upload_mode == 1) {
+        ok = upload_staged(table, off, slab, s);
+    } else if (g_upload_mode == 2) {
+        // where the system refuses to page-lock the file mapping (a memlock
+        // limit, or no read-only registration), the staged copy does the work
+        ok = upload_registered(m, table, off, slab, s);
+        if (!ok) {
+            g_upload_fallback = tcg_last_error();
+            ok = upload_staged(table, off, slab, s);
+        }
+    } else {
+        ok = true;
+        for (size_t i = 0; ok && i < table.size(); i++)
+            ok = cudaMemcpyAsync(slab + off[i], table[i].host, table[i].n * sizeof(float), cudaMemcpyHostToDevice,
+                                 s) == cudaSuccess;
+        if (cudaStreamSynchronize(s) != cudaSuccess) ok = false;
+        if (!ok) {
+            cudaGetLastError();
+            fail("weight upload: copy failed");
+        }
+    }
+    g_upload_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    return ok;
+}
+
+}  // namespace
+
 extern "C" {
+
+// Upload mode of later tcg_vit_upload / tcg_vit_upload_bcast calls (0 per
+// tensor from the mapping, 1 staged through page-locked chunks, 2 mapping
+// registered in place); returns the previous one.
+int tcg_vit_set_upload_mode(int mode)
+{
+    const int old = g_upload_mode;
+    if (mode >= 0 && mode <= 2) g_upload_mode = mode;
+    return old;
+}
+
+// Wall time of this thread's latest host-to-device weight copy, ms.
+double tcg_vit_last_upload_ms(void) { return g_upload_ms; }
+
+// Test hook: why this thread's latest upload in mode 2 fell back to the
+// staged copy ("" when it did not).
+const char *tcg_vit_upload_fallback(void) { return g_upload_fallback.c_str(); }
 
 tcg_vit_t *tcg_vit_upload(const tc_vit_t *m, int max_batch)
 {
@@ -448,15 +644,9 @@ tcg_vit_t *tcg_vit_upload(const tc_vit_t *m, int max_batch)
     tcg_vit *v = vit_alloc(m, max_batch, table, off);
     if (!v) return nullptr;
     cudaStream_t s = ctx().cur;
-    for (size_t i = 0; i < table.size(); i++) {
-        if (!table[i].host) { delete v; fail("tcg_vit_upload: weight %zu unresolved", i); return nullptr; }
-        if (cudaMemcpyAsync(v->wslab + off[i], table[i].host, table[i].n * sizeof(float),
-                            cudaMemcpyHostToDevice, s) != cudaSuccess) {
-            cudaGetLastError();
-            delete v;
-            fail("tcg_vit_upload: weight copy failed");
-            return nullptr;
-        }
+    if (!upload_tensors(m, table, off, v->wslab, s)) {
+        delete v;
+        return nullptr;
     }
     if (!split_weights(v, table, off) || cudaStreamSynchronize(s) != cudaSuccess) {
         cudaGetLastError();
@@ -610,12 +800,7 @@ tcg_vit_t *tcg_vit_upload_bcast(const tc_vit_t *m, int max_batch, int rank, int 
     if (!v) return nullptr;
     cudaStream_t s = ctx().cur;
     bool ok = true;
-    if (rank == 0) {
-        for (size_t i = 0; ok && i < table.size(); i++)
-            ok = table[i].host && cudaMemcpyAsync(v->wslab + off[i], table[i].host, table[i].n * sizeof(float),
-                                                  cudaMemcpyHostToDevice, s) == cudaSuccess;
-        if (!ok) { cudaGetLastError(); fail("tcg_vit_upload_bcast: weight copy failed"); }
-    }
+    if (rank == 0) ok = upload_tensors(m, table, off, v->wslab, s);
     // every rank enters the collective, so a failed upload on rank 0 still
     // lets the others finish (they receive whatever rank 0 holds)
     if (!broadcast_once(v->wslab, v->wslab_floats, rank, nranks, id)) ok = false;

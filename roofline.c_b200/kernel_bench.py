@@ -177,6 +177,7 @@ def case_vit(a):
     old_cfg, old_sk = L.tcg_gemm_force_cfg(a.cfg), L.tcg_gemm_set_streamk(a.streamk)
     old_pdl = L.tcg_set_pdl(a.pdl)
     old_tma = L.tcg_gemm_set_tma_store(a.tma_store)
+    old_chunk = L.tcg_gemm_set_chunk_k(a.chunk) if a.chunk else None
     m = tcg.VitModel(path)
     m.upload(a.batch)
     px = G.make_pixels(a.batch, cfg["image"], 1)
@@ -188,9 +189,42 @@ def case_vit(a):
     L.tcg_gemm_set_streamk(old_sk)
     L.tcg_set_pdl(old_pdl)
     L.tcg_gemm_set_tma_store(old_tma)
-    return {"case": "vit", "model": a.model, "layers": cfg["n_layer"], "batch": a.batch, "cfg": a.cfg,
+    if old_chunk is not None:
+        L.tcg_gemm_set_chunk_k(old_chunk)
+    return {"case": "vit", "chunk": a.chunk, "model": a.model, "layers": cfg["n_layer"], "batch": a.batch, "cfg": a.cfg,
             "streamk": a.streamk, "pdl": a.pdl, "tma_store": a.tma_store, "ms": round(ms, 4),
             "images/s": round(a.batch / ms * 1e3, 1)}
+
+
+def case_upload(a):
+    """Weight upload from the GGUF mapping in every mode (0 per tensor from
+    the mapping, 1 staged through page-locked chunks, 2 mapping registered):
+    tc_vit_load time, host-to-device time and GB/s of the weight bytes."""
+    import time
+    L = tcg.lib()
+    cache = os.environ.get("TCG_BENCH_CACHE", "/tmp/roofline_b200_bench")
+    path, cfg = G.cached_vit_gguf(cache, a.model, 0)
+    res = {"case": "upload", "model": a.model, "bytes": None, "modes": {}}
+    old = L.tcg_vit_set_upload_mode(1)
+    for rep in range(a.reps):
+        for mode in (0, 1, 2):
+            L.tcg_vit_set_upload_mode(mode)
+            t0 = time.perf_counter()
+            m = tcg.VitModel(path)
+            t1 = time.perf_counter()
+            m.upload(1)
+            t2 = time.perf_counter()
+            up = L.tcg_vit_last_upload_ms()
+            fb = (L.tcg_vit_upload_fallback() or b"").decode()
+            m.close()
+            wb = os.path.getsize(path)
+            res["bytes"] = wb
+            r = res["modes"].setdefault(str(mode), [])
+            r.append({"load_ms": round((t1 - t0) * 1e3, 2), "h2d_ms": round(up, 2),
+                      "upload_total_ms": round((t2 - t1) * 1e3, 2), "h2d_GB/s": round(wb / up / 1e6, 2),
+                      **({"fell_back": fb} if fb else {})})
+    L.tcg_vit_set_upload_mode(old)
+    return res
 
 
 def main():
@@ -228,14 +262,17 @@ def main():
     v.add_argument("--streamk", type=int, default=1, help="0: every GEMM tile computed whole")
     v.add_argument("--pdl", type=int, default=1, help="0: no programmatic dependent launch")
     v.add_argument("--tma-store", type=int, default=1, help="0: GEMM epilogues on plain stores")
-    for p in (g, gs, mv, dq, v):
+    v.add_argument("--chunk", type=int, default=0, help="K-elements per TMEM accumulator chunk (0: default)")
+    up = sub.add_parser("upload")
+    up.add_argument("--model", default="vit-b32", choices=sorted(G.VIT_CONFIGS))
+    for p in (g, gs, mv, dq, v, up):
         p.add_argument("--warmup", type=int, default=3)
         p.add_argument("--reps", type=int, default=5)
         p.add_argument("--device", type=int, default=0)
     a = ap.parse_args()
     tcg.init(a.device)
     res = {"gemm": case_gemm, "gemmsweep": case_gemmsweep, "matvec": case_matvec, "dequant": case_dequant,
-           "vit": case_vit}[a.case](a)
+           "vit": case_vit, "upload": case_upload}[a.case](a)
     res["device_error"] = tcg.lib().tcg_device_error()
     print(json.dumps(res), flush=True)
 

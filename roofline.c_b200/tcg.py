@@ -85,6 +85,12 @@ class Vit(C.Structure):
                 ("err", C.c_char * 256), ("dev", vp)]
 
 
+class Roofline(C.Structure):          # include/tcg.h tc_roofline_t
+    _fields_ = [(n, C.c_double) for n in ("weight_bytes", "hbm_gbs", "tensor_tflops", "flops_per_unit",
+                                          "mem_units_per_s", "compute_units_per_s", "ridge_batch")] + \
+               [("encoder", C.c_bool)]
+
+
 # (name, restype, argtypes) of every entry point the binding uses
 _SIGS = [
     # arena.h
@@ -159,12 +165,17 @@ _SIGS = [
     ("tcg_vit_upload", vp, [C.POINTER(Vit), i32]), ("tcg_vit_release", None, [vp]),
     ("tcg_vit_max_batch", i32, [vp]), ("tcg_vit_device_bytes", sz, [vp]),
     ("tcg_vit_use_graphs", None, [vp, boolean]),
+    ("tcg_vit_set_upload_mode", i32, [i32]), ("tcg_vit_last_upload_ms", C.c_double, []),
+    ("tcg_vit_upload_fallback", C.c_char_p, []),
     ("tcg_vit_encode_batch", boolean, [vp, vp, i32, vp, vp, vp]),
     ("tcg_vit_encode_device", boolean, [vp, vp, i32, vp]),
     ("tcg_vit_submit", boolean, [vp, vp, i32, vp, C.POINTER(C.c_int)]),
     ("tcg_vit_wait", boolean, [vp, i32]),
     ("tcg_vit_launches_per_forward", i32, [vp]), ("tcg_vit_profile_begin", None, []),
     ("tcg_vit_profile_end", boolean, [C.POINTER(C.c_float), C.POINTER(C.c_int)]),
+    ("tcg_preprocess_rgb8", boolean, [vp, vp, i32, i32, i32, i32, C.POINTER(C.c_float), C.POINTER(C.c_float), i32]),
+    ("tcg_vit_preprocess", boolean, [C.POINTER(Vit), vp, vp, i32, i32, i32]),
+    ("tc_roofline_b200", boolean, [C.POINTER(Gguf), C.c_double, C.c_double, C.POINTER(Roofline)]),
     ("tcg_nccl_unique_id", boolean, [C.c_char_p]),
     ("tcg_vit_upload_bcast", vp, [C.POINTER(Vit), i32, i32, i32, C.c_char_p]),
 ]

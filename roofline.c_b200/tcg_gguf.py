@@ -150,6 +150,8 @@ def vit_metadata(cfg: dict, activation: str = "gelu") -> dict:
         f"{a}.pooling": "cls",
         f"{a}.preprocess.mean": [0.48145466, 0.4578275, 0.40821073],
         f"{a}.preprocess.std": [0.26862954, 0.26130258, 0.27577711],
+        f"{a}.preprocess.interpolation": "bicubic",
+        f"{a}.preprocess.resize_mode": "shortest",
     }
 
 

@@ -18,6 +18,9 @@ repository, so the GPU tests never need either.
                      (oracle/_ref/libtcref.so, built from the reference
                      sources) on seeded synthetic models: embedding, CLS row
                      and per-tap float64 sums for two shapes.
+  preprocess_golden.npz  uint8 RGB images and their CLIP preprocessing by
+                     torchvision 0.26 + Pillow 12.2 (Resize of the shorter
+                     side, CenterCrop, ToTensor, Normalize), small sizes.
   vit_bench_golden.npz  the same tc_vit_encode at full depth on the
                      benchmark's own models and batches (ViT-B/32 batch 256,
                      ViT-L/14 batch 128): embeddings of the first and last
@@ -180,6 +183,38 @@ def vit_bench_fixture(threads: int = 0):
     np.savez_compressed(os.path.join(OUT, "vit_bench_golden.npz"), **out)
 
 
+# CLIP preprocessing: (height, width, image size, filter); the outputs of
+# open_clip's eval transform as torchvision + Pillow compute it.
+PRE_CASES = ((37, 53, 24, "bicubic"), (61, 40, 24, "bicubic"), (23, 90, 16, "bicubic"),
+             (64, 48, 32, "bilinear"), (24, 24, 24, "bicubic"), (50, 77, 28, "bicubic"))
+CLIP_MEAN = (0.48145466, 0.4578275, 0.40821073)
+CLIP_STD = (0.26862954, 0.26130258, 0.27577711)
+
+
+def torchvision_preprocess(rgb, image, interp):
+    """open_clip's eval transform: Resize(image) (shorter side, Pillow),
+    CenterCrop(image), ToTensor(), Normalize(mean, std)."""
+    from PIL import Image
+    from torchvision import transforms as T
+    mode = T.InterpolationMode.BICUBIC if interp == "bicubic" else T.InterpolationMode.BILINEAR
+    tf = T.Compose([T.Resize(image, interpolation=mode), T.CenterCrop(image), T.ToTensor(),
+                    T.Normalize(CLIP_MEAN, CLIP_STD)])
+    return np.stack([tf(Image.fromarray(a)).numpy() for a in rgb]).astype(np.float32)
+
+
+def preprocess_fixture():
+    out = {}
+    rng = np.random.default_rng(17)
+    for i, (h, w, image, interp) in enumerate(PRE_CASES):
+        rgb = rng.integers(0, 256, (2, h, w, 3), dtype=np.uint8)
+        out[f"case{i}.rgb"] = rgb
+        out[f"case{i}.meta"] = np.array([h, w, image, 0 if interp == "bicubic" else 1], np.int32)
+        out[f"case{i}.pixels"] = torchvision_preprocess(rgb, image, interp)
+    out["mean"] = np.array(CLIP_MEAN, np.float32)
+    out["std"] = np.array(CLIP_STD, np.float32)
+    np.savez_compressed(os.path.join(OUT, "preprocess_golden.npz"), **out)
+
+
 if __name__ == "__main__":
     if not REF or not os.path.isdir(os.path.join(REF, "src")):
         sys.exit("set TC_REFERENCE to the roofline.c source tree (the directory holding src/ and tests/)")
@@ -188,4 +223,5 @@ if __name__ == "__main__":
     kquant_fixture()
     vit_fixture()
     vit_bench_fixture()
+    preprocess_fixture()
     print("golden fixtures written to", OUT)
