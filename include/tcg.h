@@ -63,6 +63,11 @@ bool  tcg_d2h(void *dst, const void *src, size_t bytes);   /* async          */
 bool  tcg_d2d(void *dst, const void *src, size_t bytes);   /* async          */
 bool  tcg_memset(void *dst, int value, size_t bytes);      /* async          */
 
+/* Read every byte of a device buffer once (128-bit loads, nothing written):
+ * the floor under a bandwidth-bound kernel on the same bytes, timed the same
+ * way (the benchmark's ceiling for the matvec). Asynchronous. */
+bool  tcg_read_ceiling(const void *p, size_t bytes);
+
 /* CUDA events on the library stream, slots 0..63. elapsed() waits for b. */
 bool  tcg_event_record(int slot);
 float tcg_event_elapsed_ms(int slot_a, int slot_b);
@@ -140,6 +145,14 @@ bool tcg_linear_split(float *y, const float *x_hi, const float *x_lo, const floa
  * streams or host threads) race on it and must be serialised by the caller. */
 #define TCG_NOALLOC_SCRATCH_BYTES (16u << 20)
 bool tcg_linear_noalloc(float *y, const float *x, const float *W, const float *bias, int M, int N, int K);
+/* tcg_linear with W [N, K] kept packed in Q4_K blocks on the device (row n
+ * at W + n * K/256 * 144 bytes; K a multiple of 256, x and W 16-byte
+ * aligned): the tensor-core GEMM dequantises each tile of W into shared
+ * memory with the dequant seam's exact rounding and splits it into its tf32
+ * pair there, so W is read as 0.56 bytes per weight instead of 8. The result
+ * equals dequantising W (tcg_dequant) and calling tcg_linear_split on the
+ * split pair with the same tile shape. Other types are refused. */
+bool tcg_linear_q(float *y, const float *x, const void *W, const float *bias, int M, int N, int K, ggml_type_t t);
 bool tcg_layernorm(float *out, const float *x, const float *gamma, const float *beta,
                    int rows, int cols, float eps);
 bool tcg_gelu(float *out, const float *x, size_t n);
@@ -174,6 +187,16 @@ int        tcg_vit_set_upload_mode(int mode);
 /* Wall time of this thread's latest weight upload (the host-to-device part
  * of tcg_vit_upload, or of rank 0's tcg_vit_upload_bcast), milliseconds. */
 double     tcg_vit_last_upload_ms(void);
+
+/* 1 (default): GEMM weights stored as Q4_K in the GGUF (qkv, out, up, down,
+ * patch embedding) stay packed on the device at later uploads, and their
+ * GEMMs dequantise them tile by tile in shared memory (tcg_linear_q's
+ * kernel); 0 uploads the fp32 copy tc_vit_load made. Returns the previous
+ * setting. */
+int        tcg_vit_set_packed_weights(int on);
+/* Bytes of GEMM weights one forward reads: the tf32 pairs of the split
+ * weights plus the Q4_K blocks of the packed ones. */
+size_t     tcg_vit_gemm_weight_bytes(const tcg_vit_t *v);
 
 /* HOST buffers: pixels [n, 3, image, image] (already normalised), out
  * [n, d_out]. Copies in, runs, copies out, and returns after the result is

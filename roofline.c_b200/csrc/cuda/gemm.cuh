@@ -29,6 +29,11 @@ struct GemmEpi {
     // set by gemm_plan: vec, no row remapping and no rowadd; the outputs are
     // written by bulk tensor stores (GemmPlan's output maps)
     bool tma = false;
+    // B held packed in Q4_K blocks (the packed-weight configurations): row n
+    // of B at bq + n * bq_row bytes, 144 bytes per 256 weights. The kernel
+    // dequantises each K-step into its tf32 hi/lo shared-memory tiles.
+    const uint8_t *bq = nullptr;
+    size_t bq_row = 0;
 };
 
 // Device memory for the stream-K split of a GEMM's last, partial wave of
@@ -73,5 +78,7 @@ int gemm_vit_cfg(int M, int N, int K);
 // Tile widths available (index = cfg); for tests and tuning.
 int gemm_num_cfgs();
 int gemm_cfg_bn(int cfg);
+// The configuration whose B operand is Q4_K blocks (GemmEpi::bq).
+int gemm_q4k_cfg();
 
 }  // namespace tcg

@@ -39,6 +39,8 @@
 #include "numerics.cuh"
 #include "tc05.cuh"
 
+#include <cuda_fp16.h>
+
 namespace tcg {
 namespace {
 
@@ -181,7 +183,7 @@ __device__ __forceinline__ void mma_commit_pair_local(uint32_t bar)
 //             the hi*hi half. The drain adds the halves.
 enum { ACC_SEP = 0, ACC_FOLD = 1, ACC_WIDE = 2 };
 
-template <int BN, int BK, int STAGES, int EPI_W = 8, int ACC = ACC_SEP, int CG = 1>
+template <int BN, int BK, int STAGES, int EPI_W = 8, int ACC = ACC_SEP, int CG = 1, int QB = 0>
 struct Shape {
     static constexpr uint32_t A_BYTES = BM * BK * 4;
     static constexpr uint32_t B_BYTES = (BN / CG) * BK * 4;     // this CTA's share of the B tile
@@ -192,7 +194,7 @@ struct Shape {
     static constexpr uint32_t TMEM_COLS = NACC * CW <= 256 ? 256 : 512;
     static constexpr int GROUPS = EPI_W / 4;
     static constexpr int HALF = BN / GROUPS;           // columns per epilogue thread
-    static constexpr int THREADS = 64 + 32 * EPI_W;
+    static constexpr int THREADS = 64 + 32 * EPI_W + (QB ? 64 : 0);    // + two converter warps
     static constexpr int LDW = EPI_W > 8 ? 16 : 64;    // widest TMEM load of the drain
     static constexpr uint32_t EPI_STAGE_BYTES = 32 * 16 * 4;   // per epilogue warp: 32 rows x 16 columns
     static constexpr int NBAR = 2 * STAGES + 2 * NBUF + 4 + 1;
@@ -203,7 +205,14 @@ struct Shape {
     static_assert(NACC * CW <= 512, "the accumulators must fit the 512 TMEM columns");
     static_assert(ACC != ACC_WIDE || (2 * BN <= 256 && CG == 1), "a wide MMA is at most 256 columns, one CTA");
     static_assert(SMEM <= 232448, "shared memory per block");
+    static_assert(QB == 0 || (BN == 128 && BK == 32 && CG == 1), "packed B: 128 rows x one 32-weight sub-block");
 };
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, const float (&v)[4])
+{
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3])
+                 : "memory");
+}
 
 // acc[0..HALF) += (first + second) where first and second are the HALF fp32
 // columns at TMEM addresses ta and tb (this warp's lanes), 16 at a time.
@@ -525,15 +534,15 @@ __device__ bool flag_wait(const int *f, volatile int *abort, int *err, int code)
 
 // chunk_kb: K-blocks whose hi*hi products share one TMEM chunk buffer before
 // it is drained into the fp32 registers.
-template <int BN, int BK, int STAGES, int EPI_W, int ACC, int CG>
-__global__ void __launch_bounds__(Shape<BN, BK, STAGES, EPI_W, ACC, CG>::THREADS, 1)
+template <int BN, int BK, int STAGES, int EPI_W, int ACC, int CG, int QB = 0>
+__global__ void __launch_bounds__(Shape<BN, BK, STAGES, EPI_W, ACC, CG, QB>::THREADS, 1)
 gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
                    const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
                    const __grid_constant__ CUtensorMap o_plain, const __grid_constant__ CUtensorMap o_hi,
                    const __grid_constant__ CUtensorMap o_lo,
                    int M, int N, int K, int chunk_kb, GemmEpi epi, int *err, float *ws, int *flags, int sk)
 {
-    using S = Shape<BN, BK, STAGES, EPI_W, ACC, CG>;
+    using S = Shape<BN, BK, STAGES, EPI_W, ACC, CG, QB>;
     constexpr bool SEP = ACC == ACC_SEP, WIDE = ACC == ACC_WIDE;
     constexpr uint32_t CW = S::CW;
     constexpr int SWB = BK * 4;
@@ -559,7 +568,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
-            bar_init(full0 + 8 * s, 1);
+            bar_init(full0 + 8 * s, QB ? 3 : 1);     // packed B: the TMA bytes and two converter warps
             bar_init(empty0 + 8 * s, 1);
         }
         for (int b = 0; b < NBUF; b++) {
@@ -625,6 +634,12 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                         tma_load_pair(base + S::A_BYTES, &a_lo, fb, kb * BK, m0);
                         tma_load_pair(base + 2 * S::A_BYTES, &b_hi, fb, kb * BK, nb);
                         tma_load_pair(base + 2 * S::A_BYTES + S::B_BYTES, &b_lo, fb, kb * BK, nb);
+                    } else if constexpr (QB != 0) {
+                        // the converter warps write this stage's B tiles
+                        const uint32_t fb = full0 + 8 * stage;
+                        bar_expect_tx(fb, 2 * S::A_BYTES);
+                        tma_load(base, &a_hi, fb, kb * BK, m0);
+                        tma_load(base + S::A_BYTES, &a_lo, fb, kb * BK, m0);
                     } else {
                         const uint32_t fb = full0 + 8 * stage;
                         bar_expect_tx(fb, S::STAGE_BYTES);
@@ -717,7 +732,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
             bar_wait(drain, 0, abort, err, 5, false);
         }
         __syncwarp();
-    } else {
+    } else if (QB == 0 || warp < 2 + EPI_W) {
         const int q = warp & 3;                    // TMEM lanes 32q .. 32q+31 = tile rows
         const int h = (warp - 2) >> 2;             // column group of the tile
         const uint32_t lane_cols = ((uint32_t)(q * 32) << 16) + (uint32_t)(h * S::HALF);
@@ -807,6 +822,90 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                                         n0 + h * S::HALF, M, N);
         }
         if (lane == 0) bulk_wait_read<0>();          // shared memory stays until the stores have read it
+    } else {
+        if constexpr (QB != 0) {
+            // Converter warps: thread cr owns rows cr and cr + 64 of every
+            // stage's B tile. Per K-step (32-weight sub-block j of superblock
+            // kb / 8) it dequantises them with the dequant seam's rounding
+            // sequence, (d*sc)*q - (dmin*m), splits each weight into its tf32
+            // pair and writes both tiles in the 128-byte swizzle a TMA load
+            // would have produced; then makes the writes visible to the
+            // tensor cores and arrives on the stage's barrier. The 48 bytes a
+            // row needs per K-step (the superblock header and the 32 quant
+            // bytes of the sub-block's pair) are loaded one K-step ahead.
+            const int cr = (warp - 2 - EPI_W) * 32 + lane;
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            Sched sc(num_tiles, n_chunks, skm, P, p);
+            Seg sg;
+            while (ok && sc.next(sg)) {
+                const uint8_t *rowp[2];
+                bool live[2];
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const int n = (sg.tile % n_tiles) * BN + cr + 64 * h;
+                    live[h] = n < N;
+                    rowp[h] = epi.bq + (size_t)(live[h] ? n : 0) * epi.bq_row;
+                }
+                const int kb0 = sg.c0 * chunk_kb, kb_end = min(sg.c1 * chunk_kb, num_kb);
+                // [row][0]: header, [1], [2]: the 32 quant bytes
+                uint4 cur[2][3], nxt[2][3];
+                auto fetch = [&](uint4 (&dst)[2][3], int kb) {
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        const uint4 *sb = reinterpret_cast<const uint4 *>(rowp[h] + (size_t)(kb >> 3) * 144);
+                        const int cc = (kb & 7) >> 1;
+                        dst[h][0] = __ldg(sb);
+                        dst[h][1] = __ldg(sb + 1 + 2 * cc);
+                        dst[h][2] = __ldg(sb + 2 + 2 * cc);
+                    }
+                };
+                fetch(nxt, kb0);
+                for (int kb = kb0; kb < kb_end; kb++) {
+#pragma unroll
+                    for (int h = 0; h < 2; h++)
+#pragma unroll
+                        for (int i = 0; i < 3; i++) cur[h][i] = nxt[h][i];
+                    if (kb + 1 < kb_end) fetch(nxt, kb + 1);
+                    if (!bar_wait(empty0 + 8 * stage, phase ^ 1, abort, err, 9)) { ok = false; break; }
+                    const int j = kb & 7, jj = 8 * (j & 3), sh = (j & 1) * 4;
+                    const uint32_t base = su32(tiles + (size_t)stage * S::STAGE_BYTES) + 2 * S::A_BYTES;
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        const uint4 hd = cur[h][0];
+                        const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFFu)));
+                        const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
+                        const uint32_t b0 = (hd.y >> jj) & 0xFFu, b4 = (hd.z >> jj) & 0xFFu, b8 = (hd.w >> jj) & 0xFFu;
+                        const uint32_t scq = j < 4 ? (b0 & 63u) : ((b8 & 15u) | ((b0 >> 6) << 4));
+                        const uint32_t mnq = j < 4 ? (b4 & 63u) : ((b8 >> 4) | ((b4 >> 6) << 4));
+                        const float a = __fmul_rn(d, (float)scq), c = __fmul_rn(dmin, (float)mnq);
+                        const uint32_t qw[8] = { cur[h][1].x, cur[h][1].y, cur[h][1].z, cur[h][1].w,
+                                                 cur[h][2].x, cur[h][2].y, cur[h][2].z, cur[h][2].w };
+                        const int r = cr + 64 * h;
+                        const uint32_t rb = base + (uint32_t)r * 128u;
+#pragma unroll
+                        for (int c16 = 0; c16 < 8; c16++) {
+                            float hv[4], lv[4];
+#pragma unroll
+                            for (int e = 0; e < 4; e++) {
+                                const uint32_t qv = (qw[c16] >> (8 * e + sh)) & 15u;
+                                const float w = live[h] ? __fsub_rn(__fmul_rn(a, __uint_as_float(0x4B000000u | qv) - 8388608.0f), c)
+                                                        : 0.0f;
+                                split_tf32(w, hv[e], lv[e]);
+                            }
+                            const uint32_t off = (uint32_t)((c16 ^ (r & 7)) << 4);
+                            st_shared_v4(rb + off, hv);
+                            st_shared_v4(rb + S::B_BYTES + off, lv);
+                        }
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) bar_arrive(full0 + 8 * stage);
+                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                }
+            }
+        }
     }
 
     fence_before();
@@ -886,11 +985,16 @@ struct Cfg {
     int threads;
     bool sep;           // separate small-term accumulators (no stream-K)
     int epi_warps;
+    int qb;             // B packed in these K-quant blocks (0: tf32 pairs by TMA)
 };
 
 #define TCG_CFG(BN, BK, ST, EW, ACC, CG)                                                                   \
     { BN, BK, ST, Shape<BN, BK, ST, EW, ACC, CG>::SMEM, (const void *)gemm_tf32x3_kernel<BN, BK, ST, EW, ACC, CG>, \
-      CG, Shape<BN, BK, ST, EW, ACC, CG>::THREADS, ACC == ACC_SEP, EW }
+      CG, Shape<BN, BK, ST, EW, ACC, CG>::THREADS, ACC == ACC_SEP, EW, 0 }
+#define TCG_CFG_Q(BN, BK, ST, EW, ACC, QB)                                                                 \
+    { BN, BK, ST, Shape<BN, BK, ST, EW, ACC, 1, QB>::SMEM,                                                  \
+      (const void *)gemm_tf32x3_kernel<BN, BK, ST, EW, ACC, 1, QB>, 1, Shape<BN, BK, ST, EW, ACC, 1, QB>::THREADS, \
+      ACC == ACC_SEP, EW, QB }
 const Cfg CFGS[] = {
     TCG_CFG(128, 32, 3, 8, ACC_SEP, 1), TCG_CFG(64, 32, 4, 8, ACC_SEP, 1), TCG_CFG(128, 16, 6, 8, ACC_SEP, 1),
     TCG_CFG(64, 16, 8, 8, ACC_SEP, 1), TCG_CFG(96, 32, 3, 8, ACC_SEP, 1), TCG_CFG(96, 16, 7, 8, ACC_SEP, 1),
@@ -899,8 +1003,11 @@ const Cfg CFGS[] = {
     TCG_CFG(128, 32, 3, 8, ACC_FOLD, 1), TCG_CFG(128, 32, 3, 16, ACC_SEP, 1), TCG_CFG(128, 32, 3, 16, ACC_FOLD, 1),
     TCG_CFG(128, 32, 4, 16, ACC_SEP, 2),                                // CTA pair, separate small terms
     TCG_CFG(128, 32, 3, 16, ACC_WIDE, 1), TCG_CFG(128, 32, 3, 8, ACC_WIDE, 1),
+    TCG_CFG_Q(128, 32, 3, 8, ACC_WIDE, GGML_TYPE_Q4_K),                  // B in Q4_K blocks (15)
 };
 #undef TCG_CFG
+#undef TCG_CFG_Q
+constexpr int CFG_Q4K = 15;
 constexpr int NCFG = sizeof(CFGS) / sizeof(CFGS[0]);
 
 int g_force_cfg = -1;     // tuning hook: a configuration every automatic choice takes
@@ -932,7 +1039,8 @@ int gemm_throughput_cfg()
 // K-elements accumulated in TMEM between two drains into fp32 registers.
 int g_chunk_k = 256;
 
-int gemm_num_cfgs() { return NCFG; }
+// configurations with tf32-pair operands (the packed-B ones need GemmEpi::bq)
+int gemm_num_cfgs() { return CFG_Q4K; }
 
 // The configuration of one ViT GEMM: the ACC_WIDE 128 x 128 shape of
 // gemm_throughput_cfg(), except where its tiles make exactly one whole wave
@@ -956,6 +1064,8 @@ int gemm_vit_cfg(int M, int N, int K)
 }
 
 int gemm_cfg_bn(int cfg) { return cfg >= 0 && cfg < NCFG ? CFGS[cfg].bn : 0; }
+
+int gemm_q4k_cfg() { return CFG_Q4K; }
 
 size_t gemm_work_ws_floats(int ctas) { return (size_t)ctas * BM * 256; }
 size_t gemm_work_flag_count(int ctas) { return (size_t)ctas * 16; }
@@ -1000,9 +1110,18 @@ bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b
     if (cfg >= NCFG) return fail("gemm_plan: no configuration %d", cfg);
     const Cfg &c = CFGS[cfg];
     const int b_rows = c.bn / c.cg;                     // B box: this CTA's share of the tile columns
-    if (!encode_kmajor(&p.a_hi, a_hi, M, K, BM, c.bk) || !encode_kmajor(&p.a_lo, a_lo, M, K, BM, c.bk) ||
-        !encode_kmajor(&p.b_hi, b_hi, N, K, b_rows, c.bk) || !encode_kmajor(&p.b_lo, b_lo, N, K, b_rows, c.bk))
+    if (c.qb) {
+        // B comes packed: no B tensor maps (the A ones fill the unused parameters)
+        if (!epi.bq || ((uintptr_t)epi.bq & 15) || K % 256 || epi.bq_row != (size_t)(K / 256) * 144)
+            return fail("gemm_plan: packed Q4_K B needs 16-byte-aligned rows of K/256 superblocks");
+        if (!encode_kmajor(&p.a_hi, a_hi, M, K, BM, c.bk) || !encode_kmajor(&p.a_lo, a_lo, M, K, BM, c.bk))
+            return false;
+        p.b_hi = p.a_hi;
+        p.b_lo = p.a_lo;
+    } else if (!encode_kmajor(&p.a_hi, a_hi, M, K, BM, c.bk) || !encode_kmajor(&p.a_lo, a_lo, M, K, BM, c.bk) ||
+               !encode_kmajor(&p.b_hi, b_hi, N, K, b_rows, c.bk) || !encode_kmajor(&p.b_lo, b_lo, N, K, b_rows, c.bk)) {
         return false;
+    }
     p.M = M;
     p.N = N;
     p.K = K;
@@ -1197,6 +1316,36 @@ int tcg_gemm_set_tma_store(int on)
     const int old = g_tma_store;
     g_tma_store = on ? 1 : 0;
     return old;
+}
+
+// y[M,N] = x[M,K] W^T + bias with W [N,K] held packed in Q4_K blocks on the
+// device: the tensor-core GEMM dequantises W tile by tile in shared memory
+// (the fused form of tc_dequant then tc_ref_linear, src/dequant.c:40-63,
+// src/ops.c:28-35); only x is split, into the op scratch.
+bool tcg_linear_q(float *y, const float *x, const void *Wq, const float *bias, int M, int N, int K, ggml_type_t t)
+{
+    if (!need_ctx()) return false;
+    if (M < 0 || N < 0 || K < 0) return fail("tcg_linear_q: negative size");
+    if (M == 0 || N == 0) return true;
+    if (t != GGML_TYPE_Q4_K) return fail("tcg_linear_q: type %s has no packed GEMM (Q4_K only)", ggml_type_name(t));
+    if (K == 0 || K % 256) return fail("tcg_linear_q: K=%d is not a positive multiple of 256", K);
+    if (((uintptr_t)x & 15) || ((uintptr_t)Wq & 15))
+        return fail("tcg_linear_q: x and the Q4_K matrix must be 16-byte aligned");
+    cudaStream_t s = ctx().cur;
+    const size_t xa = ((size_t)M * K + 3) & ~(size_t)3;
+    float *buf = (float *)scratch(2 * xa * sizeof(float));
+    if (!buf) return false;
+    if (!launch_split(x, buf, buf + xa, (size_t)M * K, s)) return false;
+    GemmEpi e;
+    e.bias = bias;
+    e.out.plain = y;
+    e.out.ld = N;
+    e.bq = (const uint8_t *)Wq;
+    e.bq_row = (size_t)(K / 256) * 144;
+    GemmPlan p;
+    const GemmWork *w = ctx_gemm_work();
+    if (!w || !gemm_plan(p, buf, buf + xa, nullptr, nullptr, M, N, K, e, CFG_Q4K, w)) return false;
+    return gemm_run(p, s, ctx().d_err);
 }
 
 // Test hook: the grid size, stream-K flag, configuration and bulk-store

@@ -83,7 +83,8 @@ bool settle(NcclApi *api, ncclComm_t comm, double deadline, const char *what)
 
 }  // namespace
 
-bool broadcast_once(void *buf, size_t count_floats, int rank, int nranks, const unsigned char id[128])
+bool broadcast_once(void *buf, size_t count_floats, int rank, int nranks, const unsigned char id[128], void *buf2,
+                    size_t count2)
 {
     NcclApi *api = nccl();
     if (!api) return fail("NCCL (libnccl.so.2) is not available");
@@ -101,6 +102,11 @@ bool broadcast_once(void *buf, size_t count_floats, int rank, int nranks, const 
     bool ok = settle(api, comm, deadline, "ncclCommInitRank");
     if (ok) {
         r = api->broadcast(buf, buf, count_floats, ncclFloat32, 0, comm, ctx().cur);
+        ok = (r == ncclSuccess || r == ncclInProgress) ? settle(api, comm, deadline, "ncclBroadcast")
+                                                       : fail("ncclBroadcast: %s", api->error_string(r));
+    }
+    if (ok && buf2 && count2) {   // a second buffer over the same communicator, in stream order
+        r = api->broadcast(buf2, buf2, count2, ncclFloat32, 0, comm, ctx().cur);
         ok = (r == ncclSuccess || r == ncclInProgress) ? settle(api, comm, deadline, "ncclBroadcast")
                                                        : fail("ncclBroadcast: %s", api->error_string(r));
     }

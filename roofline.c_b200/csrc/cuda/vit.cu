@@ -39,16 +39,22 @@ struct tcg_vit {
     // fp32 weights, one allocation (the unit of the NCCL broadcast)
     float *wslab = nullptr;
     size_t wslab_floats = 0;
-    // tf32 hi/lo of every GEMM weight
+    // tf32 hi/lo of every GEMM weight that is not kept packed
     float *sslab = nullptr;
     size_t sslab_floats = 0;
+    // Q4_K blocks of the GEMM weights kept packed (their GEMMs dequantise
+    // them tile by tile in shared memory)
+    uint8_t *qslab = nullptr;
+    size_t qslab_bytes = 0;
 
     struct Layer {
         const float *ln1_g, *ln1_b, *qkv_b, *out_b, *ln2_g, *ln2_b, *up_b, *down_b;
         const float *qkv_h, *qkv_l, *out_h, *out_l, *up_h, *up_l, *down_h, *down_l;
+        const uint8_t *qkv_q = nullptr, *out_q = nullptr, *up_q = nullptr, *down_q = nullptr;
     };
     std::vector<Layer> layers;
     const float *patch_h = nullptr, *patch_l = nullptr, *cls = nullptr, *pos = nullptr;
+    const uint8_t *patch_q = nullptr;
     const float *ln_pre_g = nullptr, *ln_pre_b = nullptr, *ln_post_g = nullptr, *ln_post_b = nullptr;
     const float *proj = nullptr;
     const float *projT_h = nullptr, *projT_l = nullptr;   // v.proj transposed to [d_out, D], split
@@ -81,6 +87,7 @@ struct tcg_vit {
         tcg_arena_destroy(&act);
         if (wslab) cudaFree(wslab);
         if (sslab) cudaFree(sslab);
+        if (qslab) cudaFree(qslab);
         for (int i = 0; i < 2; i++) {
             if (px_slot[i] && px_slot[i] != px) cudaFree(px_slot[i]);
             if (copied[i]) cudaEventDestroy(copied[i]);
@@ -132,10 +139,25 @@ static std::vector<WEntry> weight_table(tcg_vit *v, const tc_vit_t *m)
     return t;
 }
 
+// 1 (default): GEMM weights stored as Q4_K in the GGUF stay packed on the
+// device (tcg_vit_set_packed_weights).
+int g_vit_packed = 1;
+
+// The GGUF tensor of a GEMM weight when it is kept packed: Q4_K rows of whole
+// superblocks, read in place from the mapping.
+static const gguf_tensor_t *packed_tensor(const tc_vit_t *m, const char *name)
+{
+    if (!g_vit_packed) return nullptr;
+    const gguf_tensor_t *t = gguf_tensor(&m->gguf, name);
+    if (!t || t->type != GGML_TYPE_Q4_K || !t->data || t->n_dims != 2 || t->dims[0] % 256) return nullptr;
+    return t;
+}
+
 // Allocate the slabs and activation arena, point every field; weights are
-// not copied here.
+// not copied here. qtable / qoff describe the packed GEMM weights (their
+// bytes as 4-byte words) and their places in the packed slab.
 static tcg_vit *vit_alloc(const tc_vit_t *m, int max_batch, std::vector<WEntry> &table,
-                          std::vector<size_t> &offsets)
+                          std::vector<size_t> &offsets, std::vector<WEntry> &qtable, std::vector<size_t> &qoff)
 {
     if (max_batch <= 0) { fail("tcg_vit_upload: max_batch must be positive"); return nullptr; }
     if (m->image % m->patch || m->d_model % m->n_head) { fail("tcg_vit_upload: inconsistent model dims"); return nullptr; }
@@ -149,6 +171,45 @@ static tcg_vit *vit_alloc(const tc_vit_t *m, int max_batch, std::vector<WEntry> 
     v->layers.resize(v->L);
 
     table = weight_table(v.get(), m);
+    // GEMM weights kept packed: no fp32 copy on the device, their blocks in the
+    // packed slab instead
+    struct Packed {
+        size_t entry;
+        const gguf_tensor_t *t;
+        const uint8_t **dst;
+    };
+    std::vector<Packed> packed;
+    auto consider = [&](size_t entry, const char *name, const uint8_t **dst) {
+        if (const gguf_tensor_t *t = packed_tensor(m, name)) packed.push_back({ entry, t, dst });
+    };
+    consider(0, "v.patch_embd.weight", &v->patch_q);
+    for (int i = 0; i < v->L; i++) {
+        const size_t b = 8 + 12 * (size_t)i;   // first entry of block i in weight_table
+        char name[96];
+        tcg_vit::Layer &y = v->layers[i];
+        snprintf(name, sizeof name, "v.blk.%d.attn_qkv.weight", i); consider(b + 2, name, &y.qkv_q);
+        snprintf(name, sizeof name, "v.blk.%d.attn_out.weight", i); consider(b + 4, name, &y.out_q);
+        snprintf(name, sizeof name, "v.blk.%d.ffn_up.weight", i); consider(b + 8, name, &y.up_q);
+        snprintf(name, sizeof name, "v.blk.%d.ffn_down.weight", i); consider(b + 10, name, &y.down_q);
+    }
+    qtable.clear();
+    qoff.clear();
+    size_t qfloats = 0;
+    for (const Packed &pk : packed) {
+        table[pk.entry].n = 0;
+        qtable.push_back({ (size_t)pk.t->nbytes / 4, (const float *)pk.t->data, nullptr });
+        qoff.push_back(qfloats);
+        qfloats += align_floats((size_t)pk.t->nbytes / 4);
+    }
+    if (qfloats) {
+        v->qslab_bytes = qfloats * 4;
+        if (cudaMalloc(&v->qslab, v->qslab_bytes) != cudaSuccess) {
+            cudaGetLastError();
+            fail("tcg_vit_upload: cannot allocate %zu MB of packed weights", v->qslab_bytes >> 20);
+            return nullptr;
+        }
+        for (size_t i = 0; i < packed.size(); i++) *packed[i].dst = v->qslab + 4 * qoff[i];
+    }
     offsets.resize(table.size());
     size_t total = 0;
     for (size_t i = 0; i < table.size(); i++) {
@@ -165,24 +226,35 @@ static tcg_vit *vit_alloc(const tc_vit_t *m, int max_batch, std::vector<WEntry> 
         if (table[i].dev) *table[i].dev = v->wslab + offsets[i];
 
     const size_t D = v->D, F = v->F, K0 = 3 * (size_t)v->P * v->P;
-    const size_t per_layer = 2 * align_floats(3 * D * D) + 2 * align_floats(D * D) + 2 * align_floats(F * D) +
-                             2 * align_floats(D * F);
-    v->sslab_floats = 2 * align_floats(D * K0) + per_layer * v->L + 2 * align_floats(D * (size_t)v->d_out);
+    // tf32 pairs of the GEMM weights that are not packed: sized, then placed
+    float *s = nullptr;
+    size_t need = 0;
+    auto take = [&](size_t n, bool keep) -> float * {
+        if (!keep) return nullptr;
+        float *p = s ? s + need : nullptr;
+        need += align_floats(n);
+        return p;
+    };
+    auto place = [&]() {
+        need = 0;
+        v->patch_h = take(D * K0, !v->patch_q); v->patch_l = take(D * K0, !v->patch_q);
+        for (auto &y : v->layers) {
+            y.qkv_h = take(3 * D * D, !y.qkv_q); y.qkv_l = take(3 * D * D, !y.qkv_q);
+            y.out_h = take(D * D, !y.out_q); y.out_l = take(D * D, !y.out_q);
+            y.up_h = take(F * D, !y.up_q); y.up_l = take(F * D, !y.up_q);
+            y.down_h = take(D * F, !y.down_q); y.down_l = take(D * F, !y.down_q);
+        }
+        v->projT_h = take(D * (size_t)v->d_out, true); v->projT_l = take(D * (size_t)v->d_out, true);
+    };
+    place();
+    v->sslab_floats = need;
     if (cudaMalloc(&v->sslab, v->sslab_floats * sizeof(float)) != cudaSuccess) {
         cudaGetLastError();
         fail("tcg_vit_upload: cannot allocate %zu MB of split weights", v->sslab_floats * 4 >> 20);
         return nullptr;
     }
-    float *s = v->sslab;
-    auto take = [&](size_t n) { float *p = s; s += align_floats(n); return p; };
-    v->patch_h = take(D * K0); v->patch_l = take(D * K0);
-    for (auto &y : v->layers) {
-        y.qkv_h = take(3 * D * D); y.qkv_l = take(3 * D * D);
-        y.out_h = take(D * D); y.out_l = take(D * D);
-        y.up_h = take(F * D); y.up_l = take(F * D);
-        y.down_h = take(D * F); y.down_l = take(D * F);
-    }
-    v->projT_h = take(D * (size_t)v->d_out); v->projT_l = take(D * (size_t)v->d_out);
+    s = v->sslab;
+    place();
 
     const size_t n = (size_t)max_batch, T = v->T, G2 = (size_t)v->G * v->G;
     const size_t f_floats = std::max(n * T * F, n * G2 * K0);
@@ -222,14 +294,16 @@ static bool split_weights(tcg_vit *v, const std::vector<WEntry> &table, const st
 {
     cudaStream_t s = ctx().cur;
     const size_t D = v->D, F = v->F, K0 = 3 * (size_t)v->P * v->P;
-    if (!launch_split(v->wslab + off[0], (float *)v->patch_h, (float *)v->patch_l, D * K0, s)) return false;
+    // packed weights have no fp32 copy to split
+    auto split = [&](size_t entry, const float *hi, const float *lo, size_t n) {
+        return !hi || launch_split(v->wslab + off[entry], (float *)hi, (float *)lo, n, s);
+    };
+    if (!split(0, v->patch_h, v->patch_l, D * K0)) return false;
     for (int i = 0; i < v->L; i++) {
         const size_t b = 8 + 12 * (size_t)i;   // first entry of block i in weight_table
         tcg_vit::Layer &y = v->layers[i];
-        if (!launch_split(v->wslab + off[b + 2], (float *)y.qkv_h, (float *)y.qkv_l, 3 * D * D, s) ||
-            !launch_split(v->wslab + off[b + 4], (float *)y.out_h, (float *)y.out_l, D * D, s) ||
-            !launch_split(v->wslab + off[b + 8], (float *)y.up_h, (float *)y.up_l, F * D, s) ||
-            !launch_split(v->wslab + off[b + 10], (float *)y.down_h, (float *)y.down_l, D * F, s))
+        if (!split(b + 2, y.qkv_h, y.qkv_l, 3 * D * D) || !split(b + 4, y.out_h, y.out_l, D * D) ||
+            !split(b + 8, y.up_h, y.up_l, F * D) || !split(b + 10, y.down_h, y.down_l, D * F))
             return false;
     }
     {   // v.proj is [D, d_out] (used untransposed, src/vit.c:384-386): store it as the [d_out, D] operand
@@ -257,8 +331,17 @@ static tcg_vit::Plans *plans_for(tcg_vit *v, int n)
     e.out.ld = D;
     const GemmWork *w = &v->work;
     const int tp = gemm_throughput_cfg();
-    if (!gemm_plan(p->patch, v->p_hi, v->p_lo, v->patch_h, v->patch_l, n * G2, D, K0, e, gemm_vit_cfg(n * G2, D, K0), w))
-        return nullptr;
+    // a GEMM whose weight is packed runs the packed-B configuration
+    auto plan = [&](GemmPlan &gp, const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo,
+                    const uint8_t *bq, int Mg, int Ng, int Kg, GemmEpi ep) {
+        if (bq) {
+            ep.bq = bq;
+            ep.bq_row = (size_t)(Kg / 256) * 144;
+            return gemm_plan(gp, a_hi, a_lo, nullptr, nullptr, Mg, Ng, Kg, ep, gemm_q4k_cfg(), w);
+        }
+        return gemm_plan(gp, a_hi, a_lo, b_hi, b_lo, Mg, Ng, Kg, ep, gemm_vit_cfg(Mg, Ng, Kg), w);
+    };
+    if (!plan(p->patch, v->p_hi, v->p_lo, v->patch_h, v->patch_l, v->patch_q, n * G2, D, K0, e)) return nullptr;
 
     GemmEpi pe;                                   // embedding = pooled x proj, into v->out
     pe.out.plain = v->out;
@@ -289,10 +372,10 @@ static tcg_vit::Plans *plans_for(tcg_vit *v, int n)
         d.residual = v->x;
         d.out.plain = v->x;
         d.out.ld = D;
-        if (!gemm_plan(p->qkv[i], v->h_hi, v->h_lo, y.qkv_h, y.qkv_l, M, 3 * D, D, q, gemm_vit_cfg(M, 3 * D, D), w) ||
-            !gemm_plan(p->out[i], v->h_hi, v->h_lo, y.out_h, y.out_l, M, D, D, o, gemm_vit_cfg(M, D, D), w) ||   // a aliases h
-            !gemm_plan(p->up[i], v->h_hi, v->h_lo, y.up_h, y.up_l, M, F, D, u, gemm_vit_cfg(M, F, D), w) ||
-            !gemm_plan(p->down[i], v->f_hi, v->f_lo, y.down_h, y.down_l, M, D, F, d, gemm_vit_cfg(M, D, F), w))
+        if (!plan(p->qkv[i], v->h_hi, v->h_lo, y.qkv_h, y.qkv_l, y.qkv_q, M, 3 * D, D, q) ||
+            !plan(p->out[i], v->h_hi, v->h_lo, y.out_h, y.out_l, y.out_q, M, D, D, o) ||   // a aliases h
+            !plan(p->up[i], v->h_hi, v->h_lo, y.up_h, y.up_l, y.up_q, M, F, D, u) ||
+            !plan(p->down[i], v->f_hi, v->f_lo, y.down_h, y.down_l, y.down_q, M, D, F, d))
             return nullptr;
     }
     tcg_vit::Plans *raw = p.get();
@@ -639,12 +722,13 @@ const char *tcg_vit_upload_fallback(void) { return g_upload_fallback.c_str(); }
 tcg_vit_t *tcg_vit_upload(const tc_vit_t *m, int max_batch)
 {
     if (!need_ctx()) return nullptr;
-    std::vector<WEntry> table;
-    std::vector<size_t> off;
-    tcg_vit *v = vit_alloc(m, max_batch, table, off);
+    std::vector<WEntry> table, qtable;
+    std::vector<size_t> off, qoff;
+    tcg_vit *v = vit_alloc(m, max_batch, table, off, qtable, qoff);
     if (!v) return nullptr;
     cudaStream_t s = ctx().cur;
-    if (!upload_tensors(m, table, off, v->wslab, s)) {
+    if (!upload_tensors(m, table, off, v->wslab, s) ||
+        (!qtable.empty() && !upload_tensors(m, qtable, qoff, (float *)v->qslab, s))) {
         delete v;
         return nullptr;
     }
@@ -668,7 +752,26 @@ int tcg_vit_max_batch(const tcg_vit_t *v) { return v ? v->max_batch : 0; }
 
 size_t tcg_vit_device_bytes(const tcg_vit_t *v)
 {
-    return v ? (v->wslab_floats + v->sslab_floats) * sizeof(float) + v->act.cap : 0;
+    return v ? (v->wslab_floats + v->sslab_floats) * sizeof(float) + v->qslab_bytes + v->act.cap : 0;
+}
+
+// Bytes of GEMM weights one forward reads: the tf32 pairs of the split ones
+// and the Q4_K blocks of the packed ones.
+size_t tcg_vit_gemm_weight_bytes(const tcg_vit_t *v)
+{
+    if (!v) return 0;
+    const size_t pair = (v->sslab_floats - 2 * (size_t)v->D * v->d_out) * sizeof(float);   // all but the projection
+    return pair + v->qslab_bytes;
+}
+
+// 1 (default): GEMM weights stored as Q4_K stay packed on the device at
+// later uploads; 0 dequantises them at load like every other type. Returns
+// the previous setting.
+int tcg_vit_set_packed_weights(int on)
+{
+    const int old = g_vit_packed;
+    g_vit_packed = on ? 1 : 0;
+    return old;
 }
 
 void tcg_vit_use_graphs(tcg_vit_t *v, bool on)
@@ -794,16 +897,19 @@ bool tcg_vit_encode_batch(tcg_vit_t *v, const float *pixels, int n_images, float
 tcg_vit_t *tcg_vit_upload_bcast(const tc_vit_t *m, int max_batch, int rank, int nranks, const unsigned char id[128])
 {
     if (!need_ctx()) return nullptr;
-    std::vector<WEntry> table;
-    std::vector<size_t> off;
-    tcg_vit *v = vit_alloc(m, max_batch, table, off);
+    std::vector<WEntry> table, qtable;
+    std::vector<size_t> off, qoff;
+    tcg_vit *v = vit_alloc(m, max_batch, table, off, qtable, qoff);
     if (!v) return nullptr;
     cudaStream_t s = ctx().cur;
     bool ok = true;
-    if (rank == 0) ok = upload_tensors(m, table, off, v->wslab, s);
+    if (rank == 0)
+        ok = upload_tensors(m, table, off, v->wslab, s) &&
+             (qtable.empty() || upload_tensors(m, qtable, qoff, (float *)v->qslab, s));
     // every rank enters the collective, so a failed upload on rank 0 still
     // lets the others finish (they receive whatever rank 0 holds)
-    if (!broadcast_once(v->wslab, v->wslab_floats, rank, nranks, id)) ok = false;
+    // the packed slab too (every rank found the same packed tensors in its copy of the model)
+    if (!broadcast_once(v->wslab, v->wslab_floats, rank, nranks, id, v->qslab, v->qslab_bytes / 4)) ok = false;
     if (ok) ok = split_weights(v, table, off) && cudaStreamSynchronize(s) == cudaSuccess;
     if (!ok) {
         cudaGetLastError();

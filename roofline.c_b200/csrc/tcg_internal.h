@@ -24,7 +24,10 @@ size_t tcg_vit_tap_staging_floats(const tcg_vit_t *v, int n_images);
 }
 
 namespace tcg {
-bool broadcast_once(void *buf, size_t count_floats, int rank, int nranks, const unsigned char id[128]);
+// One NCCL communicator from `id`, rank 0's buf (and buf2, when given)
+// broadcast to every rank over it, then the communicator is released.
+bool broadcast_once(void *buf, size_t count_floats, int rank, int nranks, const unsigned char id[128],
+                    void *buf2 = nullptr, size_t count2 = 0);
 }
 #endif
 

@@ -133,6 +133,7 @@ _SIGS = [
     ("tcg_host_alloc", vp, [sz]), ("tcg_host_free", boolean, [vp]),
     ("tcg_h2d", boolean, [vp, vp, sz]), ("tcg_d2h", boolean, [vp, vp, sz]),
     ("tcg_d2d", boolean, [vp, vp, sz]), ("tcg_memset", boolean, [vp, i32, sz]),
+    ("tcg_read_ceiling", boolean, [vp, sz]),
     ("tcg_event_record", boolean, [i32]), ("tcg_event_elapsed_ms", f32, [i32, i32]),
     ("tcg_arena_create", Arena, [sz, C.c_char_p]), ("tcg_arena_destroy", None, [C.POINTER(Arena)]),
     ("tcg_arena_ok", boolean, [C.POINTER(Arena)]), ("tcg_arena_alloc", vp, [C.POINTER(Arena), sz, sz]),
@@ -155,6 +156,7 @@ _SIGS = [
     ("tcg_test_gemm_withhold_flags", boolean, [i32, C.c_double]), ("tcg_gemm_throughput_cfg", i32, []),
     ("tcg_op_scratch_bytes", sz, []),
     ("tcg_linear_noalloc", boolean, [vp, vp, vp, vp, i32, i32, i32]),
+    ("tcg_linear_q", boolean, [vp, vp, vp, vp, i32, i32, i32, C.c_int]),
     ("tcg_linear_split", boolean, [vp, vp, vp, vp, vp, vp, i32, i32, i32]),
     ("tcg_linear_split_cfg", boolean, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32]),
     ("tcg_layernorm", boolean, [vp, vp, vp, vp, i32, i32, f32]),
@@ -165,7 +167,8 @@ _SIGS = [
     ("tcg_vit_upload", vp, [C.POINTER(Vit), i32]), ("tcg_vit_release", None, [vp]),
     ("tcg_vit_max_batch", i32, [vp]), ("tcg_vit_device_bytes", sz, [vp]),
     ("tcg_vit_use_graphs", None, [vp, boolean]),
-    ("tcg_vit_set_upload_mode", i32, [i32]), ("tcg_vit_last_upload_ms", C.c_double, []),
+    ("tcg_vit_set_upload_mode", i32, [i32]), ("tcg_vit_set_packed_weights", i32, [i32]),
+    ("tcg_vit_gemm_weight_bytes", sz, [vp]), ("tcg_vit_last_upload_ms", C.c_double, []),
     ("tcg_vit_upload_fallback", C.c_char_p, []),
     ("tcg_vit_encode_batch", boolean, [vp, vp, i32, vp, vp, vp]),
     ("tcg_vit_encode_device", boolean, [vp, vp, i32, vp]),

@@ -211,3 +211,44 @@ def make_kquant(qtype: int, rows: int, cols: int, seed: int) -> np.ndarray:
     nb = rows * cols // QK_K
     blk = make_q4k_blocks(nb, seed) if qtype == Q4_K else make_q6k_blocks(nb, seed)
     return blk.reshape(-1)
+
+
+def make_kquant_like(qt: int, rows: int, cols: int, seed: int, d_std: float) -> np.ndarray:
+    """Random K-quant blocks of a [rows, cols] matrix whose weights have a
+    trained model's scale: the fp16 super-scales d (and dmin) ~ |N(0, d_std)|,
+    many of them fp16 subnormals. Flat uint8."""
+    nb = rows * cols // 256
+    blk = (make_q4k_blocks if qt == Q4_K else make_q6k_blocks)(nb, seed)
+    rng = np.random.default_rng(seed + 1)
+
+    def half():
+        return np.abs(rng.normal(0.0, d_std, nb)).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    if qt == Q4_K:
+        blk[:, 0:2] = half()
+        blk[:, 2:4] = half()
+    else:
+        blk[:, 208:210] = half()
+    return blk.reshape(-1)
+
+
+def write_kquant_vit_gguf(path: str, cfg: dict, seed: int = 0, qtype: int = Q4_K, d_std: float = 4e-5) -> dict:
+    """A ViT GGUF whose block linear weights (qkv, out, up, down) are random
+    K-quant blocks at a trained model's scale; every other tensor N(0, 0.02)
+    fp32 like make_vit_weights (the 4-D patch embedding too: its innermost
+    dimension of `patch` elements is no whole number of 256-weight blocks, so
+    a ggml file keeps it unquantised). Returns the fp32 tensors and the
+    K-quant ones raw as (blocks, type, shape); dequantising them for a
+    reference model is the caller's business (this module computes nothing)."""
+    w = make_vit_weights(cfg, seed)
+    tensors, raw = [], {}
+    for k, (name, arr) in enumerate(w.items()):
+        if name.endswith(("attn_qkv.weight", "attn_out.weight", "ffn_up.weight", "ffn_down.weight")):
+            rows = arr.shape[0]
+            cols = arr.size // rows
+            blocks = make_kquant_like(qtype, rows, cols, 1000 + k, d_std)
+            tensors.append((name, blocks, qtype, arr.shape))
+            raw[name] = (blocks, qtype, arr.shape)
+        else:
+            tensors.append((name, arr, F32, arr.shape))
+    write_gguf(path, vit_metadata(cfg), tensors)
+    return {"fp32": w, "kquant": raw}

@@ -263,3 +263,48 @@ def test_streamk_split(dev, M, N, K):
         err = np.abs(r.astype(np.float64) - want).max() / np.abs(want).max()
         assert err <= GEMM_TOL, (sk, err)
     assert L.tcg_device_error() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 768, 768), (1600, 768, 3072), (129, 200, 512), (1, 64, 256),
+                                   (12800, 2304, 768), (777, 3072, 768)])
+def test_linear_q4k_packed(dev, M, N, K):
+    """tcg_linear_q: the GEMM reads W as Q4_K blocks and dequantises each
+    tile in shared memory. Against the oracle (dequantise, then the
+    reference's linear) within the GEMM bound, and bit-identical to the
+    dequantise -> split -> tensor-core GEMM path with the same tile shape."""
+    import tcg_gguf as G
+    L = tcg.lib()
+    rng = np.random.default_rng(M + N + K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    raw = G.make_kquant_like(G.Q4_K, N, K, M + K, 4e-4)
+    W = oracle.dequant(raw, N * K, G.Q4_K).reshape(N, K)
+    b = rng.standard_normal(N).astype(np.float32)
+    xp, bp = dev.put(x), dev.put(b)
+    wq = tcg.DeviceBuffer.from_array(raw)
+    dev.bufs.append(wq)
+    y = dev.empty(M * N)
+    for _ in range(2):
+        tcg.check(L.tcg_linear_q(y.ptr, xp, wq.ptr, bp, M, N, K, G.Q4_K), "tcg_linear_q")
+    got = y.download((M, N))
+    want = oracle.linear(x, W, b, M, N, K)
+    err = np.abs(got.astype(np.float64) - want).max() / np.abs(want).max()
+    assert err <= GEMM_TOL, err
+    # the same GEMM on the split fp32 weights, tile shape 14 (the packed one's twin)
+    wp = dev.put(W)
+    xh, xl, wh, wl = dev.empty(M * K), dev.empty(M * K), dev.empty(N * K), dev.empty(N * K)
+    tcg.check(L.tcg_split_tf32(xh.ptr, xl.ptr, xp, M * K))
+    tcg.check(L.tcg_split_tf32(wh.ptr, wl.ptr, wp, N * K))
+    y2 = dev.empty(M * N)
+    tcg.check(L.tcg_linear_split_cfg(y2.ptr, xh.ptr, xl.ptr, wh.ptr, wl.ptr, bp, M, N, K, 14), "cfg 14")
+    assert np.array_equal(got, y2.download((M, N)))
+    assert L.tcg_device_error() == 0
+
+
+def test_linear_q_refusals(dev):
+    import tcg_gguf as G
+    L = tcg.lib()
+    d = dev.empty(64)
+    assert not L.tcg_linear_q(d.ptr, d.ptr, d.ptr, None, 4, 4, 300, G.Q4_K)
+    assert b"multiple of 256" in L.tcg_last_error()
+    assert not L.tcg_linear_q(d.ptr, d.ptr, d.ptr, None, 4, 4, 256, G.Q6_K)
+    assert b"Q4_K only" in L.tcg_last_error()

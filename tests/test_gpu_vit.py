@@ -335,6 +335,50 @@ def test_kquant_weights_model(gpu, tmp_path):
         m.close()
 
 
+@pytest.mark.parametrize("n_img", [3, 64])
+def test_packed_q4k_weights_model(gpu, tmp_path, n_img):
+    """Every block linear weight of a ViT-B/32 (two layers) in Q4_K: the
+    device keeps them packed (144 bytes per 256 weights) and each GEMM
+    dequantises its tiles in shared memory. Against the oracle's fp32 model
+    of the dequantised weights, per tap; and against the same model uploaded
+    with the weights dequantised at load."""
+    L = tcg.lib()
+    cfg = G.vit_config("vit-b32", n_layer=2)
+    path = str(tmp_path / "q4k.gguf")
+    made = G.write_kquant_vit_gguf(path, cfg, seed=9)
+    w = dict(made["fp32"])
+    for name, (blocks, qt, shape) in made["kquant"].items():
+        w[name] = oracle.dequant(blocks, int(np.prod(shape)), qt).reshape(shape)
+    px = G.make_pixels(n_img, cfg["image"], 6)
+    outs, nbytes = {}, {}
+    for packed in (1, 0):
+        old = L.tcg_vit_set_packed_weights(packed)
+        m = tcg.VitModel(path)
+        try:
+            m.upload(n_img)
+            outs[packed] = m.encode(px, taps=True)
+            nbytes[packed] = L.tcg_vit_gemm_weight_bytes(m.dev)
+        finally:
+            m.close()
+            L.tcg_vit_set_packed_weights(old)
+    D, F, L_, K0 = cfg["d_model"], cfg["d_ffn"], cfg["n_layer"], 3 * cfg["patch"] ** 2
+    linear = L_ * (3 * D * D + D * D + 2 * F * D)
+    # packed blocks (each tensor's slot padded to 256 bytes) plus the patch embedding's tf32 pair
+    assert abs(nbytes[1] - (linear // 256 * 144 + 8 * D * K0)) <= 256 * 4 * L_
+    assert nbytes[0] == 8 * (linear + D * K0)
+    out, taps = outs[1]
+    port = oracle.PortVit(cfg, w)
+    for i in sorted({0, n_img - 1}):
+        ref = port.forward(px[i])
+        assert rel_inf(out[i], ref["embedding"]) <= TOL, i
+        assert cosine(out[i], ref["embedding"]) >= 0.9999
+        for k in TAPS:
+            assert rel_inf(taps[k][i], ref[k]) <= TOL, (i, k)
+    for i in range(n_img):
+        assert rel_inf(out[i], outs[0][0][i]) <= 1e-5, i
+    assert L.tcg_device_error() == 0
+
+
 def test_device_entry_and_limits(gpu, cache_dir):
     L = tcg.lib()
     path, cfg = model(cache_dir, "vit-b32", n_layer=1)
