@@ -353,8 +353,9 @@ def vit_kquant_aux(tcg, args, fp32_weight_bytes):
     return {"images/s": round(args.batch / (ms * 1e-3), 2), "ms_per_step": round(ms, 4),
             "gemm_weight_bytes_per_step": int(wb), "fp32_model_gemm_weight_bytes_per_step": int(fp32_weight_bytes),
             "outputs_finite": bool(np.isfinite(emb).all()),
-            "weights": "block linears Q4_K (random blocks at a trained model's scale), packed in HBM and "
-                       "dequantised per tile in the GEMM's shared memory; everything else fp32"}
+            "weights": "block linears Q4_K (random blocks at a trained model's scale), packed in HBM; at this "
+                       "batch each is dequantised into an L2-resident tf32 pair just before its GEMM (a "
+                       "GEMM of one 128-row tile dequantises inside the GEMM instead); everything else fp32"}
 
 
 # ------------------------------------------------------------ our arm

@@ -194,6 +194,12 @@ double     tcg_vit_last_upload_ms(void);
  * kernel); 0 uploads the fp32 copy tc_vit_load made. Returns the previous
  * setting. */
 int        tcg_vit_set_packed_weights(int on);
+/* From this many token rows (batch x tokens, default 129) a forward
+ * dequantises each packed weight into a tf32 pair (L2-resident) just before
+ * its GEMM instead of tile by tile inside it, where every 128-row tile would
+ * redo the work. Applies to batch sizes planned afterwards; returns the
+ * previous value. */
+long       tcg_vit_set_jit_rows(long rows);
 /* Bytes of GEMM weights one forward reads: the tf32 pairs of the split
  * weights plus the Q4_K blocks of the packed ones. */
 size_t     tcg_vit_gemm_weight_bytes(const tcg_vit_t *v);

@@ -62,6 +62,11 @@ struct GemmPlan {
     GemmEpi epi;
     GemmWork work;       // stream-K memory (null: every tile whole)
     int sk = 0;          // 1: the last partial wave of tiles is split by K chunks
+    // set by callers that keep B packed but run this plan on tf32 pairs: the
+    // Q4_K blocks to dequantise into (jit_hi, jit_lo) just before the GEMM
+    const uint8_t *jit_q = nullptr;
+    float *jit_hi = nullptr, *jit_lo = nullptr;
+    size_t jit_n = 0;
 };
 
 // work: memory for stream-K; without it every tile is computed whole.

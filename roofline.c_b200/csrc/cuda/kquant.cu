@@ -11,6 +11,7 @@
 // contraction: Q4_K w = (d*sc)*q - (dmin*m), Q6_K w = (d*sc)*q.
 #include "tcg_common.cuh"
 #include "tcg_internal.h"
+#include "numerics.cuh"
 
 #include <cuda_fp16.h>
 #include <string.h>
@@ -145,9 +146,11 @@ __device__ __forceinline__ void decode8<GGML_TYPE_Q6_K>(const uint8_t *blk, int 
 // word that holds a byte of the tensor lies in the same page as that byte, so
 // the span's edges cannot fault); each lane writes its 8 weights of every
 // superblock as two float4.
-template <int TYPE>
+// With SPLIT, each weight goes out as its tf32 pair instead (dst the hi
+// half, lo the lo half): the operand a 3xTF32 GEMM reads.
+template <int TYPE, bool SPLIT = false>
 __global__ void __launch_bounds__(WARPS * 32)
-dequant_kq_kernel(const uint8_t *__restrict__ src, float *__restrict__ dst, size_t nblocks)
+dequant_kq_kernel(const uint8_t *__restrict__ src, float *__restrict__ dst, size_t nblocks, float *__restrict__ lo = nullptr)
 {
     constexpr int BB = KQ<TYPE>::BYTES;
     constexpr int C = GROUP;
@@ -188,8 +191,19 @@ dequant_kq_kernel(const uint8_t *__restrict__ src, float *__restrict__ dst, size
             float w[8];
             decode8<TYPE>(buf[wid] + off + b * BB, lane, w);
             float4 *o = reinterpret_cast<float4 *>(dst + (b0 + b) * QK + 8 * lane);
-            o[0] = make_float4(w[0], w[1], w[2], w[3]);
-            o[1] = make_float4(w[4], w[5], w[6], w[7]);
+            if constexpr (SPLIT) {
+                float h[8], l[8];
+#pragma unroll
+                for (int i = 0; i < 8; i++) split_tf32(w[i], h[i], l[i]);
+                float4 *ol = reinterpret_cast<float4 *>(lo + (b0 + b) * QK + 8 * lane);
+                o[0] = make_float4(h[0], h[1], h[2], h[3]);
+                o[1] = make_float4(h[4], h[5], h[6], h[7]);
+                ol[0] = make_float4(l[0], l[1], l[2], l[3]);
+                ol[1] = make_float4(l[4], l[5], l[6], l[7]);
+            } else {
+                o[0] = make_float4(w[0], w[1], w[2], w[3]);
+                o[1] = make_float4(w[4], w[5], w[6], w[7]);
+            }
         }
     }
 }
@@ -683,6 +697,25 @@ static bool matvec_dispatch(float *y, const void *W, const float *x, int N, int 
     if ((long)N * 2 >= want) return launch_matvec<TYPE, 2>(y, W, x, N, K);
     if ((long)N * 4 >= want) return launch_matvec<TYPE, 4>(y, W, x, N, K);
     return launch_matvec<TYPE, 8>(y, W, x, N, K);
+}
+
+// Q4_K / Q6_K blocks to their tf32 pairs (hi, lo), 16-byte aligned outputs,
+// n a multiple of 256: dequantisation bit-identical to tcg_dequant, then the
+// split of tcg_split_tf32.
+bool launch_dequant_split(const void *src, float *hi, float *lo, size_t n, ggml_type_t t, cudaStream_t s)
+{
+    if (n % QK || ((uintptr_t)hi & 15) || ((uintptr_t)lo & 15))
+        return fail("dequant split: %zu weights / unaligned outputs", n);
+    const size_t nb = n / QK;
+    const unsigned grid = grid_for((nb + GROUP - 1) / GROUP);
+    if (t == GGML_TYPE_Q4_K)
+        dequant_kq_kernel<GGML_TYPE_Q4_K, true><<<grid, WARPS * 32, 0, s>>>((const uint8_t *)src, hi, nb, lo);
+    else if (t == GGML_TYPE_Q6_K)
+        dequant_kq_kernel<GGML_TYPE_Q6_K, true><<<grid, WARPS * 32, 0, s>>>((const uint8_t *)src, hi, nb, lo);
+    else
+        return fail("dequant split: type %s", ggml_type_name(t));
+    TCG_LAUNCHED();
+    return true;
 }
 
 }  // namespace tcg

@@ -14,6 +14,9 @@ struct OutSpec {
     int ld = 0;
 };
 
+// K-quant blocks straight to their tf32 pairs (kquant.cu).
+bool launch_dequant_split(const void *src, float *hi, float *lo, size_t n, ggml_type_t t, cudaStream_t s);
+
 // LayerNorm of `rows` rows of `cols` (src/ops.c:37-80 numerics: double
 // two-pass stats). Input row r at x + r*ld_in.
 bool launch_layernorm(const float *x, int ld_in, const float *g, const float *b, int rows, int cols,

@@ -46,6 +46,9 @@ struct tcg_vit {
     // them tile by tile in shared memory)
     uint8_t *qslab = nullptr;
     size_t qslab_bytes = 0;
+    // the tf32 pair a packed weight is dequantised into before its GEMM at
+    // large batches (the largest packed weight's size; reused GEMM by GEMM)
+    float *jit_hi = nullptr, *jit_lo = nullptr;
 
     struct Layer {
         const float *ln1_g, *ln1_b, *qkv_b, *out_b, *ln2_g, *ln2_b, *up_b, *down_b;
@@ -88,6 +91,7 @@ struct tcg_vit {
         if (wslab) cudaFree(wslab);
         if (sslab) cudaFree(sslab);
         if (qslab) cudaFree(qslab);
+        if (jit_hi) cudaFree(jit_hi);
         for (int i = 0; i < 2; i++) {
             if (px_slot[i] && px_slot[i] != px) cudaFree(px_slot[i]);
             if (copied[i]) cudaEventDestroy(copied[i]);
@@ -209,6 +213,14 @@ static tcg_vit *vit_alloc(const tc_vit_t *m, int max_batch, std::vector<WEntry> 
             return nullptr;
         }
         for (size_t i = 0; i < packed.size(); i++) *packed[i].dst = v->qslab + 4 * qoff[i];
+        size_t most = 0;
+        for (const Packed &pk : packed) most = std::max(most, (size_t)pk.t->n_elem);
+        if (cudaMalloc(&v->jit_hi, 2 * align_floats(most) * sizeof(float)) != cudaSuccess) {
+            cudaGetLastError();
+            fail("tcg_vit_upload: cannot allocate %zu MB for dequantised weights", 8 * most >> 20);
+            return nullptr;
+        }
+        v->jit_lo = v->jit_hi + align_floats(most);
     }
     offsets.resize(table.size());
     size_t total = 0;
@@ -314,6 +326,22 @@ static bool split_weights(tcg_vit *v, const std::vector<WEntry> &table, const st
     return true;
 }
 
+// Token rows from which packed weights are dequantised before their GEMMs
+// (tcg_vit_set_jit_rows). Measured on ViT-B/32 with Q4_K block linears
+// (B200, ms per forward, dequantised before the GEMM / inside it): batch 4
+// 1.61 / 1.78, 32 2.55 / 4.11, 256 12.1 / 22.5 -- inside the GEMM every
+// 128-row tile dequantises the whole weight again, so it only pays where a
+// GEMM has a single row tile.
+long g_vit_jit_rows = 129;
+
+// One GEMM of the forward, after the dequantisation of its weight when the
+// plan asks for it.
+static bool run_gemm(const GemmPlan &p, cudaStream_t s, int *err)
+{
+    if (p.jit_q && !launch_dequant_split(p.jit_q, p.jit_hi, p.jit_lo, p.jit_n, GGML_TYPE_Q4_K, s)) return false;
+    return gemm_run(p, s, err);
+}
+
 static tcg_vit::Plans *plans_for(tcg_vit *v, int n)
 {
     auto it = v->plans.find(n);
@@ -331,9 +359,23 @@ static tcg_vit::Plans *plans_for(tcg_vit *v, int n)
     e.out.ld = D;
     const GemmWork *w = &v->work;
     const int tp = gemm_throughput_cfg();
-    // a GEMM whose weight is packed runs the packed-B configuration
+    // A GEMM whose weight is packed dequantises it tile by tile in shared
+    // memory when the batch is small (the weight read dominates); from
+    // g_vit_jit_rows rows on, where every 128-row tile would dequantise the
+    // whole weight again, the weight is dequantised once into the model's
+    // tf32 pair (L2-resident) just before the GEMM, which then runs as usual.
+    const bool jit = (long)n * T >= g_vit_jit_rows;
     auto plan = [&](GemmPlan &gp, const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo,
                     const uint8_t *bq, int Mg, int Ng, int Kg, GemmEpi ep) {
+        if (bq && jit) {
+            if (!gemm_plan(gp, a_hi, a_lo, v->jit_hi, v->jit_lo, Mg, Ng, Kg, ep, gemm_vit_cfg(Mg, Ng, Kg), w))
+                return false;
+            gp.jit_q = bq;
+            gp.jit_hi = v->jit_hi;
+            gp.jit_lo = v->jit_lo;
+            gp.jit_n = (size_t)Ng * Kg;
+            return true;
+        }
         if (bq) {
             ep.bq = bq;
             ep.bq_row = (size_t)(Kg / 256) * 144;
@@ -454,7 +496,7 @@ static bool forward_body(tcg_vit *v, tcg_vit::Plans *p, int n, Tapper *tap)
     OutSpec xs; xs.plain = v->x; xs.ld = D;
     OutSpec hs; hs.hi = v->h_hi; hs.lo = v->h_lo; hs.ld = D;
 
-    PROF(K_GEMM, gemm_run(p->patch, s, err));
+    PROF(K_GEMM, run_gemm(p->patch, s, err));
     PROF(K_OTHER, launch_cls_rows(v->x, v->cls, v->pos, n, T, D, s));
     PROF(K_NORM, launch_layernorm(v->x, D, v->ln_pre_g, v->ln_pre_b, M, D, v->eps, xs, s));
     if (tap && !tap->deliver("ln_pre", v->x, n, T, D, (size_t)T * D)) return false;
@@ -462,12 +504,12 @@ static bool forward_body(tcg_vit *v, tcg_vit::Plans *p, int n, Tapper *tap)
     for (int i = 0; i < v->L; i++) {
         const tcg_vit::Layer &y = v->layers[i];
         PROF(K_NORM, launch_layernorm(v->x, D, y.ln1_g, y.ln1_b, M, D, v->eps, hs, s));
-        PROF(K_GEMM, gemm_run(p->qkv[i], s, err));
+        PROF(K_GEMM, run_gemm(p->qkv[i], s, err));
         PROF(K_ATTN, launch_mha(v->qkv, v->qkv + D, v->qkv + 2 * D, 3 * D, T, v->H, v->hd, n, hs, s));
-        PROF(K_GEMM, gemm_run(p->out[i], s, err));
+        PROF(K_GEMM, run_gemm(p->out[i], s, err));
         PROF(K_NORM, launch_layernorm(v->x, D, y.ln2_g, y.ln2_b, M, D, v->eps, hs, s));
-        PROF(K_GEMM, gemm_run(p->up[i], s, err));
-        PROF(K_GEMM, gemm_run(p->down[i], s, err));
+        PROF(K_GEMM, run_gemm(p->up[i], s, err));
+        PROF(K_GEMM, run_gemm(p->down[i], s, err));
         if (tap && i == 0 && !tap->deliver("blk0", v->x, n, T, D, (size_t)T * D)) return false;
         if (tap && i == v->L - 1 && !tap->deliver("blk_last", v->x, n, T, D, (size_t)T * D)) return false;
     }
@@ -481,7 +523,7 @@ static bool forward_body(tcg_vit *v, tcg_vit::Plans *p, int n, Tapper *tap)
     // ln_post of the CLS rows as the tf32 pair the projection GEMM reads
     OutSpec ps; ps.hi = v->pooled_hi; ps.lo = v->pooled_lo; ps.ld = D;
     PROF(K_NORM, launch_layernorm(v->x, T * D, v->ln_post_g, v->ln_post_b, n, D, v->eps, ps, s));
-    PROF(K_GEMM, gemm_run(p->proj, s, err));
+    PROF(K_GEMM, run_gemm(p->proj, s, err));
     return true;
 }
 
@@ -762,6 +804,16 @@ size_t tcg_vit_gemm_weight_bytes(const tcg_vit_t *v)
     if (!v) return 0;
     const size_t pair = (v->sslab_floats - 2 * (size_t)v->D * v->d_out) * sizeof(float);   // all but the projection
     return pair + v->qslab_bytes;
+}
+
+// Token rows (batch x tokens) from which a forward dequantises each packed
+// weight into a tf32 pair just before its GEMM instead of inside it; applies
+// to batch sizes planned afterwards. Returns the previous value.
+long tcg_vit_set_jit_rows(long rows)
+{
+    const long old = g_vit_jit_rows;
+    if (rows > 0) g_vit_jit_rows = rows;
+    return old;
 }
 
 // 1 (default): GEMM weights stored as Q4_K stay packed on the device at

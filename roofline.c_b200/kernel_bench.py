@@ -173,6 +173,12 @@ def case_vit(a):
     cache = os.environ.get("TCG_BENCH_CACHE", "/tmp/roofline_b200_bench")
     over = {"n_layer": a.layers} if a.layers else {}
     path, cfg = G.cached_vit_gguf(cache, a.model, 0, **over)
+    if a.q4k:       # block linears as Q4_K blocks, kept packed on the device
+        path = os.path.join(cache, f"{a.model}-L{cfg['n_layer']}-q4k-s0.gguf")
+        if not os.path.exists(path):
+            G.write_kquant_vit_gguf(path + ".tmp", cfg, seed=0)
+            os.replace(path + ".tmp", path)
+    old_jit = L.tcg_vit_set_jit_rows(a.jit_rows) if a.jit_rows else None
     # the GEMM plans of a batch size are made at its first forward
     old_cfg, old_sk = L.tcg_gemm_force_cfg(a.cfg), L.tcg_gemm_set_streamk(a.streamk)
     old_pdl = L.tcg_set_pdl(a.pdl)
@@ -191,7 +197,9 @@ def case_vit(a):
     L.tcg_gemm_set_tma_store(old_tma)
     if old_chunk is not None:
         L.tcg_gemm_set_chunk_k(old_chunk)
-    return {"case": "vit", "chunk": a.chunk, "model": a.model, "layers": cfg["n_layer"], "batch": a.batch, "cfg": a.cfg,
+    if old_jit is not None:
+        L.tcg_vit_set_jit_rows(old_jit)
+    return {"case": "vit", "chunk": a.chunk, "q4k": a.q4k, "jit_rows": a.jit_rows, "model": a.model, "layers": cfg["n_layer"], "batch": a.batch, "cfg": a.cfg,
             "streamk": a.streamk, "pdl": a.pdl, "tma_store": a.tma_store, "ms": round(ms, 4),
             "images/s": round(a.batch / ms * 1e3, 1)}
 
@@ -263,6 +271,9 @@ def main():
     v.add_argument("--pdl", type=int, default=1, help="0: no programmatic dependent launch")
     v.add_argument("--tma-store", type=int, default=1, help="0: GEMM epilogues on plain stores")
     v.add_argument("--chunk", type=int, default=0, help="K-elements per TMEM accumulator chunk (0: default)")
+    v.add_argument("--q4k", type=int, default=0, help="1: the model with Q4_K block linears (kept packed)")
+    v.add_argument("--jit-rows", type=int, default=0,
+                   help="token rows from which packed weights are dequantised before their GEMMs (0: default)")
     up = sub.add_parser("upload")
     up.add_argument("--model", default="vit-b32", choices=sorted(G.VIT_CONFIGS))
     for p in (g, gs, mv, dq, v, up):

@@ -168,7 +168,7 @@ _SIGS = [
     ("tcg_vit_max_batch", i32, [vp]), ("tcg_vit_device_bytes", sz, [vp]),
     ("tcg_vit_use_graphs", None, [vp, boolean]),
     ("tcg_vit_set_upload_mode", i32, [i32]), ("tcg_vit_set_packed_weights", i32, [i32]),
-    ("tcg_vit_gemm_weight_bytes", sz, [vp]), ("tcg_vit_last_upload_ms", C.c_double, []),
+    ("tcg_vit_gemm_weight_bytes", sz, [vp]), ("tcg_vit_set_jit_rows", C.c_long, [C.c_long]), ("tcg_vit_last_upload_ms", C.c_double, []),
     ("tcg_vit_upload_fallback", C.c_char_p, []),
     ("tcg_vit_encode_batch", boolean, [vp, vp, i32, vp, vp, vp]),
     ("tcg_vit_encode_device", boolean, [vp, vp, i32, vp]),

@@ -335,14 +335,16 @@ def test_kquant_weights_model(gpu, tmp_path):
         m.close()
 
 
-@pytest.mark.parametrize("n_img", [3, 64])
-def test_packed_q4k_weights_model(gpu, tmp_path, n_img):
+@pytest.mark.parametrize("n_img,jit_rows", [(3, 0), (64, 0), (3, 1), (64, 1)])
+def test_packed_q4k_weights_model(gpu, tmp_path, n_img, jit_rows):
     """Every block linear weight of a ViT-B/32 (two layers) in Q4_K: the
     device keeps them packed (144 bytes per 256 weights) and each GEMM
     dequantises its tiles in shared memory. Against the oracle's fp32 model
     of the dequantised weights, per tap; and against the same model uploaded
-    with the weights dequantised at load."""
+    with the weights dequantised at load. jit_rows 1: every batch dequantises
+    each packed weight into a tf32 pair just before its GEMM instead."""
     L = tcg.lib()
+    old_jit = L.tcg_vit_set_jit_rows(jit_rows if jit_rows else 1 << 40)
     cfg = G.vit_config("vit-b32", n_layer=2)
     path = str(tmp_path / "q4k.gguf")
     made = G.write_kquant_vit_gguf(path, cfg, seed=9)
@@ -361,6 +363,7 @@ def test_packed_q4k_weights_model(gpu, tmp_path, n_img):
         finally:
             m.close()
             L.tcg_vit_set_packed_weights(old)
+    L.tcg_vit_set_jit_rows(old_jit)
     D, F, L_, K0 = cfg["d_model"], cfg["d_ffn"], cfg["n_layer"], 3 * cfg["patch"] ** 2
     linear = L_ * (3 * D * D + D * D + 2 * F * D)
     # packed blocks (each tensor's slot padded to 256 bytes) plus the patch embedding's tf32 pair
