@@ -161,6 +161,14 @@ bool tcg_softmax_rows(float *out, const float *x, int rows, int cols);
 /* tc_ref_mha without the scratch argument: the scores stay on chip. */
 bool tcg_mha(float *out, const float *q, const float *k, const float *v,
              int T, int n_head, int head_dim);
+/* tcg_mha over n_img images whose q, k and v share one row of width
+ * 3 * n_head * head_dim (one GEMM over the fused [3D, D] weight whose three
+ * row blocks src/vit.c:271-278 applies as three linears; this library's ViT
+ * encoder keeps that layout): image i's rows are i*T .. i*T + T - 1.
+ * Output [n_img * T, n_head * head_dim] as fp32 (out) and/or as its tf32
+ * hi/lo pair (out_hi, out_lo; both or neither). */
+bool tcg_mha_images(float *out, float *out_hi, float *out_lo, const float *qkv,
+                    int T, int n_head, int head_dim, int n_img);
 bool tcg_add(float *out, const float *a, const float *b, size_t n);
 bool tcg_scale(float *out, const float *x, float s, size_t n);
 

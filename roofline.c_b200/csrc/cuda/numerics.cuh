@@ -10,11 +10,14 @@ namespace tcg {
 
 // Round-to-nearest (ties away) to tf32: the 10-bit-mantissa value the tensor
 // core consumes, returned as an fp32 bit pattern with the low 13 bits zero.
+// Integer arithmetic on the sign-magnitude pattern: half a tf32 ulp (bit 12)
+// is added to the magnitude and the 13 low bits dropped, so a carry rounds
+// the magnitude up (ties included, away from zero) and may step the exponent;
+// the same bits as cvt.rna.tf32.f32 for every finite v, without occupying the
+// conversion unit that kernels writing hi/lo pairs would otherwise queue on.
 __device__ __forceinline__ float to_tf32(float v)
 {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
-    return __uint_as_float(r);
+    return __uint_as_float((__float_as_uint(v) + 0x1000u) & 0xffffe000u);
 }
 
 // v = hi + lo + O(2^-22 |v|): the operand split of 3xTF32.

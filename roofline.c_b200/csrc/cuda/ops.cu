@@ -4,6 +4,7 @@
 #include "numerics.cuh"
 #include "gemm.cuh"
 
+#include <cuda_fp16.h>
 #include <type_traits>
 
 namespace tcg {
@@ -626,6 +627,380 @@ mha64s_kernel(const float *__restrict__ q, const float *__restrict__ k, const fl
         if (4 * ty + i < T) put4(out, base + 4 * ty + i, col + 4 * tx, o[i]);
 }
 
+// ------------------------------------------------ attention, T <= 64, mma.sync
+// head_dim 64 and T <= 64 (ViT-B/32's 50 tokens) on the m16n8k16 tensor-core
+// instruction with fp16 operands that carry an fp32 value in two pieces. A
+// block is first scaled by a power of two that puts its largest magnitude in
+// [2^14, 2^15), inside fp16's normal range (one scale per query row, one for
+// the (image, head)'s K, one for its V; P, in [0, 1], is scaled by 2^14);
+// scaling by a power of two is exact and is undone on the fp32 accumulators.
+// Pieces: x = p1 + p2 + r, p1 = x rounded to 11 bits (exact in fp16), p2 =
+// fp16(x - p1); |r| <= 2^-23 |x|, the precision of a tf32 pair. Q K^T takes the
+// four products p1k1, p1k2, p2k1, p2k2 and P V the three p1v1, p1v2, p2v1.
+// The fp32 accumulation of an MMA truncates relative to its largest addend,
+// so each accumulator sums every cross product (2^-11 of the result and
+// less) over all keys or dims first and the four p1 p1 steps last: four
+// truncations at the result's magnitude. Against the oracle this measures as
+// close as the fp32 FMA kernel, peaked softmax rows included. The softmax
+// follows src/ops.c:129-139 on the score accumulators (a row's keys sit in
+// the four lanes of a quad): scale, max, expf of the difference, sum, one
+// reciprocal (in double), multiply; a lane adds its 16 terms of a row in fp32
+// (relative error below 2^-20) and the quad's four partial sums are added in
+// double. The accumulator layout of S is the A-operand layout of P, so P
+// stays in registers. One CTA of four warps per (head, image), warp w owning
+// query rows 16w..16w+15; K and V are staged once per CTA as fp16 [key][dim]
+// planes (two pieces each) with the 16-byte chunks of a key row
+// XOR-swizzled by the key (conflict-free ldmatrix), 32 KB: five CTAs per SM.
+// Keys T..63 are zero rows, masked out of the softmax.
+constexpr int MHAM_T = 64;
+
+// two floats -> one register of fp16 halves, a in the low 16 bits
+__device__ __forceinline__ uint32_t mham_h2(float a, float b)
+{
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// (x0, x1) -> NP packed fp16 pieces, x0 in the low 16 bits of each. Every
+// piece but the last is x rounded to 11 significant bits (to_tf32's integer
+// rounding: 11 bits are fp16's precision, so the conversion is exact) and the
+// residual x - piece is an exact fp32 subtraction; the last piece is the
+// residual rounded to fp16. Pieces below fp16's normal range (2^-14, 2^-28 of
+// a block's largest magnitude) take fp16's subnormal rounding, an error of at
+// most 2^-25.
+template <int NP>
+__device__ __forceinline__ void mham_split(float x0, float x1, uint32_t (&pc)[NP])
+{
+#pragma unroll
+    for (int i = 0; i + 1 < NP; i++) {
+        const float h0 = to_tf32(x0), h1 = to_tf32(x1);
+        pc[i] = mham_h2(h0, h1);
+        x0 = __fsub_rn(x0, h0);
+        x1 = __fsub_rn(x1, h1);
+    }
+    pc[NP - 1] = mham_h2(x0, x1);
+}
+
+// e with m * 2^e in [2^14, 2^15) for a finite m > 0, at most 100; 0 when m is
+// 0 or not finite.
+__device__ __forceinline__ int mham_exp(float m)
+{
+    const int E = (__float_as_int(m) >> 23) & 0xff;
+    if (m == 0.0f || E == 0xff) return 0;
+    return min(141 - E, 100);
+}
+
+__device__ __forceinline__ float mham_pow2(int e) { return __int_as_float((127 + e) << 23); }   // |e| <= 126
+
+__device__ __forceinline__ void mham_mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
+{
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void mham_ldsm(uint32_t addr, uint32_t (&r)[4])
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+
+__device__ __forceinline__ void mham_ldsm_t(uint32_t addr, uint32_t (&r)[4])
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+
+__device__ __forceinline__ void put2(const OutSpec &o, size_t row, int col, float a, float b)
+{
+    const size_t i = row * (size_t)o.ld + col;
+    if (o.plain) *reinterpret_cast<float2 *>(o.plain + i) = make_float2(a, b);
+    if (o.hi) {
+        float ha, la, hb, lb;
+        split_tf32(a, ha, la);
+        split_tf32(b, hb, lb);
+        *reinterpret_cast<float2 *>(o.hi + i) = make_float2(ha, hb);
+        *reinterpret_cast<float2 *>(o.lo + i) = make_float2(la, lb);
+    }
+}
+
+// byte offset of (key, 16-byte chunk) in a swizzled [64][64] fp16 plane
+__device__ __forceinline__ uint32_t mham_off(int key, int chunk)
+{
+    return (uint32_t)(key * 128 + ((chunk ^ (key & 7)) << 4));
+}
+
+__global__ void __launch_bounds__(128, 5)
+mha64m_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v, int ldi,
+              int T, OutSpec out)
+{
+    pdl_wait();
+    constexpr int NQK = 2;                              // pieces of Q and K
+    constexpr uint32_t PLANE = MHAM_T * 64 * 2;
+    __shared__ __align__(128) __half kv[NQK + 2][MHAM_T * 64];    // K's NQK pieces, V's two
+    __shared__ float red[2][4];
+    const int col = blockIdx.x * 64;
+    const size_t base = (size_t)blockIdx.y * T;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int t4 = lane & 3;
+    const float2 z2 = make_float2(0.f, 0.f);
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+
+    // K and V: step it covers element i = thread + 128 it, key i >> 4, dims 4 (i & 15)..
+    float4 xk[8], xv[8];
+#pragma unroll
+    for (int it = 0; it < 8; it++) {
+        const int i = threadIdx.x + 128 * it, key = i >> 4, d = col + 4 * (i & 15);
+        xk[it] = key < T ? __ldg(reinterpret_cast<const float4 *>(k + (base + key) * (size_t)ldi + d)) : z4;
+        xv[it] = key < T ? __ldg(reinterpret_cast<const float4 *>(v + (base + key) * (size_t)ldi + d)) : z4;
+    }
+    float mk = 0.f, mv = 0.f;
+#pragma unroll
+    for (int it = 0; it < 8; it++) {
+        mk = fmaxf(mk, fmaxf(fmaxf(fabsf(xk[it].x), fabsf(xk[it].y)), fmaxf(fabsf(xk[it].z), fabsf(xk[it].w))));
+        mv = fmaxf(mv, fmaxf(fmaxf(fabsf(xv[it].x), fabsf(xv[it].y)), fmaxf(fabsf(xv[it].z), fabsf(xv[it].w))));
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        mk = fmaxf(mk, __shfl_xor_sync(0xffffffffu, mk, o));
+        mv = fmaxf(mv, __shfl_xor_sync(0xffffffffu, mv, o));
+    }
+    if (lane == 0) {
+        red[0][wid] = mk;
+        red[1][wid] = mv;
+    }
+    __syncthreads();
+    mk = fmaxf(fmaxf(red[0][0], red[0][1]), fmaxf(red[0][2], red[0][3]));
+    mv = fmaxf(fmaxf(red[1][0], red[1][1]), fmaxf(red[1][2], red[1][3]));
+    const int ek = mham_exp(mk), ev = mham_exp(mv);
+    const uint32_t s0 = (uint32_t)__cvta_generic_to_shared(&kv[0][0]);
+    // K's pieces first; then this warp's query rows are requested (their
+    // latency overlaps V's pieces) straight into A-operand order: xq[kk][0]
+    // row r0, dims 16kk + 2t4 + {0,1}; [1] row r1, same dims; [2] and [3]
+    // the dims 8 further on.
+    {
+        const float fk = mham_pow2(ek);
+#pragma unroll
+        for (int it = 0; it < 8; it++) {
+            const int i = threadIdx.x + 128 * it, key = i >> 4, c4 = i & 15;
+            const uint32_t off = mham_off(key, c4 >> 1) + 8 * (c4 & 1);
+            uint32_t a[NQK], b[NQK];
+            mham_split<NQK>(__fmul_rn(xk[it].x, fk), __fmul_rn(xk[it].y, fk), a);
+            mham_split<NQK>(__fmul_rn(xk[it].z, fk), __fmul_rn(xk[it].w, fk), b);
+#pragma unroll
+            for (int pc = 0; pc < NQK; pc++)
+                asm volatile("st.shared.v2.u32 [%0], {%1,%2};" ::"r"(s0 + pc * PLANE + off), "r"(a[pc]), "r"(b[pc]));
+        }
+    }
+    const int r0 = 16 * wid + (lane >> 2), r1 = r0 + 8;
+    float2 xq[4][4];
+#pragma unroll
+    for (int kk = 0; kk < 4; kk++) {
+        const int d = col + 16 * kk + 2 * t4;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int r = (i & 1) ? r1 : r0;
+            xq[kk][i] = r < T ? __ldg(reinterpret_cast<const float2 *>(q + (base + r) * (size_t)ldi + d + 4 * (i & 2)))
+                              : z2;
+        }
+    }
+    {
+        const float fv = mham_pow2(ev);
+#pragma unroll
+        for (int it = 0; it < 8; it++) {
+            const int i = threadIdx.x + 128 * it, key = i >> 4, c4 = i & 15;
+            const uint32_t off = mham_off(key, c4 >> 1) + 8 * (c4 & 1);
+            uint32_t c[2], e[2];
+            mham_split<2>(__fmul_rn(xv[it].x, fv), __fmul_rn(xv[it].y, fv), c);
+            mham_split<2>(__fmul_rn(xv[it].z, fv), __fmul_rn(xv[it].w, fv), e);
+#pragma unroll
+            for (int pc = 0; pc < 2; pc++)
+                asm volatile("st.shared.v2.u32 [%0], {%1,%2};" ::"r"(s0 + (NQK + pc) * PLANE + off), "r"(c[pc]), "r"(e[pc]));
+        }
+    }
+    __syncthreads();
+    if (16 * wid >= T) return;                          // no later barrier
+
+    // Q: one scale per row (a row's 64 dims sit in the four lanes of a quad)
+    float m0 = 0.f, m1 = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 4; kk++) {
+        m0 = fmaxf(m0, fmaxf(fmaxf(fabsf(xq[kk][0].x), fabsf(xq[kk][0].y)), fmaxf(fabsf(xq[kk][2].x), fabsf(xq[kk][2].y))));
+        m1 = fmaxf(m1, fmaxf(fmaxf(fabsf(xq[kk][1].x), fabsf(xq[kk][1].y)), fmaxf(fabsf(xq[kk][3].x), fabsf(xq[kk][3].y))));
+    }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+        m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+    }
+    const int eq0 = mham_exp(m0), eq1 = mham_exp(m1);
+    uint32_t qa[NQK][4][4];                             // [piece][kk][A register]
+    {
+        const float f0 = mham_pow2(eq0), f1 = mham_pow2(eq1);
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float f = (i & 1) ? f1 : f0;
+                uint32_t pc[NQK];
+                mham_split<NQK>(__fmul_rn(xq[kk][i].x, f), __fmul_rn(xq[kk][i].y, f), pc);
+#pragma unroll
+                for (int x = 0; x < NQK; x++) qa[x][kk][i] = pc[x];
+            }
+    }
+
+    // S = Q K^T: key block j (8 keys), dims 32p..32p+31 per ldmatrix; the
+    // blocks are independent accumulators, the j loop inside keeps eight
+    // (seven for T <= 56) of them in flight. Pass 0: the cross products over
+    // all 64 dims; pass 1: the four p1 k1 steps.
+    float s[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+    const bool blk7 = T > 56;
+#pragma unroll
+    for (int pass = 0; pass < 2; pass++)
+#pragma unroll
+        for (int p = 0; p < 2; p++)
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                if (j == 7 && !blk7) break;
+                const uint32_t off = mham_off(8 * j + (lane & 7), 4 * p + (lane >> 3));
+                uint32_t bk[NQK][4];
+                if (pass == 0) {
+#pragma unroll
+                    for (int x = 0; x < NQK; x++) mham_ldsm(s0 + x * PLANE + off, bk[x]);
+                } else {
+                    mham_ldsm(s0 + off, bk[0]);
+                }
+#pragma unroll
+                for (int h = 0; h < 2; h++) {           // kk = 2p + h: B registers 2h, 2h + 1
+                    const int kk = 2 * p + h, x = 2 * h, y = 2 * h + 1;
+                    if (pass == 0) {
+                        mham_mma(s[j], qa[1][kk], bk[1][x], bk[1][y]);
+                        mham_mma(s[j], qa[0][kk], bk[1][x], bk[1][y]);
+                        mham_mma(s[j], qa[1][kk], bk[0][x], bk[0][y]);
+                    } else {
+                        mham_mma(s[j], qa[0][kk], bk[0][x], bk[0][y]);
+                    }
+                }
+            }
+
+    // softmax of rows r0 (s[j][0..1]) and r1 (s[j][2..3]); key 8j + 2t4 + c.
+    // Undoing the scales and multiplying by 1/sqrt(64) = 2^-3 are exact, so
+    // one multiply by 2^-(eq + ek + 3) gives the same bits as the three
+    // whenever that power of two is a normal float.
+    const int E0 = eq0 + ek + 3, E1 = eq1 + ek + 3;
+    if (abs(E0) <= 126 && abs(E1) <= 126) {
+        const float g0 = mham_pow2(-E0), g1 = mham_pow2(-E1);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            s[j][0] = __fmul_rn(s[j][0], g0);
+            s[j][1] = __fmul_rn(s[j][1], g0);
+            s[j][2] = __fmul_rn(s[j][2], g1);
+            s[j][3] = __fmul_rn(s[j][3], g1);
+        }
+    } else {
+        const float scale = 1.0f / sqrtf(64.0f);
+        const float uk = mham_pow2(-ek), u0 = mham_pow2(-eq0), u1 = mham_pow2(-eq1);
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
+                s[j][c] = __fmul_rn(__fmul_rn(__fmul_rn(s[j][c], u0), uk), scale);
+                s[j][2 + c] = __fmul_rn(__fmul_rn(__fmul_rn(s[j][2 + c], u1), uk), scale);
+            }
+    }
+    const int jfull = T >> 3;                           // key blocks 0..jfull-1 hold no key past T
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            if (j < jfull || 8 * j + 2 * t4 + c < T) {
+                mx0 = fmaxf(mx0, s[j][c]);
+                mx1 = fmaxf(mx1, s[j][2 + c]);
+            }
+        }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+    }
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            const bool in = j < jfull || 8 * j + 2 * t4 + c < T;
+            s[j][c] = in ? expf(__fsub_rn(s[j][c], mx0)) : 0.0f;
+            s[j][2 + c] = in ? expf(__fsub_rn(s[j][2 + c], mx1)) : 0.0f;
+            ps0 = __fadd_rn(ps0, s[j][c]);
+            ps1 = __fadd_rn(ps1, s[j][2 + c]);
+        }
+    double sum0 = ps0, sum1 = ps1;
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+        sum0 += __shfl_xor_sync(0xffffffffu, sum0, o);
+        sum1 += __shfl_xor_sync(0xffffffffu, sum1, o);
+    }
+    const float inv0 = (float)(1.0 / sum0), inv1 = (float)(1.0 / sum1);
+    // e * inv * 2^14 == e * (inv * 2^14): scaling by a power of two is exact
+    const float w0 = __fmul_rn(inv0, 16384.0f), w1 = __fmul_rn(inv1, 16384.0f);
+
+    // P (times 2^14) as two pieces in A order: k-step kk covers key blocks 2kk, 2kk+1
+    uint32_t pa[2][4][4];
+#pragma unroll
+    for (int kk = 0; kk < 4; kk++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float(&sj)[4] = s[2 * kk + (i >> 1)];
+            const float w = (i & 1) ? w1 : w0;
+            const int c = 2 * (i & 1);
+            uint32_t pc[2];
+            mham_split<2>(__fmul_rn(sj[c], w), __fmul_rn(sj[c + 1], w), pc);
+            pa[0][kk][i] = pc[0];
+            pa[1][kk][i] = pc[1];
+        }
+
+    // O = P V: n-blocks 2np, 2np+1 from one transposed ldmatrix per piece;
+    // pass 0: the cross products p1 v2 and p2 v1 over all keys; pass 1: the
+    // p1 v1 steps.
+    float o[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    const int nk = (T + 15) >> 4;
+#pragma unroll
+    for (int pass = 0; pass < 2; pass++)
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+            if (kk >= nk) break;
+            const int m = lane >> 3, key = 16 * kk + 8 * (m & 1) + (lane & 7);
+#pragma unroll
+            for (int np = 0; np < 4; np++) {
+                uint32_t v1[4], v2[4];
+                const uint32_t off = mham_off(key, 2 * np + (m >> 1));
+                mham_ldsm_t(s0 + NQK * PLANE + off, v1);
+                if (pass == 0) {
+                    mham_ldsm_t(s0 + (NQK + 1) * PLANE + off, v2);
+                    mham_mma(o[2 * np], pa[0][kk], v2[0], v2[1]);
+                    mham_mma(o[2 * np], pa[1][kk], v1[0], v1[1]);
+                    mham_mma(o[2 * np + 1], pa[0][kk], v2[2], v2[3]);
+                    mham_mma(o[2 * np + 1], pa[1][kk], v1[2], v1[3]);
+                } else {
+                    mham_mma(o[2 * np], pa[0][kk], v1[0], v1[1]);
+                    mham_mma(o[2 * np + 1], pa[0][kk], v1[2], v1[3]);
+                }
+            }
+        }
+    const float uo = mham_pow2(-(14 + ev));
+#pragma unroll
+    for (int n = 0; n < 8; n++) {
+        const int c = col + 8 * n + 2 * t4;
+        if (r0 < T) put2(out, base + r0, c, __fmul_rn(o[n][0], uo), __fmul_rn(o[n][1], uo));
+        if (r1 < T) put2(out, base + r1, c, __fmul_rn(o[n][2], uo), __fmul_rn(o[n][3], uo));
+    }
+}
+
 static size_t mha64_smem(int T)
 {
     const size_t T4 = (size_t)((T + 3) & ~3);
@@ -635,6 +1010,8 @@ static size_t mha64_smem(int T)
 // T > 64: 1 (default) tensor cores where 128 <= T <= 1024, else the streaming kernel with 64-query blocks;
 // 0 whole-K/V kernel; 2 streaming kernel with 48-query blocks; 3 tensor cores where they apply
 int g_mha_variant = 1;
+// head_dim 64, T <= 64: 1 (default) fp16-split tensor cores (mha64m_kernel); 0 fp32 FMA (mha64s_kernel)
+int g_mha_short = 1;
 
 bool launch_mha(const float *q, const float *k, const float *v, int ldi, int T, int n_head, int hd,
                 int n_img, const OutSpec &out, cudaStream_t s)
@@ -645,7 +1022,8 @@ bool launch_mha(const float *q, const float *k, const float *v, int ldi, int T, 
                          !(out.ld & 3) && !(((uintptr_t)out.plain | (uintptr_t)out.hi | (uintptr_t)out.lo) & 15);
     if (hd == 64 && aligned && T <= MHAS_T) {
         dim3 grid(n_head, n_img);
-        TCG_CUDA(launch_pdl(mha64s_kernel, grid, 256, 0, s, q, k, v, ldi, T, out));
+        if (g_mha_short == 1) TCG_CUDA(launch_pdl(mha64m_kernel, grid, 128, 0, s, q, k, v, ldi, T, out));
+        else TCG_CUDA(launch_pdl(mha64s_kernel, grid, 256, 0, s, q, k, v, ldi, T, out));
         TCG_LAUNCHED();
         return true;
     }
@@ -976,6 +1354,21 @@ bool tcg_mha(float *out, const float *q, const float *k, const float *v, int T, 
     return launch_mha(q, k, v, n_head * head_dim, T, n_head, head_dim, 1, o, ctx().cur);
 }
 
+bool tcg_mha_images(float *out, float *out_hi, float *out_lo, const float *qkv, int T, int n_head, int head_dim,
+                    int n_img)
+{
+    if (!need_ctx()) return false;
+    if ((out_hi == nullptr) != (out_lo == nullptr)) return fail("attention: out_hi and out_lo go together");
+    if (!out && !out_hi) return fail("attention: no output");
+    const int D = n_head * head_dim;
+    OutSpec o;
+    o.plain = out;
+    o.hi = out_hi;
+    o.lo = out_lo;
+    o.ld = D;
+    return launch_mha(qkv, qkv + D, qkv + 2 * D, 3 * D, T, n_head, head_dim, n_img, o, ctx().cur);
+}
+
 bool tcg_add(float *out, const float *a, const float *b, size_t n)
 {
     if (!need_ctx()) return false;
@@ -1004,5 +1397,15 @@ extern "C" int tcg_set_attention_variant(int variant)
 {
     const int old = tcg::g_mha_variant;
     tcg::g_mha_variant = variant < 0 ? 0 : (variant > 3 ? 3 : variant);
+    return old;
+}
+
+// Tuning and test hook: the attention kernel for head_dim 64 and T <= 64
+// (1, the default: fp16 two-piece operands on mma.sync; 0: fp32 FMA). Returns the
+// previous setting.
+extern "C" int tcg_set_attention_short_kernel(int kernel)
+{
+    const int old = tcg::g_mha_short;
+    tcg::g_mha_short = kernel ? 1 : 0;
     return old;
 }

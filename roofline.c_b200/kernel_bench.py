@@ -7,6 +7,7 @@ profiles/ are taken with.
     python roofline.c_b200/kernel_bench.py matvec --type q4k --N 4096 --K 14336
     python roofline.c_b200/kernel_bench.py dequant --type q6k --rows 14336 --cols 4096
     python roofline.c_b200/kernel_bench.py vit --model vit-b32 --batch 256 --steps 3
+    python roofline.c_b200/kernel_bench.py attention --T 50 --heads 12 --images 256
 
 Each case runs `--warmup` untimed launches, then `--reps` timed ones with a
 256 MB memset between them (L2 flush), and prints one JSON line.
@@ -204,6 +205,29 @@ def case_vit(a):
             "images/s": round(a.batch / ms * 1e3, 1)}
 
 
+def case_attention(a):
+    """Attention over --images images of --T tokens: q, k, v in one fused
+    row of width 3D (the ViT encoder's layout), output as the tf32 hi/lo pair
+    the next GEMM reads (--plain 1: fp32)."""
+    L = tcg.lib()
+    D = a.heads * 64
+    rng = np.random.default_rng(0)
+    qkv = rng.standard_normal((a.images * a.T, 3 * D), dtype=np.float32)
+    old = L.tcg_set_attention_short_kernel(a.kernel)
+    rows = a.images * a.T
+    with tcg.DeviceBuffer.from_array(qkv) as dq, tcg.DeviceBuffer(rows * D * 4) as o1, \
+            tcg.DeviceBuffer(rows * D * 4) as o2, tcg.DeviceBuffer(256 << 20) as flush:
+        if a.plain:
+            fn = lambda: tcg.check(L.tcg_mha_images(o1.ptr, None, None, dq.ptr, a.T, a.heads, 64, a.images))  # noqa: E731
+        else:
+            fn = lambda: tcg.check(L.tcg_mha_images(None, o1.ptr, o2.ptr, dq.ptr, a.T, a.heads, 64, a.images))  # noqa: E731
+        ms, _ = timed(fn, a.warmup, a.reps, flush)
+    L.tcg_set_attention_short_kernel(old)
+    nbytes = rows * D * 4 * (3 + (1 if a.plain else 2))
+    return {"case": "attention", "T": a.T, "heads": a.heads, "images": a.images, "kernel": a.kernel,
+            "plain": a.plain, "ms": round(ms, 5), "GB/s": round(nbytes / ms / 1e6, 1)}
+
+
 def case_upload(a):
     """Weight upload from the GGUF mapping in every mode (0 per tensor from
     the mapping, 1 staged through page-locked chunks, 2 mapping registered):
@@ -274,16 +298,22 @@ def main():
     v.add_argument("--q4k", type=int, default=0, help="1: the model with Q4_K block linears (kept packed)")
     v.add_argument("--jit-rows", type=int, default=0,
                    help="token rows from which packed weights are dequantised before their GEMMs (0: default)")
+    at = sub.add_parser("attention")
+    at.add_argument("--T", type=int, default=50)
+    at.add_argument("--heads", type=int, default=12)
+    at.add_argument("--images", type=int, default=256)
+    at.add_argument("--kernel", type=int, default=1, help="T <= 64: 1 fp16-split tensor cores, 0 fp32 FMA")
+    at.add_argument("--plain", type=int, default=0, help="1: fp32 output instead of the tf32 pair")
     up = sub.add_parser("upload")
     up.add_argument("--model", default="vit-b32", choices=sorted(G.VIT_CONFIGS))
-    for p in (g, gs, mv, dq, v, up):
+    for p in (g, gs, mv, dq, v, at, up):
         p.add_argument("--warmup", type=int, default=3)
         p.add_argument("--reps", type=int, default=5)
         p.add_argument("--device", type=int, default=0)
     a = ap.parse_args()
     tcg.init(a.device)
     res = {"gemm": case_gemm, "gemmsweep": case_gemmsweep, "matvec": case_matvec, "dequant": case_dequant,
-           "vit": case_vit, "upload": case_upload}[a.case](a)
+           "vit": case_vit, "attention": case_attention, "upload": case_upload}[a.case](a)
     res["device_error"] = tcg.lib().tcg_device_error()
     print(json.dumps(res), flush=True)
 

@@ -149,7 +149,8 @@ _SIGS = [
     ("tcg_gemm_num_cfgs", i32, []), ("tcg_gemm_set_chunk_k", i32, [i32]), ("tcg_gemm_force_cfg", i32, [i32]),
     ("tcg_gemm_set_streamk", i32, [i32]), ("tcg_set_pdl", i32, [i32]),
     ("tcg_gemm_last_plan", None, [C.POINTER(C.c_int)]), ("tcg_gemm_set_tma_store", i32, [i32]),
-    ("tcg_set_attention_variant", i32, [i32]), ("tcg_matvec_last_kernel", i32, []), ("tcg_matvec_set_tc", i32, [i32]),
+    ("tcg_set_attention_variant", i32, [i32]), ("tcg_set_attention_short_kernel", i32, [i32]),
+    ("tcg_matvec_last_kernel", i32, []), ("tcg_matvec_set_tc", i32, [i32]),
     ("tcg_matvec_set_mma", i32, [i32]), ("tcg_matvec_mma_segments", i32, [i32]),
     ("tcg_matvec_set_static_weights", i32, [i32]), ("tcg_matvec_mma_slots", i32, [i32]),
     ("tcg_split_tf32", boolean, [vp, vp, vp, sz]),
@@ -163,6 +164,7 @@ _SIGS = [
     ("tcg_gelu", boolean, [vp, vp, sz]), ("tcg_gelu_quick", boolean, [vp, vp, sz]),
     ("tcg_softmax_rows", boolean, [vp, vp, i32, i32]),
     ("tcg_mha", boolean, [vp, vp, vp, vp, i32, i32, i32]),
+    ("tcg_mha_images", boolean, [vp, vp, vp, vp, i32, i32, i32, i32]),
     ("tcg_add", boolean, [vp, vp, vp, sz]), ("tcg_scale", boolean, [vp, vp, f32, sz]),
     ("tcg_vit_upload", vp, [C.POINTER(Vit), i32]), ("tcg_vit_release", None, [vp]),
     ("tcg_vit_max_batch", i32, [vp]), ("tcg_vit_device_bytes", sz, [vp]),

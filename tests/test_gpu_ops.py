@@ -125,6 +125,78 @@ def test_mha_vs_oracle(dev, T, H, HD):
     assert np.abs(got - want).max() <= 1e-5 * np.abs(want).max()
 
 
+def _mha_short(L, dev, q, k, v, T, H, kernel):
+    y = dev.empty(T * H * 64)
+    old = L.tcg_set_attention_short_kernel(kernel)
+    try:
+        tcg.check(L.tcg_mha(y.ptr, dev.put(q), dev.put(k), dev.put(v), T, H, 64), f"kernel {kernel}")
+    finally:
+        L.tcg_set_attention_short_kernel(old)
+    return y.download((T, H * 64))
+
+
+@pytest.mark.parametrize("T", [1, 2, 5, 8, 15, 16, 17, 33, 48, 49, 50, 56, 63, 64])
+def test_mha_short_kernels(dev, T):
+    """head_dim 64, T <= 64: the fp16 hi/lo tensor-core kernel (the default)
+    and the fp32 FMA kernel, each within the oracle's bound. One query row is
+    50x the others (a peaked softmax), one key row 1e-6x, and head 1's V is
+    1e4x larger than head 0's: every scale of the split is exercised."""
+    L = tcg.lib()
+    H = 3
+    rng = np.random.default_rng(1000 + T)
+    q, k, v = (rng.standard_normal((T, H * 64)).astype(np.float32) for _ in range(3))
+    q[T // 2] *= 50
+    k[(T - 1) // 3] *= 1e-6
+    v[:, 64:128] *= 1e4
+    want = oracle.mha(q, k, v, T, H, 64)
+    for kernel in (1, 0):
+        got = _mha_short(L, dev, q, k, v, T, H, kernel)
+        for h in range(H):          # each head against its own magnitude
+            w, g = want[:, 64 * h:64 * h + 64], got[:, 64 * h:64 * h + 64]
+            assert np.abs(g - w).max() <= 1e-5 * np.abs(w).max(), (kernel, h)
+    assert L.tcg_device_error() == 0
+
+
+@pytest.mark.parametrize("scale", [1e-30, 1e-8, 1e3, 1e12, 1e30])
+def test_mha_short_magnitudes(dev, scale):
+    """The power-of-two scales of the fp16 split keep the operands inside
+    fp16's range whatever the magnitude of q, k and v (scores stay finite:
+    q is scaled by 1/scale where k is scaled by scale)."""
+    L = tcg.lib()
+    T, H = 50, 2
+    rng = np.random.default_rng(7)
+    q, k, v = (rng.standard_normal((T, H * 64)).astype(np.float32) for _ in range(3))
+    q = (q / np.float32(scale)).astype(np.float32)
+    k = (k * np.float32(scale)).astype(np.float32)
+    v = (v * np.float32(scale)).astype(np.float32)
+    want = oracle.mha(q, k, v, T, H, 64)
+    got = _mha_short(L, dev, q, k, v, T, H, 1)
+    assert np.all(np.isfinite(got))
+    assert np.abs(got - want).max() <= 1e-5 * np.abs(want).max()
+
+
+@pytest.mark.parametrize("T,H,n_img", [(50, 12, 5), (64, 2, 3), (17, 4, 2), (100, 2, 2)])
+def test_mha_images_fused_qkv(dev, T, H, n_img):
+    """tcg_mha_images: n_img images whose q, k, v share one fused row of width
+    3D, written as fp32 and as the tf32 hi/lo pair in one call; hi has tf32's
+    10 mantissa bits and hi + lo is the fp32 output to 21 bits."""
+    L = tcg.lib()
+    D = H * 64
+    rng = np.random.default_rng(T * n_img)
+    qkv = rng.standard_normal((n_img * T, 3 * D)).astype(np.float32)
+    y, hi, lo = dev.empty(n_img * T * D), dev.empty(n_img * T * D), dev.empty(n_img * T * D)
+    tcg.check(L.tcg_mha_images(y.ptr, hi.ptr, lo.ptr, dev.put(qkv), T, H, 64, n_img))
+    got = y.download((n_img * T, D))
+    h, l = hi.download((n_img * T, D)), lo.download((n_img * T, D))
+    assert np.all(np.abs((h.astype(np.float64) + l) - got) <= np.abs(got) * 2.0 ** -21)
+    assert np.all((h.view(np.uint32) & 0x1FFF) == 0)
+    for i in range(n_img):
+        r = qkv[i * T:(i + 1) * T]
+        want = oracle.mha(r[:, :D].copy(), r[:, D:2 * D].copy(), r[:, 2 * D:].copy(), T, H, 64)
+        assert np.abs(got[i * T:(i + 1) * T] - want).max() <= 1e-5 * np.abs(want).max(), i
+    assert not L.tcg_mha_images(None, hi.ptr, None, dev.put(qkv), T, H, 64, n_img)
+
+
 @pytest.mark.parametrize("T,H", [(65, 2), (100, 3), (257, 2), (300, 1), (577, 2)])
 def test_mha_long_sequence_kernels_agree(dev, T, H):
     """head_dim 64, T > 64. The streamed-K/V kernel (64- or 48-query blocks)
