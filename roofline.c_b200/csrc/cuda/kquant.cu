@@ -591,7 +591,8 @@ matvec_stream_kernel(const uint8_t *__restrict__ W, const float *__restrict__ x,
     cp_wait0();
 }
 
-int g_mv_last = 0;         // kernel of the latest matvec: 2 segment stream, 3 staged, 4 tensor cores
+int g_mv_last = 0;         // kernel of the latest matvec: 2 segment stream, 3 staged, 4 tensor cores,
+                           // 5 Q4_K integer mma.sync, 6 Q6_K integer mma.sync
 
 template <int TYPE, int SEGS, int NSLOT, int ROWS>
 static bool launch_matvec_stream(float *y, const void *W, const float *x, int N, int K, size_t smem)
@@ -654,6 +655,7 @@ static bool launch_matvec(float *y, const void *W, const float *x, int N, int K)
 
 bool launch_matvec_tc_q4k(float *y, const void *W, const float *x, int N, int K, bool *used);   // mv_tc.cu
 bool launch_matvec_mma_q4k(float *y, const void *W, const float *x, int N, int K, bool *used);  // mv_mma.cu
+bool launch_matvec_mma_q6k(float *y, const void *W, const float *x, int N, int K, bool *used);  // mv_mma.cu
 
 template <int TYPE>
 static bool matvec_dispatch(float *y, const void *W, const float *x, int N, int K)
@@ -671,6 +673,14 @@ static bool matvec_dispatch(float *y, const void *W, const float *x, int N, int 
         if (!launch_matvec_mma_q4k(y, W, x, N, K, &used)) return false;
         if (used) {
             g_mv_last = 5;
+            return true;
+        }
+    } else {
+        // Q6_K on the integer mma.sync kernel where rows are whole 8-superblock segments
+        bool used = false;
+        if (!launch_matvec_mma_q6k(y, W, x, N, K, &used)) return false;
+        if (used) {
+            g_mv_last = 6;
             return true;
         }
     }

@@ -59,6 +59,13 @@ namespace {
 constexpr int MM_WARPS = 16;
 constexpr int MM_BB = 144;                  // Q4_K bytes per superblock
 constexpr int MM_XSB = 1024 + 32 + 16;      // shared bytes per superblock of x: pieces, 8 sums, scale (+pad)
+constexpr int MQ_BB = 210;                  // Q6_K bytes per superblock
+constexpr int MQ_SPB = 8;                   // Q6_K superblocks per unit: 1680 bytes, a whole number of 16
+constexpr int MQ_XSB = 1024 + 256 + 16;     // Q6_K: pieces, -32 x (sum) per (group, half, piece), scale
+
+template <int QT> struct MmType;
+template <> struct MmType<4> { static constexpr int BB = MM_BB, XSB = MM_XSB; };
+template <> struct MmType<6> { static constexpr int BB = MQ_BB, XSB = MQ_XSB; };
 
 // D = A B over one sub-block: A u8 16 x 32 (a0: row g, k 4t..4t+3; a1: row
 // g+8; a2, a3: k 16+4t..), B s8 32 x 8 (b0: k 4t..4t+3 of column g, b1: k
@@ -153,6 +160,112 @@ __device__ __forceinline__ void sb_dot(const Sb &s, const uint8_t *xsb, int g, i
     acc1 = fmaf(-dm1, fmaf(small_int_float(byte_of(m1, bm)), X.x, small_int_float(byte_of(m1, bm + 1)) * X.y), acc1);
 }
 
+// D = A B + C over one 32-weight group (layouts of mma_u8s8)
+__device__ __forceinline__ void mma_u8s8_c(int d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1, int c0, int c1)
+{
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+                 "{%8, %9}, {%10, %11, %10, %11};"
+                 : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
+}
+
+// prmt with selector sel as PTX defines it: bit 3 of a selector nibble
+// replicates the sign of the byte chosen by its bits 0-2 (the __byte_perm
+// intrinsic reads bits 0-2 only)
+__device__ __forceinline__ uint32_t prmt_s(uint32_t a, uint32_t sel)
+{
+    uint32_t r;
+    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(a), "r"(sel));
+    return r;
+}
+
+// Four bytes of shared memory at p. A Q6_K superblock is 210 bytes, so the
+// odd ones of a unit start 2 bytes past a word boundary: two aligned words
+// and a byte permute.
+template <bool ODD>
+__device__ __forceinline__ uint32_t ld_q6(const uint8_t *p)
+{
+    if constexpr (!ODD) {
+        return *reinterpret_cast<const uint32_t *>(p);
+    } else {
+        const uint32_t *w = reinterpret_cast<const uint32_t *>(p - 2);
+        return __byte_perm(w[0], w[1], 0x5432u);
+    }
+}
+
+// Q6_K superblock (src/dequant.c:40-63 with ggml's block: ql[128] low
+// nibbles, qh[64] high bit pairs, 16 int8 scales, fp16 d; weight 128h + 32j
+// + l = d * sc[8h + 2j + l/16] * (q - 32), q = nibble of ql[64h + 32(j&1) +
+// l] (low for j < 2) | bits 2j, 2j+1 of qh[32h + l] << 4). Group gi = 4h + j
+// holds 32 consecutive weights, the x sub-block gi of the pieces. One MMA
+// per group: A = q of rows g, g+8 (a0/a1 k 4t.., a2/a3 k 16+4t..); B
+// columns 0-3 the pieces of x at k < 16 (zero above), columns 4-7 the pieces
+// at k >= 16, so column c sums one 16-weight scale half (c / 4) times piece
+// c % 4; C = -32 (sum of that half's piece) makes it the sum of (q - 32) x
+// exactly. Lane (g, t) holds columns 2t, 2t+1: half s = t / 2, pieces 2(t%2),
+// 2(t%2)+1, multiplied by the rows' scale of (gi, s) in 32-bit integers
+// (|.| < 2^27 over the superblock), then converted once.
+template <bool ODD>
+__device__ __forceinline__ void sb6_dot(const uint8_t *r0, const uint8_t *r1, const uint8_t *xsb, int g, int t,
+                                        float &acc0, float &acc1)
+{
+    const int s = t >> 1;
+    uint32_t l0[2][2][2], l1[2][2][2], h0[2][2], h1[2][2];      // ql [h][j&1][k half], qh [h][k half]
+#pragma unroll
+    for (int h = 0; h < 2; h++)
+#pragma unroll
+        for (int kh = 0; kh < 2; kh++) {
+#pragma unroll
+            for (int jl = 0; jl < 2; jl++) {
+                l0[h][jl][kh] = ld_q6<ODD>(r0 + 64 * h + 32 * jl + 16 * kh + 4 * t);
+                l1[h][jl][kh] = ld_q6<ODD>(r1 + 64 * h + 32 * jl + 16 * kh + 4 * t);
+            }
+            h0[h][kh] = ld_q6<ODD>(r0 + 128 + 32 * h + 16 * kh + 4 * t);
+            h1[h][kh] = ld_q6<ODD>(r1 + 128 + 32 * h + 16 * kh + 4 * t);
+        }
+    uint32_t w0[4], w1[4];                                      // the 16 scales
+#pragma unroll
+    for (int w = 0; w < 4; w++) {
+        w0[w] = ld_q6<ODD>(r0 + 192 + 4 * w);
+        w1[w] = ld_q6<ODD>(r1 + 192 + 4 * w);
+    }
+    // scale byte 2gi + s: byte s of the word's even half, 2 + s of its odd half, sign-extended
+    const uint32_t se = 0x8880u | 0x1110u * (uint32_t)s;
+    const uint32_t sel_even = se | (uint32_t)s, sel_odd = (se + 0x2220u) | (uint32_t)(2 + s);
+    int acc[4] = { 0, 0, 0, 0 };
+#pragma unroll
+    for (int gi = 0; gi < 8; gi++) {
+        const int h = gi >> 2, j = gi & 3;
+        const auto qword = [&](uint32_t wl, uint32_t wh) {
+            const uint32_t nib = j < 2 ? wl : wl >> 4;
+            const uint32_t hb = (j < 3 ? wh << (4 - 2 * j) : wh >> 2) & 0x30303030u;
+            return (nib & 0x0F0F0F0Fu) | hb;
+        };
+        const uint32_t a0 = qword(l0[h][j & 1][0], h0[h][0]), a1 = qword(l1[h][j & 1][0], h1[h][0]);
+        const uint32_t a2 = qword(l0[h][j & 1][1], h0[h][1]), a3 = qword(l1[h][j & 1][1], h1[h][1]);
+        const uint32_t bw = *reinterpret_cast<const uint32_t *>(xsb + gi * 128 + (g & 3) * 32 + (g >> 2) * 16 + 4 * t);
+        const int2 cx = *reinterpret_cast<const int2 *>(xsb + 1024 + (2 * gi + s) * 16 + 8 * (t & 1));
+        int d[4];
+        mma_u8s8_c(d, a0, a1, a2, a3, g < 4 ? bw : 0u, g < 4 ? 0u : bw, cx.x, cx.y);
+        const uint32_t sel = (gi & 1) ? sel_odd : sel_even;
+        const int sc0 = (int)prmt_s(w0[gi >> 1], sel), sc1 = (int)prmt_s(w1[gi >> 1], sel);
+        acc[0] += d[0] * sc0;
+        acc[1] += d[1] * sc0;
+        acc[2] += d[2] * sc1;
+        acc[3] += d[3] * sc1;
+    }
+    // columns 2t, 2t+1 = pieces (0, 1) for even t, (2, 3) for odd t:
+    // x = (p0 + p1/2^7 + p2/2^14 + p3/2^21) 2^(e-6), 2^(e-13) stored
+    const float xe = *reinterpret_cast<const float *>(xsb + 1280);
+    const float k = (t & 1) ? 6.103515625e-05f : 1.0f;                     // 2^-14 : 1
+    const float f0 = fmaf((float)acc[0], 128.0f, (float)acc[1]), f1 = fmaf((float)acc[2], 128.0f, (float)acc[3]);
+    const float d0 = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(r0 + 208)));
+    const float d1 = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(r1 + 208)));
+    acc0 = fmaf(f0 * xe, d0 * k, acc0);
+    acc1 = fmaf(f1 * xe, d1 * k, acc1);
+}
+
 constexpr int MM_THREADS = MM_WARPS * 32 + 32;   // sixteen consumer warps and the producer warp
 
 // fetch-and-add with release (the warp's partial sums, ordered before it by
@@ -171,6 +284,13 @@ __device__ __forceinline__ void tma_load3(uint32_t dst, const CUtensorMap *map, 
                  ::"r"(dst), "l"((unsigned long long)map), "r"(x), "r"(y), "r"(z), "r"(bar) : "memory");
 }
 
+__device__ __forceinline__ void tma_load2(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y)
+{
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%2, %3}], [%4];"
+                 ::"r"(dst), "l"((unsigned long long)map), "r"(x), "r"(y), "r"(bar) : "memory");
+}
+
 __device__ __forceinline__ void load_sb_smem(Sb &s, const uint8_t *r0, const uint8_t *r1, int t)
 {
     s.h0 = *reinterpret_cast<const uint4 *>(r0);
@@ -183,12 +303,16 @@ __device__ __forceinline__ void load_sb_smem(Sb &s, const uint8_t *r0, const uin
 }
 
 // Shared memory: x pieces (nsl superblocks), nslot unit slots of 16 rows x rs
-// bytes, then the slots' full and empty barriers and the abort flag.
+// bytes, then the slots' full and empty barriers and the abort flag. QT 4:
+// Q4_K, a 3-D tensor copy per unit; QT 6: Q6_K, a 2-D one (8-byte elements,
+// 210 per 8-superblock row segment).
+template <int QT>
 __global__ void __launch_bounds__(MM_THREADS, 1)
-mv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restrict__ x, float *__restrict__ y,
-                  int N, int nsb, int spb, int S, int tiles, long long U, float *ws, int *cnt, int nslot, int nwork,
-                  uint32_t sigma, int x_bytes, int early, int *err)
+mv_kq_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restrict__ x, float *__restrict__ y,
+                 int N, int nsb, int spb, int S, int tiles, long long U, float *ws, int *cnt, int nslot, int nwork,
+                 int hs, uint32_t sigma, int x_bytes, int early, int *err)
 {
+    constexpr int BB = MmType<QT>::BB, XSB = MmType<QT>::XSB;
     extern __shared__ __align__(128) uint8_t smx[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
@@ -197,16 +321,21 @@ mv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restr
     const int seg_lo = (int)(u0 / tiles);
     const int sb0 = seg_lo * spb;                                   // first superblock of x this CTA holds
     const int nsl = min((int)((u1 - 1) / tiles + 1) * spb, nsb) - sb0;   // superblocks of x it holds
-    const int rs = spb * MM_BB;                                     // slot row stride
+    const int rs = spb * BB;                                        // slot row stride
     uint8_t *slots = smx + x_bytes;
     uint64_t *bars = reinterpret_cast<uint64_t *>(slots + (size_t)nslot * 16 * rs);
     const uint32_t full0 = su32(bars), empty0 = su32(bars + nslot);
     volatile int *abort = reinterpret_cast<volatile int *>(bars + 2 * nslot);
+    // whole-row units read by hs warps: their partial sums meet here, two
+    // buffers per owner (alternate units), hs x 16 rows each
+    float *cmb = reinterpret_cast<float *>(bars + 2 * nslot + 2);
+    // Q6_K slots hold spb / 8 boxes of 16 rows x 1680 bytes one after another
+    constexpr int RB = QT == 4 ? 0 : MQ_SPB * MQ_BB;                // bytes of a box row (Q6_K)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < nslot; s++) {
             bar_init(full0 + 8 * s, 1);
-            bar_init(empty0 + 8 * s, 1);
+            bar_init(empty0 + 8 * s, hs);                           // the hs warps sharing the slot
         }
         *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -223,7 +352,13 @@ mv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restr
                 const int seg = (int)(u / tiles), tile = (int)(u % tiles);
                 const uint32_t fb = full0 + 8 * (k % nslot);
                 bar_expect_tx(fb, (uint32_t)(16 * rs));
-                tma_load3(su32(slots + (size_t)(k % nslot) * 16 * rs), &wmap, fb, 0, seg * spb, tile * 16);
+                if constexpr (QT == 4) {
+                    tma_load3(su32(slots + (size_t)(k % nslot) * 16 * rs), &wmap, fb, 0, seg * spb, tile * 16);
+                } else {
+                    for (int b = 0; b < spb / MQ_SPB; b++)
+                        tma_load2(su32(slots + (size_t)(k % nslot) * 16 * rs + (size_t)b * 16 * RB), &wmap, fb,
+                                  (seg * (spb / MQ_SPB) + b) * (RB / 8), tile * 16);
+                }
             };
             int k = 0;
             // With early set, the caller guarantees that no kernel before this
@@ -266,8 +401,9 @@ mv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restr
         if (mx > 0.0f) frexpf(mx, &e);                              // max|x| < 2^e
         e = max(e, -110);                                           // keeps 2^(e-13) and 2^(6-e) normal floats
         const float sc = __uint_as_float((uint32_t)(127 + 6 - e) << 23);   // 2^(6-e): |v sc| < 64
-        uint8_t *xsb = smx + (size_t)i * MM_XSB;
+        uint8_t *xsb = smx + (size_t)i * XSB;
         uint32_t pw[4][2];
+        int psum[4] = { 0, 0, 0, 0 };                               // this lane's sum of each piece
 #pragma unroll
         for (int h = 0; h < 2; h++) {
             float r[4], p[4][4];
@@ -281,23 +417,42 @@ mv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restr
                     r[k] = (r[k] - p[piece][k]) * 128.0f;           // exact; |r| <= 64
                 }
 #pragma unroll
-            for (int piece = 0; piece < 4; piece++) pw[piece][h] = pack4(p[piece][0], p[piece][1], p[piece][2], p[piece][3]);
+            for (int piece = 0; piece < 4; piece++) {
+                pw[piece][h] = pack4(p[piece][0], p[piece][1], p[piece][2], p[piece][3]);
+                if constexpr (QT == 6)
+                    psum[piece] += __float2int_rn(p[piece][0]) + __float2int_rn(p[piece][1]) +
+                                   __float2int_rn(p[piece][2]) + __float2int_rn(p[piece][3]);
+            }
         }
         const int j = lane >> 2, pos = 8 * (lane & 3);
 #pragma unroll
         for (int piece = 0; piece < 4; piece++)
             *reinterpret_cast<uint2 *>(xsb + j * 128 + piece * 32 + pos) = make_uint2(pw[piece][0], pw[piece][1]);
-        if ((lane & 3) == 0) reinterpret_cast<float *>(xsb + 1024)[j] = sum;
-        if (lane == 0) *reinterpret_cast<float *>(xsb + 1024 + 32) = __uint_as_float((uint32_t)(127 + e - 13) << 23);
+        const float xe = __uint_as_float((uint32_t)(127 + e - 13) << 23);
+        if constexpr (QT == 4) {
+            if ((lane & 3) == 0) reinterpret_cast<float *>(xsb + 1024)[j] = sum;
+            if (lane == 0) *reinterpret_cast<float *>(xsb + 1024 + 32) = xe;
+        } else {
+            // -32 (sum of each piece over a 16-weight half): lanes 2s, 2s+1 of a group's four
+#pragma unroll
+            for (int piece = 0; piece < 4; piece++) psum[piece] += __shfl_xor_sync(0xFFFFFFFFu, psum[piece], 1);
+            if ((lane & 1) == 0)
+                *reinterpret_cast<int4 *>(xsb + 1024 + (2 * j + ((lane >> 1) & 1)) * 16) =
+                    make_int4(-32 * psum[0], -32 * psum[1], -32 * psum[2], -32 * psum[3]);
+            if (lane == 0) *reinterpret_cast<float *>(xsb + 1280) = xe;
+        }
     }
     asm volatile("bar.sync 1, %0;" ::"n"(MM_WARPS * 32) : "memory");    // the consumers only
 
-    // Consumer w takes units w, w + nwork, ...: nslot is a multiple of nwork
-    // (or no slot is reused), so every slot is read by one warp only, in
-    // unit order, and a warp never tests a slot's barrier while an earlier
-    // fill of that slot is still pending (which its parity test would read
-    // as complete).
-    for (int k = warp; warp < nwork && k < nunits; k += nwork) {
+    // Consumers: hs warps per slot owner (part p of a unit's superblocks
+    // each); owner o = w / hs takes units o, o + owners, ...: nslot is a
+    // multiple of owners (or no slot is reused), so every slot is read by
+    // one owner only, in unit order, and a warp never tests a slot's barrier
+    // while an earlier fill of that slot is still pending (which its parity
+    // test would read as complete). Each part is a partial sum of its own:
+    // SP per tile.
+    const int owner = warp / hs, part = warp - owner * hs, owners = nwork / hs, SP = S * hs;
+    for (int k = owner; warp < nwork && k < nunits; k += owners) {
         const long long u = u0 + k;
         const int seg = (int)(u / tiles), tile = (int)(u % tiles);
         const int slot = k % nslot;
@@ -305,14 +460,26 @@ mv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restr
         float acc0 = 0.0f, acc1 = 0.0f;
         const int sg = (int)((sigma >> (3 * g)) & 7u);               // this lane's slot row (and row + 8)
         if (ok) {
-            const uint8_t *r0 = slots + (size_t)slot * 16 * rs + (size_t)sg * rs;
+            const uint8_t *sl = slots + (size_t)slot * 16 * rs;
+            const uint8_t *r0 = sl + (size_t)sg * rs;               // Q4_K rows; Q6_K rows are per box
             const uint8_t *r1 = r0 + (size_t)8 * rs;
-            const uint8_t *xs = smx + (size_t)(seg * spb - sb0) * MM_XSB;
+            const uint8_t *xs = smx + (size_t)(seg * spb - sb0) * XSB;
             const int steps = min(spb, nsb - seg * spb);            // the last segment of a row may be short
-            for (int i = 0; i < steps; i++) {
-                Sb sb;
-                load_sb_smem(sb, r0 + i * MM_BB, r1 + i * MM_BB, t);
-                sb_dot(sb, xs + (size_t)i * MM_XSB, g, t, acc0, acc1);
+            if constexpr (QT == 4) {
+                for (int i = 0; i < steps; i++) {                   // hs is 1
+                    Sb sb;
+                    load_sb_smem(sb, r0 + i * BB, r1 + i * BB, t);
+                    sb_dot(sb, xs + (size_t)i * XSB, g, t, acc0, acc1);
+                }
+            } else {
+                // steps = spb (8 or 16): this part's spb / hs superblocks, an even first one
+                const int i1 = (part + 1) * (steps / hs);
+                for (int i = part * (steps / hs); i < i1; i += 2) {
+                    const uint8_t *q0 = sl + (size_t)(i / MQ_SPB) * 16 * RB + (size_t)sg * RB + (i % MQ_SPB) * BB;
+                    const uint8_t *q1 = q0 + (size_t)8 * RB;
+                    sb6_dot<false>(q0, q1, xs + (size_t)i * XSB, g, t, acc0, acc1);
+                    sb6_dot<true>(q0 + BB, q1 + BB, xs + (size_t)(i + 1) * XSB, g, t, acc0, acc1);
+                }
             }
         }
         __syncwarp();
@@ -323,27 +490,44 @@ mv_q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restr
         acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 2);
         acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 2);
         const int r0 = tile * 16 + sg, r1 = r0 + 8;
-        if (S == 1) {
+        if (SP == 1) {
             if (t == 0) {
                 if (r0 < N) y[r0] = acc0;
                 if (r1 < N) y[r1] = acc1;
             }
             continue;
         }
+        if (S == 1) {
+            // the hs parts of a whole-row unit, summed in part order by part 0
+            float *cb = cmb + ((size_t)owner * 2 + (((k - owner) / owners) & 1)) * hs * 16;
+            if (t == 0) {
+                cb[part * 16 + sg] = acc0;
+                cb[part * 16 + sg + 8] = acc1;
+            }
+            asm volatile("bar.sync %0, %1;" ::"r"(2 + owner), "r"(32 * hs) : "memory");
+            if (part == 0 && lane < 16) {
+                float v = 0.0f;
+                for (int p = 0; p < hs; p++) v += cb[p * 16 + lane];
+                const int r = tile * 16 + lane;
+                if (r < N) y[r] = v;
+            }
+            continue;
+        }
+        const int ps = seg * hs + part;                             // this partial sum's index
         if (t == 0) {
-            if (r0 < N) ws[(size_t)seg * N + r0] = acc0;
-            if (r1 < N) ws[(size_t)seg * N + r1] = acc1;
+            if (r0 < N) ws[(size_t)ps * N + r0] = acc0;
+            if (r1 < N) ws[(size_t)ps * N + r1] = acc1;
         }
         __syncwarp();
         int last = 0;
-        if (lane == 0) last = atom_add_acq_rel(cnt + tile, 1) == S - 1;
+        if (lane == 0) last = atom_add_acq_rel(cnt + tile, 1) == SP - 1;
         last = __shfl_sync(0xFFFFFFFFu, last, 0);
         if (last) {
             __syncwarp();
             const int r = tile * 16 + lane;
             if (lane < 16 && r < N) {
                 float v = 0.0f;
-                for (int s = 0; s < S; s++) v += __ldcg(ws + (size_t)s * N + r);
+                for (int s = 0; s < SP; s++) v += __ldcg(ws + (size_t)s * N + r);
                 y[r] = v;
             }
             if (lane == 0) cnt[tile] = 0;                           // ready for the next call
@@ -367,6 +551,7 @@ int g_mv_mma = 1;          // 1 (default): Q4_K matvec on this kernel where it a
 int g_mv_mma_segs = 0;     // tuning hook: K segments per tile (0: chosen per shape)
 int g_mv_early = 0;        // 1: the caller's weights are never written by the kernel before a matvec
 int g_mv_slots = 0;        // tuning hook: most unit slots per CTA (0: as many as shared memory holds)
+int g_mv_split = 1;        // tuning hook: 0 keeps one warp per Q6_K unit
 
 // Superblocks per unit (the last segment of a row may be shorter): a row of
 // at most 8 superblocks is one unit; otherwise 5-8 superblocks, the fewest
@@ -451,18 +636,35 @@ static uint32_t mm_sigma(int rs)
 // This host thread's tensor map of the latest matrix (and its shape).
 struct MmMap {
     const void *w = nullptr;
-    int n = 0, k = 0, spb = 0;
+    int n = 0, k = 0, spb = 0, qt = 0;
     CUtensorMap map;
 };
 thread_local MmMap g_mm_map[64];
 
-bool launch_matvec_mma_q4k(float *y, const void *W, const float *x, int N, int K, bool *used)
+// The identity row order (sigma(g) = g, three bits each): Q6_K slot rows are
+// 1680 bytes apart (4 banks), so rows g = 0..7 and quad lanes t = 0..3 read
+// 32 distinct banks as they are.
+constexpr uint32_t mm_sigma_identity()
 {
+    uint32_t s = 0;
+    for (int i = 0; i < 8; i++) s |= (uint32_t)i << (3 * i);
+    return s;
+}
+
+template <int QT>
+static bool launch_matvec_mma(float *y, const void *W, const float *x, int N, int K, bool *used)
+{
+    constexpr int BB = MmType<QT>::BB, XSB = MmType<QT>::XSB;
     *used = false;
     if (!g_mv_mma || ((uintptr_t)W & 15) || N <= 0 || K <= 0 || K % 256) return true;
     const int nsb = K / 256, tiles = (N + 15) / 16, sms = ctx().sms > 0 ? ctx().sms : 148;
-    // spb superblocks per unit, S segments per row (the last one may be short)
-    const int spb = g_mv_mma_segs > 0 ? (nsb + g_mv_mma_segs - 1) / g_mv_mma_segs : mm_unit_superblocks(nsb);
+    // Q6_K: a row is a whole number of 1680-byte (8-superblock) segments, so
+    // the rows and the segments start on 16-byte boundaries (TMA's rule)
+    if (QT == 6 && nsb % MQ_SPB) return true;
+    // spb superblocks per unit, S segments per row (the last one may be short);
+    // Q6_K: whole rows of one or two 1680-byte boxes, else 8-superblock segments
+    const int spb = QT == 6 ? (nsb <= 2 * MQ_SPB ? nsb : MQ_SPB)
+                            : g_mv_mma_segs > 0 ? (nsb + g_mv_mma_segs - 1) / g_mv_mma_segs : mm_unit_superblocks(nsb);
     const int S = (nsb + spb - 1) / spb;
     if (spb > 256) return true;                                  // a box holds at most 256 superblocks
     const long long U = (long long)tiles * S;
@@ -476,12 +678,13 @@ bool launch_matvec_mma_q4k(float *y, const void *W, const float *x, int N, int K
         nsl_max = n > nsl_max ? n : nsl_max;
         units_max = (int)(u1 - u0) > units_max ? (int)(u1 - u0) : units_max;
     }
-    const int rs = spb * MM_BB;
+    const int rs = spb * BB;
     const size_t cap = 232448;                                   // the most dynamic shared memory of a CTA
-    const size_t x_bytes = ((size_t)nsl_max * MM_XSB + 127) & ~(size_t)127;
+    const size_t x_bytes = ((size_t)nsl_max * XSB + 127) & ~(size_t)127;
     const size_t slot = (size_t)16 * rs;
-    if (x_bytes + 2 * (slot + 16) + 16 > cap) return true;        // not two slots: the CUDA-core kernels
-    int nslot = (int)((cap - x_bytes - 16) / (slot + 16));
+    const size_t cmb_bytes = QT == 6 ? 8 * 2 * 4 * 16 * 4 : 0;   // combine buffers: <= 8 owners x 2 x 4 parts
+    if (x_bytes + 2 * (slot + 16) + 16 + cmb_bytes > cap) return true;   // not two slots: the CUDA-core kernels
+    int nslot = (int)((cap - x_bytes - 16 - cmb_bytes) / (slot + 16));
     if (g_mv_slots >= 2 && nslot > g_mv_slots) nslot = g_mv_slots;
     // Consumers: nwork warps taking units in turn. A reused slot must belong
     // to one warp, so then nslot is a multiple of nwork.
@@ -495,14 +698,21 @@ bool launch_matvec_mma_q4k(float *y, const void *W, const float *x, int N, int K
     } else {
         nwork = nslot;
     }
-    const size_t smem = x_bytes + (size_t)nslot * slot + (size_t)nslot * 16 + 16;
+    // Q6_K units are long (16 rows x 8 or 16 superblocks of 210 bytes) and
+    // few fit: two or four warps per slot, four superblocks each at least,
+    // where the warps allow (a whole-row unit's parts meet in shared memory)
+    int hs = 1;
+    if (QT == 6 && g_mv_split)
+        while (hs < 4 && 2 * hs * nwork <= MM_WARPS && spb / (2 * hs) >= 4 && (S == 1 || hs < 2)) hs *= 2;
+    nwork *= hs;
+    const size_t smem = x_bytes + (size_t)nslot * slot + (size_t)nslot * 16 + 16 + cmb_bytes;
     float *ws = nullptr;
     int *cnt = nullptr;
     if (S > 1) {
         MmBuf &b = g_mm[ctx().device & 63];
         const int cnt_cap = tiles > b.cnt_cap ? tiles : b.cnt_cap;
         const size_t cnt_bytes = ((size_t)cnt_cap * 4 + 255) & ~(size_t)255;
-        const size_t need = cnt_bytes + (size_t)S * N * 4;
+        const size_t need = cnt_bytes + (size_t)S * hs * N * 4;
         if (need > b.bytes || cnt_cap > b.cnt_cap) {
             if (b.p) {
                 TCG_CUDA(cudaStreamSynchronize(ctx().cur));
@@ -524,42 +734,66 @@ bool launch_matvec_mma_q4k(float *y, const void *W, const float *x, int N, int K
     }
     const int dev = ctx().device & 63;
     MmMap &mp = g_mm_map[dev];
-    if (mp.w != W || mp.n != N || mp.k != K || mp.spb != spb) {
+    if (mp.w != W || mp.n != N || mp.k != K || mp.spb != spb || mp.qt != QT) {
         EncodeFn3 fn = mm_encode_fn();
         if (!fn) return fail("cuTensorMapEncodeTiled is not available from the driver");
-        // 32-bit words: 36 per superblock, nsb superblocks per row, N rows
-        cuuint64_t dims[3] = { (cuuint64_t)(MM_BB / 4), (cuuint64_t)nsb, (cuuint64_t)N };
-        cuuint64_t strides[2] = { (cuuint64_t)MM_BB, (cuuint64_t)nsb * MM_BB };
-        cuuint32_t box[3] = { (cuuint32_t)(MM_BB / 4), (cuuint32_t)spb, 16 };
-        cuuint32_t estr[3] = { 1, 1, 1 };
-        const CUresult r = fn(&mp.map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, (void *)W, dims, strides, box, estr,
-                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        CUresult r;
+        if constexpr (QT == 4) {
+            // 32-bit words: 36 per superblock, nsb superblocks per row, N rows
+            cuuint64_t dims[3] = { (cuuint64_t)(BB / 4), (cuuint64_t)nsb, (cuuint64_t)N };
+            cuuint64_t strides[2] = { (cuuint64_t)BB, (cuuint64_t)nsb * BB };
+            cuuint32_t box[3] = { (cuuint32_t)(BB / 4), (cuuint32_t)spb, 16 };
+            cuuint32_t estr[3] = { 1, 1, 1 };
+            r = fn(&mp.map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, (void *)W, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        } else {
+            // 8-byte elements: nsb * 210 / 8 per row, N rows; a box is 1680 bytes (8 superblocks) of 16 rows
+            cuuint64_t dims[2] = { (cuuint64_t)nsb * BB / 8, (cuuint64_t)N };
+            cuuint64_t strides[1] = { (cuuint64_t)nsb * BB };
+            cuuint32_t box[2] = { (cuuint32_t)(MQ_SPB * BB / 8), 16 };
+            cuuint32_t estr[2] = { 1, 1 };
+            r = fn(&mp.map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, (void *)W, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        }
         if (r != CUDA_SUCCESS) {
             mp.w = nullptr;
-            return fail("cuTensorMapEncodeTiled failed (%d) for the Q4_K matrix [%d x %d]", (int)r, N, K);
+            return fail("cuTensorMapEncodeTiled failed (%d) for the Q%d_K matrix [%d x %d]", (int)r, QT, N, K);
         }
         mp.w = W;
         mp.n = N;
         mp.k = K;
         mp.spb = spb;
+        mp.qt = QT;
     }
     static unsigned done[64];
-    if (!done[dev]) {
-        TCG_CUDA(cudaFuncSetAttribute(mv_q4k_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cap));
-        done[dev] = 1;
+    if (!(done[dev] & (1u << QT))) {
+        TCG_CUDA(cudaFuncSetAttribute(mv_kq_mma_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cap));
+        done[dev] |= 1u << QT;
     }
-    TCG_CUDA(launch_pdl(mv_q4k_mma_kernel, dim3(G), dim3(MM_THREADS), smem, ctx().cur, mp.map, x, y, N, nsb, spb, S,
-                        tiles, U, ws, cnt, nslot, nwork, mm_sigma(rs), (int)x_bytes, g_mv_early, ctx().d_err));
+    const uint32_t sigma = QT == 4 ? mm_sigma(rs) : mm_sigma_identity();
+    TCG_CUDA(launch_pdl(mv_kq_mma_kernel<QT>, dim3(G), dim3(MM_THREADS), smem, ctx().cur, mp.map, x, y, N, nsb, spb,
+                        S, tiles, U, ws, cnt, nslot, nwork, hs, sigma, (int)x_bytes, g_mv_early, ctx().d_err));
     *used = true;
     return true;
 }
 
+bool launch_matvec_mma_q4k(float *y, const void *W, const float *x, int N, int K, bool *used)
+{
+    return launch_matvec_mma<4>(y, W, x, N, K, used);
+}
+
+bool launch_matvec_mma_q6k(float *y, const void *W, const float *x, int N, int K, bool *used)
+{
+    return launch_matvec_mma<6>(y, W, x, N, K, used);
+}
+
 }  // namespace tcg
 
-// Tuning and test hook: 1 (default) runs the Q4_K matvec on the integer
-// mma.sync kernel where it applies, 0 on the CUDA-core kernels. Returns the
-// previous setting.
+// Tuning and test hook: 1 (default) runs the Q4_K and Q6_K matvecs on the
+// integer mma.sync kernel where it applies, 0 on the CUDA-core kernels.
+// Returns the previous setting.
 extern "C" int tcg_matvec_set_mma(int on)
 {
     const int old = tcg::g_mv_mma;
@@ -596,5 +830,15 @@ extern "C" int tcg_matvec_mma_slots(int n)
 {
     const int old = tcg::g_mv_slots;
     tcg::g_mv_slots = n >= 2 ? n : 0;
+    return old;
+}
+
+// Tuning hook: 1 (default) lets two warps share a Q6_K unit (four
+// superblocks each) when the slots leave warps idle; 0 keeps one warp per
+// unit. Returns the previous setting.
+extern "C" int tcg_matvec_mma_split(int on)
+{
+    const int old = tcg::g_mv_split;
+    tcg::g_mv_split = on ? 1 : 0;
     return old;
 }

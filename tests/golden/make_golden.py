@@ -143,10 +143,21 @@ def bench_indices(batch: int) -> list:
     return sorted(idx)
 
 
+# bench.py's default multi-GPU form: rank r encodes a whole batch of its own,
+# pixel seed 1 + r, and checks its first, middle and last image
+WEAK_RANKS = 8
+
+
+def weak_indices(batch: int) -> list:
+    return [0, batch // 2, batch - 1]
+
+
 def vit_bench_fixture(threads: int = 0):
     """Full-depth embeddings of the benchmark's own models (weights seed 0)
     and batches, from the reference's tc_vit_encode, one image per host
-    thread at a time."""
+    thread at a time: the shard boundaries of the pixel-seed-1 batch split
+    over 1/2/4/8 GPUs, and the first, middle and last image of every rank's
+    own batch (pixel seeds 1..8)."""
     import tempfile
     import threading
     threads = threads or os.cpu_count() or 1
@@ -154,11 +165,19 @@ def vit_bench_fixture(threads: int = 0):
     with tempfile.TemporaryDirectory() as tmp:
         for name, batch, pseed in BENCH_CASES:
             path, cfg = G.cached_vit_gguf(tmp, name, 0)
-            px = G.make_pixels(batch, cfg["image"], pseed)
-            idx = bench_indices(batch)
+            idx, widx = bench_indices(batch), weak_indices(batch)
+            seeds = list(range(pseed, pseed + WEAK_RANKS))
+            jobs = []                                   # (slot, seed, image)
+            for j, i in enumerate(idx):
+                jobs.append((("strong", j), pseed, i))
+            for r, sd in enumerate(seeds):
+                for j, i in enumerate(widx):
+                    jobs.append((("weak", r, j), sd, i))
+            px = {sd: G.make_pixels(batch, cfg["image"], sd) for sd in seeds}
             emb = np.zeros((len(idx), cfg["d_out"]), np.float32)
-            models = [oracle.RefVit(path) for _ in range(min(threads, len(idx)))]
-            todo = list(enumerate(idx))
+            wemb = np.zeros((len(seeds), len(widx), cfg["d_out"]), np.float32)
+            models = [oracle.RefVit(path) for _ in range(min(threads, len(jobs)))]
+            todo = list(jobs)
             lock = threading.Lock()
 
             def work(m):
@@ -166,8 +185,12 @@ def vit_bench_fixture(threads: int = 0):
                     with lock:
                         if not todo:
                             return
-                        j, i = todo.pop()
-                    emb[j] = m.encode(px[i], cfg["d_out"])["embedding"]
+                        slot, sd, i = todo.pop()
+                    e = m.encode(px[sd][i], cfg["d_out"])["embedding"]
+                    if slot[0] == "strong":
+                        emb[slot[1]] = e
+                    else:
+                        wemb[slot[1], slot[2]] = e
 
             ts = [threading.Thread(target=work, args=(m,)) for m in models]
             for t in ts:
@@ -179,7 +202,10 @@ def vit_bench_fixture(threads: int = 0):
             out[f"{name}.index"] = np.array(idx, np.int32)
             out[f"{name}.embedding"] = emb
             out[f"{name}.batch"] = np.array(batch, np.int32)
-            print(f"{name}: {len(idx)} images of a batch of {batch}", flush=True)
+            out[f"{name}.weak_seeds"] = np.array(seeds, np.int32)
+            out[f"{name}.weak_index"] = np.array(widx, np.int32)
+            out[f"{name}.weak_embedding"] = wemb
+            print(f"{name}: {len(idx)} + {wemb.shape[0] * wemb.shape[1]} images of batches of {batch}", flush=True)
     np.savez_compressed(os.path.join(OUT, "vit_bench_golden.npz"), **out)
 
 
@@ -219,9 +245,10 @@ if __name__ == "__main__":
     if not REF or not os.path.isdir(os.path.join(REF, "src")):
         sys.exit("set TC_REFERENCE to the roofline.c source tree (the directory holding src/ and tests/)")
     oracle.build(with_ref=True, ref_dir=REF)
-    ops_fixture()
-    kquant_fixture()
-    vit_fixture()
-    vit_bench_fixture()
-    preprocess_fixture()
+    only = set(sys.argv[1:])            # e.g. "bench": regenerate that fixture alone
+    steps = {"ops": ops_fixture, "kquant": kquant_fixture, "vit": vit_fixture, "bench": vit_bench_fixture,
+             "preprocess": preprocess_fixture}
+    for key, fn in steps.items():
+        if not only or key in only:
+            fn()
     print("golden fixtures written to", OUT)

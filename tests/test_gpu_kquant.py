@@ -139,19 +139,19 @@ def dev_matvec(raw, x, N, K, qt, repeat=1):
     (G.Q6_K, 5000, 512, 10), (G.Q4_K, 70, 4096, 11),
     (G.Q4_K, 4095, 14336, 12),     # odd row count, a partial last CTA iteration
     (G.Q4_K, 9473, 14336, 13),     # long rows, many of them: row pairs, the last pair one row
-    (G.Q6_K, 9473, 14336, 14),     # 210-byte superblocks: no 16-byte segment split, the staged kernel
+    (G.Q6_K, 9473, 14336, 14),     # long rows of 210-byte superblocks
 ])
 def test_matvec_vs_dequant_then_linear(gpu, qt, N, K, seed):
     raw = G.make_kquant(qt, N, K, seed=seed)
     x = np.random.default_rng(seed + 100).standard_normal(K).astype(np.float32)
     got = dev_matvec(raw, x, N, K, qt, repeat=3)
     kernel = tcg.lib().tcg_matvec_last_kernel()
-    # Q4_K runs the integer mma.sync kernel; Q6_K the streaming kernel at the
-    # benchmark shape, else the streaming or the staged one
+    # Q4_K runs the integer mma.sync kernel, Q6_K too where a row is whole
+    # 8-superblock (1680-byte) segments, else the streaming or the staged one
     if qt == G.Q4_K:
         assert kernel == 5, kernel
     else:
-        assert kernel == 2 if (N, K) == (128256, 4096) else kernel in (2, 3), kernel
+        assert kernel == 6 if K % 2048 == 0 else kernel in (2, 3), kernel
     want = oracle.matvec_q(raw, x, N, K, qt)
     err = np.abs(got.astype(np.float64) - want).max() / np.abs(want).max()
     assert err <= MATVEC_TOL, err
@@ -275,6 +275,61 @@ def test_matvec_q4k_mma_segments(gpu, segs):
     finally:
         L.tcg_matvec_mma_segments(old)
     want = oracle.matvec_q(raw, x, N, K, G.Q4_K).astype(np.float64)
+    assert np.abs(got.astype(np.float64) - want).max() / np.abs(want).max() <= MATVEC_TOL
+
+
+@pytest.mark.parametrize("N,K", [
+    (128256, 4096),     # the output head: 2 segments a row, ~108 units per CTA through 7 slots
+    (4096, 14336),      # 7 segments a row
+    (14336, 4096),
+    (4095, 14336),      # a ragged last tile
+    (1, 2048), (17, 2048), (100, 8192), (300, 6144),
+])
+def test_matvec_q6k_mma(gpu, N, K):
+    """The default Q6_K matvec where rows are whole 1680-byte segments:
+    integer mma.sync over the 6-bit q (nibble and high bits merged in
+    registers; odd superblocks 2 bytes off a word boundary), -32 folded into
+    the accumulator input; against the oracle (dequantise, then the
+    reference's linear) and the CUDA-core kernel, on x with wide dynamic
+    range, zero sub-blocks and tiny values; three calls give the same bits."""
+    L = tcg.lib()
+    raw = G.make_kquant(G.Q6_K, N, K, seed=N + 5 * K)
+    cases = _x_cases(K, N * 7 + K)
+    if N * K > 1 << 28:
+        cases = {"wide": cases["wide"]}
+    for name, x in cases.items():
+        got = dev_matvec(raw, x, N, K, G.Q6_K, repeat=3)
+        assert L.tcg_matvec_last_kernel() == 6
+        want = oracle.matvec_q(raw, x, N, K, G.Q6_K).astype(np.float64)
+        scale = np.abs(want).max()
+        assert scale > 0, name
+        err = np.abs(got.astype(np.float64) - want).max() / scale
+        assert err <= MATVEC_TOL, (name, err)
+        old = L.tcg_matvec_set_mma(0)
+        try:
+            cuda_cores = dev_matvec(raw, x, N, K, G.Q6_K)
+            assert L.tcg_matvec_last_kernel() in (2, 3)
+        finally:
+            L.tcg_matvec_set_mma(old)
+        assert np.abs(cuda_cores.astype(np.float64) - got).max() / scale <= 2 * MATVEC_TOL, name
+
+
+@pytest.mark.parametrize("split", [0, 1])
+@pytest.mark.parametrize("N,K", [(14336, 4096), (1000, 16384)])
+def test_matvec_q6k_mma_split(gpu, split, N, K):
+    """Q6_K units read by one warp, or by two warps (four superblocks each,
+    two partial sums per segment): the same result within rounding, each
+    against the oracle, three calls giving the same bits."""
+    L = tcg.lib()
+    raw = G.make_kquant(G.Q6_K, N, K, seed=41 + N)
+    x = _x_cases(K, 77)["wide"]
+    old = L.tcg_matvec_mma_split(split)
+    try:
+        got = dev_matvec(raw, x, N, K, G.Q6_K, repeat=3)
+        assert L.tcg_matvec_last_kernel() == 6
+    finally:
+        L.tcg_matvec_mma_split(old)
+    want = oracle.matvec_q(raw, x, N, K, G.Q6_K).astype(np.float64)
     assert np.abs(got.astype(np.float64) - want).max() / np.abs(want).max() <= MATVEC_TOL
 
 

@@ -1,8 +1,11 @@
 """The ViT forward at the shapes the benchmark times, against the
 reference's own outputs.
 
-bench.py times ViT-B/32 at batch 256 on one GPU and 128 / 64 / 32 images
-per GPU on 2 / 4 / 8 GPUs, and ViT-L/14 at batch 128 (16 per GPU on 8).
+bench.py times ViT-B/32 with a batch of 256 images per GPU, rank r's pixels
+drawn with seed 1 + r (ViT-L/14: 128 per GPU); with --strong one batch of
+256 is split into 128 / 64 / 32 images per GPU on 2 / 4 / 8 GPUs (ViT-L/14:
+16 per GPU on 8). Both forms are covered: every rank's own batch, and the
+shards of the seed-1 batch.
 Every one of those batch sizes plans its GEMMs differently (tile shapes,
 the one-wave rule, the stream-K split of the last wave) and ViT-L/14 runs
 the tensor-core attention with its one-row tail. Here each of those
@@ -86,3 +89,39 @@ def test_b32_bench_shards_full_depth_vs_reference(gpu, cache_dir, per):
 @pytest.mark.parametrize("per", [128, 16])
 def test_l14_bench_shards_full_depth_vs_reference(gpu, cache_dir, per):
     _run_shards(cache_dir, "vit-l14", per)
+
+
+def _run_rank_batches(cache_dir, name):
+    """Every rank's own batch of bench.py's default form (pixel seed 1 + r,
+    r < 8), one upload: first, middle and last image against the reference."""
+    g = vit_bench_golden()
+    seeds, widx, wref = g[f"{name}.weak_seeds"], g[f"{name}.weak_index"], g[f"{name}.weak_embedding"]
+    batch = int(g[f"{name}.batch"])
+    path, cfg = G.cached_vit_gguf(cache_dir, name, 0)
+    L = tcg.lib()
+    m = tcg.VitModel(path)
+    try:
+        m.upload(batch)
+        d_out = cfg["d_out"]
+        with tcg.DeviceBuffer(batch * 3 * cfg["image"] ** 2 * 4) as dpx, tcg.DeviceBuffer(batch * d_out * 4) as dout:
+            for r, sd in enumerate(seeds):
+                dpx.upload(G.make_pixels(batch, cfg["image"], int(sd)))
+                tcg.check(L.tcg_vit_encode_device(m.dev, dpx.ptr, batch, dout.ptr), "tcg_vit_encode_device")
+                tcg.sync()
+                out = dout.download((batch, d_out))
+                for j, i in enumerate(widx):
+                    e = rel_inf(out[i], wref[r, j])
+                    assert e <= TOL, (name, int(sd), int(i), e)
+                    assert cosine(out[i], wref[r, j]) >= 0.9999, (name, int(sd), int(i))
+        assert L.tcg_device_error() == 0
+    finally:
+        m.close()
+
+
+def test_b32_rank_batches_full_depth_vs_reference(gpu, cache_dir):
+    _run_rank_batches(cache_dir, "vit-b32")
+
+
+@pytest.mark.slow
+def test_l14_rank_batches_full_depth_vs_reference(gpu, cache_dir):
+    _run_rank_batches(cache_dir, "vit-l14")
