@@ -310,17 +310,32 @@ template <int QT>
 __global__ void __launch_bounds__(MM_THREADS, 1)
 mv_kq_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restrict__ x, float *__restrict__ y,
                  int N, int nsb, int spb, int S, int tiles, long long U, float *ws, int *cnt, int nslot, int nwork,
-                 int hs, uint32_t sigma, int x_bytes, int early, int *err)
+                 int hs, int tm, uint32_t sigma, int x_bytes, int early, int *err)
 {
     constexpr int BB = MmType<QT>::BB, XSB = MmType<QT>::XSB;
     extern __shared__ __align__(128) uint8_t smx[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
+    // Units: segment-major, one contiguous range of them per CTA (tm 0), or
+    // whole tiles per CTA, tile-major (tm 1: a tile's segments meet in
+    // shared memory)
     const long long u0 = U * blockIdx.x / gridDim.x, u1 = U * (blockIdx.x + 1) / gridDim.x;
-    const int nunits = (int)(u1 - u0);
-    const int seg_lo = (int)(u0 / tiles);
+    const int T0 = (int)((long long)tiles * blockIdx.x / gridDim.x);
+    const int T1 = (int)((long long)tiles * (blockIdx.x + 1) / gridDim.x);
+    const int nunits = tm ? (T1 - T0) * S : (int)(u1 - u0);
+    const int seg_lo = tm ? 0 : (int)(u0 / tiles);
     const int sb0 = seg_lo * spb;                                   // first superblock of x this CTA holds
-    const int nsl = min((int)((u1 - 1) / tiles + 1) * spb, nsb) - sb0;   // superblocks of x it holds
+    const int nsl = tm ? nsb : min((int)((u1 - 1) / tiles + 1) * spb, nsb) - sb0;   // superblocks of x it holds
+    const auto unit_of = [&](int k, int &seg, int &tile) {
+        if (tm) {
+            tile = T0 + k / S;
+            seg = k - (k / S) * S;
+        } else {
+            const long long u = u0 + k;
+            seg = (int)(u / tiles);
+            tile = (int)(u - (long long)seg * tiles);
+        }
+    };
     const int rs = spb * BB;                                        // slot row stride
     uint8_t *slots = smx + x_bytes;
     uint64_t *bars = reinterpret_cast<uint64_t *>(slots + (size_t)nslot * 16 * rs);
@@ -329,6 +344,10 @@ mv_kq_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restri
     // whole-row units read by hs warps: their partial sums meet here, two
     // buffers per owner (alternate units), hs x 16 rows each
     float *cmb = reinterpret_cast<float *>(bars + 2 * nslot + 2);
+    // tm: the partial sums of the CTA's tiles (S * hs x 16 rows each) and
+    // their arrival counters
+    float *tpart = cmb + (QT == 6 ? 8 * 2 * 4 * 16 : 0);
+    int *tcnt = reinterpret_cast<int *>(tpart + (tm ? (size_t)(T1 - T0) * S * hs * 16 : 0));
     // Q6_K slots hold spb / 8 boxes of 16 rows x 1680 bytes one after another
     constexpr int RB = QT == 4 ? 0 : MQ_SPB * MQ_BB;                // bytes of a box row (Q6_K)
 
@@ -340,6 +359,8 @@ mv_kq_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restri
         *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    if (tm)
+        for (int i = threadIdx.x; i < T1 - T0; i += blockDim.x) tcnt[i] = 0;
     __syncthreads();
 
     if (warp == MM_WARPS) {
@@ -348,8 +369,8 @@ mv_kq_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restri
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&wmap) : "memory");
             auto fill = [&](int k) {
-                const long long u = u0 + k;
-                const int seg = (int)(u / tiles), tile = (int)(u % tiles);
+                int seg, tile;
+                unit_of(k, seg, tile);
                 const uint32_t fb = full0 + 8 * (k % nslot);
                 bar_expect_tx(fb, (uint32_t)(16 * rs));
                 if constexpr (QT == 4) {
@@ -453,8 +474,8 @@ mv_kq_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restri
     // SP per tile.
     const int owner = warp / hs, part = warp - owner * hs, owners = nwork / hs, SP = S * hs;
     for (int k = owner; warp < nwork && k < nunits; k += owners) {
-        const long long u = u0 + k;
-        const int seg = (int)(u / tiles), tile = (int)(u % tiles);
+        int seg, tile;
+        unit_of(k, seg, tile);
         const int slot = k % nslot;
         const bool ok = bar_wait(full0 + 8 * slot, (uint32_t)((k / nslot) & 1), abort, err, 0x4D4D03);
         float acc0 = 0.0f, acc1 = 0.0f;
@@ -514,6 +535,32 @@ mv_kq_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restri
             continue;
         }
         const int ps = seg * hs + part;                             // this partial sum's index
+        if (tm) {
+            // the last of the tile's SP parts in this CTA sums them in order
+            const int tl = tile - T0;
+            float *tp = tpart + ((size_t)tl * SP + ps) * 16;
+            if (t == 0) {
+                tp[sg] = acc0;
+                tp[sg + 8] = acc1;
+            }
+            __syncwarp();
+            int last = 0;
+            if (lane == 0) {
+                __threadfence_block();
+                last = atomicAdd(tcnt + tl, 1) == SP - 1;
+            }
+            last = __shfl_sync(0xFFFFFFFFu, last, 0);
+            if (last) {
+                __threadfence_block();
+                const int r = tile * 16 + lane;
+                if (lane < 16 && r < N) {
+                    float v = 0.0f;
+                    for (int q = 0; q < SP; q++) v += tpart[((size_t)tl * SP + q) * 16 + lane];
+                    y[r] = v;
+                }
+            }
+            continue;
+        }
         if (t == 0) {
             if (r0 < N) ws[(size_t)ps * N + r0] = acc0;
             if (r1 < N) ws[(size_t)ps * N + r1] = acc1;
@@ -552,6 +599,15 @@ int g_mv_mma_segs = 0;     // tuning hook: K segments per tile (0: chosen per sh
 int g_mv_early = 0;        // 1: the caller's weights are never written by the kernel before a matvec
 int g_mv_slots = 0;        // tuning hook: most unit slots per CTA (0: as many as shared memory holds)
 int g_mv_split = 1;        // tuning hook: 0 keeps one warp per Q6_K unit
+int g_mv_tiles = -1;       // tuning hook: 1 whole tiles per CTA, 0 segment-major ranges, -1 by shape
+
+// Tiles from which whole tiles go to each CTA (tile-major, no global
+// partial sums): six per SM at least, so that shares differ by 1/6 at most
+// (measured back to back on B200: Q4_K 14336 x 4096, 896 tiles, 13.4 ->
+// 12.1 us; with fewer tiles per SM the imbalance and preparing all of x
+// cost more than the global partial sums: 4096 x 14336 13.6 -> 16.5 us,
+// 9473 x 14336 23.6 -> 28.4 us, Q6_K 4096 x 14336 16.4 -> 19.8 us).
+static int mm_tile_major_min(int sms) { return 6 * sms; }
 
 // Superblocks per unit (the last segment of a row may be shorter): a row of
 // at most 8 superblocks is one unit; otherwise 5-8 superblocks, the fewest
@@ -668,21 +724,35 @@ static bool launch_matvec_mma(float *y, const void *W, const float *x, int N, in
     const int S = (nsb + spb - 1) / spb;
     if (spb > 256) return true;                                  // a box holds at most 256 superblocks
     const long long U = (long long)tiles * S;
-    const int G = (int)(U < sms ? U : sms);
+    // whole tiles per CTA (their segments summed in shared memory) where a
+    // row has several segments and the tiles spread over every SM
+    const int tm = S > 1 && (g_mv_tiles == 1 || (g_mv_tiles < 0 && tiles >= mm_tile_major_min(sms))) ? 1 : 0;
+    const int G = tm ? (tiles < sms ? tiles : sms) : (int)(U < sms ? U : sms);
     // the most superblocks of x, and units, one CTA holds
-    int nsl_max = 0, units_max = 0;
+    int nsl_max = 0, units_max = 0, tiles_max = 0;
     for (int c = 0; c < G; c++) {
+        if (tm) {
+            const int n = (int)((long long)tiles * (c + 1) / G - (long long)tiles * c / G);
+            tiles_max = n > tiles_max ? n : tiles_max;
+            continue;
+        }
         const long long u0 = U * c / G, u1 = U * (c + 1) / G;
         const int first = (int)(u0 / tiles) * spb, last = (int)((u1 - 1) / tiles + 1) * spb;
         const int n = (last < nsb ? last : nsb) - first;
         nsl_max = n > nsl_max ? n : nsl_max;
         units_max = (int)(u1 - u0) > units_max ? (int)(u1 - u0) : units_max;
     }
+    if (tm) {
+        nsl_max = nsb;
+        units_max = tiles_max * S;
+    }
     const int rs = spb * BB;
     const size_t cap = 232448;                                   // the most dynamic shared memory of a CTA
     const size_t x_bytes = ((size_t)nsl_max * XSB + 127) & ~(size_t)127;
     const size_t slot = (size_t)16 * rs;
-    const size_t cmb_bytes = QT == 6 ? 8 * 2 * 4 * 16 * 4 : 0;   // combine buffers: <= 8 owners x 2 x 4 parts
+    // combine buffers: <= 8 owners x 2 x 4 parts (Q6_K whole rows); tm: the
+    // tiles' partial sums (at most two parts per segment) and counters
+    const size_t cmb_bytes = (QT == 6 ? 8 * 2 * 4 * 16 * 4 : 0) + (tm ? (size_t)tiles_max * (S * 2 * 16 + 1) * 4 : 0);
     if (x_bytes + 2 * (slot + 16) + 16 + cmb_bytes > cap) return true;   // not two slots: the CUDA-core kernels
     int nslot = (int)((cap - x_bytes - 16 - cmb_bytes) / (slot + 16));
     if (g_mv_slots >= 2 && nslot > g_mv_slots) nslot = g_mv_slots;
@@ -708,7 +778,7 @@ static bool launch_matvec_mma(float *y, const void *W, const float *x, int N, in
     const size_t smem = x_bytes + (size_t)nslot * slot + (size_t)nslot * 16 + 16 + cmb_bytes;
     float *ws = nullptr;
     int *cnt = nullptr;
-    if (S > 1) {
+    if (S > 1 && !tm) {
         MmBuf &b = g_mm[ctx().device & 63];
         const int cnt_cap = tiles > b.cnt_cap ? tiles : b.cnt_cap;
         const size_t cnt_bytes = ((size_t)cnt_cap * 4 + 255) & ~(size_t)255;
@@ -774,7 +844,7 @@ static bool launch_matvec_mma(float *y, const void *W, const float *x, int N, in
     }
     const uint32_t sigma = QT == 4 ? mm_sigma(rs) : mm_sigma_identity();
     TCG_CUDA(launch_pdl(mv_kq_mma_kernel<QT>, dim3(G), dim3(MM_THREADS), smem, ctx().cur, mp.map, x, y, N, nsb, spb,
-                        S, tiles, U, ws, cnt, nslot, nwork, hs, sigma, (int)x_bytes, g_mv_early, ctx().d_err));
+                        S, tiles, U, ws, cnt, nslot, nwork, hs, tm, sigma, (int)x_bytes, g_mv_early, ctx().d_err));
     *used = true;
     return true;
 }
@@ -840,5 +910,16 @@ extern "C" int tcg_matvec_mma_split(int on)
 {
     const int old = tcg::g_mv_split;
     tcg::g_mv_split = on ? 1 : 0;
+    return old;
+}
+
+// Tuning hook: 1 gives every CTA of the integer mma.sync matvec whole tiles
+// (a tile's K segments summed in shared memory), 0 contiguous ranges of
+// segment-major units (split tiles summed through global memory), -1
+// (default) chooses by shape. Returns the previous setting.
+extern "C" int tcg_matvec_mma_tiles(int mode)
+{
+    const int old = tcg::g_mv_tiles;
+    tcg::g_mv_tiles = mode < 0 ? -1 : (mode ? 1 : 0);
     return old;
 }

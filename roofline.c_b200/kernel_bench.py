@@ -133,6 +133,7 @@ def case_matvec(a):
     old_segs = L.tcg_matvec_mma_segments(a.segs)
     old_static = L.tcg_matvec_set_static_weights(a.static_weights)
     old_split = L.tcg_matvec_mma_split(a.split)
+    old_tiles = L.tcg_matvec_mma_tiles(a.tiles)
     # back to back: the matrix rotates over enough copies that each launch
     # reads from HBM, not L2 (as in a decode pass over successive layers)
     copies = max(1, min(10, -(-(300 << 20) // raw.nbytes)))
@@ -152,6 +153,7 @@ def case_matvec(a):
     L.tcg_matvec_mma_segments(old_segs)
     L.tcg_matvec_set_static_weights(old_static)
     L.tcg_matvec_mma_split(old_split)
+    L.tcg_matvec_mma_tiles(old_tiles)
     nbytes = a.N * a.K // 256 * bb + 4 * (a.N + a.K)
     return {"case": "matvec", "type": a.type, "N": a.N, "K": a.K, "kernel": kern, "ms": round(ms, 5),
             "bytes": nbytes, "GB/s": round(nbytes / ms / 1e6, 1), "b2b_ms": round(b2b, 5),
@@ -282,6 +284,8 @@ def main():
     mv.add_argument("--mma", type=int, default=1, help="0: Q4_K on the CUDA-core kernels")
     mv.add_argument("--segs", type=int, default=0, help="K segments per tile of the mma kernel (0: automatic)")
     mv.add_argument("--split", type=int, default=1, help="0: one warp per Q6_K unit of the mma kernel")
+    mv.add_argument("--tiles", type=int, default=-1,
+                    help="mma kernel: 1 whole tiles per CTA, 0 segment-major unit ranges, -1 by shape")
     mv.add_argument("--static-weights", type=int, default=0,
                     help="1: promise that no earlier kernel writes W (weights fetched before the previous ends)")
     dq = sub.add_parser("dequant")

@@ -333,6 +333,27 @@ def test_matvec_q6k_mma_split(gpu, split, N, K):
     assert np.abs(got.astype(np.float64) - want).max() / np.abs(want).max() <= MATVEC_TOL
 
 
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("qt,N,K", [(G.Q4_K, 4096, 14336), (G.Q4_K, 4095, 11008), (G.Q4_K, 14336, 4096),
+                                    (G.Q6_K, 4096, 14336), (G.Q6_K, 300, 6144)])
+def test_matvec_mma_tile_modes(gpu, mode, qt, N, K):
+    """Units in segment-major ranges (split tiles summed through global
+    memory by the last segment to arrive) or whole tiles per CTA (a tile's
+    segments summed in shared memory): each against the oracle, three calls
+    giving the same bits."""
+    L = tcg.lib()
+    raw = G.make_kquant(qt, N, K, seed=13 + N + qt)
+    x = _x_cases(K, 5)["wide"]
+    old = L.tcg_matvec_mma_tiles(mode)
+    try:
+        got = dev_matvec(raw, x, N, K, qt, repeat=3)
+        assert L.tcg_matvec_last_kernel() == (5 if qt == G.Q4_K else 6)
+    finally:
+        L.tcg_matvec_mma_tiles(old)
+    want = oracle.matvec_q(raw, x, N, K, qt).astype(np.float64)
+    assert np.abs(got.astype(np.float64) - want).max() / np.abs(want).max() <= MATVEC_TOL
+
+
 def test_matvec_rejections(gpu):
     L = tcg.lib()
     assert not L.tcg_matvec_q(None, None, None, 4, 300, G.Q4_K)
