@@ -379,6 +379,32 @@ def vit_kquant_aux(tcg, args, fp32_weight_bytes):
                        "GEMM of one 128-row tile dequantises inside the GEMM instead); everything else fp32"}
 
 
+def vit_l14_aux(tcg, steps, warmup, batch=128):
+    """ViT-L/14 (24 layers, T = 257: the tensor-core attention and its
+    one-row tail), fp32, a batch of 128 images on this GPU: images/s (device
+    time of `steps` forwards) and its first, middle and last embedding against
+    the reference's tc_vit_encode, frozen for the same model and pixels."""
+    L = tcg.lib()
+    path, cfg = G.cached_vit_gguf(CACHE, "vit-l14", 0)
+    m = tcg.VitModel(path)
+    try:
+        m.upload(batch)
+        px = G.make_pixels(batch, cfg["image"], 1)
+        with tcg.DeviceBuffer.from_array(px) as dpx, tcg.DeviceBuffer(batch * cfg["d_out"] * 4) as dout:
+            step = lambda: tcg.check(L.tcg_vit_encode_device(m.dev, dpx.ptr, batch, dout.ptr))  # noqa: E731
+            for _ in range(warmup):
+                step()
+            ms = tcg.time_ms(lambda: [step() for _ in range(steps)], 0, 1) / steps
+            emb = dout.download((batch, cfg["d_out"]))
+    finally:
+        m.close()
+    par = rank_parity("vit-l14", batch, 1, emb)
+    return {"images/s": round(batch / (ms * 1e-3), 2), "ms_per_step": round(ms, 4), "batch": batch,
+            "model_flop_per_image": sum(vit_flops_per_image(cfg)),
+            "parity_max_rel": par[0] if par and par[2] else None, "parity_images": par[2] if par else 0,
+            "min_cosine": par[1] if par and par[2] else None, "outputs_finite": bool(np.isfinite(emb).all())}
+
+
 # ------------------------------------------------------------ our arm
 
 @contextlib.contextmanager
@@ -614,6 +640,8 @@ def run_ours(args, dist):
             result["aux"]["hbm_peak_gbs"] = pk["hbm_gbs"]
             result["aux"]["peak_kind"] = pk_kind
             result["aux"]["vit_q4k_weights"] = vit_kquant_aux(tcg, args, fp32_gemm_bytes)
+            if args.model == "vit-b32":
+                result["aux"]["vit_l14_batch128"] = vit_l14_aux(tcg, args.steps, args.warmup)
         if not args.no_cpu:
             threads = host_threads()
             rate, kind, dt = reference_rate(path, cfg, pixels[:threads], threads, rounds=1)

@@ -70,7 +70,7 @@ __global__ void layernorm_kernel(const float *x, int ld_in, const float *__restr
 // double sums run in another order. (Staging gamma/beta in shared memory
 // needed 111 registers, two CTAs per SM, and ran 15% slower.)
 template <int VPL>
-__global__ void __launch_bounds__(256, 4)
+__global__ void __launch_bounds__(256, 3)
 layernorm_vec_kernel(const float *x, int ld_in, const float *__restrict__ g, const float *__restrict__ b, int rows,
                      float eps, OutSpec out)
 {
