@@ -208,9 +208,20 @@ int        tcg_vit_set_packed_weights(int on);
  * redo the work. Applies to batch sizes planned afterwards; returns the
  * previous value. */
 long       tcg_vit_set_jit_rows(long rows);
-/* Bytes of GEMM weights one forward reads: the tf32 pairs of the split
- * weights plus the Q4_K blocks of the packed ones. */
+/* Bytes of GEMM weights one forward reads: the tf32 pairs or fp16 pieces of
+ * the split weights plus the Q4_K blocks of the packed ones. */
 size_t     tcg_vit_gemm_weight_bytes(const tcg_vit_t *v);
+/* 1 (default): a model whose weights are all fp32 on the device, with
+ * d_model and d_ffn multiples of 256, runs its GEMMs on fp16 pieces (every
+ * operand split into two fp16 values of 11 significant bits after a
+ * power-of-two scale per row or per 256-element block: the precision of a
+ * tf32 pair at twice the tensor rate); the patch embedding too when 3*patch^2
+ * is a multiple of 256. 0: tf32 pairs. Applies to later uploads; returns the
+ * previous setting. */
+int        tcg_vit_set_f16(int on);
+/* 0: the model's GEMMs run on tf32 pairs; 1: on fp16 pieces except the patch
+ * embedding; 2: all but the final projection on fp16 pieces. */
+int        tcg_vit_uses_f16(const tcg_vit_t *v);
 
 /* HOST buffers: pixels [n, 3, image, image] (already normalised), out
  * [n, d_out]. Copies in, runs, copies out, and returns after the result is

@@ -34,6 +34,12 @@ struct GemmEpi {
     // dequantises each K-step into its tf32 hi/lo shared-memory tiles.
     const uint8_t *bq = nullptr;
     size_t bq_row = 0;
+    // fp16-piece operands (the fp16 configuration): A row m's K-block c
+    // (xa_blk elements) was scaled by 2^xa[c * M + m] before it was split
+    // (undone in the drain), B row n by 2^xb[n] over all of K (per tile)
+    const int8_t *xa = nullptr;
+    const int8_t *xb = nullptr;
+    int xa_blk = 128;        // elements per K-block of A (128 or 256): one TMEM chunk each
 };
 
 // Device memory for the stream-K split of a GEMM's last, partial wave of

@@ -183,10 +183,13 @@ __device__ __forceinline__ void mma_commit_pair_local(uint32_t bar)
 //             the hi*hi half. The drain adds the halves.
 enum { ACC_SEP = 0, ACC_FOLD = 1, ACC_WIDE = 2 };
 
-template <int BN, int BK, int STAGES, int EPI_W = 8, int ACC = ACC_SEP, int CG = 1, int QB = 0>
+// OPF 1: the operands are fp16 pieces (2 bytes per element, BK = 64 fills a
+// 128-byte swizzled row) for kind::f16 MMAs, scaled per 128-element K-block.
+template <int BN, int BK, int STAGES, int EPI_W = 8, int ACC = ACC_SEP, int CG = 1, int QB = 0, int OPF = 0>
 struct Shape {
-    static constexpr uint32_t A_BYTES = BM * BK * 4;
-    static constexpr uint32_t B_BYTES = (BN / CG) * BK * 4;     // this CTA's share of the B tile
+    static constexpr int ES = OPF ? 2 : 4;                      // bytes per operand element
+    static constexpr uint32_t A_BYTES = BM * BK * ES;
+    static constexpr uint32_t B_BYTES = (BN / CG) * BK * ES;    // this CTA's share of the B tile
     static constexpr uint32_t STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
     static constexpr int CW = ACC == ACC_WIDE ? 2 * BN : BN;    // columns of a chunk buffer
     static constexpr int NBUF = ACC == ACC_SEP ? 2 : (4 * CW <= 512 ? 4 : 2);   // chunk buffers
@@ -206,6 +209,7 @@ struct Shape {
     static_assert(ACC != ACC_WIDE || (2 * BN <= 256 && CG == 1), "a wide MMA is at most 256 columns, one CTA");
     static_assert(SMEM <= 232448, "shared memory per block");
     static_assert(QB == 0 || (BN == 128 && BK == 32 && CG == 1), "packed B: 128 rows x one 32-weight sub-block");
+    static_assert(OPF == 0 || (ACC == ACC_WIDE && BK == 64 && QB == 0), "fp16 pieces: the wide shape, BK = 64");
 };
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, const float (&v)[4])
@@ -227,6 +231,41 @@ __device__ __forceinline__ void drain_add2(uint32_t ta, uint32_t tb, float (&acc
 #pragma unroll
         for (int i = 0; i < 8; i++)
             acc[j + i] = __fadd_rn(acc[j + i], __fadd_rn(__uint_as_float(x[i]), __uint_as_float(y[i])));
+    }
+}
+
+// drain_add2 for fp16-piece operands: (first + second) times fa = 2^-ea,
+// the row's K-block scale undone (exactly: a power of two), added to acc.
+// The column scales are undone once per tile (scale_cols).
+template <int HALF>
+__device__ __forceinline__ void drain_add2_scaled(uint32_t ta, uint32_t tb, float (&acc)[HALF], float fa)
+{
+#pragma unroll
+    for (int j = 0; j < HALF; j += 8) {
+        uint32_t x[8], y[8];
+        tmem_ld8(ta + (uint32_t)j, x);
+        tmem_ld8(tb + (uint32_t)j, y);
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            acc[j + i] = fmaf(__fadd_rn(__uint_as_float(x[i]), __uint_as_float(y[i])), fa, acc[j + i]);
+    }
+}
+
+// acc[j] *= 2^-xb[n0 + j]: B row (output column) n was scaled by 2^xb[n] over
+// all of K. |xb| <= 63 and the row factors are at most 2^63, so the partial
+// sums stay finite and both multiplications are exact.
+template <int HALF>
+__device__ __forceinline__ void scale_cols(float (&acc)[HALF], const int8_t *xb, int n0, int N)
+{
+#pragma unroll
+    for (int j = 0; j < HALF; j += 8) {
+        uint2 e8 = make_uint2(0u, 0u);
+        if (n0 + j + 8 <= N) e8 = *reinterpret_cast<const uint2 *>(xb + n0 + j);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int eb = (int)(int8_t)(((i < 4 ? e8.x : e8.y) >> (8 * (i & 3))) & 0xFFu);
+            acc[j + i] = __fmul_rn(acc[j + i], __int_as_float((127 - eb) << 23));
+        }
     }
 }
 
@@ -534,18 +573,20 @@ __device__ bool flag_wait(const int *f, volatile int *abort, int *err, int code)
 
 // chunk_kb: K-blocks whose hi*hi products share one TMEM chunk buffer before
 // it is drained into the fp32 registers.
-template <int BN, int BK, int STAGES, int EPI_W, int ACC, int CG, int QB = 0>
-__global__ void __launch_bounds__(Shape<BN, BK, STAGES, EPI_W, ACC, CG, QB>::THREADS, 1)
+template <int BN, int BK, int STAGES, int EPI_W, int ACC, int CG, int QB = 0, int OPF = 0>
+__global__ void __launch_bounds__(Shape<BN, BK, STAGES, EPI_W, ACC, CG, QB, OPF>::THREADS, 1)
 gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
                    const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
                    const __grid_constant__ CUtensorMap o_plain, const __grid_constant__ CUtensorMap o_hi,
                    const __grid_constant__ CUtensorMap o_lo,
                    int M, int N, int K, int chunk_kb, GemmEpi epi, int *err, float *ws, int *flags, int sk)
 {
-    using S = Shape<BN, BK, STAGES, EPI_W, ACC, CG, QB>;
+    using S = Shape<BN, BK, STAGES, EPI_W, ACC, CG, QB, OPF>;
     constexpr bool SEP = ACC == ACC_SEP, WIDE = ACC == ACC_WIDE;
     constexpr uint32_t CW = S::CW;
-    constexpr int SWB = BK * 4;
+    constexpr int SWB = BK * S::ES;
+    constexpr int KPM = OPF ? 16 : 8;                            // K elements per MMA instruction
+    constexpr uint32_t FMT = OPF ? 0u : 2u;                      // A/B format: f16 or tf32
     extern __shared__ uint8_t smem_raw[];
     uint8_t *tiles = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     float *epi_stage = (float *)(tiles + (size_t)STAGES * S::STAGE_BYTES);
@@ -665,9 +706,9 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
         __syncwarp();
     } else if (warp == 1) {
         if (leader && lane == 0) {
-            const uint32_t id = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
+            const uint32_t id = (1u << 4) | (FMT << 7) | (FMT << 10) | ((uint32_t)(BN >> 3) << 17) |
                                 ((uint32_t)((CG * BM) >> 4) << 24);
-            const uint32_t id_wide = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)((2 * BN) >> 3) << 17) |
+            const uint32_t id_wide = (1u << 4) | (FMT << 7) | (FMT << 10) | ((uint32_t)((2 * BN) >> 3) << 17) |
                                      ((uint32_t)((CG * BM) >> 4) << 24);
             int stage = 0;
             uint32_t phase = 0, chunk = 0;
@@ -691,7 +732,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                         fence_after();
                         const uint32_t base = su32(tiles + (size_t)stage * S::STAGE_BYTES);
 #pragma unroll
-                        for (int k = 0; k < BK / 8; k++) {
+                        for (int k = 0; k < BK / KPM; k++) {
                             const uint32_t off = (uint32_t)k * 32u;
                             const unsigned long long ah = sdesc<SWB>(base + off);
                             const unsigned long long al = sdesc<SWB>(base + S::A_BYTES + off);
@@ -699,7 +740,10 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                             const unsigned long long bl = sdesc<SWB>(base + 2 * S::A_BYTES + S::B_BYTES + off);
                             const uint32_t acc0 = (kb > kb0 || k > 0) ? 1u : 0u;
                             const uint32_t acc1 = (!SEP || kb > ks0 || k > 0) ? 1u : 0u;
-                            if constexpr (WIDE) {
+                            if constexpr (OPF) {
+                                mma_f16(db, ah, bh, id_wide, acc0);       // [hi*hi | hi*lo]
+                                mma_f16(db, al, bh, id, 1u);              // + lo*hi
+                            } else if constexpr (WIDE) {
                                 mma_tf32(db, ah, bh, id_wide, acc0);      // [hi*hi | hi*lo]
                                 mma_tf32(db, al, bh, id, 1u);             // + lo*hi
                             } else if constexpr (CG == 2) {
@@ -761,7 +805,13 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                 const uint32_t b = chunk % NBUF;
                 if (!bar_wait(cfull0 + 8 * b, (chunk / NBUF) & 1, abort, err, 6)) { ok = false; break; }
                 fence_after();
-                if constexpr (WIDE) drain_add2<S::HALF>(tmem + lane_cols + b * CW, tmem + lane_cols + b * CW + BN, acc);
+                if constexpr (OPF) {
+                    // this chunk is one 128-element K-block: undo the row's and the columns' scales
+                    const int m = (sg.tile / n_tiles) * BM + q * 32 + lane;
+                    const int ea = m < M ? (int)epi.xa[(size_t)c * M + m] : 0;
+                    drain_add2_scaled<S::HALF>(tmem + lane_cols + b * CW, tmem + lane_cols + b * CW + BN, acc,
+                                               __int_as_float((127 - ea) << 23));
+                } else if constexpr (WIDE) drain_add2<S::HALF>(tmem + lane_cols + b * CW, tmem + lane_cols + b * CW + BN, acc);
                 else drain_add<S::HALF, S::LDW>(tmem + lane_cols + b * CW, acc);
                 fence_before();
                 __syncwarp();
@@ -814,6 +864,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                 if (!ok) break;
             }
             const int m0 = (sg.tile / n_tiles) * CG * BM + (int)rank * BM, n0 = (sg.tile % n_tiles) * BN;
+            if constexpr (OPF) scale_cols<S::HALF>(acc, epi.xb, n0 + h * S::HALF, N);
             if (epi.tma)
                 epi_store_tile_tma<S::HALF>(epi, acc, epi_stage + ew * (S::EPI_STAGE_BYTES / 4), &o_plain, &o_hi,
                                             &o_lo, m0 + q * 32, n0 + h * S::HALF, M, N, breg);
@@ -961,6 +1012,24 @@ bool encode_kmajor(CUtensorMap *m, const float *ptr, int rows, int K, int box_ro
     return true;
 }
 
+// fp16-piece operand: rows x K fp16, K-major, boxes of 64 elements (one
+// 128-byte swizzled row) x box_rows.
+bool encode_kmajor_f16(CUtensorMap *m, const void *ptr, int rows, int K, int box_rows)
+{
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail("cuTensorMapEncodeTiled is not available from the driver");
+    if (((uintptr_t)ptr & 15) || (K & 7)) return fail("fp16 GEMM operand not 16-byte aligned / K=%d not a multiple of 8", K);
+    cuuint64_t dims[2] = { (cuuint64_t)K, (cuuint64_t)rows };
+    cuuint64_t strides[1] = { (cuuint64_t)K * 2u };
+    cuuint32_t box[2] = { 64u, (cuuint32_t)box_rows };
+    cuuint32_t estr[2] = { 1, 1 };
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)ptr, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail("cuTensorMapEncodeTiled failed (%d) for fp16 [%d x %d]", (int)r, rows, K);
+    return true;
+}
+
 // Output map for the bulk-store epilogue: rows x cols fp32 with row stride
 // ld, boxes of 32 rows x 8 columns in the 32-byte swizzle.
 bool encode_out(CUtensorMap *m, const float *ptr, int rows, int cols, int ld)
@@ -986,6 +1055,7 @@ struct Cfg {
     bool sep;           // separate small-term accumulators (no stream-K)
     int epi_warps;
     int qb;             // B packed in these K-quant blocks (0: tf32 pairs by TMA)
+    int opf = 0;        // 1: fp16-piece operands (kind::f16), K-blocks of 128 scaled
 };
 
 #define TCG_CFG(BN, BK, ST, EW, ACC, CG)                                                                   \
@@ -995,6 +1065,10 @@ struct Cfg {
     { BN, BK, ST, Shape<BN, BK, ST, EW, ACC, 1, QB>::SMEM,                                                  \
       (const void *)gemm_tf32x3_kernel<BN, BK, ST, EW, ACC, 1, QB>, 1, Shape<BN, BK, ST, EW, ACC, 1, QB>::THREADS, \
       ACC == ACC_SEP, EW, QB }
+#define TCG_CFG_F16(BN, BK, ST, EW)                                                                         \
+    { BN, BK, ST, Shape<BN, BK, ST, EW, ACC_WIDE, 1, 0, 1>::SMEM,                                           \
+      (const void *)gemm_tf32x3_kernel<BN, BK, ST, EW, ACC_WIDE, 1, 0, 1>, 1,                               \
+      Shape<BN, BK, ST, EW, ACC_WIDE, 1, 0, 1>::THREADS, false, EW, 0, 1 }
 const Cfg CFGS[] = {
     TCG_CFG(128, 32, 3, 8, ACC_SEP, 1), TCG_CFG(64, 32, 4, 8, ACC_SEP, 1), TCG_CFG(128, 16, 6, 8, ACC_SEP, 1),
     TCG_CFG(64, 16, 8, 8, ACC_SEP, 1), TCG_CFG(96, 32, 3, 8, ACC_SEP, 1), TCG_CFG(96, 16, 7, 8, ACC_SEP, 1),
@@ -1004,10 +1078,13 @@ const Cfg CFGS[] = {
     TCG_CFG(128, 32, 4, 16, ACC_SEP, 2),                                // CTA pair, separate small terms
     TCG_CFG(128, 32, 3, 16, ACC_WIDE, 1), TCG_CFG(128, 32, 3, 8, ACC_WIDE, 1),
     TCG_CFG_Q(128, 32, 3, 8, ACC_WIDE, GGML_TYPE_Q4_K),                  // B in Q4_K blocks (15)
+    TCG_CFG_F16(128, 64, 3, 16),                                          // fp16 pieces, kind::f16 (16)
 };
 #undef TCG_CFG
 #undef TCG_CFG_Q
+#undef TCG_CFG_F16
 constexpr int CFG_Q4K = 15;
+constexpr int CFG_F16 = 16;
 constexpr int NCFG = sizeof(CFGS) / sizeof(CFGS[0]);
 
 int g_force_cfg = -1;     // tuning hook: a configuration every automatic choice takes
@@ -1067,6 +1144,8 @@ int gemm_cfg_bn(int cfg) { return cfg >= 0 && cfg < NCFG ? CFGS[cfg].bn : 0; }
 
 int gemm_q4k_cfg() { return CFG_Q4K; }
 
+int gemm_f16_cfg() { return CFG_F16; }
+
 size_t gemm_work_ws_floats(int ctas) { return (size_t)ctas * BM * 256; }
 size_t gemm_work_flag_count(int ctas) { return (size_t)ctas * 16; }
 
@@ -1110,7 +1189,14 @@ bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b
     if (cfg >= NCFG) return fail("gemm_plan: no configuration %d", cfg);
     const Cfg &c = CFGS[cfg];
     const int b_rows = c.bn / c.cg;                     // B box: this CTA's share of the tile columns
-    if (c.qb) {
+    if (c.opf) {
+        // fp16 pieces and their per-K-block exponents
+        if (K % epi.xa_blk || N % 8 || !epi.xa || !epi.xb || (epi.xa_blk != 128 && epi.xa_blk != 256))
+            return fail("gemm_plan: fp16-piece operands need K %% 128 == 0, N %% 8 == 0 and both exponent arrays");
+        if (!encode_kmajor_f16(&p.a_hi, a_hi, M, K, BM) || !encode_kmajor_f16(&p.a_lo, a_lo, M, K, BM) ||
+            !encode_kmajor_f16(&p.b_hi, b_hi, N, K, b_rows) || !encode_kmajor_f16(&p.b_lo, b_lo, N, K, b_rows))
+            return false;
+    } else if (c.qb) {
         // B comes packed: no B tensor maps (the A ones fill the unused parameters)
         if (!epi.bq || ((uintptr_t)epi.bq & 15) || K % 256 || epi.bq_row != (size_t)(K / 256) * 144)
             return fail("gemm_plan: packed Q4_K B needs 16-byte-aligned rows of K/256 superblocks");
@@ -1173,7 +1259,8 @@ bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b
     // wave leaves at least half the SMs idle, or when a tile has many chunks
     // (fine units); with 2-5 chunks and a fuller last wave the partial-sum
     // hand-over costs what it saves.
-    const int chunks = (K + g_chunk_k - 1) / g_chunk_k;
+    const int chunk_k = c.opf ? epi.xa_blk : g_chunk_k;
+    const int chunks = (K + chunk_k - 1) / chunk_k;
     const int last = tiles % groups;
     const bool pays = g_streamk == 2 || last <= groups / 2 || chunks >= 6;
     if (g_streamk && work && work->ws && work->flags && !c.sep && last != 0 && chunks > 1 && pays) {
@@ -1202,7 +1289,8 @@ bool gemm_run(const GemmPlan &p, cudaStream_t s, int *err)
         TCG_CUDA(cudaFuncSetAttribute(c.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem));
         attr_done[dev] |= 1ull << p.cfg;
     }
-    int chunk_kb = g_chunk_k / c.bk;
+    // fp16 pieces: one TMEM chunk per K-block of A (its scale)
+    int chunk_kb = c.opf ? p.epi.xa_blk / c.bk : g_chunk_k / c.bk;
     if (chunk_kb < 1) chunk_kb = 1;
     float *ws = p.work.ws;
     int *flags = p.work.flags;
@@ -1224,6 +1312,64 @@ bool gemm_run(const GemmPlan &p, cudaStream_t s, int *err)
         cl.val.clusterDim.x = 2; cl.val.clusterDim.y = 1; cl.val.clusterDim.z = 1;
     }
     TCG_CUDA(cudaLaunchKernelExC(&lc, c.fn, args));
+    return true;
+}
+
+// fp32 rows -> fp16 pieces: one warp per (row, 128-element K-block). The
+// block is scaled by 2^e with its largest magnitude in [2^14, 2^15), then v =
+// p1 + p2 + r with p1 = v rounded to 11 significant bits (exact in fp16), p2 =
+// fp16(v - p1), |r| <= 2^-23 |v|: the precision of a tf32 pair. ex[c * rows +
+// row] = e. e is kept in [-63, 63] (0 for an all-zero block) so that a
+// product's unscaling 2^-(ea + eb) is one normal float: blocks whose largest
+// magnitude lies in [2^-49, 2^77) are represented to that precision; smaller
+// ones lose low bits to fp16's subnormals, larger ones overflow fp16.
+// mode 0: one exponent per (row, 128-element K-block), ex[c * rows + row];
+// mode 2: per (row, 256-element K-block), ex[c * rows + row]; mode 1: one per
+// row over all of K (the B operand), ex[row]. A warp takes 128 elements; the
+// warps of a 256-element block both compute its maximum.
+__global__ void split_f16_kernel(const float *__restrict__ src, int rows, int K, __half *__restrict__ hi,
+                                 __half *__restrict__ lo, int8_t *__restrict__ ex, int mode)
+{
+    const int lane = threadIdx.x & 31;
+    const int nkb = K >> 7;
+    const long long gw = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (gw >= (long long)rows * nkb) return;
+    const int row = (int)(gw / nkb), c = (int)(gw - (long long)row * nkb);
+    const size_t o = (size_t)row * K + (size_t)c * 128 + 4 * lane;
+    const float4 v = *reinterpret_cast<const float4 *>(src + o);
+    const int per_row = mode == 1;
+    float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    if (mode == 2) {    // the other 128 elements of this 256-element block
+        const float4 w = *reinterpret_cast<const float4 *>(src + (o ^ 128));
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(w.x), fabsf(w.y)), fmaxf(fabsf(w.z), fabsf(w.w))));
+    }
+    if (per_row)        // the whole row (a few KB, L1/L2 resident for the row's warps)
+        for (int i = lane; i < K / 4; i += 32) {
+            const float4 w = *reinterpret_cast<const float4 *>(src + (size_t)row * K + 4 * i);
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(w.x), fabsf(w.y)), fmaxf(fabsf(w.z), fabsf(w.w))));
+        }
+#pragma unroll
+    for (int d = 16; d >= 1; d >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, d));
+    const int e = f16_scale_exp(m);
+    const float f = __int_as_float((127 + e) << 23);
+    const float vv[4] = { v.x, v.y, v.z, v.w };
+    uint2 h, l;
+    f16_pieces4(vv, f, h, l);
+    *reinterpret_cast<uint2 *>(hi + o) = h;
+    *reinterpret_cast<uint2 *>(lo + o) = l;
+    if (lane == 0 && (mode == 0 || (mode == 1 && c == 0) || (mode == 2 && !(c & 1))))
+        ex[mode == 1 ? (size_t)row : (size_t)(mode == 2 ? c >> 1 : c) * rows + row] = (int8_t)e;
+}
+
+bool launch_split_f16(const float *src, int rows, int K, void *hi, void *lo, int8_t *ex, int mode, cudaStream_t s)
+{
+    if (rows <= 0) return true;
+    if (K % (mode == 2 ? 256 : 128) || ((uintptr_t)src & 15) || ((uintptr_t)hi & 15) || ((uintptr_t)lo & 15))
+        return fail("fp16 split: K=%d not a multiple of the block or unaligned buffers", K);
+    const long long warps = (long long)rows * (K / 128);
+    split_f16_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(src, rows, K, (__half *)hi, (__half *)lo, ex,
+                                                                 mode);
+    TCG_LAUNCHED();
     return true;
 }
 
@@ -1307,6 +1453,41 @@ bool tcg_linear_cfg(float *y, const float *x, const float *W, const float *bias,
 }
 
 int tcg_gemm_num_cfgs(void) { return gemm_num_cfgs(); }
+
+// fp32 rows to fp16 pieces (split_f16_kernel): hi, lo [rows, K] fp16; ex
+// int8 exponents, [K / 128, rows] per (row, 128-element K-block) (mode 0),
+// [K / 256, rows] per 256-element block (mode 2), or [rows], one per row over
+// all of K (mode 1: the B operand).
+bool tcg_split_f16(void *hi, void *lo, int8_t *ex, const float *src, int rows, int K, int mode)
+{
+    if (!need_ctx()) return false;
+    return launch_split_f16(src, rows, K, hi, lo, ex, mode, ctx().cur);
+}
+
+// y = x W^T + bias on fp16-piece operands (tcg_split_f16 of x [M, K] per
+// K-block and of W [N, K] per row): kind::f16 MMAs, hi*hi + hi*lo + lo*hi per
+// product; each 128-element K-block's row scale is undone in the drain, the
+// column scales once per tile.
+bool tcg_linear_f16_split(float *y, const void *x_hi, const void *x_lo, const int8_t *x_ex, const void *w_hi,
+                          const void *w_lo, const int8_t *w_ex, const float *bias, int M, int N, int K, int x_blk)
+{
+    if (!need_ctx()) return false;
+    if (M < 0 || N < 0 || K <= 0) return fail("tcg_linear_f16_split: bad shape %dx%dx%d", M, N, K);
+    if (M == 0 || N == 0) return true;
+    GemmEpi e;
+    e.bias = bias;
+    e.out.plain = y;
+    e.out.ld = N;
+    e.xa = x_ex;
+    e.xb = w_ex;
+    e.xa_blk = x_blk;
+    GemmPlan p;
+    const GemmWork *w = ctx_gemm_work();
+    if (!w || !gemm_plan(p, (const float *)x_hi, (const float *)x_lo, (const float *)w_hi, (const float *)w_lo, M, N,
+                         K, e, CFG_F16, w))
+        return false;
+    return gemm_run(p, ctx().cur, ctx().d_err);
+}
 
 // Tuning and test hook: 0 keeps every GEMM epilogue on plain stores, 1
 // (default) uses bulk tensor stores where the output rows allow. Applies to

@@ -3,6 +3,7 @@
 // nvcc cannot contract it into FMAs.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -25,6 +26,35 @@ __device__ __forceinline__ void split_tf32(float v, float &hi, float &lo)
 {
     hi = to_tf32(v);
     lo = to_tf32(__fsub_rn(v, hi));
+}
+
+// The power-of-two exponent e that puts a block whose largest magnitude is m
+// in [2^14, 2^15) (inside fp16's normal range), kept in [-63, 63] so that a
+// product's unscaling 2^-(ea + eb) is one normal float; 0 when m is 0 or not
+// finite.
+__device__ __forceinline__ int f16_scale_exp(float m)
+{
+    const int E = (__float_as_int(m) >> 23) & 0xFF;
+    return (m == 0.0f || E == 0xFF) ? 0 : max(-63, min(141 - E, 63));
+}
+
+// Four values times f (a power of two) as fp16 pieces: p1 = the value
+// rounded to 11 significant bits (exact in fp16), p2 = fp16(value - p1),
+// packed four to a uint2 (element 0 in the low half).
+__device__ __forceinline__ void f16_pieces4(const float (&v)[4], float f, uint2 &hi, uint2 &lo)
+{
+    uint32_t h[2], l[2];
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const float x0 = __fmul_rn(v[2 * i], f), x1 = __fmul_rn(v[2 * i + 1], f);
+        const float p0 = to_tf32(x0), p1 = to_tf32(x1);
+        const __half2 a = __floats2half2_rn(p0, p1);
+        const __half2 b = __floats2half2_rn(__fsub_rn(x0, p0), __fsub_rn(x1, p1));
+        h[i] = *reinterpret_cast<const uint32_t *>(&a);
+        l[i] = *reinterpret_cast<const uint32_t *>(&b);
+    }
+    hi = make_uint2(h[0], h[1]);
+    lo = make_uint2(l[0], l[1]);
 }
 
 // 0.5f * x * (1.0f + erff(x * (1/sqrt 2)))  -- src/ops.c:82-87

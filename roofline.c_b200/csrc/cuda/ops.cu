@@ -97,6 +97,46 @@ layernorm_vec_kernel(const float *x, int ld_in, const float *__restrict__ g, con
     }
     const double var = warp_sum(ss) / (double)cols;
     const float inv = (float)(1.0 / sqrt(var + (double)eps));
+    if (out.fh) {
+        // fp16 pieces: the whole row first, then one exponent per 256-column
+        // block (float4s 2b and 2b+1 of every lane)
+        float o[VPL][4];
+#pragma unroll
+        for (int i = 0; i < VPL; i++) {
+            const int c = 4 * (lane + 32 * i);
+            const float4 gg = g ? *reinterpret_cast<const float4 *>(g + c) : make_float4(1.f, 1.f, 1.f, 1.f);
+            const float4 bv = b ? *reinterpret_cast<const float4 *>(b + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float gv[4] = { gg.x, gg.y, gg.z, gg.w }, bb4[4] = { bv.x, bv.y, bv.z, bv.w };
+            const float xv[4] = { v[i].x, v[i].y, v[i].z, v[i].w };
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                float t = __fmul_rn((float)((double)xv[k] - mean), inv);
+                if (g) t = __fmul_rn(t, gv[k]);
+                if (b) t = __fadd_rn(t, bb4[k]);
+                o[i][k] = t;
+            }
+        }
+#pragma unroll
+        for (int bk = 0; bk < VPL / 2; bk++) {
+            float m = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 4; k++) m = fmaxf(m, fmaxf(fabsf(o[2 * bk][k]), fabsf(o[2 * bk + 1][k])));
+#pragma unroll
+            for (int d = 16; d >= 1; d >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, d));
+            const int e = f16_scale_exp(m);
+            const float f = __int_as_float((127 + e) << 23);
+#pragma unroll
+            for (int i = 2 * bk; i < 2 * bk + 2; i++) {
+                uint2 h, l;
+                f16_pieces4(o[i], f, h, l);
+                const size_t at = (size_t)row * out.ld + 4 * (lane + 32 * i);
+                *reinterpret_cast<uint2 *>((__half *)out.fh + at) = h;
+                *reinterpret_cast<uint2 *>((__half *)out.fl + at) = l;
+            }
+            if (lane == 0) out.fe[(size_t)bk * out.fe_rows + row] = (int8_t)e;
+        }
+        return;
+    }
 #pragma unroll
     for (int i = 0; i < VPL; i++) {
         const int c = 4 * (lane + 32 * i);
@@ -123,6 +163,9 @@ bool launch_layernorm(const float *x, int ld_in, const float *g, const float *b,
     const auto a16 = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
     const bool vec = cols % 128 == 0 && cols <= 1024 && !(ld_in & 3) && !(out.ld & 3) && a16(x) && a16(g) &&
                      a16(b) && a16(out.plain) && a16(out.hi) && a16(out.lo);
+    if (out.fh && (!vec || cols % 256 || !out.fl || !out.fe || out.plain || out.hi || ((uintptr_t)out.fh & 7) ||
+                   ((uintptr_t)out.fl & 7)))
+        return fail("layernorm: fp16-piece output needs whole 256-column blocks (cols %d) and no other output", cols);
     const unsigned grid = ceil_div(rows, 8);
     if (vec) {
         switch (cols / 128) {
@@ -1194,6 +1237,10 @@ __global__ void patches_kernel(const float *__restrict__ px, int n_img, int S, i
         const int ch = c / (P * PV), rem = c % (P * PV), ky = rem / PV, kv = rem % PV;
         const V v = *reinterpret_cast<const V *>(px + (((size_t)img * 3 + ch) * S + gy * P + ky) * S + gx * P + kv * VEC);
         const float *f = reinterpret_cast<const float *>(&v);
+        if (!lo) {                                          // plain fp32 rows
+            reinterpret_cast<V *>(hi)[i] = v;
+            continue;
+        }
         V h, l;
         float *hf = reinterpret_cast<float *>(&h), *lf = reinterpret_cast<float *>(&l);
 #pragma unroll

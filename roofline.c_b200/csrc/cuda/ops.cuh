@@ -6,13 +6,26 @@
 namespace tcg {
 
 // Where an activation goes: plain fp32, and/or the tf32 hi/lo pair the
-// 3xTF32 GEMMs read (hi = rn_tf32(v), lo = rn_tf32(v - hi)). Row stride ld.
+// 3xTF32 GEMMs read (hi = rn_tf32(v), lo = rn_tf32(v - hi)), or the fp16
+// pieces the kind::f16 GEMM reads (fh, fl: row stride ld, in halves; fe: the
+// exponent of each (row, 256-column block), fe[block * fe_rows + row];
+// LayerNorm only). Row stride ld.
 struct OutSpec {
     float *plain = nullptr;
     float *hi = nullptr;
     float *lo = nullptr;
     int ld = 0;
+    void *fh = nullptr;
+    void *fl = nullptr;
+    int8_t *fe = nullptr;
+    int fe_rows = 0;
 };
+
+// fp32 rows -> fp16 pieces (gemm_tc.cu): mode 0 / 2 one exponent per (row,
+// 128- / 256-element K-block), mode 1 one per row.
+bool launch_split_f16(const float *src, int rows, int K, void *hi, void *lo, int8_t *ex, int mode, cudaStream_t s);
+// the configuration of the kind::f16 GEMM on fp16 pieces
+int gemm_f16_cfg();
 
 // K-quant blocks straight to their tf32 pairs (kquant.cu).
 bool launch_dequant_split(const void *src, float *hi, float *lo, size_t n, ggml_type_t t, cudaStream_t s);

@@ -88,6 +88,15 @@ __device__ __forceinline__ void mma_tf32(uint32_t d, unsigned long long a, unsig
                  ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc));
 }
 
+// kind::f16 with fp16 A and B (fp32 accumulator): K = 16 per instruction,
+// the same 32 bytes of a K-major row as kind::tf32's K = 8
+__device__ __forceinline__ void mma_f16(uint32_t d, unsigned long long a, unsigned long long b, uint32_t id, uint32_t acc)
+{
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+                 ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc));
+}
+
 __device__ __forceinline__ void mma_commit(uint32_t bar)
 {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");

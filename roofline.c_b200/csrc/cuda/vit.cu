@@ -35,6 +35,9 @@ struct tcg_vit {
     int max_batch;
     int device;
     bool graphs = true;
+    // GEMMs on fp16 pieces (kind::f16; every weight fp32 on the device and
+    // d_model, d_ffn multiples of 256); the patch GEMM too where 3 P^2 is
+    bool f16 = false, patch_f16 = false;
 
     // fp32 weights, one allocation (the unit of the NCCL broadcast)
     float *wslab = nullptr;
@@ -54,10 +57,13 @@ struct tcg_vit {
         const float *ln1_g, *ln1_b, *qkv_b, *out_b, *ln2_g, *ln2_b, *up_b, *down_b;
         const float *qkv_h, *qkv_l, *out_h, *out_l, *up_h, *up_l, *down_h, *down_l;
         const uint8_t *qkv_q = nullptr, *out_q = nullptr, *up_q = nullptr, *down_q = nullptr;
+        // fp16 pieces: each weight row's exponent (the _h/_l fields hold fp16)
+        const int8_t *qkv_e = nullptr, *out_e = nullptr, *up_e = nullptr, *down_e = nullptr;
     };
     std::vector<Layer> layers;
     const float *patch_h = nullptr, *patch_l = nullptr, *cls = nullptr, *pos = nullptr;
     const uint8_t *patch_q = nullptr;
+    const int8_t *patch_e = nullptr;
     const float *ln_pre_g = nullptr, *ln_pre_b = nullptr, *ln_post_g = nullptr, *ln_post_b = nullptr;
     const float *proj = nullptr;
     const float *projT_h = nullptr, *projT_l = nullptr;   // v.proj transposed to [d_out, D], split
@@ -67,6 +73,10 @@ struct tcg_vit {
     float *px = nullptr, *x = nullptr, *h_hi = nullptr, *h_lo = nullptr, *qkv = nullptr;
     float *f_hi = nullptr, *f_lo = nullptr, *pooled_hi = nullptr, *pooled_lo = nullptr, *out = nullptr;
     float *p_hi = nullptr, *p_lo = nullptr;   // alias f_hi / f_lo
+    // fp16-piece activations: exponents per (row, 256-column block); h's
+    // pieces live in h_hi / h_lo, f's and the patches' in f_lo (hi half
+    // first), their fp32 source in f_hi
+    int8_t *h_e = nullptr, *f_e = nullptr, *p_e = nullptr;
     tcg::GemmWork work;                       // this model's GEMM stream-K memory (in the arena)
 
     struct Plans {
@@ -147,6 +157,10 @@ static std::vector<WEntry> weight_table(tcg_vit *v, const tc_vit_t *m)
 // device (tcg_vit_set_packed_weights).
 int g_vit_packed = 1;
 
+// 1 (default): models whose weights are all fp32 run their GEMMs on fp16
+// pieces (tcg_vit_set_f16); 0: on tf32 pairs.
+int g_vit_f16 = 1;
+
 // The GGUF tensor of a GEMM weight when it is kept packed: Q4_K rows of whole
 // superblocks, read in place from the mapping.
 static const gguf_tensor_t *packed_tensor(const tc_vit_t *m, const char *name)
@@ -222,6 +236,8 @@ static tcg_vit *vit_alloc(const tc_vit_t *m, int max_batch, std::vector<WEntry> 
         }
         v->jit_lo = v->jit_hi + align_floats(most);
     }
+    v->f16 = g_vit_f16 && packed.empty() && v->D % 256 == 0 && v->F % 256 == 0;
+    v->patch_f16 = v->f16 && (3 * v->P * v->P) % 256 == 0;
     offsets.resize(table.size());
     size_t total = 0;
     for (size_t i = 0; i < table.size(); i++) {
@@ -247,14 +263,26 @@ static tcg_vit *vit_alloc(const tc_vit_t *m, int max_batch, std::vector<WEntry> 
         need += align_floats(n);
         return p;
     };
+    // a weight of `rows` rows of n / rows: its tf32 pair, or its fp16 pieces
+    // (n halves each) and one exponent per row
+    auto take_w = [&](const float *&h, const float *&l, const int8_t *&e, size_t n, size_t rows, bool keep, bool f16) {
+        if (!f16) {
+            h = take(n, keep);
+            l = take(n, keep);
+            return;
+        }
+        h = take((n + 1) / 2, keep);
+        l = take((n + 1) / 2, keep);
+        e = (const int8_t *)take((rows + 3) / 4, keep);
+    };
     auto place = [&]() {
         need = 0;
-        v->patch_h = take(D * K0, !v->patch_q); v->patch_l = take(D * K0, !v->patch_q);
+        take_w(v->patch_h, v->patch_l, v->patch_e, D * K0, D, !v->patch_q, v->patch_f16);
         for (auto &y : v->layers) {
-            y.qkv_h = take(3 * D * D, !y.qkv_q); y.qkv_l = take(3 * D * D, !y.qkv_q);
-            y.out_h = take(D * D, !y.out_q); y.out_l = take(D * D, !y.out_q);
-            y.up_h = take(F * D, !y.up_q); y.up_l = take(F * D, !y.up_q);
-            y.down_h = take(D * F, !y.down_q); y.down_l = take(D * F, !y.down_q);
+            take_w(y.qkv_h, y.qkv_l, y.qkv_e, 3 * D * D, 3 * D, !y.qkv_q, v->f16);
+            take_w(y.out_h, y.out_l, y.out_e, D * D, D, !y.out_q, v->f16);
+            take_w(y.up_h, y.up_l, y.up_e, F * D, F, !y.up_q, v->f16);
+            take_w(y.down_h, y.down_l, y.down_e, D * F, D, !y.down_q, v->f16);
         }
         v->projT_h = take(D * (size_t)v->d_out, true); v->projT_l = take(D * (size_t)v->d_out, true);
     };
@@ -272,8 +300,9 @@ static tcg_vit *vit_alloc(const tc_vit_t *m, int max_batch, std::vector<WEntry> 
     const size_t f_floats = std::max(n * T * F, n * G2 * K0);
     const int ctas = ctx().sms > 0 ? ctx().sms : 148;
     const size_t ws_floats = gemm_work_ws_floats(ctas), flag_count = gemm_work_flag_count(ctas);
+    const size_t e_bytes = n * T * (D + F) / 256 + n * G2 * K0 / 256 + 3 * 256;   // fp16-piece exponents
     const size_t want = (n * 3 * v->S * v->S + n * T * D * 3 + n * T * 3 * D + 2 * f_floats +
-                         2 * n * D + n * v->d_out + ws_floats + flag_count) * sizeof(float) + 16 * 256;
+                         2 * n * D + n * v->d_out + ws_floats + flag_count) * sizeof(float) + e_bytes + 16 * 256;
     v->act = tcg_arena_create(want, "vit activations");
     if (!tcg_arena_ok(&v->act)) return nullptr;
     auto alloc = [&](size_t floats) { return (float *)tcg_arena_alloc(&v->act, floats * sizeof(float), 256); };
@@ -289,6 +318,11 @@ static tcg_vit *vit_alloc(const tc_vit_t *m, int max_batch, std::vector<WEntry> 
     v->out = alloc(n * v->d_out);
     v->p_hi = v->f_hi;
     v->p_lo = v->f_lo;
+    if (v->f16) {
+        v->h_e = (int8_t *)tcg_arena_alloc(&v->act, n * T * D / 256, 256);
+        v->f_e = (int8_t *)tcg_arena_alloc(&v->act, n * T * F / 256, 256);
+        v->p_e = v->patch_f16 ? (int8_t *)tcg_arena_alloc(&v->act, n * G2 * K0 / 256, 256) : nullptr;
+    }
     v->work.ws = alloc(ws_floats);
     v->work.flags = (int *)alloc(flag_count);
     v->work.ctas = ctas;
@@ -310,13 +344,23 @@ static bool split_weights(tcg_vit *v, const std::vector<WEntry> &table, const st
     auto split = [&](size_t entry, const float *hi, const float *lo, size_t n) {
         return !hi || launch_split(v->wslab + off[entry], (float *)hi, (float *)lo, n, s);
     };
-    if (!split(0, v->patch_h, v->patch_l, D * K0)) return false;
+    // fp16 pieces: rows x K, one exponent per row
+    auto split16 = [&](size_t entry, const float *hi, const float *lo, const int8_t *e, size_t rows, size_t K) {
+        return !hi || launch_split_f16(v->wslab + off[entry], (int)rows, (int)K, (void *)hi, (void *)lo,
+                                       (int8_t *)e, 1, s);
+    };
+    if (!(v->patch_f16 ? split16(0, v->patch_h, v->patch_l, v->patch_e, D, K0) : split(0, v->patch_h, v->patch_l, D * K0)))
+        return false;
     for (int i = 0; i < v->L; i++) {
         const size_t b = 8 + 12 * (size_t)i;   // first entry of block i in weight_table
         tcg_vit::Layer &y = v->layers[i];
-        if (!split(b + 2, y.qkv_h, y.qkv_l, 3 * D * D) || !split(b + 4, y.out_h, y.out_l, D * D) ||
-            !split(b + 8, y.up_h, y.up_l, F * D) || !split(b + 10, y.down_h, y.down_l, D * F))
-            return false;
+        const bool ok = v->f16 ? split16(b + 2, y.qkv_h, y.qkv_l, y.qkv_e, 3 * D, D) &&
+                                     split16(b + 4, y.out_h, y.out_l, y.out_e, D, D) &&
+                                     split16(b + 8, y.up_h, y.up_l, y.up_e, F, D) &&
+                                     split16(b + 10, y.down_h, y.down_l, y.down_e, D, F)
+                               : split(b + 2, y.qkv_h, y.qkv_l, 3 * D * D) && split(b + 4, y.out_h, y.out_l, D * D) &&
+                                     split(b + 8, y.up_h, y.up_l, F * D) && split(b + 10, y.down_h, y.down_l, D * F);
+        if (!ok) return false;
     }
     {   // v.proj is [D, d_out] (used untransposed, src/vit.c:384-386): store it as the [d_out, D] operand
         if (!launch_transpose_split(v->proj, v->D, v->d_out, (float *)v->projT_h, (float *)v->projT_l, s))
@@ -383,7 +427,20 @@ static tcg_vit::Plans *plans_for(tcg_vit *v, int n)
         }
         return gemm_plan(gp, a_hi, a_lo, b_hi, b_lo, Mg, Ng, Kg, ep, gemm_vit_cfg(Mg, Ng, Kg), w);
     };
-    if (!plan(p->patch, v->p_hi, v->p_lo, v->patch_h, v->patch_l, v->patch_q, n * G2, D, K0, e)) return nullptr;
+    // fp16 pieces: A's exponents per (row, 256-column block), B's per row
+    auto plan16 = [&](GemmPlan &gp, const void *a_hi, const void *a_lo, const int8_t *a_e, const float *b_hi,
+                      const float *b_lo, const int8_t *b_e, int Mg, int Ng, int Kg, GemmEpi ep) {
+        ep.xa = a_e;
+        ep.xb = b_e;
+        ep.xa_blk = 256;
+        return gemm_plan(gp, (const float *)a_hi, (const float *)a_lo, b_hi, b_lo, Mg, Ng, Kg, ep, gemm_f16_cfg(), w);
+    };
+    const int Mp = n * G2;
+    const bool ok_patch = v->patch_f16
+        ? plan16(p->patch, v->f_lo, v->f_lo + (size_t)Mp * K0 / 2, v->p_e, v->patch_h, v->patch_l, v->patch_e, Mp, D,
+                 K0, e)
+        : plan(p->patch, v->p_hi, v->p_lo, v->patch_h, v->patch_l, v->patch_q, Mp, D, K0, e);
+    if (!ok_patch) return nullptr;
 
     GemmEpi pe;                                   // embedding = pooled x proj, into v->out
     pe.out.plain = v->out;
@@ -406,14 +463,27 @@ static tcg_vit::Plans *plans_for(tcg_vit *v, int n)
         GemmEpi u;
         u.bias = y.up_b;
         u.act = v->quick ? 2 : 1;
-        u.out.hi = v->f_hi;
-        u.out.lo = v->f_lo;
+        if (v->f16) {
+            u.out.plain = v->f_hi;                // fp32, split into pieces before the down projection
+        } else {
+            u.out.hi = v->f_hi;
+            u.out.lo = v->f_lo;
+        }
         u.out.ld = F;
         GemmEpi d;
         d.bias = y.down_b;
         d.residual = v->x;
         d.out.plain = v->x;
         d.out.ld = D;
+        if (v->f16) {
+            const float *fp_lo = v->f_lo + (size_t)M * F / 2;   // the f pieces: hi halves, then lo halves
+            if (!plan16(p->qkv[i], v->h_hi, v->h_lo, v->h_e, y.qkv_h, y.qkv_l, y.qkv_e, M, 3 * D, D, q) ||
+                !plan16(p->out[i], v->h_hi, v->h_lo, v->h_e, y.out_h, y.out_l, y.out_e, M, D, D, o) ||
+                !plan16(p->up[i], v->h_hi, v->h_lo, v->h_e, y.up_h, y.up_l, y.up_e, M, F, D, u) ||
+                !plan16(p->down[i], v->f_lo, fp_lo, v->f_e, y.down_h, y.down_l, y.down_e, M, D, F, d))
+                return nullptr;
+            continue;
+        }
         if (!plan(p->qkv[i], v->h_hi, v->h_lo, y.qkv_h, y.qkv_l, y.qkv_q, M, 3 * D, D, q) ||
             !plan(p->out[i], v->h_hi, v->h_lo, y.out_h, y.out_l, y.out_q, M, D, D, o) ||   // a aliases h
             !plan(p->up[i], v->h_hi, v->h_lo, y.up_h, y.up_l, y.up_q, M, F, D, u) ||
@@ -501,15 +571,32 @@ static bool forward_body(tcg_vit *v, tcg_vit::Plans *p, int n, Tapper *tap)
     PROF(K_NORM, launch_layernorm(v->x, D, v->ln_pre_g, v->ln_pre_b, M, D, v->eps, xs, s));
     if (tap && !tap->deliver("ln_pre", v->x, n, T, D, (size_t)T * D)) return false;
 
+    // fp16 pieces: LayerNorm writes them; the attention output and the GELU
+    // output go through f_hi as fp32 and are split
+    OutSpec h16; h16.fh = v->h_hi; h16.fl = v->h_lo; h16.fe = v->h_e; h16.fe_rows = M; h16.ld = D;
+    OutSpec a32; a32.plain = v->f_hi; a32.ld = D;
+    float *fp_lo = v->f_lo + (size_t)M * v->F / 2;
     for (int i = 0; i < v->L; i++) {
         const tcg_vit::Layer &y = v->layers[i];
-        PROF(K_NORM, launch_layernorm(v->x, D, y.ln1_g, y.ln1_b, M, D, v->eps, hs, s));
-        PROF(K_GEMM, run_gemm(p->qkv[i], s, err));
-        PROF(K_ATTN, launch_mha(v->qkv, v->qkv + D, v->qkv + 2 * D, 3 * D, T, v->H, v->hd, n, hs, s));
-        PROF(K_GEMM, run_gemm(p->out[i], s, err));
-        PROF(K_NORM, launch_layernorm(v->x, D, y.ln2_g, y.ln2_b, M, D, v->eps, hs, s));
-        PROF(K_GEMM, run_gemm(p->up[i], s, err));
-        PROF(K_GEMM, run_gemm(p->down[i], s, err));
+        if (v->f16) {
+            PROF(K_NORM, launch_layernorm(v->x, D, y.ln1_g, y.ln1_b, M, D, v->eps, h16, s));
+            PROF(K_GEMM, run_gemm(p->qkv[i], s, err));
+            PROF(K_ATTN, launch_mha(v->qkv, v->qkv + D, v->qkv + 2 * D, 3 * D, T, v->H, v->hd, n, a32, s));
+            PROF(K_OTHER, launch_split_f16(v->f_hi, M, D, v->h_hi, v->h_lo, v->h_e, 2, s));
+            PROF(K_GEMM, run_gemm(p->out[i], s, err));
+            PROF(K_NORM, launch_layernorm(v->x, D, y.ln2_g, y.ln2_b, M, D, v->eps, h16, s));
+            PROF(K_GEMM, run_gemm(p->up[i], s, err));
+            PROF(K_OTHER, launch_split_f16(v->f_hi, M, v->F, v->f_lo, fp_lo, v->f_e, 2, s));
+            PROF(K_GEMM, run_gemm(p->down[i], s, err));
+        } else {
+            PROF(K_NORM, launch_layernorm(v->x, D, y.ln1_g, y.ln1_b, M, D, v->eps, hs, s));
+            PROF(K_GEMM, run_gemm(p->qkv[i], s, err));
+            PROF(K_ATTN, launch_mha(v->qkv, v->qkv + D, v->qkv + 2 * D, 3 * D, T, v->H, v->hd, n, hs, s));
+            PROF(K_GEMM, run_gemm(p->out[i], s, err));
+            PROF(K_NORM, launch_layernorm(v->x, D, y.ln2_g, y.ln2_b, M, D, v->eps, hs, s));
+            PROF(K_GEMM, run_gemm(p->up[i], s, err));
+            PROF(K_GEMM, run_gemm(p->down[i], s, err));
+        }
         if (tap && i == 0 && !tap->deliver("blk0", v->x, n, T, D, (size_t)T * D)) return false;
         if (tap && i == v->L - 1 && !tap->deliver("blk_last", v->x, n, T, D, (size_t)T * D)) return false;
     }
@@ -535,7 +622,14 @@ static bool forward(tcg_vit *v, const float *px, int n, float *out, Tapper *tap)
     cudaStream_t s = ctx().cur;
     tcg_vit::Plans *p = plans_for(v, n);
     if (!p) return false;
-    PROF(K_OTHER, launch_patches(px, n, v->S, v->P, v->p_hi, v->p_lo, s));
+    if (v->patch_f16) {
+        // im2patch as fp32 rows, then their fp16 pieces
+        const int Mp = n * v->G * v->G, K0 = 3 * v->P * v->P;
+        PROF(K_OTHER, launch_patches(px, n, v->S, v->P, v->p_hi, nullptr, s));
+        PROF(K_OTHER, launch_split_f16(v->p_hi, Mp, K0, v->f_lo, v->f_lo + (size_t)Mp * K0 / 2, v->p_e, 2, s));
+    } else {
+        PROF(K_OTHER, launch_patches(px, n, v->S, v->P, v->p_hi, v->p_lo, s));
+    }
     if (tap || !v->graphs || g_prof.on) {
         if (!forward_body(v, p, n, tap)) return false;
     } else if (!p->graph) {
@@ -825,6 +919,15 @@ int tcg_vit_set_packed_weights(int on)
     g_vit_packed = on ? 1 : 0;
     return old;
 }
+
+int tcg_vit_set_f16(int on)
+{
+    const int old = g_vit_f16;
+    g_vit_f16 = on ? 1 : 0;
+    return old;
+}
+
+int tcg_vit_uses_f16(const tcg_vit_t *v) { return v && v->f16 ? 1 + (v->patch_f16 ? 1 : 0) : 0; }
 
 void tcg_vit_use_graphs(tcg_vit_t *v, bool on)
 {

@@ -76,19 +76,42 @@ class SplitOperands:
             b.close()
 
 
+class F16Operands(SplitOperands):
+    """x and W also as fp16 pieces with per-(row, 128-element K-block)
+    exponents (tcg_split_f16), for the kind::f16 GEMM."""
+
+    def __init__(self, M, N, K, seed=0, blk=128):
+        super().__init__(M, N, K, seed)
+        L = tcg.lib()
+        self.blk = blk
+        self.f = [tcg.DeviceBuffer(n) for n in (M * K * 2, M * K * 2, M * K // 128, N * K * 2, N * K * 2, N * K // 128)]
+        self.bufs += self.f
+        tcg.check(L.tcg_split_f16(self.f[0].ptr, self.f[1].ptr, self.f[2].ptr, self.bufs[0].ptr, M, K,
+                                  0 if blk == 128 else 2))
+        tcg.check(L.tcg_split_f16(self.f[3].ptr, self.f[4].ptr, self.f[5].ptr, self.bufs[1].ptr, N, K, 1))
+
+    def run(self, cfg):
+        f = self.f
+        tcg.check(tcg.lib().tcg_linear_f16_split(self.y.ptr, f[0].ptr, f[1].ptr, f[2].ptr, f[3].ptr, f[4].ptr,
+                                                 f[5].ptr, self.bufs[2].ptr, self.M, self.N, self.K, self.blk),
+                  "f16 GEMM")
+
+
 def case_gemm(a):
     old_sk = tcg.lib().tcg_gemm_set_streamk(a.streamk)
     old_tma = tcg.lib().tcg_gemm_set_tma_store(a.tma_store)
-    ops = SplitOperands(a.M, a.N, a.K)
+    ops = F16Operands(a.M, a.N, a.K, blk=a.f16) if a.f16 else SplitOperands(a.M, a.N, a.K)
     with tcg.DeviceBuffer(256 << 20) as flush:
         ms, _ = timed(lambda: ops.run(a.cfg), a.warmup, a.reps, flush)
+    err = ops.rel_err()
     plan = (ctypes.c_int * 4)()
     tcg.lib().tcg_gemm_last_plan(plan)
     ops.close()
     tcg.lib().tcg_gemm_set_streamk(old_sk)
     tcg.lib().tcg_gemm_set_tma_store(old_tma)
     flops = 2.0 * a.M * a.N * a.K
-    return {"case": "gemm", "M": a.M, "N": a.N, "K": a.K, "cfg": a.cfg, "streamk": a.streamk, "ms": round(ms, 4),
+    return {"case": "gemm", "M": a.M, "N": a.N, "K": a.K, "cfg": a.cfg, "f16": a.f16, "rel_err": err,
+            "streamk": a.streamk, "ms": round(ms, 4),
             "tflops": round(flops / ms / 1e9, 1), "grid": plan[0], "split": plan[1], "tma_store": plan[3]}
 
 
@@ -273,6 +296,8 @@ def main():
     g.add_argument("--cfg", type=int, default=-1)
     g.add_argument("--streamk", type=int, default=1)
     g.add_argument("--tma-store", type=int, default=1)
+    g.add_argument("--f16", type=int, default=0,
+                   help="128 or 256: fp16-piece operands on kind::f16 MMAs, A scaled per K-block of that size")
     gs = sub.add_parser("gemmsweep")
     gs.add_argument("--chunks", default="32,64,128,256,4096")
     gs.add_argument("--cfgs", default="all")

@@ -166,11 +166,14 @@ _SIGS = [
     ("tcg_softmax_rows", boolean, [vp, vp, i32, i32]),
     ("tcg_mha", boolean, [vp, vp, vp, vp, i32, i32, i32]),
     ("tcg_mha_images", boolean, [vp, vp, vp, vp, i32, i32, i32, i32]),
+    ("tcg_split_f16", boolean, [vp, vp, vp, vp, i32, i32, i32]),
+    ("tcg_linear_f16_split", boolean, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32]),
     ("tcg_add", boolean, [vp, vp, vp, sz]), ("tcg_scale", boolean, [vp, vp, f32, sz]),
     ("tcg_vit_upload", vp, [C.POINTER(Vit), i32]), ("tcg_vit_release", None, [vp]),
     ("tcg_vit_max_batch", i32, [vp]), ("tcg_vit_device_bytes", sz, [vp]),
     ("tcg_vit_use_graphs", None, [vp, boolean]),
     ("tcg_vit_set_upload_mode", i32, [i32]), ("tcg_vit_set_packed_weights", i32, [i32]),
+    ("tcg_vit_set_f16", i32, [i32]), ("tcg_vit_uses_f16", i32, [vp]),
     ("tcg_vit_gemm_weight_bytes", sz, [vp]), ("tcg_vit_set_jit_rows", C.c_long, [C.c_long]), ("tcg_vit_last_upload_ms", C.c_double, []),
     ("tcg_vit_upload_fallback", C.c_char_p, []),
     ("tcg_vit_encode_batch", boolean, [vp, vp, i32, vp, vp, vp]),

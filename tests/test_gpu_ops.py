@@ -247,6 +247,42 @@ def test_mha_tensor_core_long(dev, T, H):
     assert L.tcg_device_error() == 0
 
 
+@pytest.mark.parametrize("blk", [128, 256])
+@pytest.mark.parametrize("M,N,K", [(128, 128, 256), (300, 768, 768), (1600, 768, 768), (257, 3072, 768),
+                                   (513, 768, 3072), (12800, 768, 768)])
+def test_linear_f16_pieces(dev, M, N, K, blk):
+    """kind::f16 GEMM on fp16-piece operands (tcg_split_f16: power-of-two
+    scales per (row, 128-element K-block) of x and per row of W, two pieces of
+    11 bits): within
+    the tf32-pair GEMM's bound of the oracle, on rows spanning 1e-12 .. 1e12,
+    a weight row of 1e9 and a zero K-block (blocks are exact for largest
+    magnitudes in [2^-49, 2^77))."""
+    L = tcg.lib()
+    rng = np.random.default_rng(M + N + K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    x[: M // 4] *= np.float32(1e-12)
+    x[M // 4: M // 2] *= np.float32(1e12)
+    x[:, :blk] *= 0
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    W[N // 3] *= np.float32(1e9)
+    b = rng.standard_normal(N).astype(np.float32)
+    xd, Wd, bd = dev.put(x), dev.put(W), dev.put(b)
+    f = [dev.empty(n) for n in (M * K // 2, M * K // 2, M * K // 512 + 1, N * K // 2, N * K // 2, N * K // 512 + 1)]
+    tcg.check(L.tcg_split_f16(f[0].ptr, f[1].ptr, f[2].ptr, xd, M, K, 0 if blk == 128 else 2))
+    tcg.check(L.tcg_split_f16(f[3].ptr, f[4].ptr, f[5].ptr, Wd, N, K, 1))
+    y = dev.empty(M * N)
+    tcg.check(L.tcg_linear_f16_split(y.ptr, f[0].ptr, f[1].ptr, f[2].ptr, f[3].ptr, f[4].ptr, f[5].ptr, bd,
+                                     M, N, K, blk))
+    got = y.download((M, N)).astype(np.float64)
+    want = x.astype(np.float64) @ W.astype(np.float64).T + b
+    # each row band against its own magnitude (the rows differ by 24 decades)
+    for lo, hi in ((0, M // 4), (M // 4, M // 2), (M // 2, M)):
+        if hi > lo:
+            g, w = got[lo:hi], want[lo:hi]
+            assert np.abs(g - w).max() <= GEMM_TOL * np.abs(w).max(), (lo, hi)
+    assert L.tcg_device_error() == 0
+
+
 SHAPES = [(1, 64, 4), (127, 100, 12), (129, 200, 588), (300, 768, 768), (50, 2304, 768), (261, 130, 3072)]
 
 

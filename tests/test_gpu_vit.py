@@ -92,7 +92,11 @@ def test_b32_one_wave_shapes_vs_oracle(gpu, cache_dir):
     px = G.make_pixels(64, cfg["image"], 3)
     m = tcg.VitModel(path)
     try:
-        m.upload(64)
+        old_f16 = L.tcg_vit_set_f16(0)          # the tf32-pair GEMMs' shape rule
+        try:
+            m.upload(64)
+        finally:
+            L.tcg_vit_set_f16(old_f16)
         out, taps = m.encode(px, taps=True)
         plan = (ctypes.c_int * 4)()
         L.tcg_gemm_last_plan(plan)              # the last plan made: the last layer's down projection
@@ -352,7 +356,7 @@ def test_packed_q4k_weights_model(gpu, tmp_path, n_img, jit_rows):
     for name, (blocks, qt, shape) in made["kquant"].items():
         w[name] = oracle.dequant(blocks, int(np.prod(shape)), qt).reshape(shape)
     px = G.make_pixels(n_img, cfg["image"], 6)
-    outs, nbytes = {}, {}
+    outs, nbytes, f16 = {}, {}, {}
     for packed in (1, 0):
         old = L.tcg_vit_set_packed_weights(packed)
         m = tcg.VitModel(path)
@@ -360,6 +364,7 @@ def test_packed_q4k_weights_model(gpu, tmp_path, n_img, jit_rows):
             m.upload(n_img)
             outs[packed] = m.encode(px, taps=True)
             nbytes[packed] = L.tcg_vit_gemm_weight_bytes(m.dev)
+            f16[packed] = L.tcg_vit_uses_f16(m.dev)
         finally:
             m.close()
             L.tcg_vit_set_packed_weights(old)
@@ -367,8 +372,13 @@ def test_packed_q4k_weights_model(gpu, tmp_path, n_img, jit_rows):
     D, F, L_, K0 = cfg["d_model"], cfg["d_ffn"], cfg["n_layer"], 3 * cfg["patch"] ** 2
     linear = L_ * (3 * D * D + D * D + 2 * F * D)
     # packed blocks (each tensor's slot padded to 256 bytes) plus the patch embedding's tf32 pair
+    assert f16[1] == 0
     assert abs(nbytes[1] - (linear // 256 * 144 + 8 * D * K0)) <= 256 * 4 * L_
-    assert nbytes[0] == 8 * (linear + D * K0)
+    # dequantised at load, every weight fp32 on the device: fp16 pieces (4 bytes
+    # a weight, one exponent per row, slots padded to 256 bytes)
+    assert f16[0] == 2
+    rows = L_ * (3 * D + D + F + D) + D
+    assert 4 * (linear + D * K0) + rows <= nbytes[0] <= 4 * (linear + D * K0) + rows + 3 * 256 * (4 * L_ + 1)
     out, taps = outs[1]
     port = oracle.PortVit(cfg, w)
     for i in sorted({0, n_img - 1}):
@@ -379,6 +389,39 @@ def test_packed_q4k_weights_model(gpu, tmp_path, n_img, jit_rows):
             assert rel_inf(taps[k][i], ref[k]) <= TOL, (i, k)
     for i in range(n_img):
         assert rel_inf(out[i], outs[0][0][i]) <= 1e-5, i
+    assert L.tcg_device_error() == 0
+
+
+@pytest.mark.parametrize("n_img", [3, 64])
+def test_fp16_piece_and_tf32_pair_gemms(gpu, cache_dir, n_img):
+    """The same fp32 ViT-B/32 (two layers) with its GEMMs on fp16 pieces
+    (tcg_vit_set_f16(1), the default: LayerNorm writes the pieces, the
+    attention and GELU outputs are split) and on tf32 pairs: both against the
+    oracle per tap, and against each other."""
+    L = tcg.lib()
+    path, cfg = model(cache_dir, "vit-b32", n_layer=2)
+    px = G.make_pixels(n_img, cfg["image"], 12)
+    outs = {}
+    for mode in (1, 0):
+        old = L.tcg_vit_set_f16(mode)
+        m = tcg.VitModel(path)
+        try:
+            m.upload(n_img)
+            assert L.tcg_vit_uses_f16(m.dev) == (2 if mode else 0)
+            outs[mode] = m.encode(px, taps=True)
+        finally:
+            m.close()
+            L.tcg_vit_set_f16(old)
+    port = oracle.PortVit(cfg, G.make_vit_weights(cfg, 0))
+    for i in range(n_img):
+        assert rel_inf(outs[1][0][i], outs[0][0][i]) <= 1e-5, i
+    for mode in (1, 0):
+        out, taps = outs[mode]
+        for i in sorted({0, n_img - 1}):
+            ref = port.forward(px[i])
+            assert rel_inf(out[i], ref["embedding"]) <= TOL, (mode, i)
+            for k in TAPS:
+                assert rel_inf(taps[k][i], ref[k]) <= TOL, (mode, i, k)
     assert L.tcg_device_error() == 0
 
 
