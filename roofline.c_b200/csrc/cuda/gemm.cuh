@@ -39,7 +39,14 @@ struct GemmEpi {
     // (undone in the drain), B row n by 2^xb[n] over all of K (per tile)
     const int8_t *xa = nullptr;
     const int8_t *xb = nullptr;
-    int xa_blk = 128;        // elements per K-block of A (128 or 256): one TMEM chunk each
+    int xa_blk = 128;        // elements per K-block of A (128 or 256: one TMEM chunk each; 0: one per row, xa[m])
+    // fp16-piece output (out.fh, out.fl, out.fe: one exponent per row), the
+    // exponent taken from a bound on every value of the row:
+    // |value| <= rnorm[row] * bounds[0] + bounds[1] (the row's input norm times
+    // the largest weight-row norm, plus the largest |bias|, which bounds a
+    // linear layer's output and, after it, GELU's)
+    const float *rnorm = nullptr;
+    const float *bounds = nullptr;
 };
 
 // Device memory for the stream-K split of a GEMM's last, partial wave of

@@ -254,8 +254,9 @@ __device__ __forceinline__ void drain_add2_scaled(uint32_t ta, uint32_t tb, floa
 // acc[j] *= 2^-xb[n0 + j]: B row (output column) n was scaled by 2^xb[n] over
 // all of K. |xb| <= 63 and the row factors are at most 2^63, so the partial
 // sums stay finite and both multiplications are exact.
+// (ea: the row's exponent when A is scaled per row, else 0)
 template <int HALF>
-__device__ __forceinline__ void scale_cols(float (&acc)[HALF], const int8_t *xb, int n0, int N)
+__device__ __forceinline__ void scale_cols(float (&acc)[HALF], const int8_t *xb, int n0, int N, int ea)
 {
 #pragma unroll
     for (int j = 0; j < HALF; j += 8) {
@@ -264,9 +265,40 @@ __device__ __forceinline__ void scale_cols(float (&acc)[HALF], const int8_t *xb,
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             const int eb = (int)(int8_t)(((i < 4 ? e8.x : e8.y) >> (8 * (i & 3))) & 0xFFu);
-            acc[j + i] = __fmul_rn(acc[j + i], __int_as_float((127 - eb) << 23));
+            acc[j + i] = __fmul_rn(acc[j + i], __int_as_float((127 - ea - eb) << 23));
         }
     }
+}
+
+// fp16-piece output of this lane's row, columns n0 .. n0 + HALF - 1: bias and
+// activation as epi_value, then the row's power-of-two scale from the bound
+// rnorm[m] * bounds[0] + bounds[1] (with 1/256 to spare for rounding), then
+// the two pieces; the exponent is written by the lanes of column 0.
+template <int HALF>
+__device__ __forceinline__ void epi_store_f16(const GemmEpi &e, const float (&acc)[HALF], int m, int n0, int M, int N)
+{
+    if (m >= M) return;
+    const float bound = __fmul_rn(fmaf(e.rnorm[m], e.bounds[0], e.bounds[1]), 1.00390625f);
+    const int ex = f16_scale_exp(bound);
+    const float f = __int_as_float((127 + ex) << 23);
+    __half *fh = (__half *)e.out.fh, *fl = (__half *)e.out.fl;
+#pragma unroll
+    for (int j = 0; j < HALF; j += 8) {
+        if (n0 + j >= N) break;
+        float a[4], b[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            a[i] = epi_value(e, acc[j + i], m, n0 + j + i);
+            b[i] = epi_value(e, acc[j + 4 + i], m, n0 + j + 4 + i);
+        }
+        uint2 ha, la, hb, lb;
+        f16_pieces4(a, f, ha, la);
+        f16_pieces4(b, f, hb, lb);
+        const size_t at = (size_t)m * e.out.ld + n0 + j;
+        *reinterpret_cast<uint4 *>(fh + at) = make_uint4(ha.x, ha.y, hb.x, hb.y);
+        *reinterpret_cast<uint4 *>(fl + at) = make_uint4(la.x, la.y, lb.x, lb.y);
+    }
+    if (n0 == 0) e.out.fe[m] = (int8_t)ex;
 }
 
 __device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
@@ -457,6 +489,61 @@ __device__ __forceinline__ void epi_store_tile_tma(const GemmEpi &e, const float
         rc0 = rn0;
         rc1 = rn1;
     }
+}
+
+// epi_store_f16 through bulk tensor stores: 16-column units (32 bytes of
+// each of the warp's 32 rows, the fp32 path's 8-column geometry) of the hi
+// pieces, then of the lo pieces, staged in the warp's two 32 x 32-byte
+// buffers (32-byte swizzle) and stored by fp16 output maps.
+template <int HALF>
+__device__ __forceinline__ void epi_store_f16_tma(const GemmEpi &e, const float (&acc)[HALF], float *stage,
+                                                  const CUtensorMap *mh, const CUtensorMap *ml, int row0, int n0,
+                                                  int M, int N, const float (&breg)[(HALF + 31) / 32])
+{
+    static_assert(HALF % 16 == 0, "16-column store units");
+    if (row0 >= M) return;
+    const int lane = threadIdx.x & 31;
+    const int r = row0 + lane;
+    const float bound = r < M ? __fmul_rn(fmaf(e.rnorm[r], e.bounds[0], e.bounds[1]), 1.00390625f) : 0.0f;
+    const int ex = f16_scale_exp(bound);
+    const float f = __int_as_float((127 + ex) << 23);
+    const int sw = (lane >> 2) & 1;
+    int buf = 0;
+#pragma unroll
+    for (int u = 0; u < HALF / 16; u++) {
+        const int n = n0 + 16 * u;
+        if (n >= N) break;
+        float x[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            const int c = 16 * u + j;
+            float v = acc[c];
+            if (e.bias) v = __fadd_rn(v, __shfl_sync(0xffffffffu, breg[c / 32], c % 32));
+            if (e.act == 1) v = gelu_exact(v);
+            else if (e.act == 2) v = gelu_quick(v);
+            x[j] = v;
+        }
+        uint2 h[4], l[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const float v4[4] = { x[4 * q], x[4 * q + 1], x[4 * q + 2], x[4 * q + 3] };
+            f16_pieces4(v4, f, h[q], l[q]);
+        }
+#pragma unroll
+        for (int o = 0; o < 2; o++) {
+            const uint2 *y = o == 0 ? h : l;
+            if (lane == 0) bulk_wait_read<1>();     // the store that used this buffer last has read it
+            __syncwarp();
+            float *b = stage + buf * 256;
+            *reinterpret_cast<uint4 *>(b + lane * 8 + 4 * sw) = make_uint4(y[0].x, y[0].y, y[1].x, y[1].y);
+            *reinterpret_cast<uint4 *>(b + lane * 8 + 4 * (sw ^ 1)) = make_uint4(y[2].x, y[2].y, y[3].x, y[3].y);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) tma_store(o == 0 ? mh : ml, su32(b), n, row0);
+            buf ^= 1;
+        }
+    }
+    if (n0 == 0 && r < M) e.out.fe[r] = (int8_t)ex;
 }
 
 // acc[0..HALF) += the HALF fp32 columns at TMEM address taddr (this warp's
@@ -806,11 +893,15 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                 if (!bar_wait(cfull0 + 8 * b, (chunk / NBUF) & 1, abort, err, 6)) { ok = false; break; }
                 fence_after();
                 if constexpr (OPF) {
-                    // this chunk is one 128-element K-block: undo the row's and the columns' scales
-                    const int m = (sg.tile / n_tiles) * BM + q * 32 + lane;
-                    const int ea = m < M ? (int)epi.xa[(size_t)c * M + m] : 0;
-                    drain_add2_scaled<S::HALF>(tmem + lane_cols + b * CW, tmem + lane_cols + b * CW + BN, acc,
-                                               __int_as_float((127 - ea) << 23));
+                    if (epi.xa_blk) {
+                        // this chunk is one K-block of A: undo the row's scale of the block
+                        const int m = (sg.tile / n_tiles) * BM + q * 32 + lane;
+                        const int ea = m < M ? (int)epi.xa[(size_t)c * M + m] : 0;
+                        drain_add2_scaled<S::HALF>(tmem + lane_cols + b * CW, tmem + lane_cols + b * CW + BN, acc,
+                                                   __int_as_float((127 - ea) << 23));
+                    } else {
+                        drain_add2<S::HALF>(tmem + lane_cols + b * CW, tmem + lane_cols + b * CW + BN, acc);
+                    }
                 } else if constexpr (WIDE) drain_add2<S::HALF>(tmem + lane_cols + b * CW, tmem + lane_cols + b * CW + BN, acc);
                 else drain_add<S::HALF, S::LDW>(tmem + lane_cols + b * CW, acc);
                 fence_before();
@@ -864,7 +955,18 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                 if (!ok) break;
             }
             const int m0 = (sg.tile / n_tiles) * CG * BM + (int)rank * BM, n0 = (sg.tile % n_tiles) * BN;
-            if constexpr (OPF) scale_cols<S::HALF>(acc, epi.xb, n0 + h * S::HALF, N);
+            if constexpr (OPF) {
+                const int m = m0 + q * 32 + lane;
+                scale_cols<S::HALF>(acc, epi.xb, n0 + h * S::HALF, N, epi.xa_blk || m >= M ? 0 : (int)epi.xa[m]);
+                if (epi.out.fh) {
+                    if (epi.tma)
+                        epi_store_f16_tma<S::HALF>(epi, acc, epi_stage + ew * (S::EPI_STAGE_BYTES / 4), &o_hi, &o_lo,
+                                                   m0 + q * 32, n0 + h * S::HALF, M, N, breg);
+                    else
+                        epi_store_f16<S::HALF>(epi, acc, m, n0 + h * S::HALF, M, N);
+                    continue;
+                }
+            }
             if (epi.tma)
                 epi_store_tile_tma<S::HALF>(epi, acc, epi_stage + ew * (S::EPI_STAGE_BYTES / 4), &o_plain, &o_hi,
                                             &o_lo, m0 + q * 32, n0 + h * S::HALF, M, N, breg);
@@ -1030,6 +1132,22 @@ bool encode_kmajor_f16(CUtensorMap *m, const void *ptr, int rows, int K, int box
     return true;
 }
 
+// fp16-piece output map: rows x cols fp16, row stride ld elements, boxes of
+// 32 rows x 16 columns (32 bytes) in the 32-byte swizzle.
+bool encode_out_f16(CUtensorMap *m, const void *ptr, int rows, int cols, int ld)
+{
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail("cuTensorMapEncodeTiled is not available from the driver");
+    cuuint64_t dims[2] = { (cuuint64_t)cols, (cuuint64_t)rows };
+    cuuint64_t strides[1] = { (cuuint64_t)ld * 2u };
+    cuuint32_t box[2] = { 16, 32 };
+    cuuint32_t estr[2] = { 1, 1 };
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)ptr, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 // Output map for the bulk-store epilogue: rows x cols fp32 with row stride
 // ld, boxes of 32 rows x 8 columns in the 32-byte swizzle.
 bool encode_out(CUtensorMap *m, const float *ptr, int rows, int cols, int ld)
@@ -1191,7 +1309,10 @@ bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b
     const int b_rows = c.bn / c.cg;                     // B box: this CTA's share of the tile columns
     if (c.opf) {
         // fp16 pieces and their per-K-block exponents
-        if (K % epi.xa_blk || N % 8 || !epi.xa || !epi.xb || (epi.xa_blk != 128 && epi.xa_blk != 256))
+        if ((epi.xa_blk && K % epi.xa_blk) || N % 8 || !epi.xa || !epi.xb ||
+            (epi.xa_blk != 0 && epi.xa_blk != 128 && epi.xa_blk != 256) ||
+            (epi.out.fh && (!epi.out.fl || !epi.out.fe || !epi.rnorm || !epi.bounds || epi.out.ld % 8 ||
+                            epi.out.plain || epi.out.hi)))
             return fail("gemm_plan: fp16-piece operands need K %% 128 == 0, N %% 8 == 0 and both exponent arrays");
         if (!encode_kmajor_f16(&p.a_hi, a_hi, M, K, BM) || !encode_kmajor_f16(&p.a_lo, a_lo, M, K, BM) ||
             !encode_kmajor_f16(&p.b_hi, b_hi, N, K, b_rows) || !encode_kmajor_f16(&p.b_lo, b_lo, N, K, b_rows))
@@ -1220,7 +1341,11 @@ bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b
                     !(epi.rowadd && epi.residual);
         // bulk tensor stores need one output row per GEMM row (no remap)
         p.epi.tma = false;
-        if (g_tma_store && p.epi.vec && !epi.rowadd && epi.rgroup >= M && epi.roff >= 0) {
+        if (g_tma_store && epi.out.fh && N % 16 == 0 && epi.out.ld % 8 == 0 && !epi.rowadd && epi.rgroup >= M &&
+            epi.roff == 0 && !(((uintptr_t)epi.out.fh | (uintptr_t)epi.out.fl) & 15))
+            p.epi.tma = encode_out_f16(&p.o_hi, epi.out.fh, M, N, epi.out.ld) &&
+                        encode_out_f16(&p.o_lo, epi.out.fl, M, N, epi.out.ld);
+        if (g_tma_store && p.epi.vec && !epi.rowadd && epi.rgroup >= M && epi.roff >= 0 && !epi.out.fh) {
             const size_t off = (size_t)epi.roff * epi.out.ld;
             p.epi.tma = (!epi.out.plain || encode_out(&p.o_plain, epi.out.plain + off, M, N, epi.out.ld)) &&
                         (!epi.out.hi || encode_out(&p.o_hi, epi.out.hi + off, M, N, epi.out.ld)) &&
@@ -1259,7 +1384,7 @@ bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b
     // wave leaves at least half the SMs idle, or when a tile has many chunks
     // (fine units); with 2-5 chunks and a fuller last wave the partial-sum
     // hand-over costs what it saves.
-    const int chunk_k = c.opf ? epi.xa_blk : g_chunk_k;
+    const int chunk_k = c.opf && epi.xa_blk ? epi.xa_blk : g_chunk_k;
     const int chunks = (K + chunk_k - 1) / chunk_k;
     const int last = tiles % groups;
     const bool pays = g_streamk == 2 || last <= groups / 2 || chunks >= 6;
@@ -1290,7 +1415,7 @@ bool gemm_run(const GemmPlan &p, cudaStream_t s, int *err)
         attr_done[dev] |= 1ull << p.cfg;
     }
     // fp16 pieces: one TMEM chunk per K-block of A (its scale)
-    int chunk_kb = c.opf ? p.epi.xa_blk / c.bk : g_chunk_k / c.bk;
+    int chunk_kb = c.opf && p.epi.xa_blk ? p.epi.xa_blk / c.bk : g_chunk_k / c.bk;
     if (chunk_kb < 1) chunk_kb = 1;
     float *ws = p.work.ws;
     int *flags = p.work.flags;

@@ -116,6 +116,16 @@ layernorm_vec_kernel(const float *x, int ld_in, const float *__restrict__ g, con
                 o[i][k] = t;
             }
         }
+        if (out.rnorm) {
+            float ss = 0.0f;
+#pragma unroll
+            for (int i = 0; i < VPL; i++)
+#pragma unroll
+                for (int k = 0; k < 4; k++) ss = fmaf(o[i][k], o[i][k], ss);
+#pragma unroll
+            for (int d = 16; d >= 1; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
+            if (lane == 0) out.rnorm[row] = sqrtf(ss);
+        }
 #pragma unroll
         for (int bk = 0; bk < VPL / 2; bk++) {
             float m = 0.0f;
@@ -1248,6 +1258,32 @@ __global__ void patches_kernel(const float *__restrict__ px, int n_img, int S, i
         reinterpret_cast<V *>(hi)[i] = h;
         reinterpret_cast<V *>(lo)[i] = l;
     }
+}
+
+// One warp per row of W: its 2-norm (and |b| of the row) into bounds by an
+// integer max on the bit patterns (non-negative floats order as integers).
+__global__ void weight_bounds_kernel(const float *__restrict__ W, int rows, int K, const float *__restrict__ b,
+                                     float *bounds)
+{
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    float ss = 0.0f;
+    for (int k = lane; k < K; k += 32) ss = fmaf(W[(size_t)row * K + k], W[(size_t)row * K + k], ss);
+#pragma unroll
+    for (int d = 16; d >= 1; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
+    if (lane == 0) {
+        atomicMax(reinterpret_cast<int *>(bounds), __float_as_int(sqrtf(ss)));
+        if (b) atomicMax(reinterpret_cast<int *>(bounds) + 1, __float_as_int(fabsf(b[row])));
+    }
+}
+
+bool launch_weight_bounds(const float *W, int rows, int K, const float *b, float *bounds, cudaStream_t s)
+{
+    if (rows <= 0) return true;
+    weight_bounds_kernel<<<ceil_div(rows, 8), 256, 0, s>>>(W, rows, K, b, bounds);
+    TCG_LAUNCHED();
+    return true;
 }
 
 bool launch_patches(const float *px, int n_img, int S, int P, float *hi, float *lo, cudaStream_t s)

@@ -19,7 +19,12 @@ struct OutSpec {
     void *fl = nullptr;
     int8_t *fe = nullptr;
     int fe_rows = 0;
+    float *rnorm = nullptr;    // LayerNorm with fp16 pieces: each output row's 2-norm
 };
+
+// bounds[0] = the largest 2-norm of W's rows ([rows, K]), bounds[1] = the
+// largest |b| (b: rows values, or none); bounds must start at zero.
+bool launch_weight_bounds(const float *W, int rows, int K, const float *b, float *bounds, cudaStream_t s);
 
 // fp32 rows -> fp16 pieces (gemm_tc.cu): mode 0 / 2 one exponent per (row,
 // 128- / 256-element K-block), mode 1 one per row.

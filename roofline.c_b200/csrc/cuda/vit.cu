@@ -77,6 +77,10 @@ struct tcg_vit {
     // pieces live in h_hi / h_lo, f's and the patches' in f_lo (hi half
     // first), their fp32 source in f_hi
     int8_t *h_e = nullptr, *f_e = nullptr, *p_e = nullptr;
+    // fp16 pieces: LN2's output row norms and each layer's up-projection
+    // bounds (largest weight-row norm, largest |bias|): the GELU output's
+    // per-row scale is taken from them in the up projection's epilogue
+    float *rnorm = nullptr, *up_bounds = nullptr;
     tcg::GemmWork work;                       // this model's GEMM stream-K memory (in the arena)
 
     struct Plans {
@@ -300,7 +304,8 @@ static tcg_vit *vit_alloc(const tc_vit_t *m, int max_batch, std::vector<WEntry> 
     const size_t f_floats = std::max(n * T * F, n * G2 * K0);
     const int ctas = ctx().sms > 0 ? ctx().sms : 148;
     const size_t ws_floats = gemm_work_ws_floats(ctas), flag_count = gemm_work_flag_count(ctas);
-    const size_t e_bytes = n * T * (D + F) / 256 + n * G2 * K0 / 256 + 3 * 256;   // fp16-piece exponents
+    const size_t e_bytes = n * T * (D + F) / 256 + n * G2 * K0 / 256 + 3 * 256 +   // fp16-piece exponents,
+                           (n * T + 2 * (size_t)v->L) * sizeof(float) + 2 * 256;        // row norms, bounds
     const size_t want = (n * 3 * v->S * v->S + n * T * D * 3 + n * T * 3 * D + 2 * f_floats +
                          2 * n * D + n * v->d_out + ws_floats + flag_count) * sizeof(float) + e_bytes + 16 * 256;
     v->act = tcg_arena_create(want, "vit activations");
@@ -322,6 +327,8 @@ static tcg_vit *vit_alloc(const tc_vit_t *m, int max_batch, std::vector<WEntry> 
         v->h_e = (int8_t *)tcg_arena_alloc(&v->act, n * T * D / 256, 256);
         v->f_e = (int8_t *)tcg_arena_alloc(&v->act, n * T * F / 256, 256);
         v->p_e = v->patch_f16 ? (int8_t *)tcg_arena_alloc(&v->act, n * G2 * K0 / 256, 256) : nullptr;
+        v->rnorm = alloc(n * T);
+        v->up_bounds = alloc(2 * (size_t)v->L);
     }
     v->work.ws = alloc(ws_floats);
     v->work.flags = (int *)alloc(flag_count);
@@ -351,6 +358,7 @@ static bool split_weights(tcg_vit *v, const std::vector<WEntry> &table, const st
     };
     if (!(v->patch_f16 ? split16(0, v->patch_h, v->patch_l, v->patch_e, D, K0) : split(0, v->patch_h, v->patch_l, D * K0)))
         return false;
+    if (v->f16) TCG_CUDA(cudaMemsetAsync(v->up_bounds, 0, 2 * (size_t)v->L * sizeof(float), s));
     for (int i = 0; i < v->L; i++) {
         const size_t b = 8 + 12 * (size_t)i;   // first entry of block i in weight_table
         tcg_vit::Layer &y = v->layers[i];
@@ -361,6 +369,8 @@ static bool split_weights(tcg_vit *v, const std::vector<WEntry> &table, const st
                                : split(b + 2, y.qkv_h, y.qkv_l, 3 * D * D) && split(b + 4, y.out_h, y.out_l, D * D) &&
                                      split(b + 8, y.up_h, y.up_l, F * D) && split(b + 10, y.down_h, y.down_l, D * F);
         if (!ok) return false;
+        if (v->f16 && !launch_weight_bounds(v->wslab + off[b + 8], (int)F, (int)D, y.up_b, v->up_bounds + 2 * i, s))
+            return false;
     }
     {   // v.proj is [D, d_out] (used untransposed, src/vit.c:384-386): store it as the [d_out, D] operand
         if (!launch_transpose_split(v->proj, v->D, v->d_out, (float *)v->projT_h, (float *)v->projT_l, s))
@@ -463,8 +473,14 @@ static tcg_vit::Plans *plans_for(tcg_vit *v, int n)
         GemmEpi u;
         u.bias = y.up_b;
         u.act = v->quick ? 2 : 1;
+        const float *fp_lo0 = v->f_lo + (size_t)M * F / 2;   // the f pieces: hi halves, then lo halves
         if (v->f16) {
-            u.out.plain = v->f_hi;                // fp32, split into pieces before the down projection
+            // fp16 pieces of the GELU output, one exponent per row from LN2's row norm and the bounds
+            u.out.fh = v->f_lo;
+            u.out.fl = (void *)fp_lo0;
+            u.out.fe = v->f_e;
+            u.rnorm = v->rnorm;
+            u.bounds = v->up_bounds + 2 * i;
         } else {
             u.out.hi = v->f_hi;
             u.out.lo = v->f_lo;
@@ -476,11 +492,14 @@ static tcg_vit::Plans *plans_for(tcg_vit *v, int n)
         d.out.plain = v->x;
         d.out.ld = D;
         if (v->f16) {
-            const float *fp_lo = v->f_lo + (size_t)M * F / 2;   // the f pieces: hi halves, then lo halves
+            GemmEpi d16 = d;
+            d16.xa = v->f_e;                        // one exponent per row (the GELU output's bound)
+            d16.xb = y.down_e;
+            d16.xa_blk = 0;
             if (!plan16(p->qkv[i], v->h_hi, v->h_lo, v->h_e, y.qkv_h, y.qkv_l, y.qkv_e, M, 3 * D, D, q) ||
                 !plan16(p->out[i], v->h_hi, v->h_lo, v->h_e, y.out_h, y.out_l, y.out_e, M, D, D, o) ||
                 !plan16(p->up[i], v->h_hi, v->h_lo, v->h_e, y.up_h, y.up_l, y.up_e, M, F, D, u) ||
-                !plan16(p->down[i], v->f_lo, fp_lo, v->f_e, y.down_h, y.down_l, y.down_e, M, D, F, d))
+                !gemm_plan(p->down[i], v->f_lo, fp_lo0, y.down_h, y.down_l, M, D, F, d16, gemm_f16_cfg(), w))
                 return nullptr;
             continue;
         }
@@ -571,11 +590,11 @@ static bool forward_body(tcg_vit *v, tcg_vit::Plans *p, int n, Tapper *tap)
     PROF(K_NORM, launch_layernorm(v->x, D, v->ln_pre_g, v->ln_pre_b, M, D, v->eps, xs, s));
     if (tap && !tap->deliver("ln_pre", v->x, n, T, D, (size_t)T * D)) return false;
 
-    // fp16 pieces: LayerNorm writes them; the attention output and the GELU
-    // output go through f_hi as fp32 and are split
+    // fp16 pieces: LayerNorm and the up projection write them; the attention
+    // output goes through f_hi as fp32 and is split
     OutSpec h16; h16.fh = v->h_hi; h16.fl = v->h_lo; h16.fe = v->h_e; h16.fe_rows = M; h16.ld = D;
+    OutSpec h16n = h16; h16n.rnorm = v->rnorm;     // LN2: also the row norms for the GELU output's scale
     OutSpec a32; a32.plain = v->f_hi; a32.ld = D;
-    float *fp_lo = v->f_lo + (size_t)M * v->F / 2;
     for (int i = 0; i < v->L; i++) {
         const tcg_vit::Layer &y = v->layers[i];
         if (v->f16) {
@@ -584,9 +603,8 @@ static bool forward_body(tcg_vit *v, tcg_vit::Plans *p, int n, Tapper *tap)
             PROF(K_ATTN, launch_mha(v->qkv, v->qkv + D, v->qkv + 2 * D, 3 * D, T, v->H, v->hd, n, a32, s));
             PROF(K_OTHER, launch_split_f16(v->f_hi, M, D, v->h_hi, v->h_lo, v->h_e, 2, s));
             PROF(K_GEMM, run_gemm(p->out[i], s, err));
-            PROF(K_NORM, launch_layernorm(v->x, D, y.ln2_g, y.ln2_b, M, D, v->eps, h16, s));
+            PROF(K_NORM, launch_layernorm(v->x, D, y.ln2_g, y.ln2_b, M, D, v->eps, h16n, s));
             PROF(K_GEMM, run_gemm(p->up[i], s, err));
-            PROF(K_OTHER, launch_split_f16(v->f_hi, M, v->F, v->f_lo, fp_lo, v->f_e, 2, s));
             PROF(K_GEMM, run_gemm(p->down[i], s, err));
         } else {
             PROF(K_NORM, launch_layernorm(v->x, D, y.ln1_g, y.ln1_b, M, D, v->eps, hs, s));
