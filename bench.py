@@ -47,11 +47,12 @@ CACHE = os.environ.get("TCG_BENCH_CACHE", "/tmp/roofline_b200_bench")
 PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
-# DRAM bytes (read + write) per launch of the dominant kernel, the 3xTF32
-# GEMM, averaged over the 50 GEMM launches of one ViT-B/32 forward at batch
-# 256: one-pass ncu capture of dram__bytes_read.sum + dram__bytes_write.sum
-# over that forward's launches. It applies to that workload only.
-NCU_GEMM_TRAFFIC_PER_LAUNCH = 289.5e6
+# DRAM bytes (read + write) per launch of the dominant kernel, the GEMM,
+# averaged over the 50 GEMM launches of one ViT-B/32 forward at batch 256:
+# one-pass ncu capture of dram__bytes_read.sum + dram__bytes_write.sum over
+# that forward's launches, per GEMM path (fp16 pieces, tf32 pairs). It
+# applies to that workload only.
+NCU_GEMM_TRAFFIC_PER_LAUNCH = {"f16": None, "tf32": 289.5e6}
 NCU_GEMM_TRAFFIC_WORKLOAD = ("vit-b32", 256)
 
 
@@ -545,6 +546,7 @@ def run_ours(args, dist):
     tcg.check(L.tcg_vit_profile_end(kms, kcount), "profile")
     launches = L.tcg_vit_launches_per_forward(model.dev)
     fp32_gemm_bytes = L.tcg_vit_gemm_weight_bytes(model.dev)
+    f16 = L.tcg_vit_uses_f16(model.dev) > 0
     derr = L.tcg_device_error()
 
     par_checked = dist.sum(par[2] if par else 0)
@@ -560,11 +562,22 @@ def run_ours(args, dist):
     if dist.rank == 0:
         gf, af, pf = vit_flops_per_image(cfg)
         gemm_launches = kcount[0] / args.steps
-        tf_peak = pk["bf16_tflops_sustained"] / 2.0 / 3.0
-        tf_burst = pk["bf16_tflops"] / 2.0 / 3.0
+        # three MMAs per fp32 product, at the fp16 rate (fp16 pieces) or half of it (tf32 pairs)
+        rate = 1.0 if f16 else 2.0
+        tf_peak = pk["bf16_tflops_sustained"] / rate / 3.0
+        tf_burst = pk["bf16_tflops"] / rate / 3.0
         achieved = gf * per / (gemm_ms * 1e-3) / 1e12           # per rank, slowest rank's time
         # the captured figure belongs to one per-GPU workload; other shards move other bytes
-        traffic = NCU_GEMM_TRAFFIC_PER_LAUNCH if (args.model, per) == NCU_GEMM_TRAFFIC_WORKLOAD else None
+        traffic = (NCU_GEMM_TRAFFIC_PER_LAUNCH["f16" if f16 else "tf32"]
+                   if (args.model, per) == NCU_GEMM_TRAFFIC_WORKLOAD else None)
+        gemm_desc = ("fp16 pieces on tcgen05 kind::f16: every fp32 operand split into two fp16 values of 11 "
+                     "significant bits after a power-of-two scale (A per row and 256-element K-block, B per row), "
+                     "hi*hi, hi*lo, lo*hi per fp32 product (an N=256 MMA for hi*hi|hi*lo and an N=128 one for "
+                     "lo*hi), fp32 TMEM chunk accumulators unscaled into fp32 registers; stream-K tail"
+                     if f16 else
+                     "3xTF32 on tcgen05: hi*hi, hi*lo, lo*hi tf32 products per fp32 product (an N=256 MMA for "
+                     "hi*hi|hi*lo and an N=128 one for lo*hi), fp32 TMEM chunk accumulators drained every 256 K "
+                     "into fp32 registers; stream-K tail")
         result = {
             "metric": "ViT-B/32 images/sec",
             "value": round(global_batch / (ms_max * 1e-3), 2),
@@ -579,20 +592,23 @@ def run_ours(args, dist):
                        "model": args.model, "global_batch": global_batch, "per_gpu_batch": per,
                        "seq_len": cfg["n_token"], "parallelism": f"dp{dist.world} (image batches, no per-step "
                        "collective; weights broadcast once by NCCL)",
-                       "l2": "inputs larger than L2: 703 MB of tf32 hi/lo weights + activations per step",
-                       "gemm": "3xTF32 on tcgen05: hi*hi, hi*lo, lo*hi tf32 products per fp32 product (an "
-                               "N=256 MMA for hi*hi|hi*lo and an N=128 one for lo*hi), fp32 TMEM chunk "
-                               "accumulators drained every 256 K into fp32 registers; stream-K tail"},
-            "roofline": {"kernel": "gemm_tf32x3 (tcgen05, TMA-fed)", "bound": "tensor",
+                       "l2": f"inputs larger than L2: {fp32_gemm_bytes / 1e6:.0f} MB of "
+                             f"{'fp16-piece' if f16 else 'tf32-pair'} GEMM weights + activations per step",
+                       "gemm": gemm_desc},
+            "roofline": {"kernel": ("gemm_tf32x3_kernel<..., fp16 pieces> (tcgen05 kind::f16, TMA-fed)" if f16
+                                    else "gemm_tf32x3 (tcgen05 kind::tf32, TMA-fed)"), "bound": "tensor",
                          "achieved": round(achieved, 1), "peak": round(tf_peak, 1), "unit": "TFLOP/s",
                          "frac": round(achieved / tf_peak, 3),
-                         "peak_basis": f"{pk_kind} bf16_tflops_sustained {pk['bf16_tflops_sustained']} / 2 "
-                                       "(tf32 rate) / 3 (MMAs per fp32 product)",
+                         "peak_basis": (f"{pk_kind} bf16_tflops_sustained {pk['bf16_tflops_sustained']} / 3 "
+                                        "(MMAs per fp32 product at the fp16 rate)" if f16 else
+                                        f"{pk_kind} bf16_tflops_sustained {pk['bf16_tflops_sustained']} / 2 "
+                                        "(tf32 rate) / 3 (MMAs per fp32 product)"),
                          # the sustained figure was taken at the clock the power cap allowed then
                          # (MEASURED_PEAKS clocks_under_load); this GEMM may run faster, so the
                          # burst figure is the stricter denominator
                          "peak_burst": round(tf_burst, 1), "frac_burst": round(achieved / tf_burst, 3),
-                         "peak_burst_basis": f"{pk_kind} bf16_tflops {pk['bf16_tflops']} / 2 / 3",
+                         "peak_burst_basis": (f"{pk_kind} bf16_tflops {pk['bf16_tflops']} / 3" if f16 else
+                                              f"{pk_kind} bf16_tflops {pk['bf16_tflops']} / 2 / 3"),
                          "traffic": traffic,
                          "flop_per_launch": round(gf * per / gemm_launches) if gemm_launches else None,
                          "avg_launch_ms": round(gemm_ms / gemm_launches, 4) if gemm_launches else None,
