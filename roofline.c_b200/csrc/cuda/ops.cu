@@ -1409,6 +1409,33 @@ bool tcg_layernorm(float *out, const float *x, const float *gamma, const float *
     return launch_layernorm(x, cols, gamma, beta, rows, cols, eps, o, ctx().cur);
 }
 
+// LayerNorm into fp16 pieces (the kind::f16 GEMM's A operand): hi, lo
+// [rows, cols] fp16, ex [cols / 256, rows] one exponent per 256-column block,
+// rnorm [rows] each output row's 2-norm (may be null).
+bool tcg_layernorm_f16(void *hi, void *lo, int8_t *ex, float *rnorm, const float *x, const float *gamma,
+                       const float *beta, int rows, int cols, float eps)
+{
+    if (!need_ctx()) return false;
+    if (rows <= 0 || cols <= 0) return rows == 0 || cols == 0 ? true : fail("tcg_layernorm_f16: bad shape");
+    OutSpec o;
+    o.fh = hi;
+    o.fl = lo;
+    o.fe = ex;
+    o.fe_rows = rows;
+    o.rnorm = rnorm;
+    o.ld = cols;
+    return launch_layernorm(x, cols, gamma, beta, rows, cols, eps, o, ctx().cur);
+}
+
+// bounds[0] = max over rows of ||W[row]||_2, bounds[1] = max |b| (W [rows, K],
+// b may be null); overwrites bounds.
+bool tcg_weight_bounds(float *bounds, const float *W, int rows, int K, const float *b)
+{
+    if (!need_ctx()) return false;
+    TCG_CUDA(cudaMemsetAsync(bounds, 0, 2 * sizeof(float), ctx().cur));
+    return launch_weight_bounds(W, rows, K, b, bounds, ctx().cur);
+}
+
 bool tcg_gelu(float *out, const float *x, size_t n)
 {
     return need_ctx() && launch_gelu(out, x, n, false, ctx().cur);

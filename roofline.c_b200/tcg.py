@@ -167,6 +167,8 @@ _SIGS = [
     ("tcg_mha", boolean, [vp, vp, vp, vp, i32, i32, i32]),
     ("tcg_mha_images", boolean, [vp, vp, vp, vp, i32, i32, i32, i32]),
     ("tcg_split_f16", boolean, [vp, vp, vp, vp, i32, i32, i32]),
+    ("tcg_layernorm_f16", boolean, [vp, vp, vp, vp, vp, vp, vp, i32, i32, C.c_float]),
+    ("tcg_weight_bounds", boolean, [vp, vp, i32, i32, vp]),
     ("tcg_linear_f16_split", boolean, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32]),
     ("tcg_add", boolean, [vp, vp, vp, sz]), ("tcg_scale", boolean, [vp, vp, f32, sz]),
     ("tcg_vit_upload", vp, [C.POINTER(Vit), i32]), ("tcg_vit_release", None, [vp]),

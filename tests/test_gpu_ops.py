@@ -114,6 +114,50 @@ def test_layernorm_vs_oracle(dev, rows, cols):
     assert ulp.max() <= 2 and (ulp == 0).mean() > 0.999
 
 
+def _pieces(hi, lo, ex, rows, cols, blk):
+    """fp16 pieces back to values: (hi + lo) * 2^-e per (row, blk-column block)."""
+    h = hi.view(np.float16).astype(np.float64).reshape(rows, cols)
+    l = lo.view(np.float16).astype(np.float64).reshape(rows, cols)
+    e = ex.view(np.int8)[: rows * (cols // blk)].reshape(cols // blk, rows).T.astype(np.float64)
+    return (h + l) * np.repeat(2.0 ** -e, blk, axis=1)
+
+
+@pytest.mark.parametrize("rows,cols", [(300, 768), (17, 1024), (5, 256)])
+def test_layernorm_f16_pieces(dev, rows, cols):
+    """LayerNorm written as fp16 pieces: per 256-column block the largest
+    value scaled into [2^14, 2^15), hi + lo within 2^-21 of the block's
+    largest of the oracle's output; the row norms of that output."""
+    L = tcg.lib()
+    rng = np.random.default_rng(rows)
+    x = rng.standard_normal((rows, cols)).astype(np.float32)
+    x[rows // 2] += 1e4
+    g = (1 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+    g[:256] *= np.float32(1e-3)                        # one block far smaller than the others
+    b = (0.1 * rng.standard_normal(cols)).astype(np.float32)
+    hi, lo, ex, rn = dev.empty(rows * cols // 2), dev.empty(rows * cols // 2), dev.empty(rows * cols // 1024 + 1), dev.empty(rows)
+    tcg.check(L.tcg_layernorm_f16(hi.ptr, lo.ptr, ex.ptr, rn.ptr, dev.put(x), dev.put(g), dev.put(b), rows, cols, 1e-5))
+    want = oracle.layernorm(x, g, b, rows, cols, 1e-5).astype(np.float64)
+    got = _pieces(hi.download(rows * cols // 2, np.uint32), lo.download(rows * cols // 2, np.uint32),
+                  ex.download(rows * cols // 1024 + 1, np.uint32), rows, cols, 256)
+    for c in range(0, cols, 256):
+        w, gv = want[:, c:c + 256], got[:, c:c + 256]
+        assert np.all(np.abs(gv - w) <= 2.0 ** -21 * np.abs(w).max(axis=1, keepdims=True)), c
+    assert np.allclose(rn.download(rows), np.linalg.norm(want, axis=1), rtol=1e-5)
+
+
+def test_weight_bounds(dev):
+    L = tcg.lib()
+    rng = np.random.default_rng(3)
+    W = rng.standard_normal((1000, 768)).astype(np.float32)
+    W[417] *= 3
+    bias = rng.standard_normal(1000).astype(np.float32)
+    out = dev.empty(2)
+    tcg.check(L.tcg_weight_bounds(out.ptr, dev.put(W), 1000, 768, dev.put(bias)))
+    got = out.download(2)
+    assert np.isclose(got[0], np.linalg.norm(W.astype(np.float64), axis=1).max(), rtol=1e-5)
+    assert got[1] == np.abs(bias).max()
+
+
 @pytest.mark.parametrize("T,H,HD", [(50, 12, 64), (56, 3, 64), (57, 2, 64), (64, 2, 64), (1, 3, 64), (5, 2, 64), (257, 16, 64), (17, 4, 16), (33, 2, 96)])
 def test_mha_vs_oracle(dev, T, H, HD):
     L = tcg.lib()
