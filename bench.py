@@ -52,7 +52,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # one-pass ncu capture of dram__bytes_read.sum + dram__bytes_write.sum over
 # that forward's launches, per GEMM path (fp16 pieces, tf32 pairs). It
 # applies to that workload only.
-NCU_GEMM_TRAFFIC_PER_LAUNCH = {"f16": None, "tf32": 289.5e6}
+NCU_GEMM_TRAFFIC_PER_LAUNCH = {"f16": 143.1e6, "tf32": 289.5e6}
 NCU_GEMM_TRAFFIC_WORKLOAD = ("vit-b32", 256)
 
 
@@ -290,7 +290,10 @@ def kquant_aux(tcg, hbm_peak):
     - b2b: launches back to back, the total over the launches; each launch
       touches more than the 126 MB L2 holds (dequant 268 MB, Q6_K matvec
       431 MB; the 33 MB Q4_K matrix rotates over 10 copies, 331 MB), as in a
-      decode pass over successive layers."""
+      decode pass over successive layers. A device delay holds the stream
+      while the host queues the launches, so the host's launch rate leaves no
+      gaps; the matvecs run with the decode-pass promise of static weights
+      (each fetches its weights while the one before it finishes)."""
     L = tcg.lib()
     flush = tcg.DeviceBuffer(256 << 20)
     out = {}
@@ -307,7 +310,11 @@ def kquant_aux(tcg, hbm_peak):
     def b2b(fns, reps=10):
         for f in fns[:2]:
             f()
-        return statistics.median(tcg.time_ms(lambda: [f() for f in fns], 2, 3) / len(fns) for _ in range(reps))
+        ts = []
+        for _ in range(reps):
+            tcg.check(L.tcg_device_delay_us(500))
+            ts.append(tcg.time_ms(lambda: [f() for f in fns], 2, 3) / len(fns))
+        return statistics.median(ts)
 
     def row(nbytes, ms, ms_b2b, launches):
         gbs, gbs2 = nbytes / ms / 1e6, nbytes / ms_b2b / 1e6
@@ -332,7 +339,9 @@ def kquant_aux(tcg, hbm_peak):
         with tcg.DeviceBuffer.from_array(x) as xb, tcg.DeviceBuffer(N * 4) as y:
             mv = [lambda w=w: tcg.check(L.tcg_matvec_q(y.ptr, w.ptr, xb.ptr, N, K, qt)) for w in ws]
             ms = timed(mv[0])
+            old_static = L.tcg_matvec_set_static_weights(1)
             ms2 = b2b(mv * (10 // copies))
+            L.tcg_matvec_set_static_weights(old_static)
             # the floor: the same matrices only read, back to back the same way
             rd = [lambda w=w: tcg.check(L.tcg_read_ceiling(w.ptr, raw.nbytes)) for w in ws]
             ms_read = b2b(rd * (10 // copies))

@@ -68,6 +68,11 @@ bool  tcg_memset(void *dst, int value, size_t bytes);      /* async          */
  * way (the benchmark's ceiling for the matvec). Asynchronous. */
 bool  tcg_read_ceiling(const void *p, size_t bytes);
 
+/* Hold the library stream for `us` microseconds (1 thread, at most 20,000):
+ * queued before a timed sequence of launches, it lets the host queue the
+ * whole sequence first, so the sequence runs back to back. Asynchronous. */
+bool  tcg_device_delay_us(int us);
+
 /* CUDA events on the library stream, slots 0..63. elapsed() waits for b. */
 bool  tcg_event_record(int slot);
 float tcg_event_elapsed_ms(int slot_a, int slot_b);
@@ -112,6 +117,13 @@ const void *tcg_tensor_upload(const gguf_tensor_t *t, tcg_arena_t *a);
  * accumulation. Equivalent to tc_dequant followed by tc_ref_linear with M=1
  * (src/ops.c:28-35), up to summation order. */
 bool tcg_matvec_q(float *y, const void *W, const float *x, int N, int K, ggml_type_t t);
+
+/* Decode-pass promise for tcg_matvec_q (default 0): 1 asserts that no kernel
+ * queued before a matvec writes its weight matrix (weights uploaded once).
+ * Successive matvecs then overlap: each fetches its weights while the one
+ * before it finishes, and reads x only after that one completes. Returns the
+ * previous setting. */
+int  tcg_matvec_set_static_weights(int on);
 
 /* --------------------------------------------------- ops (src/ops.h)
  * Same argument order and meaning as the reference's tc_ref_* (src/ops.h:

@@ -351,6 +351,11 @@ mv_kq_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restri
     // Q6_K slots hold spb / 8 boxes of 16 rows x 1680 bytes one after another
     constexpr int RB = QT == 4 ? 0 : MQ_SPB * MQ_BB;                // bytes of a box row (Q6_K)
 
+    // With early set (a decode pass over static weights) the kernel queued
+    // after this one may be scheduled as this one's CTAs retire: a matvec
+    // then fetches its weights on the SMs freed first, and waits for this
+    // kernel's completion (pdl_wait) before it reads x or writes anything.
+    if (early) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (threadIdx.x == 0) {
         for (int s = 0; s < nslot; s++) {
             bar_init(full0 + 8 * s, 1);
@@ -881,11 +886,12 @@ extern "C" int tcg_matvec_mma_segments(int segs)
     return old;
 }
 
-// Q4_K matvec promise (default 0): with 1, the caller guarantees that the
-// kernel queued just before a matvec on the same stream never writes that
-// matvec's weight matrix (true of a decode pass whose weights are uploaded
-// once), and the matvec starts fetching its weights while that kernel is
-// still finishing. x may still be produced by it. Returns the previous value.
+// Matvec promise (default 0): with 1, the caller guarantees that the kernel
+// queued just before a matvec on the same stream never writes that matvec's
+// weight matrix (true of a decode pass whose weights are uploaded once). The
+// integer-MMA matvec then starts fetching its weights while that kernel is
+// still finishing (x may still be produced by it), and lets the kernel after
+// it be scheduled as its own CTAs retire. Returns the previous value.
 extern "C" int tcg_matvec_set_static_weights(int on)
 {
     const int old = tcg::g_mv_early;

@@ -275,6 +275,35 @@ __global__ void __launch_bounds__(512) read_all_kernel(const uint4 *__restrict__
 }
 }  // namespace
 
+/* ------------------------------------------------------- queue delay
+ * One thread waits on the global nanosecond timer, then returns. Queued ahead
+ * of a timed sequence of launches, it holds the stream while the host queues
+ * the sequence, so that the sequence runs back to back without gaps set by
+ * the host's launch rate. Bounded twice: by the timer and by 4 SM cycles per
+ * nanosecond asked for (the SM clock is at most 2 GHz). */
+namespace {
+__global__ void delay_kernel(unsigned long long ns)
+{
+    unsigned long long t0, t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    const long long c0 = clock64(), cmax = 4 * (long long)ns;
+    do {
+        __nanosleep(500);
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    } while (t - t0 < ns && clock64() - c0 < cmax);
+}
+}  // namespace
+
+bool tcg_device_delay_us(int us)
+{
+    if (!tcg::need_ctx()) return false;
+    if (us <= 0) return true;
+    if (us > 20000) return tcg::fail("tcg_device_delay_us: %d us is above the 20 ms limit", us);
+    delay_kernel<<<1, 1, 0, ctx().cur>>>((unsigned long long)us * 1000ull);
+    TCG_LAUNCHED();
+    return true;
+}
+
 bool tcg_read_ceiling(const void *p, size_t bytes)
 {
     if (!tcg::need_ctx()) return false;

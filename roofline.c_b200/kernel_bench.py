@@ -166,8 +166,22 @@ def case_matvec(a):
         mv = [lambda w=w: tcg.check(L.tcg_matvec_q(y.ptr, w.ptr, xb.ptr, a.N, a.K, qt)) for w in ws]
         ms, _ = timed(mv[0], a.warmup, a.reps, flush)
         launches = max(10, copies)
-        b2b, _ = timed(lambda: [mv[i % copies]() for i in range(launches)], a.warmup, a.reps)
-        b2b /= launches
+        seq = lambda: [mv[i % copies]() for i in range(launches)]
+        for _ in range(a.warmup):
+            seq()
+        ts = []
+        for _ in range(a.reps):
+            if a.delay:
+                tcg.check(L.tcg_device_delay_us(a.delay))
+            ts.append(tcg.time_ms(seq, 2, 3))
+        b2b = statistics.median(ts) / launches
+        rd = lambda: [tcg.check(L.tcg_read_ceiling(ws[i % copies].ptr, raw.nbytes)) for i in range(launches)]
+        ts = []
+        for _ in range(a.reps):
+            if a.delay:
+                tcg.check(L.tcg_device_delay_us(a.delay))
+            ts.append(tcg.time_ms(rd, 2, 3))
+        read_b2b = statistics.median(ts) / launches
     for w in ws:
         w.close()
     kern = L.tcg_matvec_last_kernel()
@@ -180,7 +194,8 @@ def case_matvec(a):
     nbytes = a.N * a.K // 256 * bb + 4 * (a.N + a.K)
     return {"case": "matvec", "type": a.type, "N": a.N, "K": a.K, "kernel": kern, "ms": round(ms, 5),
             "bytes": nbytes, "GB/s": round(nbytes / ms / 1e6, 1), "b2b_ms": round(b2b, 5),
-            "b2b_GB/s": round(nbytes / b2b / 1e6, 1), "copies": copies}
+            "b2b_GB/s": round(nbytes / b2b / 1e6, 1), "read_b2b_ms": round(read_b2b, 5), "copies": copies,
+            "static_weights": a.static_weights, "delay_us": a.delay}
 
 
 def case_dequant(a):
@@ -311,6 +326,8 @@ def main():
     mv.add_argument("--split", type=int, default=1, help="0: one warp per Q6_K unit of the mma kernel")
     mv.add_argument("--tiles", type=int, default=-1,
                     help="mma kernel: 1 whole tiles per CTA, 0 segment-major unit ranges, -1 by shape")
+    mv.add_argument("--delay", type=int, default=500,
+                    help="us of device delay queued before each back-to-back sequence (0: none)")
     mv.add_argument("--static-weights", type=int, default=0,
                     help="1: promise that no earlier kernel writes W (weights fetched before the previous ends)")
     dq = sub.add_parser("dequant")

@@ -133,7 +133,7 @@ _SIGS = [
     ("tcg_host_alloc", vp, [sz]), ("tcg_host_free", boolean, [vp]),
     ("tcg_h2d", boolean, [vp, vp, sz]), ("tcg_d2h", boolean, [vp, vp, sz]),
     ("tcg_d2d", boolean, [vp, vp, sz]), ("tcg_memset", boolean, [vp, i32, sz]),
-    ("tcg_read_ceiling", boolean, [vp, sz]),
+    ("tcg_read_ceiling", boolean, [vp, sz]), ("tcg_device_delay_us", boolean, [i32]),
     ("tcg_event_record", boolean, [i32]), ("tcg_event_elapsed_ms", f32, [i32, i32]),
     ("tcg_arena_create", Arena, [sz, C.c_char_p]), ("tcg_arena_destroy", None, [C.POINTER(Arena)]),
     ("tcg_arena_ok", boolean, [C.POINTER(Arena)]), ("tcg_arena_alloc", vp, [C.POINTER(Arena), sz, sz]),

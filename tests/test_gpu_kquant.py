@@ -354,6 +354,53 @@ def test_matvec_mma_tile_modes(gpu, mode, qt, N, K):
     assert np.abs(got.astype(np.float64) - want).max() / np.abs(want).max() <= MATVEC_TOL
 
 
+@pytest.mark.parametrize("static", [0, 1])
+def test_matvec_decode_chain(gpu, static):
+    """A decode-like chain on one stream, each matvec reading the one before
+    it's output: y1 = W1 x, y2 = W2 y1, y3 = W3 y2 (Q4_K, Q6_K, Q4_K), queued
+    behind a device delay so that they run back to back. With the
+    static-weights promise the kernels overlap (each fetches its weights while
+    the one before it finishes); x must still be read only after it is
+    written. Each output against the oracle on the device's own input."""
+    L = tcg.lib()
+    n = 4096
+    qts = [G.Q4_K, G.Q6_K, G.Q4_K]
+    raws = [G.make_kquant(qt, n, n, seed=40 + i) for i, qt in enumerate(qts)]
+    x = np.random.default_rng(44).standard_normal(n).astype(np.float32)
+    ws = [tcg.DeviceBuffer.from_array(r) for r in raws]
+    ys = [tcg.DeviceBuffer.from_array(x)] + [tcg.DeviceBuffer(n * 4) for _ in qts]
+    old = L.tcg_matvec_set_static_weights(static)
+    try:
+        for rep in range(3):
+            for b in ys[1:]:
+                tcg.check(L.tcg_memset(b.ptr, 0xFF, n * 4))           # NaN: a read before the write shows
+            tcg.check(L.tcg_device_delay_us(300))
+            for i, qt in enumerate(qts):
+                tcg.check(L.tcg_matvec_q(ys[i + 1].ptr, ws[i].ptr, ys[i].ptr, n, n, qt), "tcg_matvec_q")
+            outs = [b.download(n) for b in ys]
+            assert L.tcg_device_error() == 0
+            for i, qt in enumerate(qts):
+                want = oracle.matvec_q(raws[i], outs[i], n, n, qt).astype(np.float64)
+                got = outs[i + 1].astype(np.float64)
+                assert np.isfinite(got).all()
+                assert np.abs(got - want).max() / np.abs(want).max() <= MATVEC_TOL
+    finally:
+        L.tcg_matvec_set_static_weights(old)
+        for b in ws + ys:
+            b.close()
+
+
+def test_device_delay(gpu):
+    """The queue delay holds the stream for about the time asked, and refuses
+    more than 20 ms."""
+    L = tcg.lib()
+    ms = tcg.time_ms(lambda: tcg.check(L.tcg_device_delay_us(400)), 2, 3)
+    assert 0.3 <= ms <= 5.0
+    assert not L.tcg_device_delay_us(20001)
+    assert b"20 ms" in L.tcg_last_error()
+    assert L.tcg_device_delay_us(0)
+
+
 def test_matvec_rejections(gpu):
     L = tcg.lib()
     assert not L.tcg_matvec_q(None, None, None, 4, 300, G.Q4_K)
