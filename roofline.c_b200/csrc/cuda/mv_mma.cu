@@ -73,10 +73,20 @@ template <> struct MmType<6> { static constexpr int BB = MQ_BB, XSB = MQ_XSB; };
 __device__ __forceinline__ void mma_u8s8(int d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1)
 {
-    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
                  "{%8, %9}, {%10, %10, %10, %10};"
                  : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// D += A B (layouts of mma_u8s8)
+__device__ __forceinline__ void mma_u8s8_acc(int d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1)
+{
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ uint32_t byte_of(uint32_t w, int b) { return __byte_perm(w, 0u, 0x4440u | (unsigned)b); }
@@ -111,42 +121,46 @@ __device__ __forceinline__ float f16hi(uint32_t w) { return __half2float(__ushor
 // a small non-negative integer (< 2^23) as a float, exactly
 __device__ __forceinline__ float small_int_float(uint32_t v) { return __uint_as_float(0x4B000000u | v) - 8388608.0f; }
 
-// Accumulate superblock s (x pieces at xsb) of rows g, g+8 into acc0 / acc1
-// (this lane's share: the p-pair sums for t < 2, the min terms of sub-blocks
-// 2t, 2t+1 for every t).
+// Accumulate superblock s (x pieces at xsb) of rows g, g+8 into acc0 / acc1.
+// Each 32-byte chunk c holds sub-block 2c in its low nibbles and 2c + 1 in
+// its high nibbles. Two chained MMAs give both sub-blocks in one D: B columns
+// 0-3 carry the pieces of x's sub-block 2c and meet the low nibbles (zero in
+// columns 4-7), then columns 4-7 carry the pieces of sub-block 2c + 1 and
+// meet the high nibbles kept in place, 16 q (zero in columns 0-3). Lane (g,
+// t) holds columns 2t, 2t + 1: sub-block 2c + t / 2, pieces 2 (t % 2) and
+// 2 (t % 2) + 1, multiplied by that sub-block's scale of rows g, g + 8 in
+// 32-bit integers (|.| < 2^27 over the superblock). Its share of the min
+// terms: sub-blocks 2t, 2t + 1.
 __device__ __forceinline__ void sb_dot(const Sb &s, const uint8_t *xsb, int g, int t, float &acc0, float &acc1)
 {
     uint32_t sc0l, sc0h, mn0l, mn0h, sc1l, sc1h, mn1l, mn1h;
     scales_of(s.h0, sc0l, sc0h, mn0l, mn0h);
     scales_of(s.h1, sc1l, sc1h, mn1l, mn1h);
-    int lo[4] = { 0, 0, 0, 0 }, hi[4] = { 0, 0, 0, 0 };
+    const uint32_t th = (uint32_t)t >> 1;                           // 0: low-nibble sub-block, 1: high
+    const bool bhi = g >= 4;                                        // this lane's B column: 2c + 1
+    const uint8_t *xb = xsb + (bhi ? 128 : 0) + (g & 3) * 32 + 8 * t;
+    int a[4] = { 0, 0, 0, 0 };
 #pragma unroll
     for (int c = 0; c < 4; c++) {
-        const uint32_t w0 = c < 2 ? sc0l : sc0h, w1 = c < 2 ? sc1l : sc1h;
-        const int bl = 2 * (c & 1);
-        const int sA0 = (int)byte_of(w0, bl), sA1 = (int)byte_of(w1, bl);           // sub-block 2c
-        const int sB0 = (int)byte_of(w0, bl + 1), sB1 = (int)byte_of(w1, bl + 1);   // sub-block 2c + 1
-        uint32_t b0 = 0, b1 = 0, e0 = 0, e1 = 0;
-        if (g < 4) {
-            const uint2 bl2 = *reinterpret_cast<const uint2 *>(xsb + (2 * c) * 128 + g * 32 + 8 * t);
-            const uint2 bh2 = *reinterpret_cast<const uint2 *>(xsb + (2 * c + 1) * 128 + g * 32 + 8 * t);
-            b0 = bl2.x; b1 = bl2.y; e0 = bh2.x; e1 = bh2.y;
-        }
+        const uint2 bx = *reinterpret_cast<const uint2 *>(xb + c * 256);
+        const uint32_t bl0 = bhi ? 0u : bx.x, bl1 = bhi ? 0u : bx.y;
+        const uint32_t bh0 = bhi ? bx.x : 0u, bh1 = bhi ? bx.y : 0u;
         int d[4];
         mma_u8s8(d, s.q0[c].x & 0x0F0F0F0Fu, s.q1[c].x & 0x0F0F0F0Fu, s.q0[c].y & 0x0F0F0F0Fu,
-                 s.q1[c].y & 0x0F0F0F0Fu, b0, b1);
-        lo[0] += d[0] * sA0; lo[1] += d[1] * sA0; lo[2] += d[2] * sA1; lo[3] += d[3] * sA1;
-        mma_u8s8(d, s.q0[c].x & 0xF0F0F0F0u, s.q1[c].x & 0xF0F0F0F0u, s.q0[c].y & 0xF0F0F0F0u,
-                 s.q1[c].y & 0xF0F0F0F0u, e0, e1);
-        hi[0] += d[0] * sB0; hi[1] += d[1] * sB0; hi[2] += d[2] * sB1; hi[3] += d[3] * sB1;
+                 s.q1[c].y & 0x0F0F0F0Fu, bl0, bl1);
+        mma_u8s8_acc(d, s.q0[c].x & 0xF0F0F0F0u, s.q1[c].x & 0xF0F0F0F0u, s.q0[c].y & 0xF0F0F0F0u,
+                     s.q1[c].y & 0xF0F0F0F0u, bh0, bh1);
+        // scale of sub-block 2c + th: byte 2 (c % 2) + th of the low (c < 2) or high scale word
+        const uint32_t sel = 0x4440u | (2u * (c & 1) + th);
+        const int s0 = (int)__byte_perm(c < 2 ? sc0l : sc0h, 0u, sel);
+        const int s1 = (int)__byte_perm(c < 2 ? sc1l : sc1h, 0u, sel);
+        a[0] += d[0] * s0; a[1] += d[1] * s0; a[2] += d[2] * s1; a[3] += d[3] * s1;
     }
-    // 16 * (sum over the superblock); |.| < 2^28
-    const float v0 = (float)(lo[0] * 16 + hi[0]), v1 = (float)(lo[1] * 16 + hi[1]);
-    const float v2 = (float)(lo[2] * 16 + hi[2]), v3 = (float)(lo[3] * 16 + hi[3]);
-    // piece pair of this lane: (p0, p1) for t = 0, (p2, p3) for t = 1 (t > 1: zero sums)
+    // pieces (0, 1) for even t, (2, 3) for odd t: x = (p0 + p1/2^7 + p2/2^14
+    // + p3/2^21) 2^(e-6), 2^(e-13) stored; the high sub-block's sums are 16x
     const float xe = *reinterpret_cast<const float *>(xsb + 1024 + 32);      // 2^(e - 13)
-    const float k = t == 1 ? 3.814697265625e-06f : 0.0625f;                   // 2^-18 : 2^-4 (the 16 above)
-    const float f0 = fmaf(v0, 128.0f, v1), f1 = fmaf(v2, 128.0f, v3);
+    const float k = ((t & 1) ? 6.103515625e-05f : 1.0f) * (th ? 0.0625f : 1.0f);
+    const float f0 = fmaf((float)a[0], 128.0f, (float)a[1]), f1 = fmaf((float)a[2], 128.0f, (float)a[3]);
     const float d0 = f16lo(s.h0.x), d1 = f16lo(s.h1.x);
     // (f xe) (d k): both factors stay normal floats for every d and exponent
     acc0 = fmaf(f0 * xe, d0 * k, acc0);
@@ -164,7 +178,7 @@ __device__ __forceinline__ void sb_dot(const Sb &s, const uint8_t *xsb, int g, i
 __device__ __forceinline__ void mma_u8s8_c(int d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                            uint32_t b0, uint32_t b1, int c0, int c1)
 {
-    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
                  "{%8, %9}, {%10, %11, %10, %11};"
                  : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
@@ -267,6 +281,7 @@ __device__ __forceinline__ void sb6_dot(const uint8_t *r0, const uint8_t *r1, co
 }
 
 constexpr int MM_THREADS = MM_WARPS * 32 + 32;   // sixteen consumer warps and the producer warp
+constexpr int MM_CMB_FLOATS = 2 * MM_WARPS * 16; // the parts' sums: owners x hs <= MM_WARPS, two buffers, 16 rows
 
 // fetch-and-add with release (the warp's partial sums, ordered before it by
 // __syncwarp) and acquire (the other segments' sums, for the last to arrive)
@@ -284,11 +299,33 @@ __device__ __forceinline__ void tma_load3(uint32_t dst, const CUtensorMap *map, 
                  ::"r"(dst), "l"((unsigned long long)map), "r"(x), "r"(y), "r"(z), "r"(bar) : "memory");
 }
 
+// the bytes of a 3-D box into L2 (nothing written to shared memory)
+__device__ __forceinline__ void tma_prefetch3(const CUtensorMap *map, int x, int y, int z)
+{
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];"
+                 ::"l"((unsigned long long)map), "r"(x), "r"(y), "r"(z) : "memory");
+}
+
 __device__ __forceinline__ void tma_load2(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y)
 {
     asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
                  " [%0], [%1, {%2, %3}], [%4];"
                  ::"r"(dst), "l"((unsigned long long)map), "r"(x), "r"(y), "r"(bar) : "memory");
+}
+
+// The same from global memory: rows r0, r1 (null past the matrix: zeros),
+// superblock at byte offset o
+__device__ __forceinline__ void load_sb_global(Sb &s, const uint8_t *r0, const uint8_t *r1, int o, int t)
+{
+    const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+    const uint2 z2 = make_uint2(0u, 0u);
+    s.h0 = r0 ? __ldg(reinterpret_cast<const uint4 *>(r0 + o)) : z4;
+    s.h1 = r1 ? __ldg(reinterpret_cast<const uint4 *>(r1 + o)) : z4;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        s.q0[c] = r0 ? __ldg(reinterpret_cast<const uint2 *>(r0 + o + 16 + 32 * c + 8 * t)) : z2;
+        s.q1[c] = r1 ? __ldg(reinterpret_cast<const uint2 *>(r1 + o + 16 + 32 * c + 8 * t)) : z2;
+    }
 }
 
 __device__ __forceinline__ void load_sb_smem(Sb &s, const uint8_t *r0, const uint8_t *r1, int t)
@@ -310,7 +347,7 @@ template <int QT>
 __global__ void __launch_bounds__(MM_THREADS, 1)
 mv_kq_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restrict__ x, float *__restrict__ y,
                  int N, int nsb, int spb, int S, int tiles, long long U, float *ws, int *cnt, int nslot, int nwork,
-                 int hs, int tm, uint32_t sigma, int x_bytes, int early, int *err)
+                 int hs, int tm, uint32_t sigma, int x_bytes, int early, const void *Wg, int direct, int *err)
 {
     constexpr int BB = MmType<QT>::BB, XSB = MmType<QT>::XSB;
     extern __shared__ __align__(128) uint8_t smx[];
@@ -341,13 +378,13 @@ mv_kq_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restri
     uint64_t *bars = reinterpret_cast<uint64_t *>(slots + (size_t)nslot * 16 * rs);
     const uint32_t full0 = su32(bars), empty0 = su32(bars + nslot);
     volatile int *abort = reinterpret_cast<volatile int *>(bars + 2 * nslot);
-    // whole-row units read by hs warps: their partial sums meet here, two
-    // buffers per owner (alternate units), hs x 16 rows each
+    // units read by several warps (hs > 1, or direct units): the parts' sums
+    // meet here, two buffers per group of warps (alternate units)
     float *cmb = reinterpret_cast<float *>(bars + 2 * nslot + 2);
-    // tm: the partial sums of the CTA's tiles (S * hs x 16 rows each) and
-    // their arrival counters
-    float *tpart = cmb + (QT == 6 ? 8 * 2 * 4 * 16 : 0);
-    int *tcnt = reinterpret_cast<int *>(tpart + (tm ? (size_t)(T1 - T0) * S * hs * 16 : 0));
+    // tm: the partial sums of the CTA's tiles (S x 16 rows each) and their
+    // arrival counters
+    float *tpart = cmb + (hs > 1 || direct ? MM_CMB_FLOATS : 0);
+    int *tcnt = reinterpret_cast<int *>(tpart + (tm ? (size_t)(T1 - T0) * S * 16 : 0));
     // Q6_K slots hold spb / 8 boxes of 16 rows x 1680 bytes one after another
     constexpr int RB = QT == 4 ? 0 : MQ_SPB * MQ_BB;                // bytes of a box row (Q6_K)
 
@@ -386,14 +423,29 @@ mv_kq_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restri
                                   (seg * (spb / MQ_SPB) + b) * (RB / 8), tile * 16);
                 }
             };
+            // direct: units past the slots are read from global memory by
+            // the idle consumer warps; L2 gets them first
+            const auto prefetch_rest = [&]() {
+                if constexpr (QT == 4) {
+                    for (int j = nslot; direct && j < nunits; j++) {
+                        int seg, tile;
+                        unit_of(j, seg, tile);
+                        tma_prefetch3(&wmap, 0, seg * spb, tile * 16);
+                    }
+                }
+            };
+            const int nfill = direct ? min(nunits, nslot) : nunits;
             int k = 0;
             // With early set, the caller guarantees that no kernel before this
             // one on the stream writes W: the first slots fill while that
             // kernel finishes.
-            if (early)
-                for (; k < nslot && k < nunits; k++) fill(k);
+            if (early) {
+                for (; k < nslot && k < nfill; k++) fill(k);
+                prefetch_rest();
+            }
             pdl_wait();
-            for (; k < nunits; k++) {
+            if (!early) prefetch_rest();
+            for (; k < nfill; k++) {
                 const int slot = k % nslot;
                 if (k >= nslot && !bar_wait(empty0 + 8 * slot, (uint32_t)((k / nslot - 1) & 1), abort, err, 0x4D4D01))
                     break;
@@ -406,6 +458,27 @@ mv_kq_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restri
         return;
     }
     pdl_wait();
+    if (QT == 4 && direct && warp >= nwork && warp < MM_WARPS) {
+        // the spare warps' shares of the direct units into L1 while x is
+        // prepared (the producer has asked L2 for them)
+        const int nspare = MM_WARPS - nwork, dp = warp - nwork;
+        const int sg = (int)((sigma >> (3 * g)) & 7u);
+        for (int k = nslot; k < nunits; k++) {
+            int seg, tile;
+            unit_of(k, seg, tile);
+            const int steps = min(spb, nsb - seg * spb);
+            const int i0 = dp * steps / nspare, i1 = (dp + 1) * steps / nspare;
+            for (int h = 0; h < 2; h++) {
+                const int r = tile * 16 + sg + 8 * h;
+                if (r >= N) continue;
+                const uint8_t *row = static_cast<const uint8_t *>(Wg) + ((size_t)r * nsb + (size_t)seg * spb) * BB;
+                // lane t: byte 0, 48, 96 or 143 of each 144-byte superblock,
+                // so every 128-byte line it touches is asked for
+                for (int i = i0; i < i1; i++)
+                    asm volatile("prefetch.global.L1 [%0];" ::"l"(row + (size_t)i * BB + (t < 3 ? 48 * t : BB - 1)));
+            }
+        }
+    }
 
     // x pieces of the CTA's superblocks: warp per superblock, lane l holds
     // x 8l .. 8l+7 (sub-block l/4, positions 8(l%4) ..)
@@ -470,76 +543,20 @@ mv_kq_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restri
     }
     asm volatile("bar.sync 1, %0;" ::"n"(MM_WARPS * 32) : "memory");    // the consumers only
 
-    // Consumers: hs warps per slot owner (part p of a unit's superblocks
-    // each); owner o = w / hs takes units o, o + owners, ...: nslot is a
-    // multiple of owners (or no slot is reused), so every slot is read by
-    // one owner only, in unit order, and a warp never tests a slot's barrier
-    // while an earlier fill of that slot is still pending (which its parity
-    // test would read as complete). Each part is a partial sum of its own:
-    // SP per tile.
-    const int owner = warp / hs, part = warp - owner * hs, owners = nwork / hs, SP = S * hs;
-    for (int k = owner; warp < nwork && k < nunits; k += owners) {
-        int seg, tile;
-        unit_of(k, seg, tile);
-        const int slot = k % nslot;
-        const bool ok = bar_wait(full0 + 8 * slot, (uint32_t)((k / nslot) & 1), abort, err, 0x4D4D03);
-        float acc0 = 0.0f, acc1 = 0.0f;
-        const int sg = (int)((sigma >> (3 * g)) & 7u);               // this lane's slot row (and row + 8)
-        if (ok) {
-            const uint8_t *sl = slots + (size_t)slot * 16 * rs;
-            const uint8_t *r0 = sl + (size_t)sg * rs;               // Q4_K rows; Q6_K rows are per box
-            const uint8_t *r1 = r0 + (size_t)8 * rs;
-            const uint8_t *xs = smx + (size_t)(seg * spb - sb0) * XSB;
-            const int steps = min(spb, nsb - seg * spb);            // the last segment of a row may be short
-            if constexpr (QT == 4) {
-                for (int i = 0; i < steps; i++) {                   // hs is 1
-                    Sb sb;
-                    load_sb_smem(sb, r0 + i * BB, r1 + i * BB, t);
-                    sb_dot(sb, xs + (size_t)i * XSB, g, t, acc0, acc1);
-                }
-            } else {
-                // steps = spb (8 or 16): this part's spb / hs superblocks, an even first one
-                const int i1 = (part + 1) * (steps / hs);
-                for (int i = part * (steps / hs); i < i1; i += 2) {
-                    const uint8_t *q0 = sl + (size_t)(i / MQ_SPB) * 16 * RB + (size_t)sg * RB + (i % MQ_SPB) * BB;
-                    const uint8_t *q1 = q0 + (size_t)8 * RB;
-                    sb6_dot<false>(q0, q1, xs + (size_t)i * XSB, g, t, acc0, acc1);
-                    sb6_dot<true>(q0 + BB, q1 + BB, xs + (size_t)(i + 1) * XSB, g, t, acc0, acc1);
-                }
-            }
-        }
-        __syncwarp();
-        if (lane == 0) bar_arrive(empty0 + 8 * slot);               // the slot's bytes are read
-        // the quad's four shares of rows g and g+8
-        acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 1);
-        acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 1);
-        acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 2);
-        acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 2);
+    // A unit's sums of rows sg, sg + 8 (every lane of the warp holds its
+    // quad's): into y, or the K segment's partial sum, the last of a tile's
+    // S partial sums to arrive adding them in segment order
+    const int SP = S;
+    const auto emit = [&](float acc0, float acc1, int seg, int tile, int sg) {
         const int r0 = tile * 16 + sg, r1 = r0 + 8;
         if (SP == 1) {
             if (t == 0) {
                 if (r0 < N) y[r0] = acc0;
                 if (r1 < N) y[r1] = acc1;
             }
-            continue;
+            return;
         }
-        if (S == 1) {
-            // the hs parts of a whole-row unit, summed in part order by part 0
-            float *cb = cmb + ((size_t)owner * 2 + (((k - owner) / owners) & 1)) * hs * 16;
-            if (t == 0) {
-                cb[part * 16 + sg] = acc0;
-                cb[part * 16 + sg + 8] = acc1;
-            }
-            asm volatile("bar.sync %0, %1;" ::"r"(2 + owner), "r"(32 * hs) : "memory");
-            if (part == 0 && lane < 16) {
-                float v = 0.0f;
-                for (int p = 0; p < hs; p++) v += cb[p * 16 + lane];
-                const int r = tile * 16 + lane;
-                if (r < N) y[r] = v;
-            }
-            continue;
-        }
-        const int ps = seg * hs + part;                             // this partial sum's index
+        const int ps = seg;                                         // this partial sum's index
         if (tm) {
             // the last of the tile's SP parts in this CTA sums them in order
             const int tl = tile - T0;
@@ -564,7 +581,7 @@ mv_kq_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restri
                     y[r] = v;
                 }
             }
-            continue;
+            return;
         }
         if (t == 0) {
             if (r0 < N) ws[(size_t)ps * N + r0] = acc0;
@@ -584,6 +601,116 @@ mv_kq_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restri
             }
             if (lane == 0) cnt[tile] = 0;                           // ready for the next call
         }
+    };
+    // the parts' sums of rows sg, sg + 8 (np warps, part p, buffer cb of two
+    // alternating ones, named barrier id): part 0's lanes get the totals
+    const auto meet = [&](float &acc0, float &acc1, float *cb, int p, int np, int id, int sg) {
+        if (t == 0) {
+            cb[p * 16 + sg] = acc0;
+            cb[p * 16 + sg + 8] = acc1;
+        }
+        asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(32 * np) : "memory");
+        if (p != 0) return false;
+        acc0 = acc1 = 0.0f;
+        for (int q = 0; q < np; q++) {
+            acc0 += cb[q * 16 + sg];
+            acc1 += cb[q * 16 + sg + 8];
+        }
+        return true;
+    };
+    const int sg = (int)((sigma >> (3 * g)) & 7u);                  // this lane's slot row (and row + 8)
+
+    if (direct && warp >= nwork) {
+        // Units past the slots (Q4_K, at most a few per CTA): the nspare
+        // warps the slots leave idle read them from global memory (L2 and
+        // L1 have been asked for them), a share of each unit's superblocks
+        // per warp
+        if constexpr (QT == 4) {
+            const int nspare = MM_WARPS - nwork, dp = warp - nwork;
+            const size_t rowb = (size_t)nsb * BB;
+            for (int k = nslot, j = 0; k < nunits; k++, j++) {
+                int seg, tile;
+                unit_of(k, seg, tile);
+                const int steps = min(spb, nsb - seg * spb);
+                const int i0 = dp * steps / nspare, i1 = (dp + 1) * steps / nspare;
+                const int ra = tile * 16 + sg, rb = ra + 8;
+                const uint8_t *w0 = static_cast<const uint8_t *>(Wg);
+                const uint8_t *g0 = ra < N ? w0 + (size_t)ra * rowb + (size_t)seg * spb * BB : nullptr;
+                const uint8_t *g1 = rb < N ? w0 + (size_t)rb * rowb + (size_t)seg * spb * BB : nullptr;
+                const uint8_t *xs = smx + (size_t)(seg * spb - sb0) * XSB;
+                float acc0 = 0.0f, acc1 = 0.0f;
+                for (int i = i0; i < i1; i++) {
+                    Sb sb;
+                    load_sb_global(sb, g0, g1, i * BB, t);
+                    sb_dot(sb, xs + (size_t)i * XSB, g, t, acc0, acc1);
+                }
+                acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 1);
+                acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 1);
+                acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 2);
+                acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 2);
+                if (nspare > 1 && !meet(acc0, acc1, cmb + (size_t)nwork * 32 + (size_t)(j & 1) * nspare * 16, dp,
+                                        nspare, 15, sg))
+                    continue;
+                emit(acc0, acc1, seg, tile, sg);
+            }
+        }
+        return;
+    }
+
+    // Consumers: owners of hs warps each. Unit k lives in slot k % nslot and
+    // belongs to the slot's owner, (k % nslot) % owners: every slot is read
+    // by one owner only, in unit order, so a warp never tests a slot's
+    // barrier while an earlier fill of that slot is still pending (which its
+    // parity test would read as complete). The hs warps (parts) of an owner
+    // take a share of the unit's superblocks each and add their sums in
+    // shared memory, in part order; part 0 emits the unit's sum. With
+    // direct set the slots hold units 0 .. nslot - 1 only.
+    const int owner = warp / hs, part = warp - owner * hs, owners = nwork / hs;
+    const int nslotted = direct ? min(nunits, nslot) : nunits;
+    // rounds of nslot units, the owner's slots in each (no division per unit)
+    int seq = 0;                                                    // units this owner has taken
+    for (int round = 0, kr = 0; warp < nwork && kr < nslotted; round++, kr += nslot)
+    for (int slot = owner; slot < nslot && kr + slot < nslotted; slot += owners) {
+        const int k = kr + slot;
+        int seg, tile;
+        unit_of(k, seg, tile);
+        const bool ok = bar_wait(full0 + 8 * slot, (uint32_t)(round & 1), abort, err, 0x4D4D03);
+        float acc0 = 0.0f, acc1 = 0.0f;
+        if (ok) {
+            const uint8_t *sl = slots + (size_t)slot * 16 * rs;
+            const uint8_t *r0 = sl + (size_t)sg * rs;               // Q4_K rows; Q6_K rows are per box
+            const uint8_t *r1 = r0 + (size_t)8 * rs;
+            const uint8_t *xs = smx + (size_t)(seg * spb - sb0) * XSB;
+            const int steps = min(spb, nsb - seg * spb);            // the last segment of a row may be short
+            const int i0 = hs > 1 ? part * steps / hs : 0, i1 = hs > 1 ? (part + 1) * steps / hs : steps;
+            if constexpr (QT == 4) {
+                for (int i = i0; i < i1; i++) {
+                    Sb sb;
+                    load_sb_smem(sb, r0 + i * BB, r1 + i * BB, t);
+                    sb_dot(sb, xs + (size_t)i * XSB, g, t, acc0, acc1);
+                }
+            } else {
+                // steps = spb (8 or 16), a multiple of 2 hs: this part's share starts even
+                for (int i = i0; i < i1; i += 2) {
+                    const uint8_t *q0 = sl + (size_t)(i / MQ_SPB) * 16 * RB + (size_t)sg * RB + (i % MQ_SPB) * BB;
+                    const uint8_t *q1 = q0 + (size_t)8 * RB;
+                    sb6_dot<false>(q0, q1, xs + (size_t)i * XSB, g, t, acc0, acc1);
+                    sb6_dot<true>(q0 + BB, q1 + BB, xs + (size_t)(i + 1) * XSB, g, t, acc0, acc1);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) bar_arrive(empty0 + 8 * slot);               // the slot's bytes are read
+        // the quad's four shares of rows g and g+8
+        acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 1);
+        acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 1);
+        acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 2);
+        acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 2);
+        // two buffers per owner, so that the next unit's sums never overwrite
+        // these before part 0 has read them (it must pass the next barrier first)
+        if (hs > 1 && !meet(acc0, acc1, cmb + ((size_t)owner * 2 + (seq++ & 1)) * hs * 16, part, hs, 2 + owner, sg))
+            continue;
+        emit(acc0, acc1, seg, tile, sg);
     }
 }
 
@@ -603,8 +730,9 @@ int g_mv_mma = 1;          // 1 (default): Q4_K matvec on this kernel where it a
 int g_mv_mma_segs = 0;     // tuning hook: K segments per tile (0: chosen per shape)
 int g_mv_early = 0;        // 1: the caller's weights are never written by the kernel before a matvec
 int g_mv_slots = 0;        // tuning hook: most unit slots per CTA (0: as many as shared memory holds)
-int g_mv_split = 1;        // tuning hook: 0 keeps one warp per Q6_K unit
+int g_mv_split = 1;        // tuning hook: warps per unit (1: by shape, 0: one, 2 or 4)
 int g_mv_tiles = -1;       // tuning hook: 1 whole tiles per CTA, 0 segment-major ranges, -1 by shape
+int g_mv_direct = 1;       // tuning hook: 0 refills slots instead of reading the units past them directly
 
 // Tiles from which whole tiles go to each CTA (tile-major, no global
 // partial sums): six per SM at least, so that shares differ by 1/6 at most
@@ -732,7 +860,13 @@ static bool launch_matvec_mma(float *y, const void *W, const float *x, int N, in
     // whole tiles per CTA (their segments summed in shared memory) where a
     // row has several segments and the tiles spread over every SM
     const int tm = S > 1 && (g_mv_tiles == 1 || (g_mv_tiles < 0 && tiles >= mm_tile_major_min(sms))) ? 1 : 0;
-    const int G = tm ? (tiles < sms ? tiles : sms) : (int)(U < sms ? U : sms);
+    // With the static-weights promise each matvec lets the next be scheduled
+    // as its CTAs retire, and the next one's last CTA gets the SM of this
+    // one's last CTA only after this grid has completed: it starts ~2 us
+    // late and ends last (measured per CTA, Q4_K 4096 x 14336 back to back).
+    // One CTA fewer than SMs leaves an SM for that CTA instead.
+    const int gmax = sms - (QT == 4 && g_mv_early && sms > 1 ? 1 : 0);
+    const int G = tm ? (tiles < gmax ? tiles : gmax) : (int)(U < gmax ? U : gmax);
     // the most superblocks of x, and units, one CTA holds
     int nsl_max = 0, units_max = 0, tiles_max = 0;
     for (int c = 0; c < G; c++) {
@@ -755,31 +889,48 @@ static bool launch_matvec_mma(float *y, const void *W, const float *x, int N, in
     const size_t cap = 232448;                                   // the most dynamic shared memory of a CTA
     const size_t x_bytes = ((size_t)nsl_max * XSB + 127) & ~(size_t)127;
     const size_t slot = (size_t)16 * rs;
-    // combine buffers: <= 8 owners x 2 x 4 parts (Q6_K whole rows); tm: the
-    // tiles' partial sums (at most two parts per segment) and counters
-    const size_t cmb_bytes = (QT == 6 ? 8 * 2 * 4 * 16 * 4 : 0) + (tm ? (size_t)tiles_max * (S * 2 * 16 + 1) * 4 : 0);
-    if (x_bytes + 2 * (slot + 16) + 16 + cmb_bytes > cap) return true;   // not two slots: the CUDA-core kernels
-    int nslot = (int)((cap - x_bytes - 16 - cmb_bytes) / (slot + 16));
-    if (g_mv_slots >= 2 && nslot > g_mv_slots) nslot = g_mv_slots;
-    // Consumers: nwork warps taking units in turn. A reused slot must belong
-    // to one warp, so then nslot is a multiple of nwork.
-    int nwork;
-    if (nslot >= units_max) {
-        nslot = units_max;                                       // every unit its own slot
-        nwork = nslot < MM_WARPS ? nslot : MM_WARPS;
-    } else if (nslot >= MM_WARPS) {
-        nslot -= nslot % MM_WARPS;
-        nwork = MM_WARPS;
-    } else {
-        nwork = nslot;
-    }
-    // Q6_K units are long (16 rows x 8 or 16 superblocks of 210 bytes) and
-    // few fit: two or four warps per slot, four superblocks each at least,
-    // where the warps allow (a whole-row unit's parts meet in shared memory)
+    // combine buffers: the parts' sums (hs > 1 or direct units); tm: the
+    // tiles' partial sums (one per K segment) and counters
+    const size_t tm_bytes = tm ? (size_t)tiles_max * (S * 16 + 1) * 4 : 0;
+    const auto slots_for = [&](size_t cmb) {
+        if (x_bytes + 2 * (slot + 16) + 16 + cmb > cap) return 0;
+        int n = (int)((cap - x_bytes - 16 - cmb) / (slot + 16));
+        if (g_mv_slots >= 2 && n > g_mv_slots) n = g_mv_slots;
+        return n < units_max ? n : units_max;                    // at most every unit its own slot
+    };
+    int nslot = slots_for(tm_bytes);
+    if (!nslot) return true;                                     // not two slots: the CUDA-core kernels
+    // hs warps (parts) per unit, a share of its superblocks each, their sums
+    // met in shared memory (two buffers per owner). Q6_K units are long and
+    // few fit: two or four parts of four superblocks at least, while the
+    // warps allow. Q4_K keeps one warp per unit: measured back to back
+    // (4096 x 14336), two parts ran 14.6 us and four 17.1 against 12.8; the
+    // parts' barriers and uneven shares cost more than they save. Then
+    // owners = min(nslot, MM_WARPS / hs) groups of hs warps take the slots.
     int hs = 1;
-    if (QT == 6 && g_mv_split)
-        while (hs < 4 && 2 * hs * nwork <= MM_WARPS && spb / (2 * hs) >= 4 && (S == 1 || hs < 2)) hs *= 2;
-    nwork *= hs;
+    if (g_mv_split == 2 || g_mv_split == 4) {
+        hs = g_mv_split;
+    } else if (g_mv_split && QT == 6) {
+        const int o = nslot < MM_WARPS ? nslot : MM_WARPS;
+        while (hs < 4 && 2 * hs * o <= MM_WARPS && spb / (2 * hs) >= 4) hs *= 2;
+    }
+    // direct (Q4_K): the units past the slots, at most three per CTA and
+    // three superblocks per idle warp, go to the consumer warps the slots
+    // leave idle, read from global memory, so that no slot is refilled: a
+    // refill waits for its slot's whole first unit to be consumed, and the
+    // CTA's last unit then starts late (measured back to back, 4096 x 14336:
+    // 13.0 -> 11.2 us; with 24 superblocks on 5 warps, 14336 x 4096, 13.0 ->
+    // 13.8 us)
+    const bool direct_try = QT == 4 && g_mv_direct && hs == 1 && units_max > nslot && units_max - nslot <= 3 &&
+                            nslot < MM_WARPS && (units_max - nslot) * spb <= 3 * (MM_WARPS - nslot);
+    const size_t cmb_bytes = tm_bytes + (hs > 1 || direct_try ? MM_CMB_FLOATS * 4 : 0);
+    if (hs > 1 || direct_try) nslot = slots_for(cmb_bytes);
+    if (!nslot) return true;
+    const int owners = nslot < MM_WARPS / hs ? nslot : MM_WARPS / hs;
+    const int nwork = owners * hs;
+    const int direct =
+        direct_try && nwork < MM_WARPS && units_max - nslot <= 3 && (units_max - nslot) * spb <= 3 * (MM_WARPS - nwork)
+            ? 1 : 0;
     const size_t smem = x_bytes + (size_t)nslot * slot + (size_t)nslot * 16 + 16 + cmb_bytes;
     float *ws = nullptr;
     int *cnt = nullptr;
@@ -787,7 +938,7 @@ static bool launch_matvec_mma(float *y, const void *W, const float *x, int N, in
         MmBuf &b = g_mm[ctx().device & 63];
         const int cnt_cap = tiles > b.cnt_cap ? tiles : b.cnt_cap;
         const size_t cnt_bytes = ((size_t)cnt_cap * 4 + 255) & ~(size_t)255;
-        const size_t need = cnt_bytes + (size_t)S * hs * N * 4;
+        const size_t need = cnt_bytes + (size_t)S * N * 4;
         if (need > b.bytes || cnt_cap > b.cnt_cap) {
             if (b.p) {
                 TCG_CUDA(cudaStreamSynchronize(ctx().cur));
@@ -849,7 +1000,8 @@ static bool launch_matvec_mma(float *y, const void *W, const float *x, int N, in
     }
     const uint32_t sigma = QT == 4 ? mm_sigma(rs) : mm_sigma_identity();
     TCG_CUDA(launch_pdl(mv_kq_mma_kernel<QT>, dim3(G), dim3(MM_THREADS), smem, ctx().cur, mp.map, x, y, N, nsb, spb,
-                        S, tiles, U, ws, cnt, nslot, nwork, hs, tm, sigma, (int)x_bytes, g_mv_early, ctx().d_err));
+                        S, tiles, U, ws, cnt, nslot, nwork, hs, tm, sigma, (int)x_bytes, g_mv_early, W, direct,
+                        ctx().d_err));
     *used = true;
     return true;
 }
@@ -909,13 +1061,23 @@ extern "C" int tcg_matvec_mma_slots(int n)
     return old;
 }
 
-// Tuning hook: 1 (default) lets two warps share a Q6_K unit (four
-// superblocks each) when the slots leave warps idle; 0 keeps one warp per
-// unit. Returns the previous setting.
-extern "C" int tcg_matvec_mma_split(int on)
+// Tuning hook: warps per unit of the integer-MMA matvec. 1 (default)
+// chooses by type and shape, 0 keeps one warp per unit, 2 or 4 sets it.
+// Returns the previous setting.
+extern "C" int tcg_matvec_mma_split(int mode)
 {
     const int old = tcg::g_mv_split;
-    tcg::g_mv_split = on ? 1 : 0;
+    tcg::g_mv_split = mode == 2 || mode == 4 ? mode : mode ? 1 : 0;
+    return old;
+}
+
+// Tuning hook: 1 (default) lets the idle consumer warps of the Q4_K
+// integer-MMA matvec read the few units past a CTA's slots from global
+// memory; 0 refills the slots instead. Returns the previous setting.
+extern "C" int tcg_matvec_mma_direct(int on)
+{
+    const int old = tcg::g_mv_direct;
+    tcg::g_mv_direct = on ? 1 : 0;
     return old;
 }
 

@@ -157,6 +157,7 @@ def case_matvec(a):
     old_static = L.tcg_matvec_set_static_weights(a.static_weights)
     old_split = L.tcg_matvec_mma_split(a.split)
     old_tiles = L.tcg_matvec_mma_tiles(a.tiles)
+    old_direct = L.tcg_matvec_mma_direct(a.direct)
     # back to back: the matrix rotates over enough copies that each launch
     # reads from HBM, not L2 (as in a decode pass over successive layers)
     copies = max(1, min(10, -(-(300 << 20) // raw.nbytes)))
@@ -191,6 +192,7 @@ def case_matvec(a):
     L.tcg_matvec_set_static_weights(old_static)
     L.tcg_matvec_mma_split(old_split)
     L.tcg_matvec_mma_tiles(old_tiles)
+    L.tcg_matvec_mma_direct(old_direct)
     nbytes = a.N * a.K // 256 * bb + 4 * (a.N + a.K)
     return {"case": "matvec", "type": a.type, "N": a.N, "K": a.K, "kernel": kern, "ms": round(ms, 5),
             "bytes": nbytes, "GB/s": round(nbytes / ms / 1e6, 1), "b2b_ms": round(b2b, 5),
@@ -323,9 +325,10 @@ def main():
     mv.add_argument("--tc", type=int, default=0, help="1: Q4_K on the tensor cores (opt-in kernel)")
     mv.add_argument("--mma", type=int, default=1, help="0: Q4_K on the CUDA-core kernels")
     mv.add_argument("--segs", type=int, default=0, help="K segments per tile of the mma kernel (0: automatic)")
-    mv.add_argument("--split", type=int, default=1, help="0: one warp per Q6_K unit of the mma kernel")
+    mv.add_argument("--split", type=int, default=1, help="warps per unit of the mma kernel: 1 by shape, 0 one, 2, 4")
     mv.add_argument("--tiles", type=int, default=-1,
                     help="mma kernel: 1 whole tiles per CTA, 0 segment-major unit ranges, -1 by shape")
+    mv.add_argument("--direct", type=int, default=1, help="0: refill slots instead of direct units (Q4_K mma)")
     mv.add_argument("--delay", type=int, default=500,
                     help="us of device delay queued before each back-to-back sequence (0: none)")
     mv.add_argument("--static-weights", type=int, default=0,

@@ -354,6 +354,45 @@ def test_matvec_mma_tile_modes(gpu, mode, qt, N, K):
     assert np.abs(got.astype(np.float64) - want).max() / np.abs(want).max() <= MATVEC_TOL
 
 
+def _q4k_vs_oracle(N, K, seed, hook, mode):
+    L = tcg.lib()
+    raw = G.make_kquant(G.Q4_K, N, K, seed=seed)
+    x = _x_cases(K, seed + 1)["wide"]
+    old = hook(mode)
+    try:
+        got = dev_matvec(raw, x, N, K, G.Q4_K, repeat=3)
+        assert L.tcg_matvec_last_kernel() == 5
+    finally:
+        hook(old)
+    want = oracle.matvec_q(raw, x, N, K, G.Q4_K).astype(np.float64)
+    assert np.abs(got.astype(np.float64) - want).max() / np.abs(want).max() <= MATVEC_TOL
+
+
+@pytest.mark.parametrize("direct", [0, 1])
+@pytest.mark.parametrize("N,K", [(4096, 14336), (4090, 14336), (14336, 4096), (14330, 4096)])
+def test_matvec_q4k_direct_units(gpu, direct, N, K):
+    """The few units past a CTA's slots read from global memory by the idle
+    consumer warps (after L2 and L1 prefetches), or the slots refilled:
+    segment-major (4096 x 14336) and tile-major (14336 x 4096) ranges, ragged
+    last tiles; each against the oracle, three calls giving the same bits."""
+    _q4k_vs_oracle(N, K, 21 + N, tcg.lib().tcg_matvec_mma_direct, direct)
+
+
+@pytest.mark.parametrize("static", [0, 1])
+@pytest.mark.parametrize("N,K", [(4096, 14336), (4090, 14336)])
+def test_matvec_q4k_static_grid(gpu, static, N, K):
+    """With the static-weights promise the Q4_K matvec runs one CTA fewer
+    than SMs (other unit ranges, direct units): against the oracle."""
+    _q4k_vs_oracle(N, K, 41 + N, tcg.lib().tcg_matvec_set_static_weights, static)
+
+
+@pytest.mark.parametrize("split", [2, 4])
+@pytest.mark.parametrize("N,K", [(4096, 14336), (14336, 4096), (4095, 11008)])
+def test_matvec_q4k_parts(gpu, split, N, K):
+    """Two or four warps per Q4_K unit (their sums met in shared memory)."""
+    _q4k_vs_oracle(N, K, 31 + N, tcg.lib().tcg_matvec_mma_split, split)
+
+
 @pytest.mark.parametrize("static", [0, 1])
 def test_matvec_decode_chain(gpu, static):
     """A decode-like chain on one stream, each matvec reading the one before
