@@ -158,6 +158,7 @@ def case_matvec(a):
     old_split = L.tcg_matvec_mma_split(a.split)
     old_tiles = L.tcg_matvec_mma_tiles(a.tiles)
     old_direct = L.tcg_matvec_mma_direct(a.direct)
+    old_slots = L.tcg_matvec_mma_slots(a.slots)
     # back to back: the matrix rotates over enough copies that each launch
     # reads from HBM, not L2 (as in a decode pass over successive layers)
     copies = max(1, min(10, -(-(300 << 20) // raw.nbytes)))
@@ -193,6 +194,7 @@ def case_matvec(a):
     L.tcg_matvec_mma_split(old_split)
     L.tcg_matvec_mma_tiles(old_tiles)
     L.tcg_matvec_mma_direct(old_direct)
+    L.tcg_matvec_mma_slots(old_slots)
     nbytes = a.N * a.K // 256 * bb + 4 * (a.N + a.K)
     return {"case": "matvec", "type": a.type, "N": a.N, "K": a.K, "kernel": kern, "ms": round(ms, 5),
             "bytes": nbytes, "GB/s": round(nbytes / ms / 1e6, 1), "b2b_ms": round(b2b, 5),
@@ -328,6 +330,7 @@ def main():
     mv.add_argument("--split", type=int, default=1, help="warps per unit of the mma kernel: 1 by shape, 0 one, 2, 4")
     mv.add_argument("--tiles", type=int, default=-1,
                     help="mma kernel: 1 whole tiles per CTA, 0 segment-major unit ranges, -1 by shape")
+    mv.add_argument("--slots", type=int, default=0, help="most unit slots per CTA of the mma kernel (0: all that fit)")
     mv.add_argument("--direct", type=int, default=1, help="0: refill slots instead of direct units (Q4_K mma)")
     mv.add_argument("--delay", type=int, default=500,
                     help="us of device delay queued before each back-to-back sequence (0: none)")
