@@ -689,7 +689,8 @@ mha64s_kernel(const float *__restrict__ q, const float *__restrict__ k, const fl
 // scaling by a power of two is exact and is undone on the fp32 accumulators.
 // Pieces: x = p1 + p2 + r, p1 = x rounded to 11 bits (exact in fp16), p2 =
 // fp16(x - p1); |r| <= 2^-23 |x|, the precision of a tf32 pair. Q K^T takes the
-// four products p1k1, p1k2, p2k1, p2k2 and P V the three p1v1, p1v2, p2v1.
+// three products p1k1, p1k2, p2k1 and P V the three p1v1, p1v2, p2v1 (the
+// fourth, p2 p2, is below 2^-24 of the product: under fp32's own rounding).
 // The fp32 accumulation of an MMA truncates relative to its largest addend,
 // so each accumulator sums every cross product (2^-11 of the result and
 // less) over all keys or dims first and the four p1 p1 steps last: four
@@ -929,7 +930,6 @@ mha64m_kernel(const float *__restrict__ q, const float *__restrict__ k, const fl
                 for (int h = 0; h < 2; h++) {           // kk = 2p + h: B registers 2h, 2h + 1
                     const int kk = 2 * p + h, x = 2 * h, y = 2 * h + 1;
                     if (pass == 0) {
-                        mham_mma(s[j], qa[1][kk], bk[1][x], bk[1][y]);
                         mham_mma(s[j], qa[0][kk], bk[1][x], bk[1][y]);
                         mham_mma(s[j], qa[1][kk], bk[0][x], bk[0][y]);
                     } else {
