@@ -184,7 +184,8 @@ __device__ __forceinline__ void mma_commit_pair_local(uint32_t bar)
 enum { ACC_SEP = 0, ACC_FOLD = 1, ACC_WIDE = 2 };
 
 // OPF 1: the operands are fp16 pieces (2 bytes per element, BK = 64 fills a
-// 128-byte swizzled row) for kind::f16 MMAs, scaled per 128-element K-block.
+// 128-byte swizzled row, BK = 32 a 64-byte one) for kind::f16 MMAs, scaled
+// per 128- or 256-element K-block.
 template <int BN, int BK, int STAGES, int EPI_W = 8, int ACC = ACC_SEP, int CG = 1, int QB = 0, int OPF = 0>
 struct Shape {
     static constexpr int ES = OPF ? 2 : 4;                      // bytes per operand element
@@ -209,7 +210,9 @@ struct Shape {
     static_assert(ACC != ACC_WIDE || (2 * BN <= 256 && CG == 1), "a wide MMA is at most 256 columns, one CTA");
     static_assert(SMEM <= 232448, "shared memory per block");
     static_assert(QB == 0 || (BN == 128 && BK == 32 && CG == 1), "packed B: 128 rows x one 32-weight sub-block");
-    static_assert(OPF == 0 || (ACC == ACC_WIDE && BK == 64 && QB == 0), "fp16 pieces: the wide shape, BK = 64");
+    static_assert(OPF == 0 || (QB == 0 && ((ACC == ACC_WIDE && (BK == 64 || BK == 32)) ||
+                                           (ACC == ACC_FOLD && CG == 2 && BK == 64))),
+                  "fp16 pieces: the wide shape (BK = 64 or 32), or a CTA pair folded (BK = 64)");
 };
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, const float (&v)[4])
@@ -251,6 +254,20 @@ __device__ __forceinline__ void drain_add2_scaled(uint32_t ta, uint32_t tb, floa
     }
 }
 
+// drain_add for fp16-piece operands with one chunk buffer: the HALF columns
+// at taddr times fa = 2^-ea (the row's K-block scale undone) added to acc.
+template <int HALF>
+__device__ __forceinline__ void drain_add_scaled(uint32_t taddr, float (&acc)[HALF], float fa)
+{
+#pragma unroll
+    for (int j = 0; j < HALF; j += 8) {
+        uint32_t x[8];
+        tmem_ld8(taddr + (uint32_t)j, x);
+#pragma unroll
+        for (int i = 0; i < 8; i++) acc[j + i] = fmaf(__uint_as_float(x[i]), fa, acc[j + i]);
+    }
+}
+
 // acc[j] *= 2^-xb[n0 + j]: B row (output column) n was scaled by 2^xb[n] over
 // all of K. |xb| <= 63 and the row factors are at most 2^63, so the partial
 // sums stay finite and both multiplications are exact.
@@ -262,6 +279,22 @@ __device__ __forceinline__ void scale_cols(float (&acc)[HALF], const int8_t *xb,
     for (int j = 0; j < HALF; j += 8) {
         uint2 e8 = make_uint2(0u, 0u);
         if (n0 + j + 8 <= N) e8 = *reinterpret_cast<const uint2 *>(xb + n0 + j);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int eb = (int)(int8_t)(((i < 4 ? e8.x : e8.y) >> (8 * (i & 3))) & 0xFFu);
+            acc[j + i] = __fmul_rn(acc[j + i], __int_as_float((127 - ea - eb) << 23));
+        }
+    }
+}
+
+// scale_cols with the column exponents already in registers (8 per uint2,
+// zero past N)
+template <int HALF>
+__device__ __forceinline__ void scale_cols_r(float (&acc)[HALF], const uint2 (&xbr)[HALF / 8], int ea)
+{
+#pragma unroll
+    for (int j = 0; j < HALF; j += 8) {
+        const uint2 e8 = xbr[j / 8];
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             const int eb = (int)(int8_t)(((i < 4 ? e8.x : e8.y) >> (8 * (i & 3))) & 0xFFu);
@@ -827,7 +860,11 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                             const unsigned long long bl = sdesc<SWB>(base + 2 * S::A_BYTES + S::B_BYTES + off);
                             const uint32_t acc0 = (kb > kb0 || k > 0) ? 1u : 0u;
                             const uint32_t acc1 = (!SEP || kb > ks0 || k > 0) ? 1u : 0u;
-                            if constexpr (OPF) {
+                            if constexpr (OPF && CG == 2) {
+                                mma_f16_pair(db, ah, bh, id, acc0);       // hi*hi, then the small terms
+                                mma_f16_pair(db, al, bh, id, 1u);
+                                mma_f16_pair(db, ah, bl, id, 1u);
+                            } else if constexpr (OPF) {
                                 mma_f16(db, ah, bh, id_wide, acc0);       // [hi*hi | hi*lo]
                                 mma_f16(db, al, bh, id, 1u);              // + lo*hi
                             } else if constexpr (WIDE) {
@@ -888,15 +925,36 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                 const int cc = 32 * i + lane, nn = (sg.tile % n_tiles) * BN + h * S::HALF + cc;
                 breg[i] = epi.tma && epi.bias && cc < S::HALF && nn < N ? epi.bias[nn] : 0.0f;
             }
+            // fp16 pieces: this warp's column exponents and the first chunk's
+            // row exponent now, each next chunk's during the drain before it,
+            // so that no load waits in the drain or the column scaling
+            uint2 xbr[OPF ? S::HALF / 8 : 1];
+            int ea_next = 0;
+            const int mrow = (sg.tile / n_tiles) * CG * BM + (int)rank * BM + q * 32 + lane;
+            if constexpr (OPF) {
+                const int nx = (sg.tile % n_tiles) * BN + h * S::HALF;
+#pragma unroll
+                for (int j = 0; j < S::HALF / 8; j++)
+                    xbr[j] = nx + 8 * j + 8 <= N ? *reinterpret_cast<const uint2 *>(epi.xb + nx + 8 * j)
+                                                 : make_uint2(0u, 0u);
+                if (epi.xa_blk && mrow < M) ea_next = (int)epi.xa[(size_t)sg.c0 * M + mrow];
+            }
             for (int c = sg.c0; c < sg.c1; c++, chunk++) {
                 const uint32_t b = chunk % NBUF;
+                const int ea = ea_next;                    // this chunk's row exponent (fp16 pieces)
+                if (OPF && epi.xa_blk && c + 1 < sg.c1 && mrow < M) ea_next = (int)epi.xa[(size_t)(c + 1) * M + mrow];
                 if (!bar_wait(cfull0 + 8 * b, (chunk / NBUF) & 1, abort, err, 6)) { ok = false; break; }
                 fence_after();
-                if constexpr (OPF) {
+                if constexpr (OPF && !WIDE) {
                     if (epi.xa_blk) {
                         // this chunk is one K-block of A: undo the row's scale of the block
-                        const int m = (sg.tile / n_tiles) * BM + q * 32 + lane;
-                        const int ea = m < M ? (int)epi.xa[(size_t)c * M + m] : 0;
+                        drain_add_scaled<S::HALF>(tmem + lane_cols + b * CW, acc, __int_as_float((127 - ea) << 23));
+                    } else {
+                        drain_add<S::HALF, S::LDW>(tmem + lane_cols + b * CW, acc);
+                    }
+                } else if constexpr (OPF) {
+                    if (epi.xa_blk) {
+                        // this chunk is one K-block of A: undo the row's scale of the block
                         drain_add2_scaled<S::HALF>(tmem + lane_cols + b * CW, tmem + lane_cols + b * CW + BN, acc,
                                                    __int_as_float((127 - ea) << 23));
                     } else {
@@ -957,7 +1015,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
             const int m0 = (sg.tile / n_tiles) * CG * BM + (int)rank * BM, n0 = (sg.tile % n_tiles) * BN;
             if constexpr (OPF) {
                 const int m = m0 + q * 32 + lane;
-                scale_cols<S::HALF>(acc, epi.xb, n0 + h * S::HALF, N, epi.xa_blk || m >= M ? 0 : (int)epi.xa[m]);
+                scale_cols_r<S::HALF>(acc, xbr, epi.xa_blk || m >= M ? 0 : (int)epi.xa[m]);
                 if (epi.out.fh) {
                     if (epi.tma)
                         epi_store_f16_tma<S::HALF>(epi, acc, epi_stage + ew * (S::EPI_STAGE_BYTES / 4), &o_hi, &o_lo,
@@ -1114,19 +1172,20 @@ bool encode_kmajor(CUtensorMap *m, const float *ptr, int rows, int K, int box_ro
     return true;
 }
 
-// fp16-piece operand: rows x K fp16, K-major, boxes of 64 elements (one
-// 128-byte swizzled row) x box_rows.
-bool encode_kmajor_f16(CUtensorMap *m, const void *ptr, int rows, int K, int box_rows)
+// fp16-piece operand: rows x K fp16, K-major, boxes of box_k elements (64:
+// one 128-byte swizzled row; 32: one 64-byte swizzled row) x box_rows.
+bool encode_kmajor_f16(CUtensorMap *m, const void *ptr, int rows, int K, int box_rows, int box_k)
 {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return fail("cuTensorMapEncodeTiled is not available from the driver");
     if (((uintptr_t)ptr & 15) || (K & 7)) return fail("fp16 GEMM operand not 16-byte aligned / K=%d not a multiple of 8", K);
     cuuint64_t dims[2] = { (cuuint64_t)K, (cuuint64_t)rows };
     cuuint64_t strides[1] = { (cuuint64_t)K * 2u };
-    cuuint32_t box[2] = { 64u, (cuuint32_t)box_rows };
+    cuuint32_t box[2] = { (cuuint32_t)box_k, (cuuint32_t)box_rows };
     cuuint32_t estr[2] = { 1, 1 };
+    const CUtensorMapSwizzle swz = box_k == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)ptr, dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail("cuTensorMapEncodeTiled failed (%d) for fp16 [%d x %d]", (int)r, rows, K);
     return true;
@@ -1183,6 +1242,10 @@ struct Cfg {
     { BN, BK, ST, Shape<BN, BK, ST, EW, ACC, 1, QB>::SMEM,                                                  \
       (const void *)gemm_tf32x3_kernel<BN, BK, ST, EW, ACC, 1, QB>, 1, Shape<BN, BK, ST, EW, ACC, 1, QB>::THREADS, \
       ACC == ACC_SEP, EW, QB }
+#define TCG_CFG_F16P(BN, BK, ST, EW)                                                                        \
+    { BN, BK, ST, Shape<BN, BK, ST, EW, ACC_FOLD, 2, 0, 1>::SMEM,                                           \
+      (const void *)gemm_tf32x3_kernel<BN, BK, ST, EW, ACC_FOLD, 2, 0, 1>, 2,                               \
+      Shape<BN, BK, ST, EW, ACC_FOLD, 2, 0, 1>::THREADS, false, EW, 0, 1 }
 #define TCG_CFG_F16(BN, BK, ST, EW)                                                                         \
     { BN, BK, ST, Shape<BN, BK, ST, EW, ACC_WIDE, 1, 0, 1>::SMEM,                                           \
       (const void *)gemm_tf32x3_kernel<BN, BK, ST, EW, ACC_WIDE, 1, 0, 1>, 1,                               \
@@ -1197,10 +1260,14 @@ const Cfg CFGS[] = {
     TCG_CFG(128, 32, 3, 16, ACC_WIDE, 1), TCG_CFG(128, 32, 3, 8, ACC_WIDE, 1),
     TCG_CFG_Q(128, 32, 3, 8, ACC_WIDE, GGML_TYPE_Q4_K),                  // B in Q4_K blocks (15)
     TCG_CFG_F16(128, 64, 3, 16),                                          // fp16 pieces, kind::f16 (16)
+    TCG_CFG_F16(128, 32, 6, 16),                                          // the same, six 32-element stages (17)
+    TCG_CFG_F16P(256, 64, 3, 16),                                         // fp16 pieces, CTA pair, 256 x 256 (18)
+    TCG_CFG_F16P(128, 64, 4, 16),                                         // fp16 pieces, CTA pair, 256 x 128 (19)
 };
 #undef TCG_CFG
 #undef TCG_CFG_Q
 #undef TCG_CFG_F16
+#undef TCG_CFG_F16P
 constexpr int CFG_Q4K = 15;
 constexpr int CFG_F16 = 16;
 constexpr int NCFG = sizeof(CFGS) / sizeof(CFGS[0]);
@@ -1262,7 +1329,9 @@ int gemm_cfg_bn(int cfg) { return cfg >= 0 && cfg < NCFG ? CFGS[cfg].bn : 0; }
 
 int gemm_q4k_cfg() { return CFG_Q4K; }
 
-int gemm_f16_cfg() { return CFG_F16; }
+// The fp16-piece configuration the ViT and the fp16 entry points plan with
+int g_f16_cfg = CFG_F16;
+int gemm_f16_cfg() { return g_f16_cfg; }
 
 size_t gemm_work_ws_floats(int ctas) { return (size_t)ctas * BM * 256; }
 size_t gemm_work_flag_count(int ctas) { return (size_t)ctas * 16; }
@@ -1314,8 +1383,9 @@ bool gemm_plan(GemmPlan &p, const float *a_hi, const float *a_lo, const float *b
             (epi.out.fh && (!epi.out.fl || !epi.out.fe || !epi.rnorm || !epi.bounds || epi.out.ld % 8 ||
                             epi.out.plain || epi.out.hi)))
             return fail("gemm_plan: fp16-piece operands need K %% 128 == 0, N %% 8 == 0 and both exponent arrays");
-        if (!encode_kmajor_f16(&p.a_hi, a_hi, M, K, BM) || !encode_kmajor_f16(&p.a_lo, a_lo, M, K, BM) ||
-            !encode_kmajor_f16(&p.b_hi, b_hi, N, K, b_rows) || !encode_kmajor_f16(&p.b_lo, b_lo, N, K, b_rows))
+        if (!encode_kmajor_f16(&p.a_hi, a_hi, M, K, BM, c.bk) || !encode_kmajor_f16(&p.a_lo, a_lo, M, K, BM, c.bk) ||
+            !encode_kmajor_f16(&p.b_hi, b_hi, N, K, b_rows, c.bk) ||
+            !encode_kmajor_f16(&p.b_lo, b_lo, N, K, b_rows, c.bk))
             return false;
     } else if (c.qb) {
         // B comes packed: no B tensor maps (the A ones fill the unused parameters)
@@ -1609,9 +1679,22 @@ bool tcg_linear_f16_split(float *y, const void *x_hi, const void *x_lo, const in
     GemmPlan p;
     const GemmWork *w = ctx_gemm_work();
     if (!w || !gemm_plan(p, (const float *)x_hi, (const float *)x_lo, (const float *)w_hi, (const float *)w_lo, M, N,
-                         K, e, CFG_F16, w))
+                         K, e, gemm_f16_cfg(), w))
         return false;
     return gemm_run(p, ctx().cur, ctx().d_err);
+}
+
+// Tuning hook: the fp16-piece GEMM configuration that ViT plans and
+// tcg_linear_f16_split use afterwards: 16 (default) three stages of 64
+// K-elements, 17 six stages of 32, 18 and 19 a CTA pair on 256 x 256 and
+// 256 x 128 tiles (the three products folded into one accumulator). Other
+// values only read the setting.
+// Returns the previous one.
+extern "C" int tcg_gemm_set_f16_cfg(int cfg)
+{
+    const int old = tcg::g_f16_cfg;
+    if (cfg >= 16 && cfg <= 19) tcg::g_f16_cfg = cfg;
+    return old;
 }
 
 // Tuning and test hook: 0 keeps every GEMM epilogue on plain stores, 1

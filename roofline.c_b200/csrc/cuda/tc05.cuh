@@ -97,6 +97,15 @@ __device__ __forceinline__ void mma_f16(uint32_t d, unsigned long long a, unsign
                  ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc));
 }
 
+// the same over a CTA pair (the leader issues; M = 256, B halves in both CTAs)
+__device__ __forceinline__ void mma_f16_pair(uint32_t d, unsigned long long a, unsigned long long b, uint32_t id,
+                                             uint32_t acc)
+{
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+                 ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc));
+}
+
 __device__ __forceinline__ void mma_commit(uint32_t bar)
 {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");

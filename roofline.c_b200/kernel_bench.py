@@ -100,6 +100,7 @@ class F16Operands(SplitOperands):
 def case_gemm(a):
     old_sk = tcg.lib().tcg_gemm_set_streamk(a.streamk)
     old_tma = tcg.lib().tcg_gemm_set_tma_store(a.tma_store)
+    old_f16 = tcg.lib().tcg_gemm_set_f16_cfg(a.f16_cfg)
     ops = F16Operands(a.M, a.N, a.K, blk=a.f16) if a.f16 else SplitOperands(a.M, a.N, a.K)
     with tcg.DeviceBuffer(256 << 20) as flush:
         ms, _ = timed(lambda: ops.run(a.cfg), a.warmup, a.reps, flush)
@@ -109,8 +110,10 @@ def case_gemm(a):
     ops.close()
     tcg.lib().tcg_gemm_set_streamk(old_sk)
     tcg.lib().tcg_gemm_set_tma_store(old_tma)
+    tcg.lib().tcg_gemm_set_f16_cfg(old_f16)
     flops = 2.0 * a.M * a.N * a.K
-    return {"case": "gemm", "M": a.M, "N": a.N, "K": a.K, "cfg": a.cfg, "f16": a.f16, "rel_err": err,
+    return {"case": "gemm", "M": a.M, "N": a.N, "K": a.K, "cfg": a.cfg, "f16": a.f16, "f16_cfg": a.f16_cfg,
+            "rel_err": err,
             "streamk": a.streamk, "ms": round(ms, 4),
             "tflops": round(flops / ms / 1e9, 1), "grid": plan[0], "split": plan[1], "tma_store": plan[3]}
 
@@ -226,6 +229,7 @@ def case_vit(a):
             G.write_kquant_vit_gguf(path + ".tmp", cfg, seed=0)
             os.replace(path + ".tmp", path)
     old_jit = L.tcg_vit_set_jit_rows(a.jit_rows) if a.jit_rows else None
+    old_f16 = L.tcg_gemm_set_f16_cfg(a.f16_cfg)
     # the GEMM plans of a batch size are made at its first forward
     old_cfg, old_sk = L.tcg_gemm_force_cfg(a.cfg), L.tcg_gemm_set_streamk(a.streamk)
     old_pdl = L.tcg_set_pdl(a.pdl)
@@ -246,7 +250,8 @@ def case_vit(a):
         L.tcg_gemm_set_chunk_k(old_chunk)
     if old_jit is not None:
         L.tcg_vit_set_jit_rows(old_jit)
-    return {"case": "vit", "chunk": a.chunk, "q4k": a.q4k, "jit_rows": a.jit_rows, "model": a.model, "layers": cfg["n_layer"], "batch": a.batch, "cfg": a.cfg,
+    L.tcg_gemm_set_f16_cfg(old_f16)
+    return {"case": "vit", "f16_cfg": a.f16_cfg, "chunk": a.chunk, "q4k": a.q4k, "jit_rows": a.jit_rows, "model": a.model, "layers": cfg["n_layer"], "batch": a.batch, "cfg": a.cfg,
             "streamk": a.streamk, "pdl": a.pdl, "tma_store": a.tma_store, "ms": round(ms, 4),
             "images/s": round(a.batch / ms * 1e3, 1)}
 
@@ -315,6 +320,7 @@ def main():
     g.add_argument("--cfg", type=int, default=-1)
     g.add_argument("--streamk", type=int, default=1)
     g.add_argument("--tma-store", type=int, default=1)
+    g.add_argument("--f16-cfg", type=int, default=16, help="fp16-piece GEMM configuration: 16 or 17")
     g.add_argument("--f16", type=int, default=0,
                    help="128 or 256: fp16-piece operands on kind::f16 MMAs, A scaled per K-block of that size")
     gs = sub.add_parser("gemmsweep")
@@ -350,6 +356,7 @@ def main():
     v.add_argument("--pdl", type=int, default=1, help="0: no programmatic dependent launch")
     v.add_argument("--tma-store", type=int, default=1, help="0: GEMM epilogues on plain stores")
     v.add_argument("--chunk", type=int, default=0, help="K-elements per TMEM accumulator chunk (0: default)")
+    v.add_argument("--f16-cfg", type=int, default=16, help="fp16-piece GEMM configuration: 16 or 17")
     v.add_argument("--q4k", type=int, default=0, help="1: the model with Q4_K block linears (kept packed)")
     v.add_argument("--jit-rows", type=int, default=0,
                    help="token rows from which packed weights are dequantised before their GEMMs (0: default)")

@@ -152,7 +152,7 @@ _SIGS = [
     ("tcg_set_attention_variant", i32, [i32]), ("tcg_set_attention_short_kernel", i32, [i32]),
     ("tcg_matvec_last_kernel", i32, []), ("tcg_matvec_set_tc", i32, [i32]),
     ("tcg_matvec_set_mma", i32, [i32]), ("tcg_matvec_mma_segments", i32, [i32]),
-    ("tcg_matvec_set_static_weights", i32, [i32]), ("tcg_matvec_mma_slots", i32, [i32]), ("tcg_matvec_mma_direct", i32, [i32]),
+    ("tcg_matvec_set_static_weights", i32, [i32]), ("tcg_matvec_mma_slots", i32, [i32]), ("tcg_gemm_set_f16_cfg", i32, [i32]), ("tcg_matvec_mma_direct", i32, [i32]),
     ("tcg_matvec_mma_split", i32, [i32]), ("tcg_matvec_mma_tiles", i32, [i32]),
     ("tcg_split_tf32", boolean, [vp, vp, vp, sz]),
     ("tcg_test_gemm_withhold_flags", boolean, [i32, C.c_double]), ("tcg_gemm_throughput_cfg", i32, []),

@@ -291,10 +291,11 @@ def test_mha_tensor_core_long(dev, T, H):
     assert L.tcg_device_error() == 0
 
 
+@pytest.mark.parametrize("cfg", [16, 17, 18, 19])
 @pytest.mark.parametrize("blk", [128, 256])
 @pytest.mark.parametrize("M,N,K", [(128, 128, 256), (300, 768, 768), (1600, 768, 768), (257, 3072, 768),
                                    (513, 768, 3072), (12800, 768, 768)])
-def test_linear_f16_pieces(dev, M, N, K, blk):
+def test_linear_f16_pieces(dev, M, N, K, blk, cfg):
     """kind::f16 GEMM on fp16-piece operands (tcg_split_f16: power-of-two
     scales per (row, 128-element K-block) of x and per row of W, two pieces of
     11 bits): within
@@ -315,8 +316,12 @@ def test_linear_f16_pieces(dev, M, N, K, blk):
     tcg.check(L.tcg_split_f16(f[0].ptr, f[1].ptr, f[2].ptr, xd, M, K, 0 if blk == 128 else 2))
     tcg.check(L.tcg_split_f16(f[3].ptr, f[4].ptr, f[5].ptr, Wd, N, K, 1))
     y = dev.empty(M * N)
-    tcg.check(L.tcg_linear_f16_split(y.ptr, f[0].ptr, f[1].ptr, f[2].ptr, f[3].ptr, f[4].ptr, f[5].ptr, bd,
-                                     M, N, K, blk))
+    old = L.tcg_gemm_set_f16_cfg(cfg)           # 16: 3 stages of 64, 17: 6 of 32, 18/19: CTA pairs
+    try:
+        tcg.check(L.tcg_linear_f16_split(y.ptr, f[0].ptr, f[1].ptr, f[2].ptr, f[3].ptr, f[4].ptr, f[5].ptr, bd,
+                                         M, N, K, blk))
+    finally:
+        L.tcg_gemm_set_f16_cfg(old)
     got = y.download((M, N)).astype(np.float64)
     want = x.astype(np.float64) @ W.astype(np.float64).T + b
     # each row band against its own magnitude (the rows differ by 24 decades)
