@@ -211,8 +211,8 @@ struct Shape {
     static_assert(SMEM <= 232448, "shared memory per block");
     static_assert(QB == 0 || (BN == 128 && BK == 32 && CG == 1), "packed B: 128 rows x one 32-weight sub-block");
     static_assert(OPF == 0 || (QB == 0 && ((ACC == ACC_WIDE && (BK == 64 || BK == 32)) ||
-                                           (ACC == ACC_FOLD && CG == 2 && BK == 64))),
-                  "fp16 pieces: the wide shape (BK = 64 or 32), or a CTA pair folded (BK = 64)");
+                                           (ACC == ACC_FOLD && BK == 64))),
+                  "fp16 pieces: the wide shape (BK = 64 or 32), or the three products folded (BK = 64)");
 };
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, const float (&v)[4])
@@ -864,6 +864,10 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_consta
                                 mma_f16_pair(db, ah, bh, id, acc0);       // hi*hi, then the small terms
                                 mma_f16_pair(db, al, bh, id, 1u);
                                 mma_f16_pair(db, ah, bl, id, 1u);
+                            } else if constexpr (OPF && !WIDE) {
+                                mma_f16(db, ah, bh, id, acc0);            // hi*hi, then the small terms
+                                mma_f16(db, al, bh, id, 1u);
+                                mma_f16(db, ah, bl, id, 1u);
                             } else if constexpr (OPF) {
                                 mma_f16(db, ah, bh, id_wide, acc0);       // [hi*hi | hi*lo]
                                 mma_f16(db, al, bh, id, 1u);              // + lo*hi
@@ -1246,6 +1250,10 @@ struct Cfg {
     { BN, BK, ST, Shape<BN, BK, ST, EW, ACC_FOLD, 2, 0, 1>::SMEM,                                           \
       (const void *)gemm_tf32x3_kernel<BN, BK, ST, EW, ACC_FOLD, 2, 0, 1>, 2,                               \
       Shape<BN, BK, ST, EW, ACC_FOLD, 2, 0, 1>::THREADS, false, EW, 0, 1 }
+#define TCG_CFG_F16F(BN, BK, ST, EW)                                                                        \
+    { BN, BK, ST, Shape<BN, BK, ST, EW, ACC_FOLD, 1, 0, 1>::SMEM,                                           \
+      (const void *)gemm_tf32x3_kernel<BN, BK, ST, EW, ACC_FOLD, 1, 0, 1>, 1,                               \
+      Shape<BN, BK, ST, EW, ACC_FOLD, 1, 0, 1>::THREADS, false, EW, 0, 1 }
 #define TCG_CFG_F16(BN, BK, ST, EW)                                                                         \
     { BN, BK, ST, Shape<BN, BK, ST, EW, ACC_WIDE, 1, 0, 1>::SMEM,                                           \
       (const void *)gemm_tf32x3_kernel<BN, BK, ST, EW, ACC_WIDE, 1, 0, 1>, 1,                               \
@@ -1263,11 +1271,13 @@ const Cfg CFGS[] = {
     TCG_CFG_F16(128, 32, 6, 16),                                          // the same, six 32-element stages (17)
     TCG_CFG_F16P(256, 64, 3, 16),                                         // fp16 pieces, CTA pair, 256 x 256 (18)
     TCG_CFG_F16P(128, 64, 4, 16),                                         // fp16 pieces, CTA pair, 256 x 128 (19)
+    TCG_CFG_F16F(128, 64, 3, 16),                                         // fp16 pieces, products folded (20)
 };
 #undef TCG_CFG
 #undef TCG_CFG_Q
 #undef TCG_CFG_F16
 #undef TCG_CFG_F16P
+#undef TCG_CFG_F16F
 constexpr int CFG_Q4K = 15;
 constexpr int CFG_F16 = 16;
 constexpr int NCFG = sizeof(CFGS) / sizeof(CFGS[0]);
@@ -1687,13 +1697,14 @@ bool tcg_linear_f16_split(float *y, const void *x_hi, const void *x_lo, const in
 // Tuning hook: the fp16-piece GEMM configuration that ViT plans and
 // tcg_linear_f16_split use afterwards: 16 (default) three stages of 64
 // K-elements, 17 six stages of 32, 18 and 19 a CTA pair on 256 x 256 and
-// 256 x 128 tiles (the three products folded into one accumulator). Other
-// values only read the setting.
+// 256 x 128 tiles (the three products folded into one accumulator), 20 one
+// CTA with the three products folded (four chunk buffers). Other values only
+// read the setting.
 // Returns the previous one.
 extern "C" int tcg_gemm_set_f16_cfg(int cfg)
 {
     const int old = tcg::g_f16_cfg;
-    if (cfg >= 16 && cfg <= 19) tcg::g_f16_cfg = cfg;
+    if (cfg >= 16 && cfg <= 20) tcg::g_f16_cfg = cfg;
     return old;
 }
 

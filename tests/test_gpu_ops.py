@@ -291,7 +291,7 @@ def test_mha_tensor_core_long(dev, T, H):
     assert L.tcg_device_error() == 0
 
 
-@pytest.mark.parametrize("cfg", [16, 17, 18, 19])
+@pytest.mark.parametrize("cfg", [16, 17, 18, 19, 20])
 @pytest.mark.parametrize("blk", [128, 256])
 @pytest.mark.parametrize("M,N,K", [(128, 128, 256), (300, 768, 768), (1600, 768, 768), (257, 3072, 768),
                                    (513, 768, 3072), (12800, 768, 768)])

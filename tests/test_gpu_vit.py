@@ -428,13 +428,14 @@ def test_fp16_piece_and_tf32_pair_gemms(gpu, cache_dir, n_img):
 def test_fp16_piece_gemm_configurations(gpu, cache_dir):
     """The fp16-piece ViT forward with each fp16 GEMM configuration (128 x 128
     tiles with three stages of 64 K-elements or six of 32; CTA pairs on 256 x
-    256 or 256 x 128 tiles): against the default and the oracle."""
+    256 or 256 x 128 tiles; the three products folded): against the default
+    and the oracle."""
     L = tcg.lib()
     path, cfg = model(cache_dir, "vit-b32", n_layer=2)
     n_img = 64
     px = G.make_pixels(n_img, cfg["image"], 13)
     outs = {}
-    for c in (16, 17, 18, 19):
+    for c in (16, 17, 18, 19, 20):
         old = L.tcg_gemm_set_f16_cfg(c)
         m = tcg.VitModel(path)
         try:
@@ -446,7 +447,7 @@ def test_fp16_piece_gemm_configurations(gpu, cache_dir):
             L.tcg_gemm_set_f16_cfg(old)
     port = oracle.PortVit(cfg, G.make_vit_weights(cfg, 0))
     refs = {i: port.forward(px[i])["embedding"] for i in (0, n_img - 1)}
-    for c in (17, 18, 19):
+    for c in (17, 18, 19, 20):
         for i in range(n_img):
             assert rel_inf(outs[c][i], outs[16][i]) <= 1e-5, (c, i)
         for i in refs:
